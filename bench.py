@@ -1,0 +1,388 @@
+#!/usr/bin/env python
+"""Benchmark of the Holmes linear hot path on B200.
+
+Workload (one "step"): one encrypted 4096 x 4096 complex weight page applied to the 16 input ciphertexts of a
+128-token prefill -- the QKV projection of one Llama-3-8B layer in the reference's feature-major layout
+(llama3fhe/operators/linear/prefill/qkv_kernel.py:678-940: 8 complex FM pairs and their conjugates, 8 token
+lanes, one page) -- through ``LinearOperator.apply`` with the production schedule (baby 64, 8 chunks of
+8 giants, llama3fhe/operators/linear/config.py:123-134), the production CKKS parameters (N = 2^16,
+59/60-bit primes, depth 37, dnum 5 -> alpha 8, K 8; llama3fhe/parallel/presets.py:63-127) at the linear
+entry level of 13 limbs (parallel/prefill/stations.py:190).  Every step rebuilds the 64-rotation baby
+basis, re-encodes all 4096 diagonal rows online (pack -> special FFT -> round -> NTT) and rescales, as the
+reference does per projection.  Weights ~ N(0, 0.02^2) (complex), pre-multiplied by a seeded +-1 Walsh-
+Hadamard rotation (QuaRot); inputs ~ N(0, 1); all synthetic and seeded.
+
+Multi-GPU (torchrun): the 16 inputs are token-sharded over the ranks (16 / W each), as the reference's
+feature-major token ownership does (parallel/prefill/ownership.py:1-44); no data-path collective.
+
+``--impl reference`` times the CPU restatement of the same path (``oracle/``) on the host cores, on a bounded
+sample scaled to one page.  EasyFHE, the reference's engine, is not distributed with the reference and
+cannot run here.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "encrypted Llama-3-8B prefill-128 linear page latency (QKV page: 16 ciphertexts x 4096x4096)"
+UNIT = "s"
+LOG_N, DEPTH, DNUM, DCRT, FIRST = 16, 37, 5, 59, 60
+CUR_LIMBS = 13
+DIM, LANES, INPUTS = 4096, 8, 16
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json"), encoding="utf-8") as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+# ----------------------------------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int) -> None:
+        self.device_index = device_index
+        self.lines: list[str] = []
+        self.proc = None
+        self.thread = None
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device_index}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self) -> None:
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------------------------------- workload
+def hadamard_rotation(dim: int, seed: int) -> np.ndarray:
+    """Seeded +-1 diagonal times the normalised Walsh-Hadamard matrix (QuaRot-style rotation)."""
+    from scipy.linalg import hadamard
+
+    rng = np.random.default_rng(seed)
+    signs = rng.choice([-1.0, 1.0], size=dim)
+    return (hadamard(dim).astype(np.float64) / np.sqrt(dim)) * signs[None, :]
+
+
+def make_weight(seed: int = 1) -> np.ndarray:
+    rng = np.random.default_rng(seed)
+    w = rng.normal(scale=0.02, size=(DIM, DIM)) + 1j * rng.normal(scale=0.02, size=(DIM, DIM))
+    return w @ hadamard_rotation(DIM, seed + 1)
+
+
+def make_inputs(n_inputs: int, seed: int = 0) -> np.ndarray:
+    """FM-packed complex carriers: slot(d, t) = d * 8 + t, z = x_even + i x_odd (and conjugates)."""
+    rng = np.random.default_rng(seed)
+    x = rng.normal(size=(n_inputs, LANES, DIM)) + 1j * rng.normal(size=(n_inputs, LANES, DIM))
+    return np.ascontiguousarray(x.transpose(0, 2, 1).reshape(n_inputs, DIM * LANES))
+
+
+def spec_for(cur_limbs: int):
+    from holmes_b200 import fhe as F
+    from holmes_b200 import linear as LN
+
+    cfg = LN.LLAMA3_LINEAR_SCHEDULES.qkv
+    rots = LN.linear_rotations(dimension=DIM, token_lanes=LANES, operator_config=cfg)
+    return F.CKKSContextSpec(depth=DEPTH, log_n=LOG_N, dnum=DNUM, dcrt_bits=DCRT, first_mod=FIRST, special_bits=60,
+                             hamming_weight=192, seed=0, rotations=tuple(rots), auto_load_keys=False,
+                             rotation_key_limb_limits={int(r): cur_limbs for r in rots}), cfg, rots
+
+
+def run_engine(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from holmes_b200 import _lib
+    from holmes_b200 import fhe as F
+    from holmes_b200 import linear as LN
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+    n_inputs = args.inputs
+    mine = list(range(rank * n_inputs // world, (rank + 1) * n_inputs // world))
+    cur = args.limbs
+    spec, cfg, rots = spec_for(cur)
+    client, ctx = F.generate_client_context(spec, f"cuda:{local}")
+    session = LN.Session(client, ctx)
+    ctx.generate_rotation_keys(rots, cur)
+    level = ctx.L - cur
+    weight = make_weight()
+    carriers = make_inputs(n_inputs)
+    cts = [session.encrypt(carriers[i], level=level, counter=i) for i in mine]
+    op = LN.LinearOperator(crypto_context=session, token_lanes=LANES, config=cfg)
+    lw = LN.LinearWeight(weight, dtype=np.complex128, crypto_context=session)
+    lw.prepare(cfg)
+    torch.cuda.synchronize()
+
+    def step():
+        op.clear_baby_cache()
+        outs, _ = op.apply(cts, lw)
+        return outs
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    count0 = _lib.ctypes.c_ulonglong()
+    _lib.call("holmes_launch_count", _lib.ctypes.byref(count0))
+    F.OPTIMER.reset()
+    F.OPTIMER.enabled = True
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record()
+    for _ in range(args.steps):
+        outs = step()
+    end.record()
+    torch.cuda.synchronize()
+    F.OPTIMER.enabled = False
+    count1 = _lib.ctypes.c_ulonglong()
+    _lib.call("holmes_launch_count", _lib.ctypes.byref(count1))
+    clocks = sampler.stop()
+    ms = start.elapsed_time(end) / args.steps
+    ops = F.OPTIMER.summary()
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        dist.barrier()
+
+    # ---- end to end through the public API: inputs and weight from pinned host memory, outputs back
+    host_in = [torch.stack([c.cv[0][0], c.cv[1][0]]).cpu().pin_memory() for c in cts]
+    host_w = torch.from_numpy(np.ascontiguousarray(weight)).pin_memory()
+    out_bytes = 0
+
+    def e2e_step():
+        nonlocal out_bytes
+        dev_in = []
+        for h in host_in:
+            d = h.to(ctx.device, non_blocking=True)
+            dev_in.append(F.Cipher([d[0:1], d[1:2]], cts[0].state, cts[0].slots, False, 1, ctx))
+        w_dev = host_w.to(ctx.device, non_blocking=True)
+        with LN.LinearWeight(w_dev, dtype=np.complex128, crypto_context=session) as lw2:
+            with LN.LinearOperator(crypto_context=session, token_lanes=LANES, config=cfg) as op2:
+                res, _ = op2.apply(dev_in, lw2)
+        back = [torch.stack([r.cv[0][0], r.cv[1][0]]).to("cpu", non_blocking=True) for r in res]
+        out_bytes = sum(b.numel() * 8 for b in back)
+        return back
+
+    e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    in_bytes = sum(h.numel() * 8 for h in host_in) + host_w.numel() * 16
+
+    # ---- a parity spot check of this run's output (decrypted vs NumPy), outside all timing
+    check = None
+    if rank == 0 and args.check:
+        dec = session.decrypt(outs[0]).reshape(DIM, LANES)
+        x = carriers[mine[0]].reshape(DIM, LANES)
+        check = float(np.abs(dec - weight @ x).max())
+
+    if rank == 0:
+        hbm, kind = peaks()
+        dominant = max(ops.items(), key=lambda kv: kv[1]["ms"]) if ops else None
+        roofline = None
+        if dominant:
+            name, d = dominant
+            per_launch_s = d["ms"] / 1e3 / d["launches"]
+            achieved = d["bytes"] / d["launches"] / per_launch_s / 1e9
+            roofline = {"bound": "hbm", "kernel": name, "achieved": round(achieved, 1), "peak": hbm,
+                        "peak_kind": kind, "unit": "GB/s", "frac": round(achieved / hbm, 4), "traffic": None,
+                        "algorithmic_bytes_per_launch": d["bytes"] // d["launches"],
+                        "avg_launch_ms": round(d["ms"] / d["launches"], 4),
+                        "share_of_step": round(d["ms"] / args.steps / ms, 4)}
+        cpu = None
+        if args.cpu_baseline:
+            cpu = cpu_baseline(sample=args.cpu_sample)
+        line = {
+            "metric": METRIC, "value": round(ms / 1e3, 5), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 3), "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "u64 (RNS residues, 59/60-bit primes)", "data": "synthetic (seeded)",
+            "config": {"workload": f"QKV-shaped linear page: {n_inputs} ciphertexts x one 4096x4096 complex page, "
+                                   f"N=2^16, {cur}/{DEPTH + 1} limbs, dnum {DNUM} (alpha {ctx.alpha}, K {ctx.K}), "
+                                   f"baby 64, 8 chunks x 8 giants, lanes 8, rescale",
+                       "parallelism": f"token-sharded x{world}", "inputs_per_rank": len(mine),
+                       "l2": "working set (plaintext chunks 3.4 GB, baby basis 13.6 GB) >> 126 MB L2",
+                       "keys": f"{len(rots)} rotation keys capped at {cur} limbs"},
+            "roofline": roofline, "kernels": {k: {"launches": v["launches"], "ms_per_step": round(v["ms"] / args.steps, 3)}
+                                              for k, v in ops.items()},
+            "cpu_baseline": cpu, "clocks": clocks,
+            "e2e": {"value": round(e2e_ms / 1e3, 5), "unit": UNIT, "h2d_bytes_per_step": in_bytes,
+                    "d2h_bytes_per_step": out_bytes},
+            "gpu_launches": int(count1.value - count0.value) // args.steps,
+            "parity_check_max_abs_err": check,
+        }
+        print(json.dumps(line), flush=True)
+    lw.close()
+    op.close()
+    ctx.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ----------------------------------------------------------------------------------------------------- CPU leg
+def cpu_baseline(sample: str = "small") -> dict:
+    """Time the CPU restatement (oracle/) on a bounded sample of the page and scale it to one page.
+
+    Sample: 8 diagonal rows encoded at 13 limbs, their MAC against one input's 8 babies, and 2 hoisted baby
+    key switches + 1 Horner giant key switch; the page is 4096 rows x 16 inputs, 16 x 63 baby and
+    16 x (8 x 7 + 7) giant / alignment key switches.
+    """
+    os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
+    from oracle.oracle import Oracle, OracleParams
+
+    cores = int(os.environ["OMP_NUM_THREADS"])
+    pr = OracleParams(log_n=LOG_N, limbs=DEPTH + 1, dnum=DNUM, dcrt_bits=DCRT, first_mod_bits=FIRST, special_bits=60,
+                      hamming=192, seed=0)
+    o = Oracle(pr)
+    cur = CUR_LIMBS
+    rng = np.random.default_rng(0)
+    rows = 8
+    z = rng.normal(scale=0.02, size=(rows, pr.n // 2)) + 1j * rng.normal(scale=0.02, size=(rows, pr.n // 2))
+    t0 = time.perf_counter()
+    pts = np.stack([o.encode(z[r], cur) for r in range(rows)])
+    t_enc = (time.perf_counter() - t0) / rows
+    ct = o.encrypt(rng.normal(size=pr.n // 2), cur, counter=0)
+    babies = [(ct[0], ct[1])] * rows
+    t0 = time.perf_counter()
+    o.bsgs_mac(pts, babies, 1)
+    t_mac = (time.perf_counter() - t0) / rows
+    o.rotation_key(o.galois(8), cap=cur)
+    o.rotation_key(o.galois(16), cap=cur)
+    o.rotation_key(o.galois(512), cap=cur)
+    t0 = time.perf_counter()
+    digits = o.modup(ct[1])
+    t_modup = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    o.rotate(ct, 8, digits=digits, cap=cur)
+    o.rotate(ct, 16, digits=digits, cap=cur)
+    t_hoisted = (time.perf_counter() - t0) / 2
+    t0 = time.perf_counter()
+    o.rotate(ct, 512, cap=cur)
+    t_rot = time.perf_counter() - t0
+    page = (4096 * t_enc + 4096 * INPUTS * t_mac + INPUTS * (t_modup + 63 * t_hoisted)
+            + INPUTS * (8 * 7 + 7) * t_rot)
+    return {"value": round(page, 2), "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": "8 rows encoded + MAC'd at N=2^16 / 13 limbs, 1 ModUp, 2 hoisted + 1 full key switch; "
+                      "scaled to 4096 rows x 16 inputs, 16x63 baby and 16x63 giant/alignment key switches",
+            "per_op_s": {"encode_row": round(t_enc, 4), "mac_row_input": round(t_mac, 4), "modup": round(t_modup, 4),
+                         "hoisted_ks": round(t_hoisted, 4), "rotation": round(t_rot, 4)}}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    for _ in range(args.warmup):
+        pass
+    vals = []
+    cpu = None
+    for _ in range(max(1, args.steps)):
+        cpu = cpu_baseline()
+        vals.append(cpu["value"])
+    v = statistics.median(vals)
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": UNIT, "n_gpus": int(os.environ.get("WORLD_SIZE", "1")),
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "u64 (RNS residues)", "data": "synthetic (seeded)",
+            "config": {"workload": "QKV-shaped linear page (CPU restatement of the reference path; EasyFHE itself "
+                                   "is not distributed and cannot run here)"},
+            "cpu_baseline": {**cpu, "value": v},
+            "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("holmes", "reference"), default="holmes")
+    ap.add_argument("--inputs", type=int, default=INPUTS)
+    ap.add_argument("--limbs", type=int, default=CUR_LIMBS)
+    ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--cpu-sample", default="small")
+    ap.add_argument("--no-check", dest="check", action="store_false")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_engine(args)
+
+
+if __name__ == "__main__":
+    main()

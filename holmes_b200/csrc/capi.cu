@@ -1,0 +1,225 @@
+// extern "C" entry points of libholmes_cuda (declared in include/holmes_cuda.h).
+#include "../../include/holmes_cuda.h"
+#include "ops.h"
+
+using namespace holmes;
+
+namespace holmes {
+int build_context(HolmesCtx& c, int log_n, int limbs, int dnum, int dcrt_bits, int first_mod_bits, int special_bits,
+                  int special_limbs, int hamming, u64 seed);
+void free_context(HolmesCtx& c);
+}  // namespace holmes
+
+static inline cudaStream_t S(void* s) { return (cudaStream_t)s; }
+static inline HolmesCtx* C(void* c) { return (HolmesCtx*)c; }
+
+extern "C" {
+
+int holmes_ctx_create(const holmes_params* p, void** ctx_out) {
+  if (!p || !ctx_out) return -1;
+  HolmesCtx* c = new HolmesCtx();
+  int rc = build_context(*c, p->log_n, p->limbs, p->dnum, p->dcrt_bits, p->first_mod_bits, p->special_bits,
+                         p->special_limbs, p->hamming, p->seed);
+  if (!rc) rc = secret_ntt(*c, 0);
+  if (rc) {
+    free_context(*c);
+    delete c;
+    return rc;
+  }
+  *ctx_out = c;
+  return 0;
+}
+
+int holmes_ctx_destroy(void* ctx) {
+  if (!ctx) return -1;
+  free_context(*C(ctx));
+  delete C(ctx);
+  return 0;
+}
+
+int holmes_ctx_moduli(void* ctx, uint64_t* out) {
+  if (!ctx || !out) return -1;
+  for (int i = 0; i < C(ctx)->T; ++i) out[i] = C(ctx)->q[i];
+  return 0;
+}
+
+int holmes_ctx_dims(void* ctx, int* out) {
+  if (!ctx || !out) return -1;
+  const HolmesCtx& c = *C(ctx);
+  out[0] = c.log_n;
+  out[1] = c.L;
+  out[2] = c.K;
+  out[3] = c.alpha;
+  out[4] = c.dnum;
+  out[5] = c.beta_max;
+  return 0;
+}
+
+int holmes_ctx_secret(void* ctx, void** out) {
+  if (!ctx || !out) return -1;
+  *out = C(ctx)->d_secret;
+  return 0;
+}
+
+int holmes_galois(void* ctx, long long rotation, uint64_t* out) {
+  if (!ctx || !out) return -1;
+  const HolmesCtx& c = *C(ctx);
+  const u64 m = 2ull * (u64)c.n;
+  if (rotation == (long long)(m - 1)) {
+    *out = m - 1;
+    return 0;
+  }
+  const long long half = c.n / 2;
+  long long r = rotation % half;
+  if (r < 0) r += half;
+  u64 g = 1;
+  for (long long i = 0; i < r; ++i) g = (g * 5) % m;
+  *out = g;
+  return 0;
+}
+
+int holmes_key_words(void* ctx, int cap, long long* out) {
+  if (!ctx || !out) return -1;
+  const HolmesCtx& c = *C(ctx);
+  if (cap < 1 || cap > c.L) return -2;
+  *out = 2LL * c.beta(cap) * (cap + c.K) * (long long)c.n;
+  return 0;
+}
+
+int holmes_keygen(void* ctx, uint64_t galois, int cap, uint64_t* key, void* stream) {
+  if (!ctx || !key) return -1;
+  if (galois != 0 && !(galois & 1)) return -3;
+  return keygen(*C(ctx), galois, cap, key, S(stream));
+}
+
+int holmes_encrypt(void* ctx, const uint64_t* m, int cur, uint64_t counter, uint64_t* c0, uint64_t* c1, void* stream) {
+  if (!ctx || !m || !c0 || !c1) return -1;
+  return encrypt(*C(ctx), m, cur, counter, c0, c1, S(stream));
+}
+
+int holmes_decrypt(void* ctx, const uint64_t* c0, const uint64_t* c1, int cur, uint64_t* out, void* stream) {
+  if (!ctx || !c0 || !c1 || !out) return -1;
+  return decrypt_coef(*C(ctx), c0, c1, cur, out, S(stream));
+}
+
+int holmes_ntt(void* ctx, uint64_t* data, int items, int limbs, long long item_stride, int first_mod, int inverse,
+               void* stream) {
+  if (!ctx || !data) return -1;
+  const HolmesCtx& c = *C(ctx);
+  if (items < 1 || limbs < 1 || first_mod < 0 || first_mod + limbs > c.T) return -2;
+  PolyMap pm = poly_map(limbs, item_stride, c.n, first_mod);
+  return ntt_plain(c, data, data, pm, items * limbs, inverse != 0, S(stream));
+}
+
+int holmes_encode(void* ctx, double* z, long long row_stride, int rows, int slots, double scale, int cur, uint64_t* out,
+                  long long out_row_stride, int* flag, void* stream) {
+  if (!ctx || !z || !out || !flag) return -1;
+  if (rows < 1) return 0;
+  int rc = fft_special_inv(*C(ctx), z, row_stride, rows, slots, S(stream));
+  if (rc) return rc;
+  return encode_rows(*C(ctx), z, row_stride, rows, slots, scale, cur, out, out_row_stride, flag, S(stream));
+}
+
+int holmes_fft_special_inv(void* ctx, double* z, long long row_stride, int rows, int slots, void* stream) {
+  if (!ctx || !z) return -1;
+  return fft_special_inv(*C(ctx), z, row_stride, rows, slots, S(stream));
+}
+
+int holmes_encode_fft(void* ctx, const double* u, long long row_stride, int rows, int slots, double scale, int cur,
+                      uint64_t* out, long long out_row_stride, int* flag, void* stream) {
+  if (!ctx || !u || !out || !flag) return -1;
+  if (rows < 1) return 0;
+  return encode_rows(*C(ctx), u, row_stride, rows, slots, scale, cur, out, out_row_stride, flag, S(stream));
+}
+
+int holmes_pack_diagonals(const double* weight, int weight_complex, int dim, int lanes, int baby, int giant_base,
+                          int giant_count, int lane_shift, int slots, double* out, long long row_stride, void* stream) {
+  if (!weight || !out) return -1;
+  return pack_diagonals(weight, weight_complex, dim, lanes, baby, giant_base, giant_count, lane_shift, slots, out,
+                        row_stride, S(stream));
+}
+
+int holmes_elementwise(void* ctx, int op, const uint64_t* a, const uint64_t* b, uint64_t* out, int items, int limbs,
+                       long long a_item, long long b_item, long long out_item, void* stream) {
+  if (!ctx || !a || !out || (op != EW_NEG && !b) || op < 0 || op > 3) return -1;
+  return elementwise(*C(ctx), op, a, b, out, items, limbs, a_item, b_item, out_item, S(stream));
+}
+
+int holmes_mul_i(void* ctx, const uint64_t* a, uint64_t* out, int items, int limbs, long long a_item, long long out_item,
+                 void* stream) {
+  if (!ctx || !a || !out) return -1;
+  return mul_i(*C(ctx), a, out, items, limbs, a_item, out_item, S(stream));
+}
+
+int holmes_automorph(void* ctx, const uint64_t* a, uint64_t* out, uint64_t galois, int items, int limbs,
+                     long long a_item, long long out_item, void* stream) {
+  if (!ctx || !a || !out) return -1;
+  return automorph(*C(ctx), a, out, galois, items, limbs, a_item, out_item, S(stream));
+}
+
+int holmes_mul_const(void* ctx, const uint64_t* a, const uint64_t* consts, uint64_t* out, int items, int limbs,
+                     long long a_item, long long out_item, void* stream) {
+  if (!ctx || !a || !consts || !out) return -1;
+  return mul_const(*C(ctx), a, consts, out, items, limbs, a_item, out_item, S(stream));
+}
+
+int holmes_rescale(void* ctx, const uint64_t* in, long long in_stride, uint64_t* out, long long out_stride, int cur,
+                   int comps, uint64_t* scratch, void* stream) {
+  if (!ctx || !in || !out || !scratch || comps < 1) return -1;
+  return rescale(*C(ctx), in, in_stride, out, out_stride, cur, comps, scratch, S(stream));
+}
+
+int holmes_modup(void* ctx, const uint64_t* c1, long long c1_item, int cur, int items, uint64_t* digits,
+                 long long digit_item, uint64_t* scratch, void* stream) {
+  if (!ctx || !c1 || !digits || !scratch) return -1;
+  return modup(*C(ctx), c1, c1_item, cur, items, digits, digit_item, scratch, S(stream));
+}
+
+int holmes_keyswitch(void* ctx, const uint64_t* digits, long long digit_item, int cur, const uint64_t* key, int key_cap,
+                     uint64_t galois, const uint64_t* add0, const uint64_t* add1, long long add_item,
+                     const uint64_t* post0, const uint64_t* post1, long long post_item, uint64_t* out0, uint64_t* out1,
+                     long long out_item, int items, uint64_t* scratch, void* stream) {
+  if (!ctx || !digits || !key || !out0 || !out1 || !scratch) return -1;
+  if (galois > 1 && !(galois & 1)) return -3;
+  KsArgs a{digits, digit_item, cur,   key,  key_cap,  galois, add0,  add1,    add_item,
+           post0,  post1,      post_item, out0, out1, out_item, items, scratch};
+  return ks_apply(*C(ctx), a, S(stream));
+}
+
+int holmes_bsgs_mac(void* ctx, uint64_t* res, const uint64_t* const* c0s, const uint64_t* const* c1s, long long bstride,
+                    int nb, int inputs, const uint64_t* pts, long long pstride, int groups, int limbs, void* stream) {
+  if (!ctx || !res || !c0s || !c1s || !pts) return -1;
+  const HolmesCtx& c = *C(ctx);
+  if (limbs < 1 || limbs > c.L) return -2;
+  ModSrc ms{c.d_mod, 0, nullptr, nullptr, nullptr};
+  return bsgs_mac(ms, res, c0s, c1s, bstride, nb, inputs, pts, pstride, groups, limbs, c.n, S(stream));
+}
+
+int holmes_modsum(void* ctx, const uint64_t* const* srcs, int nsrc, uint64_t* out, int items, int limbs,
+                  long long item_stride, void* stream) {
+  if (!ctx || !srcs || !out) return -1;
+  return modsum(*C(ctx), srcs, nsrc, out, items, limbs, item_stride, S(stream));
+}
+
+int holmes_launch_count(unsigned long long* out) {
+  if (!out) return -1;
+  *out = launch_counter().load();
+  return 0;
+}
+
+int holmes_mac_multi(uint64_t* res, const uint64_t* const* c0s, const uint64_t* const* c1s, long long bstride, int nb,
+                     int inputs, const uint64_t* pts, long long pstride, int groups, int ti, int limbs,
+                     const uint64_t* primes, const uint64_t* ratios, const uint64_t* ks, void* stream_ptr) {
+  if (inputs < 1 || inputs > 32) return -1;
+  if (nb < 1) return -2;
+  if (groups < 1 || groups > 16) return -3;
+  if (groups > 8 && ti != 10116) return -3;
+  static const int valid[] = {1, 2, 4, 404, 408, 802, 804, 1601, 1602, 10108, 10116, 10204, 10208, 10402, 10404};
+  bool ok = false;
+  for (int v : valid) ok |= (v == ti);
+  if (!ok) return -4;
+  ModSrc ms{nullptr, 0, primes, ratios, ks};
+  return bsgs_mac(ms, res, c0s, c1s, bstride, nb, inputs, pts, pstride, groups, limbs, 1 << 16, S(stream_ptr));
+}
+
+}  // extern "C"

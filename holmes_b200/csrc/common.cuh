@@ -1,0 +1,124 @@
+// Shared types and 64-bit modular arithmetic for libholmes_cuda (sm_100a).
+//
+// Residues are uint64 words of primes q < 2^60 (the reference's 59/60-bit production primes and
+// the ~50-bit sweep primes).  Three reductions are used:
+//   * Shoup multiplication by a constant w with w' = floor(w 2^64 / q): a w - floor(a w' / 2^64) q
+//     lies in [0, 2q) for every a < 2^64;
+//   * Barrett reduction of a 128-bit x with mu = floor(2^k / q), k = floor(log2 q) + 63 (the
+//     reference's ctx.barret_ratio / barret_k convention, bench/cmp/kernels/holmes_mac.cu:23-40):
+//     est = floor(x mu / 2^k) (computed exactly from the top 128 bits of x mu) undershoots
+//     floor(x / q) by less than x / 2^k + 1, so for x < 14 2^k -- e.g. 16 products of canonical
+//     residues with q < 2^60, or 12 products of a 60-bit source residue with a 50-bit target
+//     constant -- the remainder x - est q stays below 16 q < 2^64 and four conditional
+//     subtractions (8q, 4q, 2q, q) make it canonical;
+//   * lazy sums: the forward NTT keeps values in [0, 4q), the inverse in [0, 2q) (Harvey).
+#pragma once
+#include <atomic>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace holmes {
+
+// Kernels launched by this library since load (read through holmes_launch_count).
+inline std::atomic<unsigned long long>& launch_counter() {
+  static std::atomic<unsigned long long> c{0};
+  return c;
+}
+inline void count_launch() { launch_counter().fetch_add(1, std::memory_order_relaxed); }
+
+typedef uint64_t u64;
+typedef int64_t i64;
+typedef uint32_t u32;
+
+// A constant and its Shoup companion, stored together so one 16-byte load fetches both.
+struct __align__(16) Tw {
+  u64 w, ws;
+};
+
+struct Mod {
+  u64 q;      // prime
+  u64 mu;     // floor(2^k / q)
+  u32 shift;  // k - 64 = floor(log2 q) - 1
+  u32 pad;
+};
+
+__device__ __forceinline__ u64 add_mod(u64 a, u64 b, u64 q) {
+  u64 s = a + b;
+  return s >= q ? s - q : s;
+}
+__device__ __forceinline__ u64 sub_mod(u64 a, u64 b, u64 q) { return a >= b ? a - b : a + q - b; }
+
+// Modulus of limb l either from a context table or from the reference's three per-limb arrays
+// (ctx.primes / ctx.barret_ratio / ctx.barret_k, bench/cmp/holmes_multi_mac.py:140-141).
+struct ModSrc {
+  const Mod* mods;
+  int first;
+  const u64* primes;
+  const u64* ratios;
+  const u64* ks;
+  __device__ __forceinline__ Mod get(int limb) const {
+    if (mods) return mods[first + limb];
+    Mod m;
+    m.q = primes[limb];
+    m.mu = ratios[limb];
+    m.shift = (u32)(ks[limb] - 64);
+    m.pad = 0;
+    return m;
+  }
+};
+
+// a * w mod q, result in [0, 2q)
+__device__ __forceinline__ u64 shoup_lazy(u64 a, Tw t, u64 q) {
+  const u64 hi = __umul64hi(a, t.ws);
+  return a * t.w - hi * q;
+}
+__device__ __forceinline__ u64 shoup(u64 a, Tw t, u64 q) {
+  const u64 r = shoup_lazy(a, t, q);
+  return r >= q ? r - q : r;
+}
+
+// 128-bit accumulator helpers
+struct U128 {
+  u64 lo, hi;
+};
+__device__ __forceinline__ void mac128(U128& acc, u64 a, u64 b) {
+  const u64 plo = a * b, phi = __umul64hi(a, b);
+  asm("add.cc.u64 %0, %0, %2;\n\taddc.u64 %1, %1, %3;" : "+l"(acc.lo), "+l"(acc.hi) : "l"(plo), "l"(phi));
+}
+
+// x = hi:lo mod q for x < 14 2^k (see header)
+__device__ __forceinline__ u64 reduce128(u64 hi, u64 lo, const Mod& m) {
+  const u64 t0 = __umul64hi(lo, m.mu);
+  const u64 t1lo = hi * m.mu, t1hi = __umul64hi(hi, m.mu);
+  u64 mid, top;
+  asm("add.cc.u64 %0, %2, %3;\n\taddc.u64 %1, %4, 0;" : "=l"(mid), "=l"(top) : "l"(t0), "l"(t1lo), "l"(t1hi));
+  const u64 est = (mid >> m.shift) | (top << (64 - m.shift));
+  u64 r = lo - est * m.q;
+  const u64 q = m.q;
+  if (r >= (q << 3)) r -= (q << 3);
+  if (r >= (q << 2)) r -= (q << 2);
+  if (r >= (q << 1)) r -= (q << 1);
+  if (r >= q) r -= q;
+  return r;
+}
+__device__ __forceinline__ u64 mul_mod(u64 a, u64 b, const Mod& m) { return reduce128(__umul64hi(a, b), a * b, m); }
+__device__ __forceinline__ u64 reduce128(const U128& x, const Mod& m) { return reduce128(x.hi, x.lo, m); }
+
+// bit reversal of the low `bits` bits
+__device__ __forceinline__ u32 brev_bits(u32 v, int bits) { return __brev(v) >> (32 - bits); }
+
+// Source word of the NTT-domain automorphism X -> X^g: out[k] = in[perm(k)], where word k holds the
+// evaluation at psi^(2 bitrev(k) + 1) (forward NTT with bit-reversed root powers).
+__device__ __forceinline__ u32 automorph_src(u32 k, u64 g, int log_n) {
+  const u32 mask = (2u << log_n) - 1u;
+  const u32 e = (u32)(((2ull * brev_bits(k, log_n) + 1ull) * g) & mask);
+  return brev_bits((e - 1u) >> 1, log_n);
+}
+
+}  // namespace holmes
+
+#define HOLMES_CUDA_TRY(expr)                         \
+  do {                                                \
+    cudaError_t _e = (expr);                          \
+    if (_e != cudaSuccess) return (int)_e;            \
+  } while (0)

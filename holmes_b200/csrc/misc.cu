@@ -1,0 +1,308 @@
+// Kernels that are not NTT-shaped: elementwise RNS arithmetic, the BSGS plaintext multiply-accumulate,
+// the CKKS special FFT of the encoder, diagonal packing, and the mod-q sum of peer partials.
+#include "ops.h"
+
+namespace holmes {
+
+static inline int grid_for(size_t work, int threads) {
+  count_launch();  // every grid_for result feeds exactly one launch
+  size_t b = (work + threads - 1) / threads;
+  if (b > 148 * 16) b = 148 * 16;
+  return (int)(b ? b : 1);
+}
+
+// --------------------------------------------------------------------------------------------- elementwise
+// Two words per thread (16-byte accesses); words of limb l of item i at i * item + l * N.
+__global__ void k_elementwise(int op, const u64* __restrict__ a, const u64* __restrict__ b, u64* __restrict__ o,
+                              int items, int limbs, long long ai, long long bi, long long oi, int log_n,
+                              const Mod* __restrict__ mods) {
+  const size_t per_item = (size_t)limbs << log_n;
+  const size_t total = (size_t)items * per_item / 2;
+  for (size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x; t < total; t += (size_t)gridDim.x * blockDim.x) {
+    const size_t w = 2 * t;
+    const int item = (int)(w / per_item);
+    const size_t r = w - (size_t)item * per_item;
+    const int limb = (int)(r >> log_n);
+    const Mod m = mods[limb];
+    const ulonglong2 x = *reinterpret_cast<const ulonglong2*>(a + item * ai + r);
+    ulonglong2 y = make_ulonglong2(0, 0);
+    if (op != EW_NEG) y = *reinterpret_cast<const ulonglong2*>(b + item * bi + r);
+    ulonglong2 z;
+    switch (op) {
+      case EW_ADD: z = make_ulonglong2(add_mod(x.x, y.x, m.q), add_mod(x.y, y.y, m.q)); break;
+      case EW_SUB: z = make_ulonglong2(sub_mod(x.x, y.x, m.q), sub_mod(x.y, y.y, m.q)); break;
+      case EW_MUL: z = make_ulonglong2(mul_mod(x.x, y.x, m), mul_mod(x.y, y.y, m)); break;
+      default: z = make_ulonglong2(x.x ? m.q - x.x : 0, x.y ? m.q - x.y : 0); break;
+    }
+    *reinterpret_cast<ulonglong2*>(o + item * oi + r) = z;
+  }
+}
+
+int elementwise(const HolmesCtx& c, int op, const u64* a, const u64* b, u64* out, int items, int limbs,
+                long long a_item, long long b_item, long long o_item, cudaStream_t st) {
+  if (limbs < 1 || limbs > c.T || items < 1) return -2;
+  const size_t work = ((size_t)items * limbs * c.n) / 2;
+  k_elementwise<<<grid_for(work, 256), 256, 0, st>>>(op, a, b, out, items, limbs, a_item, b_item, o_item, c.log_n,
+                                                      c.d_mod);
+  return (int)cudaGetLastError();
+}
+
+// multiply by X^(N/2): NTT word k holds the evaluation at psi^(2 bitrev(k)+1), and
+// psi^((2 bitrev(k)+1) N/2) = psi^(N/2) for k < N/2 (bitrev(k) even), -psi^(N/2) above.
+__global__ void k_mul_i(const u64* __restrict__ a, u64* __restrict__ o, int items, int limbs, long long ai,
+                        long long oi, int log_n, const Mod* __restrict__ mods, const Tw* __restrict__ unit,
+                        const Tw* __restrict__ unit_neg) {
+  const size_t per_item = (size_t)limbs << log_n;
+  const size_t total = (size_t)items * per_item;
+  const size_t half = (size_t)1 << (log_n - 1);
+  for (size_t w = blockIdx.x * (size_t)blockDim.x + threadIdx.x; w < total; w += (size_t)gridDim.x * blockDim.x) {
+    const int item = (int)(w / per_item);
+    const size_t r = w - (size_t)item * per_item;
+    const int limb = (int)(r >> log_n);
+    const size_t n = r & (((size_t)1 << log_n) - 1);
+    const u64 q = mods[limb].q;
+    o[item * oi + r] = shoup(a[item * ai + r], n < half ? unit[limb] : unit_neg[limb], q);
+  }
+}
+int mul_i(const HolmesCtx& c, const u64* a, u64* out, int items, int limbs, long long a_item, long long o_item,
+          cudaStream_t st) {
+  if (limbs < 1 || limbs > c.T || items < 1) return -2;
+  const size_t work = (size_t)items * limbs * c.n;
+  k_mul_i<<<grid_for(work, 256), 256, 0, st>>>(a, out, items, limbs, a_item, o_item, c.log_n, c.d_mod, c.d_unit,
+                                                c.d_unit_neg);
+  return (int)cudaGetLastError();
+}
+
+__global__ void k_automorph(const u64* __restrict__ a, u64* __restrict__ o, u64 g, int items, int limbs, long long ai,
+                            long long oi, int log_n) {
+  const size_t per_item = (size_t)limbs << log_n;
+  const size_t total = (size_t)items * per_item;
+  for (size_t w = blockIdx.x * (size_t)blockDim.x + threadIdx.x; w < total; w += (size_t)gridDim.x * blockDim.x) {
+    const int item = (int)(w / per_item);
+    const size_t r = w - (size_t)item * per_item;
+    const size_t row = r >> log_n << log_n;
+    const u32 n = (u32)(r - row);
+    o[item * oi + r] = a[item * ai + row + automorph_src(n, g, log_n)];
+  }
+}
+int automorph(const HolmesCtx& c, const u64* a, u64* out, u64 galois, int items, int limbs, long long a_item,
+              long long o_item, cudaStream_t st) {
+  if (limbs < 1 || items < 1 || !(galois & 1)) return -2;
+  const size_t work = (size_t)items * limbs * c.n;
+  k_automorph<<<grid_for(work, 256), 256, 0, st>>>(a, out, galois, items, limbs, a_item, o_item, c.log_n);
+  return (int)cudaGetLastError();
+}
+
+// multiply limb l by the constant consts[l] (canonical residues)
+__global__ void k_mul_const(const u64* __restrict__ a, const u64* __restrict__ k, u64* __restrict__ o, int items,
+                            int limbs, long long ai, long long oi, int log_n, const Mod* __restrict__ mods) {
+  const size_t per_item = (size_t)limbs << log_n;
+  const size_t total = (size_t)items * per_item;
+  for (size_t w = blockIdx.x * (size_t)blockDim.x + threadIdx.x; w < total; w += (size_t)gridDim.x * blockDim.x) {
+    const int item = (int)(w / per_item);
+    const size_t r = w - (size_t)item * per_item;
+    const int limb = (int)(r >> log_n);
+    o[item * oi + r] = mul_mod(a[item * ai + r], k[limb], mods[limb]);
+  }
+}
+int mul_const(const HolmesCtx& c, const u64* a, const u64* consts, u64* out, int items, int limbs, long long a_item,
+              long long o_item, cudaStream_t st) {
+  if (limbs < 1 || limbs > c.T || items < 1) return -2;
+  const size_t work = (size_t)items * limbs * c.n;
+  k_mul_const<<<grid_for(work, 256), 256, 0, st>>>(a, consts, out, items, limbs, a_item, o_item, c.log_n, c.d_mod);
+  return (int)cudaGetLastError();
+}
+
+// --------------------------------------------------------------------------------------------- BSGS MAC
+// res[c][g][i][limb][j] = sum_b pts[g nb + b][limb][j] * baby_i[b][c][limb][j]  (mod q_limb)
+// (semantics of the reference's mac_multi, bench/cmp/kernels/holmes_mac.cu:1-13, 116-190).
+// Block: 32 consecutive words x 8 inputs; each thread keeps TG giants x 2 components as 128-bit lazy
+// sums (reduced every 16 baby steps: 16 products of canonical residues stay below 14 2^k).  Warps of
+// one block read the same plaintext words, so the plaintext row is fetched from HBM once per block
+// and served from L1 to the other inputs.
+constexpr int kMaxInputs = 32;
+struct InPtrs {
+  const u64* c0[kMaxInputs];
+  const u64* c1[kMaxInputs];
+};
+template <int TG>
+__global__ void __launch_bounds__(256) k_bsgs_mac(u64* __restrict__ res, InPtrs in, long long bstride, int nb,
+                                                  int inputs, int G, const u64* __restrict__ pts, long long pstride,
+                                                  int limbs, ModSrc ms, int log_n) {
+  const int lane = threadIdx.x & 31, wi = threadIdx.x >> 5;
+  const int itiles = (inputs + 7) / 8;
+  const int j = (blockIdx.x / itiles) * 32 + lane;
+  const int i = (blockIdx.x % itiles) * 8 + wi;
+  const int limb = blockIdx.y, g0 = blockIdx.z * TG;
+  if (i >= inputs) return;
+  const Mod m = ms.get(limb);
+  const size_t lj = ((size_t)limb << log_n) + j;
+  const u64* __restrict__ b0 = in.c0[i] + lj;
+  const u64* __restrict__ b1 = in.c1[i] + lj;
+  const u64* pp[TG];
+#pragma unroll
+  for (int g = 0; g < TG; ++g) pp[g] = pts + (size_t)(g0 + g < G ? g0 + g : g0) * nb * pstride + lj;
+  U128 acc[2][TG];
+#pragma unroll
+  for (int g = 0; g < TG; ++g) acc[0][g] = acc[1][g] = U128{0, 0};
+  for (int b = 0; b < nb; ++b) {
+    const u64 v0 = b0[(size_t)b * bstride], v1 = b1[(size_t)b * bstride];
+#pragma unroll
+    for (int g = 0; g < TG; ++g) {
+      const u64 w = __ldg(pp[g] + (size_t)b * pstride);
+      mac128(acc[0][g], v0, w);
+      mac128(acc[1][g], v1, w);
+    }
+    if ((b & 15) == 15) {
+#pragma unroll
+      for (int g = 0; g < TG; ++g) {
+        acc[0][g] = U128{reduce128(acc[0][g], m), 0};
+        acc[1][g] = U128{reduce128(acc[1][g], m), 0};
+      }
+    }
+  }
+  const size_t is = (size_t)limbs << log_n, gs = (size_t)inputs * is;
+#pragma unroll
+  for (int g = 0; g < TG; ++g) {
+    if (g0 + g >= G) break;
+    res[((size_t)0 * G + g0 + g) * gs + (size_t)i * is + lj] = reduce128(acc[0][g], m);
+    res[((size_t)1 * G + g0 + g) * gs + (size_t)i * is + lj] = reduce128(acc[1][g], m);
+  }
+}
+
+int bsgs_mac(ModSrc ms, u64* res, const u64* const* c0s, const u64* const* c1s,
+             long long bstride, int nb, int inputs, const u64* pts, long long pstride, int groups, int limbs, int n,
+             cudaStream_t st) {
+  if (inputs < 1 || inputs > kMaxInputs) return -1;
+  if (nb < 1) return -2;
+  if (groups < 1) return -3;
+  if (n < 1024 || (n & (n - 1))) return -5;
+  int log_n = 0;
+  while ((1 << log_n) < n) ++log_n;
+  InPtrs in;
+  for (int i = 0; i < kMaxInputs; ++i) {
+    in.c0[i] = c0s[i < inputs ? i : 0];
+    in.c1[i] = c1s[i < inputs ? i : 0];
+  }
+  constexpr int TG = 8;
+  dim3 grid((unsigned)((n / 32) * ((inputs + 7) / 8)), (unsigned)limbs, (unsigned)((groups + TG - 1) / TG));
+  count_launch();
+  k_bsgs_mac<TG><<<grid, 256, 0, st>>>(res, in, bstride, nb, inputs, groups, pts, pstride, limbs, ms, log_n);
+  return (int)cudaGetLastError();
+}
+
+// --------------------------------------------------------------------------------------------- special FFT
+// Inverse CKKS embedding of `slots` complex values per row (Cheon-Kim-Kim-Song 2017 "special FFT"):
+// butterfly sweeps len = slots .. 2 with twiddle ksi[(4 len - rot[j] mod 4 len) * M / (4 len)], then
+// bit reversal and a 1 / slots scale.  Every double operation is written out with _rn intrinsics in
+// the same order as the CPU restatement, so both produce identical bits.
+__global__ void k_fft_special_inv(double* __restrict__ z, long long row_stride, int slots, int log_slots,
+                                  const u64* __restrict__ rot, const double* __restrict__ ksi, u64 M) {
+  double2* r = reinterpret_cast<double2*>(z + blockIdx.x * row_stride);
+  for (int len = slots; len >= 2; len >>= 1) {
+    const int half = len >> 1;
+    const u64 lenq = (u64)len << 2, stride = M / lenq;
+    for (int t = threadIdx.x; t < slots / 2; t += blockDim.x) {
+      const int j = t & (half - 1);
+      const int i = (t / half) * len;
+      const u64 k = (lenq - (rot[j] & (lenq - 1))) * stride;
+      const double2 a = r[i + j], b = r[i + j + half];
+      const double wr = ksi[2 * k], wi = ksi[2 * k + 1];
+      const double ur = __dadd_rn(a.x, b.x), ui = __dadd_rn(a.y, b.y);
+      const double vr = __dsub_rn(a.x, b.x), vi = __dsub_rn(a.y, b.y);
+      const double p1 = __dmul_rn(vr, wr), p2 = __dmul_rn(vi, wi), p3 = __dmul_rn(vr, wi), p4 = __dmul_rn(vi, wr);
+      r[i + j] = make_double2(ur, ui);
+      r[i + j + half] = make_double2(__dsub_rn(p1, p2), __dadd_rn(p3, p4));
+    }
+    __syncthreads();
+  }
+  const double inv = 1.0 / (double)slots;
+  for (int i = threadIdx.x; i < slots; i += blockDim.x) {
+    const int j = (int)(__brev((unsigned)i) >> (32 - log_slots));
+    if (i < j) {
+      const double2 a = r[i], b = r[j];
+      r[i] = make_double2(__dmul_rn(b.x, inv), __dmul_rn(b.y, inv));
+      r[j] = make_double2(__dmul_rn(a.x, inv), __dmul_rn(a.y, inv));
+    } else if (i == j) {
+      const double2 a = r[i];
+      r[i] = make_double2(__dmul_rn(a.x, inv), __dmul_rn(a.y, inv));
+    }
+  }
+}
+
+int fft_special_inv(const HolmesCtx& c, double* z, long long row_stride, int rows, int slots, cudaStream_t st) {
+  if (slots < 2 || slots > c.n / 2 || (slots & (slots - 1))) return -3;
+  if (rows < 1) return 0;
+  int log_slots = 0;
+  while ((1 << log_slots) < slots) ++log_slots;
+  const int threads = slots / 2 < 1024 ? (slots / 2 < 32 ? 32 : slots / 2) : 1024;
+  count_launch();
+  k_fft_special_inv<<<rows, threads, 0, st>>>(z, row_stride, slots, log_slots, c.d_rot_group, c.d_ksi,
+                                              2ull * (u64)c.n);
+  return (int)cudaGetLastError();
+}
+
+// --------------------------------------------------------------------------------------------- packing
+// Diagonal rows of one chunk (llama3fhe/operators/linear/weight.py:122-154,
+// gpu_packer.py:157-200): row(g, b)[s] = W[(f - g B) mod D, (f + b + lane_shift lane) mod D],
+// f = s / lanes, lane = s % lanes, g = giant_base + row / B, b = row % B.  Output complex
+// interleaved [rows][slots][2]; a real weight gives zero imaginary parts.
+__global__ void k_pack(const double* __restrict__ w, int cplx, int dim, int lanes, int baby, int giant_base,
+                       int lane_shift, int slots, double* __restrict__ out, long long row_stride) {
+  const int row = blockIdx.y;
+  const int g = giant_base + row / baby, b = row % baby;
+  double2* o = reinterpret_cast<double2*>(out + row * row_stride);
+  for (int s = blockIdx.x * blockDim.x + threadIdx.x; s < slots; s += gridDim.x * blockDim.x) {
+    const int f = s / lanes, lane = s - f * lanes;
+    int of = (f - g * baby) % dim;
+    if (of < 0) of += dim;
+    const int inf = (int)(((long long)f + b + (long long)lane_shift * lane) % dim);
+    const long long idx = (long long)of * dim + inf;
+    o[s] = cplx ? reinterpret_cast<const double2*>(w)[idx] : make_double2(w[idx], 0.0);
+  }
+}
+int pack_diagonals(const double* weight, int weight_complex, int dim, int lanes, int baby, int giant_base,
+                   int giant_count, int lane_shift, int slots, double* out, long long row_stride, cudaStream_t st) {
+  if (dim < 1 || lanes < 1 || baby < 1 || giant_count < 1 || giant_base < 0) return -2;
+  dim3 grid((unsigned)((slots + 255) / 256 < 64 ? (slots + 255) / 256 : 64), (unsigned)(giant_count * baby));
+  count_launch();
+  k_pack<<<grid, 256, 0, st>>>(weight, weight_complex, dim, lanes, baby, giant_base, lane_shift, slots, out,
+                               row_stride);
+  return (int)cudaGetLastError();
+}
+
+// --------------------------------------------------------------------------------------------- mod-q sum
+constexpr int kMaxSrc = 16;
+struct SrcPtrs {
+  const u64* p[kMaxSrc];
+};
+__global__ void k_modsum(SrcPtrs s, int nsrc, u64* __restrict__ out, int items, int limbs, long long item_stride,
+                         int log_n, const Mod* __restrict__ mods) {
+  const size_t per_item = (size_t)limbs << log_n;
+  const size_t total = (size_t)items * per_item / 2;
+  for (size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x; t < total; t += (size_t)gridDim.x * blockDim.x) {
+    const size_t w = 2 * t;
+    const int item = (int)(w / per_item);
+    const size_t r = w - (size_t)item * per_item;
+    const u64 q = mods[r >> log_n].q;
+    const size_t off = item * item_stride + r;
+    u64 a = 0, b = 0;
+    for (int k = 0; k < nsrc; ++k) {
+      const ulonglong2 x = *reinterpret_cast<const ulonglong2*>(s.p[k] + off);
+      a = add_mod(a, x.x, q);
+      b = add_mod(b, x.y, q);
+    }
+    *reinterpret_cast<ulonglong2*>(out + off) = make_ulonglong2(a, b);
+  }
+}
+int modsum(const HolmesCtx& c, const u64* const* srcs, int nsrc, u64* out, int items, int limbs, long long item_stride,
+           cudaStream_t st) {
+  if (nsrc < 1 || nsrc > kMaxSrc) return -2;
+  SrcPtrs s;
+  for (int k = 0; k < kMaxSrc; ++k) s.p[k] = srcs[k < nsrc ? k : 0];
+  const size_t work = ((size_t)items * limbs * c.n) / 2;
+  k_modsum<<<grid_for(work, 256), 256, 0, st>>>(s, nsrc, out, items, limbs, item_stride, c.log_n, c.d_mod);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace holmes

@@ -1,0 +1,730 @@
+// NTT-family kernels: every operation whose cost is dominated by a forward or inverse NTT, with its
+// elementwise pre- and post-processing fused into the NTT's global loads and stores.
+//
+//   plain NTT / iNTT              batched [items][limbs][N]
+//   ModUp                         iNTT(c1) * N^-1 (Q_j/q_k)^-1  ->  per digit: base conversion fused
+//                                 into the forward NTT of every target limb
+//   key switch (hybrid, ModDown)  P limbs: inner product (digits through the automorphism) fused into
+//                                 the iNTT with N^-1 (P/p_k)^-1; Q limbs: base conversion P->q_i fused
+//                                 into the NTT, inner product + subtract + P^-1 + automorphed addend
+//                                 fused into its store
+//   rescale                       iNTT of the last limb; centred reduction fused into the NTT of the
+//                                 other limbs, (c - v) q_last^-1 fused into its store
+//   encode                        llround(v * scale) and the signed reduction fused into the NTT load
+//   decrypt, keygen, encrypt      c0 + c1 s / CBD error sampling fused into the NTT load; the key /
+//                                 ciphertext assembly fused into the store
+#include "ntt.cuh"
+#include "ops.h"
+#include "sampler.cuh"
+
+namespace holmes {
+
+constexpr int MAXA = 16;  // largest digit width (alpha) and special-limb count K supported
+
+#define HOLMES_LOGN_SWITCH(logn, MACRO) \
+  switch (logn) {                       \
+    case 10: MACRO(10);                 \
+    case 11: MACRO(11);                 \
+    case 12: MACRO(12);                 \
+    case 13: MACRO(13);                 \
+    case 14: MACRO(14);                 \
+    case 15: MACRO(15);                 \
+    case 16: MACRO(16);                 \
+    default: return -1;                 \
+  }
+
+// --------------------------------------------------------------------------------------------- functors
+struct LdPlain {
+  const u64* src;
+  PolyMap pm;
+  struct S { const u64* p; };
+  __device__ S prep(int p) const { return S{src + pm.off(p)}; }
+  __device__ u64 load(const S& s, int n) const { return s.p[n]; }
+};
+struct StPlain {
+  u64* dst;
+  PolyMap pm;
+  struct S { u64* p; };
+  __device__ S prep(int p) const { return S{dst + pm.off(p)}; }
+  __device__ void store(const S& s, int n, u64 v) const { s.p[n] = v; }
+};
+
+template <int LOGN>
+__global__ void __launch_bounds__(NttGeom<LOGN>::THREADS) k_fwd_plain(NttTables T, PolyMap pm, LdPlain ld, StPlain st) {
+  const int p = blockIdx.x / NttGeom<LOGN>::CL;
+  ntt_forward_body<LOGN>(p, pm.mod(p), T, ld, st);
+}
+template <int LOGN>
+__global__ void __launch_bounds__(NttGeom<LOGN>::THREADS) k_inv_plain(NttTables T, PolyMap pm, const Tw* scale,
+                                                                       int scale_by_limb, LdPlain ld, StPlain st) {
+  const int p = blockIdx.x / NttGeom<LOGN>::CL;
+  const int mi = pm.mod(p);
+  ntt_inverse_body<LOGN>(p, mi, scale[scale_by_limb ? p % pm.limbs : mi], T, ld, st);
+}
+
+int ntt_plain(const HolmesCtx& c, const u64* src, u64* dst, PolyMap pm, int polys, bool inverse, cudaStream_t st) {
+  NttTables T{inverse ? c.d_itw : c.d_tw, c.d_mod};
+  LdPlain ld{src, pm};
+  StPlain sp{dst, pm};
+#define L_(LG)                                                                                                   \
+  {                                                                                                              \
+    using G = NttGeom<LG>;                                                                                       \
+    return inverse ? (int)launch_ntt(k_inv_plain<LG>, G::LOGCL, G::THREADS, G::SMEM, polys, st, T, pm, c.d_ninv, \
+                                     0, ld, sp)                                                                  \
+                   : (int)launch_ntt(k_fwd_plain<LG>, G::LOGCL, G::THREADS, G::SMEM, polys, st, T, pm, ld, sp);  \
+  }
+  HOLMES_LOGN_SWITCH(c.log_n, L_)
+#undef L_
+}
+
+// --------------------------------------------------------------------------------------------- ModUp
+// Base conversion of one digit's scaled coefficients y_a (a < w) to modulus m: sum_a y_a hat_a mod m.
+// Polynomial p of a digit launch: item p / ntgt, target limb t (the digit's own limbs skipped).
+struct LdConv {
+  const u64* y;      // scratch + lo * N: [items][cur][N], digit limbs from lo
+  long long y_item;
+  const u64* hat;    // mu_hat(cur) + (j * A) * T: [A][T]
+  const Mod* mods;
+  int w, lo, cur, ntgt, L, T, log_n;
+  struct S {
+    const u64* y;
+    Mod m;
+    u64 h[MAXA];
+  };
+  __device__ int target(int p) const {
+    const int r = p % ntgt;
+    return r < lo ? r : r + w;
+  }
+  __device__ S prep(int p) const {
+    const int t = target(p);
+    const int mi = t < cur ? t : L + t - cur;
+    S s;
+    s.y = y + (p / ntgt) * y_item;
+    s.m = mods[mi];
+#pragma unroll
+    for (int a = 0; a < MAXA; ++a) s.h[a] = a < w ? hat[a * T + mi] : 0;
+    return s;
+  }
+  __device__ u64 load(const S& s, int n) const {
+    U128 acc{0, 0};
+#pragma unroll
+    for (int a = 0; a < MAXA; ++a)
+      if (a < w) mac128(acc, s.y[((size_t)a << log_n) + n], s.h[a]);
+    return reduce128(acc, s.m);
+  }
+};
+struct StDigit {
+  u64* out;  // digits[item][j]: [cur + K][N]
+  long long out_item;
+  int lo, w, ntgt, log_n;
+  struct S { u64* p; };
+  __device__ S prep(int p) const {
+    const int r = p % ntgt;
+    const int t = r < lo ? r : r + w;
+    return S{out + (p / ntgt) * out_item + ((size_t)t << log_n)};
+  }
+  __device__ void store(const S& s, int n, u64 v) const { s.p[n] = v; }
+};
+
+template <int LOGN>
+__global__ void __launch_bounds__(NttGeom<LOGN>::THREADS) k_modup_ntt(NttTables T, LdConv ld, StDigit st) {
+  const int p = blockIdx.x / NttGeom<LOGN>::CL;
+  const int t = ld.target(p);
+  const int mi = t < ld.cur ? t : ld.L + t - ld.cur;
+  ntt_forward_body<LOGN>(p, mi, T, ld, st);
+}
+
+int modup(const HolmesCtx& c, const u64* c1, long long c1_item, int cur, int items, u64* digits, long long dig_item,
+          u64* scratch, cudaStream_t st) {
+  if (cur < 1 || cur > c.L || items < 1) return -2;
+  if (c.alpha > MAXA || c.K > MAXA) return -3;
+  const int N = c.n, A = c.alpha, K = c.K;
+  const long long y_item = (long long)cur * N;
+  // y_k = iNTT(c1_k) * N^-1 (Q_j / q_k)^-1 -> scratch [items][cur][N]
+  {
+    NttTables T{c.d_itw, c.d_mod};
+    PolyMap pm = poly_map(cur, c1_item, N, 0);
+    PolyMap ps = poly_map(cur, y_item, N, 0);
+    LdPlain ld{c1, pm};
+    StPlain sp{scratch, ps};
+#define L_(LG)                                                                                                     \
+  {                                                                                                                \
+    using G = NttGeom<LG>;                                                                                         \
+    cudaError_t e = launch_ntt(k_inv_plain<LG>, G::LOGCL, G::THREADS, G::SMEM, items * cur, st, T, pm,           \
+                               c.mu_scale(cur), 1, ld, sp);                                                        \
+    if (e != cudaSuccess) return (int)e;                                                                           \
+    break;                                                                                                         \
+  }
+    HOLMES_LOGN_SWITCH(c.log_n, L_)
+#undef L_
+  }
+  const int beta = c.beta(cur);
+  const size_t dstride = (size_t)(cur + K) * N;
+  for (int j = 0; j < beta; ++j) {
+    const int lo = j * A, w = std::min(A, cur - lo);
+    u64* dj = digits + (size_t)j * dstride;
+    // the digit's own limbs are the input limbs themselves
+    HOLMES_CUDA_TRY(cudaMemcpy2DAsync(dj + (size_t)lo * N, (size_t)dig_item * 8, c1 + (size_t)lo * N,
+                                      (size_t)c1_item * 8, (size_t)w * N * 8, (size_t)items, cudaMemcpyDeviceToDevice,
+                                      st));
+    NttTables T{c.d_tw, c.d_mod};
+    const int ntgt = cur + K - w;
+    LdConv ld{scratch + (size_t)lo * N, y_item, c.mu_hat(cur) + (size_t)j * A * c.T, c.d_mod, w, lo, cur, ntgt, c.L,
+              c.T, c.log_n};
+    StDigit sd{dj, dig_item, lo, w, ntgt, c.log_n};
+    const int polys = items * ntgt;
+#define L_(LG)                                                                                                   \
+  {                                                                                                              \
+    using G = NttGeom<LG>;                                                                                       \
+    cudaError_t e = launch_ntt(k_modup_ntt<LG>, G::LOGCL, G::THREADS, G::SMEM, polys, st, T, ld, sd);           \
+    if (e != cudaSuccess) return (int)e;                                                                         \
+    break;                                                                                                       \
+  }
+    HOLMES_LOGN_SWITCH(c.log_n, L_)
+#undef L_
+  }
+  return 0;
+}
+
+// --------------------------------------------------------------------------------------------- key switch
+// P limbs: acc_c[k][n] = sum_j D_j[cur + k][perm(n)] key_c[j][cap + k][n]
+struct LdKsP {
+  const u64* digits;
+  long long dig_item;
+  const u64* key;
+  const Mod* mods;
+  u64 galois;
+  int cur, cap, K, L, beta, key_beta, log_n;
+  struct S {
+    const u64* d;
+    const u64* k;
+    Mod m;
+  };
+  __device__ S prep(int p) const {
+    const int item = p / (2 * K), r = p % (2 * K), c = r / K, k = r % K;
+    S s;
+    s.d = digits + item * dig_item + ((size_t)(cur + k) << log_n);
+    s.k = key + ((((size_t)c * key_beta) * (cap + K) + cap + k) << log_n);
+    s.m = mods[L + k];
+    return s;
+  }
+  __device__ u64 load(const S& s, int n) const {
+    const u32 src = galois > 1 ? automorph_src((u32)n, galois, log_n) : (u32)n;
+    const size_t dstep = ((size_t)(cur + K)) << log_n, kstep = ((size_t)(cap + K)) << log_n;
+    U128 acc{0, 0};
+#pragma unroll 4
+    for (int j = 0; j < beta; ++j) mac128(acc, s.d[j * dstep + src], s.k[j * kstep + n]);
+    return reduce128(acc, s.m);
+  }
+};
+struct StScratch {
+  u64* dst;
+  int log_n;
+  struct S { u64* p; };
+  __device__ S prep(int p) const { return S{dst + ((size_t)p << log_n)}; }
+  __device__ void store(const S& s, int n, u64 v) const { s.p[n] = v; }
+};
+template <int LOGN>
+__global__ void __launch_bounds__(NttGeom<LOGN>::THREADS) k_ks_p(NttTables T, const Tw* md_scale, LdKsP ld,
+                                                                  StScratch st) {
+  const int p = blockIdx.x / NttGeom<LOGN>::CL;
+  const int k = (p % (2 * ld.K)) % ld.K;
+  ntt_inverse_body<LOGN>(p, ld.L + k, md_scale[k], T, ld, st);
+}
+
+// Q limbs: conv_c[i] = NTT(sum_k y_c[k] (P/p_k) mod q_i); out = (inner - conv) P^-1 + perm(add)
+struct LdKsQ {
+  const u64* scratch;  // [items][2][K][N]
+  const u64* md_hat;   // [K][L]
+  const Mod* mods;
+  int cur, K, L, log_n;
+  struct S {
+    const u64* y;
+    Mod m;
+    u64 h[MAXA];
+  };
+  __device__ S prep(int p) const {
+    const int item = p / (2 * cur), r = p % (2 * cur), c = r / cur, i = r % cur;
+    S s;
+    s.y = scratch + (((size_t)item * 2 + c) * K << log_n);
+    s.m = mods[i];
+#pragma unroll
+    for (int k = 0; k < MAXA; ++k) s.h[k] = k < K ? md_hat[k * L + i] : 0;
+    return s;
+  }
+  __device__ u64 load(const S& s, int n) const {
+    U128 acc{0, 0};
+#pragma unroll
+    for (int k = 0; k < MAXA; ++k)
+      if (k < K) mac128(acc, s.y[((size_t)k << log_n) + n], s.h[k]);
+    return reduce128(acc, s.m);
+  }
+};
+struct StKsQ {
+  const u64* digits;
+  long long dig_item;
+  const u64* key;
+  const u64* add0;
+  const u64* add1;
+  long long add_item;
+  const u64* post0;
+  const u64* post1;
+  long long post_item;
+  u64* out0;
+  u64* out1;
+  long long out_item;
+  const Mod* mods;
+  const Tw* pinv;
+  u64 galois;
+  int cur, cap, K, beta, key_beta, log_n;
+  struct S {
+    const u64* d;
+    const u64* k;
+    const u64* a;
+    const u64* pa;
+    u64* o;
+    Mod m;
+    Tw pi;
+  };
+  __device__ S prep(int p) const {
+    const int item = p / (2 * cur), r = p % (2 * cur), c = r / cur, i = r % cur;
+    S s;
+    s.d = digits + item * dig_item + ((size_t)i << log_n);
+    s.k = key + ((((size_t)c * key_beta) * (cap + K) + i) << log_n);
+    const u64* add = c ? add1 : add0;
+    s.a = add ? add + item * add_item + ((size_t)i << log_n) : nullptr;
+    const u64* post = c ? post1 : post0;
+    s.pa = post ? post + item * post_item + ((size_t)i << log_n) : nullptr;
+    s.o = (c ? out1 : out0) + item * out_item + ((size_t)i << log_n);
+    s.m = mods[i];
+    s.pi = pinv[i];
+    return s;
+  }
+  __device__ void store(const S& s, int n, u64 v) const {
+    const u32 src = galois > 1 ? automorph_src((u32)n, galois, log_n) : (u32)n;
+    const size_t dstep = ((size_t)(cur + K)) << log_n, kstep = ((size_t)(cap + K)) << log_n;
+    U128 acc{0, 0};
+#pragma unroll 4
+    for (int j = 0; j < beta; ++j) mac128(acc, s.d[j * dstep + src], s.k[j * kstep + n]);
+    const u64 inner = reduce128(acc, s.m);
+    u64 r = shoup(sub_mod(inner, v, s.m.q), s.pi, s.m.q);
+    if (s.a) r = add_mod(r, s.a[src], s.m.q);
+    if (s.pa) r = add_mod(r, s.pa[n], s.m.q);
+    s.o[n] = r;
+  }
+};
+template <int LOGN>
+__global__ void __launch_bounds__(NttGeom<LOGN>::THREADS) k_ks_q(NttTables T, LdKsQ ld, StKsQ st) {
+  const int p = blockIdx.x / NttGeom<LOGN>::CL;
+  ntt_forward_body<LOGN>(p, (p % (2 * ld.cur)) % ld.cur, T, ld, st);
+}
+
+int ks_apply(const HolmesCtx& c, const KsArgs& a, cudaStream_t st) {
+  if (a.cur < 1 || a.cur > a.key_cap || a.key_cap > c.L) return -2;
+  if (c.alpha > MAXA || c.K > MAXA) return -3;
+  if (a.items < 1) return -4;
+  const int beta = c.beta(a.cur), key_beta = c.beta(a.key_cap), K = c.K;
+  const u64 g = a.galois <= 1 ? 1 : a.galois;
+  {
+    NttTables T{c.d_itw, c.d_mod};
+    LdKsP ld{a.digits, a.dig_item, a.key, c.d_mod, g, a.cur, a.key_cap, K, c.L, beta, key_beta, c.log_n};
+    StScratch ss{a.scratch, c.log_n};
+    const int polys = a.items * 2 * K;
+#define L_(LG)                                                                                              \
+  {                                                                                                         \
+    using G = NttGeom<LG>;                                                                                  \
+    cudaError_t e = launch_ntt(k_ks_p<LG>, G::LOGCL, G::THREADS, G::SMEM, polys, st, T, c.d_md_scale, ld, ss); \
+    if (e != cudaSuccess) return (int)e;                                                                    \
+    break;                                                                                                  \
+  }
+    HOLMES_LOGN_SWITCH(c.log_n, L_)
+#undef L_
+  }
+  {
+    NttTables T{c.d_tw, c.d_mod};
+    LdKsQ ld{a.scratch, c.d_md_hat, c.d_mod, a.cur, K, c.L, c.log_n};
+    StKsQ sq{a.digits, a.dig_item, a.key, a.add0, a.add1, a.add_item, a.post0, a.post1, a.post_item, a.out0, a.out1,
+             a.out_item, c.d_mod,
+             c.d_md_pinv, g, a.cur, a.key_cap, K, beta, key_beta, c.log_n};
+    const int polys = a.items * 2 * a.cur;
+#define L_(LG)                                                                                        \
+  {                                                                                                   \
+    using G = NttGeom<LG>;                                                                            \
+    cudaError_t e = launch_ntt(k_ks_q<LG>, G::LOGCL, G::THREADS, G::SMEM, polys, st, T, ld, sq);       \
+    if (e != cudaSuccess) return (int)e;                                                              \
+    break;                                                                                            \
+  }
+    HOLMES_LOGN_SWITCH(c.log_n, L_)
+#undef L_
+  }
+  return 0;
+}
+
+// --------------------------------------------------------------------------------------------- rescale
+struct LdRescale {
+  const u64* x;  // scratch [comps][N]: coefficients of the last limb
+  const Mod* mods;
+  u64 ql;
+  int cur, log_n;
+  struct S {
+    const u64* x;
+    Mod m;
+    u64 qlm;
+  };
+  __device__ S prep(int p) const {
+    const int e = p / (cur - 1), i = p % (cur - 1);
+    S s;
+    s.x = x + ((size_t)e << log_n);
+    s.m = mods[i];
+    s.qlm = reduce128(0, ql, s.m);
+    return s;
+  }
+  __device__ u64 load(const S& s, int n) const {
+    const u64 v = s.x[n];
+    const u64 r = reduce128(0, v, s.m);
+    return v > (ql >> 1) ? sub_mod(r, s.qlm, s.m.q) : r;
+  }
+};
+struct StRescale {
+  const u64* in;
+  long long in_stride;
+  u64* out;
+  long long out_stride;
+  const Mod* mods;
+  const Tw* qinv;
+  int cur, log_n;
+  struct S {
+    const u64* a;
+    u64* o;
+    u64 q;
+    Tw t;
+  };
+  __device__ S prep(int p) const {
+    const int e = p / (cur - 1), i = p % (cur - 1);
+    S s;
+    s.a = in + e * in_stride + ((size_t)i << log_n);
+    s.o = out + e * out_stride + ((size_t)i << log_n);
+    s.q = mods[i].q;
+    s.t = qinv[i];
+    return s;
+  }
+  __device__ void store(const S& s, int n, u64 v) const { s.o[n] = shoup(sub_mod(s.a[n], v, s.q), s.t, s.q); }
+};
+template <int LOGN>
+__global__ void __launch_bounds__(NttGeom<LOGN>::THREADS) k_rescale(NttTables T, LdRescale ld, StRescale st) {
+  const int p = blockIdx.x / NttGeom<LOGN>::CL;
+  ntt_forward_body<LOGN>(p, p % (ld.cur - 1), T, ld, st);
+}
+
+int rescale(const HolmesCtx& c, const u64* in, long long in_stride, u64* out, long long out_stride, int cur, int comps,
+            u64* scratch, cudaStream_t st) {
+  if (cur < 2 || cur > c.L) return -2;
+  const int N = c.n;
+  {
+    NttTables T{c.d_itw, c.d_mod};
+    PolyMap pin = poly_map(1, in_stride, N, cur - 1);
+    PolyMap pout = poly_map(1, N, N, cur - 1);
+    LdPlain ld{in + (size_t)(cur - 1) * N, pin};
+    StPlain sp{scratch, pout};
+#define L_(LG)                                                                                                   \
+  {                                                                                                              \
+    using G = NttGeom<LG>;                                                                                       \
+    cudaError_t e = launch_ntt(k_inv_plain<LG>, G::LOGCL, G::THREADS, G::SMEM, comps, st, T, pin, c.d_ninv, 0,   \
+                               ld, sp);                                                                          \
+    if (e != cudaSuccess) return (int)e;                                                                         \
+    break;                                                                                                       \
+  }
+    HOLMES_LOGN_SWITCH(c.log_n, L_)
+#undef L_
+  }
+  {
+    NttTables T{c.d_tw, c.d_mod};
+    LdRescale ld{scratch, c.d_mod, c.q[cur - 1], cur, c.log_n};
+    StRescale sr{in, in_stride, out, out_stride, c.d_mod, c.rs_qinv(cur), cur, c.log_n};
+    const int polys = comps * (cur - 1);
+#define L_(LG)                                                                                      \
+  {                                                                                                 \
+    using G = NttGeom<LG>;                                                                          \
+    return (int)launch_ntt(k_rescale<LG>, G::LOGCL, G::THREADS, G::SMEM, polys, st, T, ld, sr);     \
+  }
+    HOLMES_LOGN_SWITCH(c.log_n, L_)
+#undef L_
+  }
+}
+
+// --------------------------------------------------------------------------------------------- encode
+// Coefficient n of a row: Re(u[n / gap]) for n < N/2, Im(u[(n - N/2) / gap]) above, 0 off the gap grid;
+// rounded with llround(v * scale) (bench/cmp/kernels/holmes_encode.cu:136-159) and reduced mod q_i.
+struct LdEncode {
+  const double* u;
+  long long row_stride;  // doubles
+  const Mod* mods;
+  double scale;
+  int cur, gap_log, log_n;
+  int* flag;
+  struct S {
+    const double* r;
+    Mod m;
+  };
+  __device__ S prep(int p) const {
+    S s;
+    s.r = u + (p / cur) * row_stride;
+    s.m = mods[p % cur];
+    return s;
+  }
+  __device__ u64 load(const S& s, int n) const {
+    const int half = 1 << (log_n - 1);
+    const int im = n >= half;
+    const int k = n - im * half;
+    if (k & ((1 << gap_log) - 1)) return 0;
+    const double v = __dmul_rn(s.r[2 * (k >> gap_log) + im], scale);
+    if (!(fabs(v) < 2305843009213693952.0)) {
+      *flag = 1;
+      return 0;
+    }
+    return signed_residue((i64)llround(v), s.m);
+  }
+};
+template <int LOGN>
+__global__ void __launch_bounds__(NttGeom<LOGN>::THREADS) k_encode(NttTables T, LdEncode ld, StPlain st) {
+  const int p = blockIdx.x / NttGeom<LOGN>::CL;
+  ntt_forward_body<LOGN>(p, p % ld.cur, T, ld, st);
+}
+
+int encode_rows(const HolmesCtx& c, const double* u, long long row_stride, int rows, int slots, double scale, int cur,
+                u64* out, long long out_row_stride, int* flag, cudaStream_t st) {
+  if (cur < 1 || cur > c.T) return -2;
+  if (slots < 1 || slots > c.n / 2 || (slots & (slots - 1))) return -3;
+  int gap_log = 0;
+  while ((slots << (gap_log + 1)) < c.n) ++gap_log;
+  NttTables T{c.d_tw, c.d_mod};
+  LdEncode ld{u, row_stride, c.d_mod, scale, cur, gap_log, c.log_n, flag};
+  StPlain sp{out, poly_map(cur, out_row_stride, c.n, 0)};
+#define L_(LG)                                                                                          \
+  {                                                                                                     \
+    using G = NttGeom<LG>;                                                                              \
+    return (int)launch_ntt(k_encode<LG>, G::LOGCL, G::THREADS, G::SMEM, rows * cur, st, T, ld, sp);    \
+  }
+  HOLMES_LOGN_SWITCH(c.log_n, L_)
+#undef L_
+}
+
+// --------------------------------------------------------------------------------------------- decrypt
+struct LdDecrypt {
+  const u64* c0;
+  const u64* c1;
+  const u64* s;
+  const Mod* mods;
+  int log_n;
+  struct S {
+    const u64* a;
+    const u64* b;
+    const u64* sk;
+    Mod m;
+  };
+  __device__ S prep(int p) const {
+    const size_t o = (size_t)p << log_n;
+    return S{c0 + o, c1 + o, s + o, mods[p]};
+  }
+  __device__ u64 load(const S& s, int n) const { return add_mod(s.a[n], mul_mod(s.b[n], s.sk[n], s.m), s.m.q); }
+};
+template <int LOGN>
+__global__ void __launch_bounds__(NttGeom<LOGN>::THREADS) k_decrypt(NttTables T, const Tw* ninv, LdDecrypt ld,
+                                                                     StScratch st) {
+  const int p = blockIdx.x / NttGeom<LOGN>::CL;
+  ntt_inverse_body<LOGN>(p, p, ninv[p], T, ld, st);
+}
+int decrypt_coef(const HolmesCtx& c, const u64* c0, const u64* c1, int cur, u64* out, cudaStream_t st) {
+  if (cur < 1 || cur > c.L) return -2;
+  NttTables T{c.d_itw, c.d_mod};
+  LdDecrypt ld{c0, c1, c.d_secret, c.d_mod, c.log_n};
+  StScratch ss{out, c.log_n};
+#define L_(LG)                                                                                          \
+  {                                                                                                     \
+    using G = NttGeom<LG>;                                                                              \
+    return (int)launch_ntt(k_decrypt<LG>, G::LOGCL, G::THREADS, G::SMEM, cur, st, T, c.d_ninv, ld, ss); \
+  }
+  HOLMES_LOGN_SWITCH(c.log_n, L_)
+#undef L_
+}
+
+// --------------------------------------------------------------------------------------------- secret / keys
+struct LdSigned {
+  const i64* v;
+  const Mod* mods;
+  struct S { Mod m; };
+  __device__ S prep(int p) const { return S{mods[p]}; }
+  __device__ u64 load(const S& s, int n) const { return signed_residue(v[n], s.m); }
+};
+template <int LOGN>
+__global__ void __launch_bounds__(NttGeom<LOGN>::THREADS) k_secret(NttTables T, LdSigned ld, StScratch st) {
+  const int p = blockIdx.x / NttGeom<LOGN>::CL;
+  ntt_forward_body<LOGN>(p, p, T, ld, st);
+}
+
+void host_secret_coeffs(const HolmesCtx& c, std::vector<i64>& s);
+
+int secret_ntt(HolmesCtx& c, cudaStream_t st) {
+  std::vector<i64> s;
+  host_secret_coeffs(c, s);
+  i64* d = nullptr;
+  HOLMES_CUDA_TRY(cudaMalloc(&d, sizeof(i64) * c.n));
+  HOLMES_CUDA_TRY(cudaMemcpy(d, s.data(), sizeof(i64) * c.n, cudaMemcpyHostToDevice));
+  NttTables T{c.d_tw, c.d_mod};
+  LdSigned ld{d, c.d_mod};
+  StScratch ss{c.d_secret, c.log_n};
+  int rc = 0;
+#define L_(LG)                                                                                           \
+  {                                                                                                      \
+    using G = NttGeom<LG>;                                                                               \
+    rc = (int)launch_ntt(k_secret<LG>, G::LOGCL, G::THREADS, G::SMEM, c.T, st, T, ld, ss);              \
+    break;                                                                                               \
+  }
+  HOLMES_LOGN_SWITCH(c.log_n, L_)
+#undef L_
+  cudaError_t e = cudaStreamSynchronize(st);
+  cudaFree(d);
+  return rc ? rc : (int)e;
+}
+
+// uniform part of a key / ciphertext: out[row][n] for `rows` rows, modulus index of row r given by the map
+__global__ void k_sample_uniform(u64* out, int rows, int log_n, u64 seed, u32 domain, u32 tag, u32 digit_word,
+                                 PolyMap pm, const Mod* mods) {
+  const size_t total = (size_t)rows << log_n;
+  for (size_t idx = blockIdx.x * (size_t)blockDim.x + threadIdx.x; idx < total; idx += (size_t)gridDim.x * blockDim.x) {
+    const int r = (int)(idx >> log_n), n = (int)(idx & ((1u << log_n) - 1));
+    const int mi = pm.mod(r);
+    out[idx] = sample_uniform(seed, domain, tag, digit_word | (u32)mi, (u32)n, mods[mi]);
+  }
+}
+
+struct LdError {
+  u64 seed;
+  u32 domain, tag, word;
+  const Mod* mods;
+  PolyMap pm;
+  struct S { Mod m; };
+  __device__ S prep(int p) const { return S{mods[pm.mod(p)]}; }
+  __device__ u64 load(const S& s, int n) const { return signed_residue(sample_cbd(seed, domain, tag, word, (u32)n), s.m); }
+};
+// key digit: b = e - a s + [modulus in digit] (P mod q) t,  t = sigma_g(s) (g > 1) or s^2 (g == 0)
+struct StKey {
+  u64* b;
+  const u64* a;
+  const u64* s;
+  const u64* p_mod_q;
+  const Mod* mods;
+  PolyMap pm;
+  u64 g;
+  int lo, hi, L, log_n;
+  struct S {
+    u64* b;
+    const u64* a;
+    const u64* s;
+    Mod m;
+    int in_digit;
+    u64 pq;
+  };
+  __device__ S prep(int p) const {
+    const int mi = pm.mod(p);
+    S st;
+    st.b = b + ((size_t)p << log_n);
+    st.a = a + ((size_t)p << log_n);
+    st.s = s + ((size_t)mi << log_n);
+    st.m = mods[mi];
+    st.in_digit = mi < L && mi >= lo && mi < hi;
+    st.pq = st.in_digit ? p_mod_q[mi] : 0;
+    return st;
+  }
+  __device__ void store(const S& st, int n, u64 e) const {
+    u64 v = sub_mod(e, mul_mod(st.a[n], st.s[n], st.m), st.m.q);
+    if (st.in_digit) {
+      const u64 t = g > 1 ? st.s[automorph_src((u32)n, g, log_n)] : mul_mod(st.s[n], st.s[n], st.m);
+      v = add_mod(v, mul_mod(st.pq, t, st.m), st.m.q);
+    }
+    st.b[n] = v;
+  }
+};
+template <int LOGN>
+__global__ void __launch_bounds__(NttGeom<LOGN>::THREADS) k_keygen(NttTables T, LdError ld, StKey st) {
+  const int p = blockIdx.x / NttGeom<LOGN>::CL;
+  ntt_forward_body<LOGN>(p, st.pm.mod(p), T, ld, st);
+}
+
+int keygen(const HolmesCtx& c, u64 galois, int cap, u64* key, cudaStream_t st) {
+  if (cap < 1 || cap > c.L) return -2;
+  const int N = c.n, K = c.K, rows = cap + K, kb = c.beta(cap);
+  const size_t digit_words = (size_t)rows * N;
+  const u32 tag = (u32)galois;
+  for (int j = 0; j < kb; ++j) {
+    u64* bj = key + (size_t)j * digit_words;
+    u64* aj = key + ((size_t)kb + j) * digit_words;
+    PolyMap pm = poly_map(rows, 0, N, 0, cap, c.L);
+    count_launch();
+    k_sample_uniform<<<592, 256, 0, st>>>(aj, rows, c.log_n, c.seed, 2, tag, (u32)j << 16, pm, c.d_mod);
+    HOLMES_CUDA_TRY(cudaGetLastError());
+    NttTables T{c.d_tw, c.d_mod};
+    LdError ld{c.seed, 3, tag, ((u32)j << 16) | 0xFFFFu, c.d_mod, pm};
+    const int lo = j * c.alpha, hi = std::min(lo + c.alpha, c.L);
+    StKey sk{bj, aj, c.d_secret, c.d_p_mod_q, c.d_mod, pm, galois, lo, hi, c.L, c.log_n};
+#define L_(LG)                                                                                          \
+  {                                                                                                     \
+    using G = NttGeom<LG>;                                                                              \
+    cudaError_t e = launch_ntt(k_keygen<LG>, G::LOGCL, G::THREADS, G::SMEM, rows, st, T, ld, sk);       \
+    if (e != cudaSuccess) return (int)e;                                                                \
+    break;                                                                                              \
+  }
+    HOLMES_LOGN_SWITCH(c.log_n, L_)
+#undef L_
+  }
+  return 0;
+}
+
+// encryption: c1 = a (uniform), c0 = e - a s + m
+struct StEnc {
+  u64* c0;
+  const u64* a;
+  const u64* s;
+  const u64* m;
+  const Mod* mods;
+  int log_n;
+  struct S {
+    u64* c0;
+    const u64* a;
+    const u64* s;
+    const u64* m;
+    Mod md;
+  };
+  __device__ S prep(int p) const {
+    const size_t o = (size_t)p << log_n;
+    return S{c0 + o, a + o, s + o, m + o, mods[p]};
+  }
+  __device__ void store(const S& s, int n, u64 e) const {
+    s.c0[n] = add_mod(sub_mod(e, mul_mod(s.a[n], s.s[n], s.md), s.md.q), s.m[n], s.md.q);
+  }
+};
+template <int LOGN>
+__global__ void __launch_bounds__(NttGeom<LOGN>::THREADS) k_encrypt(NttTables T, LdError ld, StEnc st) {
+  const int p = blockIdx.x / NttGeom<LOGN>::CL;
+  ntt_forward_body<LOGN>(p, p, T, ld, st);
+}
+
+int encrypt(const HolmesCtx& c, const u64* m, int cur, u64 counter, u64* c0, u64* c1, cudaStream_t st) {
+  if (cur < 1 || cur > c.L) return -2;
+  PolyMap pm = poly_map(cur, 0, c.n, 0);
+  count_launch();
+  k_sample_uniform<<<592, 256, 0, st>>>(c1, cur, c.log_n, c.seed, 4, (u32)counter, 0u, pm, c.d_mod);
+  HOLMES_CUDA_TRY(cudaGetLastError());
+  NttTables T{c.d_tw, c.d_mod};
+  LdError ld{c.seed, 5, (u32)counter, 0xFFFFu, c.d_mod, pm};
+  StEnc se{c0, c1, c.d_secret, m, c.d_mod, c.log_n};
+#define L_(LG)                                                                                  \
+  {                                                                                             \
+    using G = NttGeom<LG>;                                                                      \
+    return (int)launch_ntt(k_encrypt<LG>, G::LOGCL, G::THREADS, G::SMEM, cur, st, T, ld, se);  \
+  }
+  HOLMES_LOGN_SWITCH(c.log_n, L_)
+#undef L_
+}
+
+}  // namespace holmes

@@ -1,0 +1,801 @@
+"""EasyFHE-shaped CKKS API over libholmes_cuda.
+
+The reference's operators (``llama3fhe``) reach their engine through ``from easyfhe import fhe`` and
+the session object's ``fhe`` / ``context`` / ``client`` fields (``llama3fhe/backend.py:249-396``).  This
+module provides the subset of that surface the linear / key-switch hot path uses, with the same names,
+argument meanings and error behaviour (``ValueError`` on state mismatches):
+
+* ``CKKSContextSpec``, ``generate_client_context`` -> ``(Client, Context)``  (backend.py:556-596)
+* ``CipherState``, ``Cipher`` (``cv`` = two uint64 tensors ``[batch][limbs][N]``, ``state``, ``slots``,
+  ``is_ext``, ``batch_size``, ``cipher_like``, ``deep_copy``; parallel/wire.py:81-200)
+* ``homo_add``, ``homo_sub``, ``homo_mul_i``, ``rescale``, ``align_to``, ``homo_rotate`` (rotation index
+  ``M - 1`` = conjugation, qkv_kernel.py:832), ``prepare_hoisted_baby_rotations``, ``hoisted_mac_sum``,
+  ``homo_mul_pt``, ``homo_mul_relin``, ``homo_mul_no_relin``, ``homo_relinearize``
+* ``ConstantBundle`` / ``PackedRaw`` / ``UnpackedRaw`` (weight.py:471-545, backend.py:352-370)
+
+Every arithmetic step runs in libholmes_cuda on the current torch CUDA stream; torch only owns the
+device buffers.  There is no CPU path: without the library or a CUDA device these calls raise.
+"""
+from __future__ import annotations
+
+import dataclasses
+import math
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from . import _lib
+
+# ----------------------------------------------------------------------------------------------------- timing
+
+
+class OpTimer:
+    """CUDA-event timing of the engine's kernel families, with the algorithmic bytes each launch must move.
+
+    Disabled by default; ``bench.py`` enables it over its timed region.  ``summary()`` synchronises."""
+
+    def __init__(self) -> None:
+        self.enabled = False
+        self.records: dict = {}
+
+    def start(self, name: str):
+        if not self.enabled:
+            return None
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        return (name, e)
+
+    def stop(self, token, nbytes: int) -> None:
+        if token is None:
+            return
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        self.records.setdefault(token[0], []).append((token[1], e, int(nbytes)))
+
+    def reset(self) -> None:
+        self.records = {}
+
+    def summary(self) -> dict:
+        torch.cuda.synchronize()
+        out = {}
+        for name, recs in self.records.items():
+            ms = sum(a.elapsed_time(b) for a, b, _ in recs)
+            out[name] = {"launches": len(recs), "ms": ms, "bytes": sum(n for _, _, n in recs)}
+        return out
+
+
+OPTIMER = OpTimer()
+
+# ----------------------------------------------------------------------------------------------------- state
+
+
+@dataclass(frozen=True)
+class CipherState:
+    cur_limbs: int
+    scale_degree: int = 1
+    scaling_factor: float | None = None
+
+    def replace(self, **changes) -> "CipherState":
+        return dataclasses.replace(self, **changes)
+
+
+class Cipher:
+    """A CKKS ciphertext (two components) or a plaintext batch (one component).
+
+    ``cv[c]`` is a ``torch.uint64`` tensor ``[batch][limbs_alloc][N]``; only the first
+    ``state.cur_limbs`` limbs are meaningful.
+    """
+
+    def __init__(self, cv, state: CipherState, slots: int, is_ext: bool = False, batch_size: int | None = None,
+                 context=None) -> None:
+        self.cv = list(cv)
+        self.state = state
+        self.slots = int(slots)
+        self.is_ext = bool(is_ext)
+        self.batch_size = int(self.cv[0].shape[0] if batch_size is None else batch_size)
+        self.context = context
+
+    def cipher_like(self, cv, *, state=None, slots=None, is_ext=None, batch_size=None) -> "Cipher":
+        return type(self)(cv, self.state if state is None else state, self.slots if slots is None else slots,
+                          self.is_ext if is_ext is None else is_ext, batch_size, self.context)
+
+    def deep_copy(self) -> "Cipher":
+        return self.cipher_like([c.clone() for c in self.cv])
+
+    def release(self) -> None:
+        self.cv = []
+
+    @property
+    def device(self):
+        return self.cv[0].device
+
+    def __repr__(self) -> str:
+        return (f"Cipher(batch={self.batch_size}, limbs={self.state.cur_limbs}, degree={self.state.scale_degree}, "
+                f"slots={self.slots})")
+
+
+class Plaintext(Cipher):
+    """One-component batch of NTT plaintexts ``cv[0]`` [rows][limbs][N]."""
+
+
+# ----------------------------------------------------------------------------------------------------- context
+
+
+@dataclass
+class CKKSContextSpec:
+    depth: int
+    log_n: int
+    dnum: int
+    dcrt_bits: int
+    first_mod: int
+    secret_key_dist: str = "SPARSE_TERNARY"
+    scale_mode: str = "fixed"
+    rescale_policy: str = "manual"
+    rotations: tuple = ()
+    auto_load_keys: bool = True
+    # engine parameters beyond the reference's spec
+    special_bits: int = 60
+    special_limbs: int | None = None
+    hamming_weight: int = 192
+    seed: int = 0
+    scale_bits: int | None = None
+    #: rotation -> largest limb count it is applied to (trimmed keys, parallel/prefill/keys.py:118-140)
+    rotation_key_limb_limits: dict = field(default_factory=dict)
+    relinearization: bool = True
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+class Context:
+    """Evaluation context: moduli, device tables and switching keys (EasyFHE ``context``)."""
+
+    def __init__(self, spec: CKKSContextSpec, device: str = "cuda") -> None:
+        if not torch.cuda.is_available():
+            raise _lib.HolmesError("libholmes_cuda needs a CUDA device")
+        self.spec = spec
+        self.device = torch.device(device if device != "cuda" else f"cuda:{torch.cuda.current_device()}")
+        torch.cuda.set_device(self.device)
+        params = _lib.HolmesParams()
+        params.log_n = int(spec.log_n)
+        params.limbs = int(spec.depth) + 1
+        params.dnum = int(spec.dnum)
+        params.dcrt_bits = int(spec.dcrt_bits)
+        params.first_mod_bits = int(spec.first_mod)
+        params.special_bits = int(spec.special_bits)
+        params.special_limbs = int(spec.special_limbs or 0)
+        dist = str(spec.secret_key_dist).upper()
+        params.hamming = int(spec.hamming_weight) if dist.startswith("SPARSE") else 0
+        params.seed = int(spec.seed)
+        handle = _lib.ctypes.c_void_p()
+        _lib.call("holmes_ctx_create", _lib.ctypes.byref(params), _lib.ctypes.byref(handle))
+        self.handle = handle
+        dims = (_lib.ctypes.c_int * 6)()
+        _lib.call("holmes_ctx_dims", handle, dims)
+        self.logN, self.L, self.K, self.alpha, self.dnum, self.beta_max = (int(v) for v in dims)
+        self.N = 1 << self.logN
+        self.M = 2 * self.N
+        self.max_slots = self.N // 2
+        moduli = (_lib.ctypes.c_uint64 * (self.L + self.K))()
+        _lib.call("holmes_ctx_moduli", handle, moduli)
+        self.moduli = [int(v) for v in moduli]
+        self.scale = float(2.0 ** (spec.scale_bits if spec.scale_bits is not None else spec.dcrt_bits))
+        # EasyFHE-style per-limb tables on the device (reference-ABI callers read these)
+        ks = [q.bit_length() - 1 + 63 for q in self.moduli]
+        self.primes = torch.tensor(self.moduli, dtype=torch.uint64, device=self.device)
+        self.barret_k = torch.tensor(ks, dtype=torch.uint64, device=self.device)
+        self.barret_ratio = torch.tensor([(1 << k) // q for k, q in zip(ks, self.moduli)], dtype=torch.uint64,
+                                         device=self.device)
+        self._keys: dict = {}
+        self._caps = None
+        self._galois_cache: dict = {}
+        self._requested = set(int(r) for r in spec.rotations)
+        self._work: dict = {}
+        self._flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._enc_counter = 0
+        self.key_bytes = 0
+
+    # -- bookkeeping ---------------------------------------------------------------------------------------
+    def scale_at(self, cur_limbs: int) -> float:
+        del cur_limbs
+        return self.scale
+
+    def q(self, i: int) -> int:
+        return self.moduli[i]
+
+    def beta(self, cur: int) -> int:
+        return -(-int(cur) // self.alpha)
+
+    def galois(self, rotation: int) -> int:
+        g = self._galois_cache.get(int(rotation))
+        if g is None:
+            out = _lib.ctypes.c_uint64()
+            _lib.call("holmes_galois", self.handle, int(rotation), _lib.ctypes.byref(out))
+            g = self._galois_cache[int(rotation)] = int(out.value)
+        return g
+
+    def workspace(self, name: str, words: int) -> torch.Tensor:
+        buf = self._work.get(name)
+        if buf is None or buf.numel() < words:
+            buf = torch.empty(int(words), dtype=torch.uint64, device=self.device)
+            self._work[name] = buf
+        return buf
+
+    def key_words(self, cap: int) -> int:
+        out = _lib.ctypes.c_longlong()
+        _lib.call("holmes_key_words", self.handle, int(cap), _lib.ctypes.byref(out))
+        return int(out.value)
+
+    def _make_key(self, galois: int, cap: int) -> torch.Tensor:
+        key = torch.empty(self.key_words(cap), dtype=torch.uint64, device=self.device)
+        _lib.call("holmes_keygen", self.handle, int(galois), int(cap), key.data_ptr(), _stream())
+        self.key_bytes += key.numel() * 8
+        return key
+
+    def switch_key(self, galois: int, cur_limbs: int):
+        """(key tensor, cap) for X -> X^galois (0 = relinearisation) usable at ``cur_limbs``."""
+        entry = self._keys.get(galois)
+        if entry is not None and entry[1] >= cur_limbs:
+            return entry
+        if self._caps is None:
+            limits = self.spec.rotation_key_limb_limits or {}
+            self._caps = {self.galois(int(r)): int(c) for r, c in limits.items()}
+        cap_default = self._caps.get(galois, self.L) if galois else self.L
+        if entry is None or entry[1] < cur_limbs:
+            cap = max(cap_default, int(cur_limbs))
+            entry = (self._make_key(galois, min(cap, self.L)), min(cap, self.L))
+            self._keys[galois] = entry
+        return entry
+
+    def get_rotation_key_for_limbs(self, rotation: int, cur_limbs: int):
+        return self.switch_key(self.galois(rotation), cur_limbs)
+
+    def generate_rotation_keys(self, rotations, cur_limbs: int | None = None) -> None:
+        for r in rotations:
+            self.switch_key(self.galois(int(r)), self.L if cur_limbs is None else int(cur_limbs))
+
+    def clear_cuda_rotation_cache(self, keep_rotations=()) -> None:
+        keep = {self.galois(int(r)) for r in keep_rotations} | {0}
+        for g in list(self._keys):
+            if g not in keep:
+                self.key_bytes -= self._keys[g][0].numel() * 8
+                del self._keys[g]
+
+    def check_encode_range(self) -> None:
+        """One device read: raise if any encode since the last check reached the 2^61 limit."""
+        if int(self._flag.item()):
+            self._flag.zero_()
+            raise ValueError("encoded value exceeds the 2^61 encoder range")
+
+    def close(self) -> None:
+        if getattr(self, "handle", None) is not None:
+            torch.cuda.synchronize(self.device)
+            self._keys.clear()
+            self._work.clear()
+            _lib.call("holmes_ctx_destroy", self.handle)
+            self.handle = None
+
+    def __del__(self):  # pragma: no cover - interpreter shutdown order varies
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ----------------------------------------------------------------------------------------------------- encoding
+
+
+def _as_slots(values, slots: int) -> np.ndarray:
+    z = np.asarray(values)
+    z = z.astype(np.complex128).reshape(-1)
+    if z.size > slots:
+        raise ValueError(f"{z.size} values do not fit {slots} slots")
+    if z.size < slots:
+        z = np.concatenate([z, np.zeros(slots - z.size, dtype=np.complex128)])
+    return z
+
+
+def encode_rows(ctx: Context, rows: torch.Tensor, cur_limbs: int, scale: float, slots: int,
+                already_transformed: bool = False) -> torch.Tensor:
+    """[rows][slots] complex128 (device) -> NTT plaintexts [rows][cur][N]."""
+    if rows.dim() == 1:
+        rows = rows.reshape(1, -1)
+    nrows = int(rows.shape[0])
+    if int(rows.shape[1]) != slots:
+        raise ValueError(f"plaintext rows have {rows.shape[1]} slots, expected {slots}")
+    z = rows.to(device=ctx.device, dtype=torch.complex128).contiguous()
+    if z.data_ptr() == rows.data_ptr() and not already_transformed:
+        z = z.clone()
+    zr = torch.view_as_real(z)
+    out = torch.empty((nrows, int(cur_limbs), ctx.N), dtype=torch.uint64, device=ctx.device)
+    if not already_transformed:
+        tok = OPTIMER.start("fft_special")
+        _lib.call("holmes_fft_special_inv", ctx.handle, zr.data_ptr(), 2 * slots, nrows, slots, _stream())
+        OPTIMER.stop(tok, 2 * nrows * slots * 16)
+    tok = OPTIMER.start("encode_ntt")
+    _lib.call("holmes_encode_fft", ctx.handle, zr.data_ptr(), 2 * slots, nrows, slots, float(scale), int(cur_limbs),
+              out.data_ptr(), int(cur_limbs) * ctx.N, ctx._flag.data_ptr(), _stream())
+    OPTIMER.stop(tok, nrows * slots * 16 + nrows * int(cur_limbs) * ctx.N * 8)
+    return out
+
+
+def fft_special_inv_rows(ctx: Context, rows: torch.Tensor, slots: int) -> torch.Tensor:
+    z = rows.to(device=ctx.device, dtype=torch.complex128).reshape(-1, slots)
+    if z.data_ptr() == rows.data_ptr():
+        z = z.clone()
+    zr = torch.view_as_real(z)
+    tok = OPTIMER.start("fft_special")
+    _lib.call("holmes_fft_special_inv", ctx.handle, zr.data_ptr(), 2 * slots, int(z.shape[0]), slots, _stream())
+    OPTIMER.stop(tok, 2 * int(z.shape[0]) * slots * 16)
+    return z
+
+
+def _fft_special_np(z: np.ndarray, M: int) -> np.ndarray:
+    """Forward CKKS embedding (decode) of one slot vector, vectorised per butterfly level."""
+    n = z.size
+    bits = n.bit_length() - 1
+    idx = np.array([int(format(i, f"0{bits}b")[::-1], 2) if bits else 0 for i in range(n)])
+    v = z[idx].copy()
+    rot = np.array([pow(5, j, M) for j in range(max(1, n // 2))], dtype=np.int64)
+    length = 2
+    while length <= n:
+        half = length // 2
+        lenq = length * 4
+        k = (rot[:half] % lenq) * (M // lenq)
+        w = np.exp(2j * np.pi * k / M)
+        v = v.reshape(-1, length)
+        u = v[:, :half].copy()
+        t = v[:, half:] * w
+        v[:, :half] = u + t
+        v[:, half:] = u - t
+        v = v.reshape(-1)
+        length *= 2
+    return v
+
+
+class Client:
+    """Secret-key holder of a simulation context (EasyFHE ``client``)."""
+
+    def __init__(self, context: Context) -> None:
+        self.context = context
+
+    def encrypt(self, values, device=None, slots: int | None = None, cur_limbs: int | None = None,
+                scaling_factor: float | None = None, counter: int | None = None) -> Cipher:
+        ctx = self.context
+        del device
+        slots = ctx.max_slots if slots is None else int(slots)
+        cur = ctx.L if cur_limbs is None else int(cur_limbs)
+        if not 1 <= cur <= ctx.L:
+            raise ValueError(f"cur_limbs={cur} outside [1, {ctx.L}]")
+        scale = ctx.scale_at(cur) if scaling_factor is None else float(scaling_factor)
+        z = torch.from_numpy(_as_slots(values, slots)).to(ctx.device).reshape(1, slots)
+        m = encode_rows(ctx, z, cur, scale, slots)
+        ctx.check_encode_range()
+        if counter is None:
+            counter = ctx._enc_counter
+            ctx._enc_counter += 1
+        storage = torch.empty((2, 1, cur, ctx.N), dtype=torch.uint64, device=ctx.device)
+        _lib.call("holmes_encrypt", ctx.handle, m.data_ptr(), cur, int(counter), storage[0].data_ptr(),
+                  storage[1].data_ptr(), _stream())
+        return Cipher([storage[0], storage[1]], CipherState(cur, 1, scale), slots, False, 1, ctx)
+
+    def decrypt_coefficients(self, cipher: Cipher, item: int = 0) -> list[int]:
+        ctx = self.context
+        cur = int(cipher.state.cur_limbs)
+        c0 = cipher.cv[0][item, :cur].contiguous()
+        c1 = cipher.cv[1][item, :cur].contiguous()
+        out = torch.empty((cur, ctx.N), dtype=torch.uint64, device=ctx.device)
+        _lib.call("holmes_decrypt", ctx.handle, c0.data_ptr(), c1.data_ptr(), cur, out.data_ptr(), _stream())
+        res = out.cpu().numpy()
+        use = min(cur, 4)
+        moduli = [ctx.q(i) for i in range(use)]
+        Q = math.prod(moduli)
+        acc = np.zeros(ctx.N, dtype=object)
+        for i, qi in enumerate(moduli):
+            hat = Q // qi
+            inv = pow(hat % qi, -1, qi)
+            acc = acc + ((res[i].astype(object) * inv) % qi) * hat
+        acc = acc % Q
+        return [int(v) - Q if int(v) > Q // 2 else int(v) for v in acc]
+
+    def decrypt(self, cipher: Cipher, item: int = 0) -> np.ndarray:
+        ctx = self.context
+        coeffs = np.array([float(v) for v in self.decrypt_coefficients(cipher, item)], dtype=np.float64)
+        slots = int(cipher.slots)
+        gap = ctx.N // (2 * slots)
+        scale = float(cipher.state.scaling_factor)
+        z = coeffs[0:ctx.N // 2:gap][:slots] / scale + 1j * coeffs[ctx.N // 2::gap][:slots] / scale
+        return _fft_special_np(z, ctx.M)
+
+
+def generate_client_context(spec: CKKSContextSpec, device: str = "cuda"):
+    ctx = Context(spec, device)
+    if spec.auto_load_keys:
+        for r in spec.rotations:
+            ctx.switch_key(ctx.galois(int(r)), ctx.L)
+        if spec.relinearization:
+            ctx.switch_key(0, ctx.L)
+    return Client(ctx), ctx
+
+
+# ----------------------------------------------------------------------------------------------------- helpers
+
+
+def _new_cipher(ctx: Context, batch: int, limbs: int, state: CipherState, slots: int) -> Cipher:
+    storage = torch.empty((2, batch, limbs, ctx.N), dtype=torch.uint64, device=ctx.device)
+    return Cipher([storage[0], storage[1]], state, slots, False, batch, ctx)
+
+
+def _item_stride(t: torch.Tensor) -> int:
+    return int(t.stride(0))
+
+
+def _check_same(a: Cipher, b: Cipher, what: str) -> None:
+    if int(a.state.cur_limbs) != int(b.state.cur_limbs):
+        raise ValueError(f"{what}: limb mismatch {a.state.cur_limbs} != {b.state.cur_limbs}")
+    if int(a.state.scale_degree) != int(b.state.scale_degree):
+        raise ValueError(f"{what}: scale degree mismatch {a.state.scale_degree} != {b.state.scale_degree}")
+    if a.is_ext or b.is_ext:
+        raise ValueError(f"{what}: extended ciphertexts are not supported")
+    if a.batch_size != b.batch_size:
+        raise ValueError(f"{what}: batch mismatch {a.batch_size} != {b.batch_size}")
+
+
+def _ew(ctx: Context, op: int, a: torch.Tensor, b: torch.Tensor | None, out: torch.Tensor, limbs: int) -> None:
+    _lib.call("holmes_elementwise", ctx.handle, op, a.data_ptr(), 0 if b is None else b.data_ptr(), out.data_ptr(),
+              int(a.shape[0]), int(limbs), _item_stride(a), 0 if b is None else _item_stride(b), _item_stride(out),
+              _stream())
+
+
+def _ctx(ctx) -> Context:
+    return ctx.context if hasattr(ctx, "context") and isinstance(ctx.context, Context) else ctx
+
+
+# ----------------------------------------------------------------------------------------------------- ops
+
+
+def homo_add(a: Cipher, b: Cipher, ctx) -> Cipher:
+    ctx = _ctx(ctx)
+    _check_same(a, b, "homo_add")
+    cur = int(a.state.cur_limbs)
+    out = _new_cipher(ctx, a.batch_size, cur, a.state, a.slots)
+    for c in range(2):
+        _ew(ctx, 0, a.cv[c], b.cv[c], out.cv[c], cur)
+    return out
+
+
+def homo_sub(a: Cipher, b: Cipher, ctx) -> Cipher:
+    ctx = _ctx(ctx)
+    _check_same(a, b, "homo_sub")
+    cur = int(a.state.cur_limbs)
+    out = _new_cipher(ctx, a.batch_size, cur, a.state, a.slots)
+    for c in range(2):
+        _ew(ctx, 1, a.cv[c], b.cv[c], out.cv[c], cur)
+    return out
+
+
+def homo_mul_i(a: Cipher, ctx) -> Cipher:
+    ctx = _ctx(ctx)
+    cur = int(a.state.cur_limbs)
+    out = _new_cipher(ctx, a.batch_size, cur, a.state, a.slots)
+    for c in range(2):
+        _lib.call("holmes_mul_i", ctx.handle, a.cv[c].data_ptr(), out.cv[c].data_ptr(), a.batch_size, cur,
+                  _item_stride(a.cv[c]), _item_stride(out.cv[c]), _stream())
+    return out
+
+
+def rescale(a: Cipher, ctx) -> Cipher:
+    ctx = _ctx(ctx)
+    cur = int(a.state.cur_limbs)
+    if cur < 2:
+        raise ValueError("rescale needs at least two limbs")
+    ql = ctx.q(cur - 1)
+    sf = None if a.state.scaling_factor is None else float(a.state.scaling_factor) / ql
+    state = CipherState(cur - 1, max(1, int(a.state.scale_degree) - 1), sf)
+    out = _new_cipher(ctx, a.batch_size, cur - 1, state, a.slots)
+    scratch = ctx.workspace("rescale", a.batch_size * ctx.N)
+    tok = OPTIMER.start("rescale")
+    for c in range(2):
+        _lib.call("holmes_rescale", ctx.handle, a.cv[c].data_ptr(), _item_stride(a.cv[c]), out.cv[c].data_ptr(),
+                  _item_stride(out.cv[c]), cur, a.batch_size, scratch.data_ptr(), _stream())
+    OPTIMER.stop(tok, 2 * a.batch_size * (2 * cur - 1) * ctx.N * 8)
+    return out
+
+
+def align_to(a: Cipher, target: CipherState, ctx) -> Cipher:
+    """Bring ``a`` to ``target``: rescale while its degree is above the target's, then drop limbs."""
+    ctx = _ctx(ctx)
+    cur = a
+    while int(cur.state.scale_degree) > int(target.scale_degree):
+        cur = rescale(cur, ctx)
+    want = int(target.cur_limbs)
+    have = int(cur.state.cur_limbs)
+    if want > have:
+        raise ValueError(f"align_to: cannot raise {have} limbs to {want}")
+    if want == have:
+        return cur
+    state = cur.state.replace(cur_limbs=want)
+    return cur.cipher_like([c[:, :want].contiguous() for c in cur.cv], state=state)
+
+
+def _modup(ctx: Context, c1: torch.Tensor, cur: int, items: int) -> tuple[torch.Tensor, int]:
+    dig_item = ctx.beta(cur) * (cur + ctx.K) * ctx.N
+    digits = torch.empty(items * dig_item, dtype=torch.uint64, device=ctx.device)
+    scratch = ctx.workspace("modup", items * cur * ctx.N)
+    tok = OPTIMER.start("modup")
+    _lib.call("holmes_modup", ctx.handle, c1.data_ptr(), _item_stride(c1), cur, items, digits.data_ptr(), dig_item,
+              scratch.data_ptr(), _stream())
+    OPTIMER.stop(tok, items * (cur + dig_item // ctx.N) * ctx.N * 8)
+    return digits, dig_item
+
+
+def _keyswitch(ctx: Context, digits: torch.Tensor, dig_item: int, cur: int, galois: int, key, add0, add1, add_item,
+               out0: torch.Tensor, out1: torch.Tensor, items: int, post0=None, post1=None, post_item: int = 0) -> None:
+    key_t, cap = key
+    scratch = ctx.workspace("ks", items * 2 * ctx.K * ctx.N)
+    beta = ctx.beta(cur)
+    words = items * (beta * (cur + ctx.K) + 2 * cur) + 2 * beta * (cur + ctx.K)
+    words += items * cur * ((add0 is not None) + (add1 is not None) + (post0 is not None) + (post1 is not None))
+    tok = OPTIMER.start("keyswitch")
+    _lib.call("holmes_keyswitch", ctx.handle, digits.data_ptr(), dig_item, cur, key_t.data_ptr(), cap, int(galois),
+              0 if add0 is None else add0.data_ptr(), 0 if add1 is None else add1.data_ptr(), int(add_item),
+              0 if post0 is None else post0.data_ptr(), 0 if post1 is None else post1.data_ptr(), int(post_item),
+              out0.data_ptr(), out1.data_ptr(), _item_stride(out0), items, scratch.data_ptr(), _stream())
+    OPTIMER.stop(tok, words * ctx.N * 8)
+
+
+def rotate_batch(ctx: Context, c0: torch.Tensor, c1: torch.Tensor, cur: int, rotation: int, out0: torch.Tensor,
+                 out1: torch.Tensor, post0=None, post1=None) -> None:
+    """out = rot((c0, c1), rotation) [+ post] for a batch [items][>= cur][N] sharing one key."""
+    items = int(c0.shape[0])
+    g = ctx.galois(rotation)
+    if g == 1:
+        if post0 is None:
+            out0.copy_(c0[:, :cur])
+            out1.copy_(c1[:, :cur])
+        else:
+            _ew(ctx, 0, c0, post0, out0, cur)
+            _ew(ctx, 0, c1, post1, out1, cur)
+        return
+    digits, dig_item = _modup(ctx, c1, cur, items)
+    _keyswitch(ctx, digits, dig_item, cur, g, ctx.switch_key(g, cur), c0, None, _item_stride(c0), out0, out1, items,
+               post0, post1, 0 if post0 is None else _item_stride(post0))
+
+
+def homo_rotate(a: Cipher, rotation: int, ctx) -> Cipher:
+    ctx = _ctx(ctx)
+    cur = int(a.state.cur_limbs)
+    out = _new_cipher(ctx, a.batch_size, cur, a.state, a.slots)
+    rotate_batch(ctx, a.cv[0], a.cv[1], cur, int(rotation), out.cv[0], out.cv[1])
+    return out
+
+
+def fast_rotate(a: Cipher, rotation: int, ctx) -> Cipher:
+    return homo_rotate(a, rotation, ctx)
+
+
+def prepare_hoisted_baby_rotations(a: Cipher, baby_offsets, ctx, strategy: str = "normal",
+                                   baby_anchor_step: int = -1):
+    """Baby basis rot(a, offset) for every offset from one hoisted ModUp; one block ``[nb]`` batch.
+
+    Every hoist strategy name of the reference is accepted; all return the ModDown'ed (non-extended)
+    basis, which is the ``normal`` strategy's result.
+    """
+    del strategy, baby_anchor_step
+    ctx = _ctx(ctx)
+    if a.batch_size != 1:
+        raise ValueError("prepare_hoisted_baby_rotations expects one ciphertext")
+    offsets = [int(o) for o in baby_offsets]
+    cur = int(a.state.cur_limbs)
+    block = _new_cipher(ctx, len(offsets), cur, a.state, a.slots)
+    digits = dig_item = None
+    for b, off in enumerate(offsets):
+        g = ctx.galois(off)
+        if g == 1:
+            block.cv[0][b].copy_(a.cv[0][0, :cur])
+            block.cv[1][b].copy_(a.cv[1][0, :cur])
+            continue
+        if digits is None:
+            digits, dig_item = _modup(ctx, a.cv[1], cur, 1)
+        _keyswitch(ctx, digits, dig_item, cur, g, ctx.switch_key(g, cur), a.cv[0], None, 0, block.cv[0][b:b + 1],
+                   block.cv[1][b:b + 1], 1)
+    return (block,)
+
+
+def bsgs_partial_sums(ctx: Context, baby_blocks, plaintexts: Plaintext, giants: int) -> torch.Tensor:
+    """res [2][giants][inputs][cur][N] = sum_b pt[g B + b] * baby_i[b] for every input's baby block."""
+    blocks = list(baby_blocks)
+    cur = int(blocks[0].state.cur_limbs)
+    nb = int(blocks[0].batch_size)
+    pv = plaintexts.cv[0]
+    if int(pv.shape[0]) != giants * nb:
+        raise ValueError(f"plaintext chunk has {pv.shape[0]} rows, expected {giants} x {nb}")
+    if int(plaintexts.state.cur_limbs) < cur or int(pv.shape[1]) < cur:
+        raise ValueError("plaintext chunk has fewer limbs than the baby basis")
+    res = torch.empty((2, giants, len(blocks), cur, ctx.N), dtype=torch.uint64, device=ctx.device)
+    bstride = _item_stride(blocks[0].cv[0])
+    c0s = _lib.ptr_array([b.cv[0].data_ptr() for b in blocks])
+    c1s = _lib.ptr_array([b.cv[1].data_ptr() for b in blocks])
+    tok = OPTIMER.start("bsgs_mac")
+    _lib.call("holmes_bsgs_mac", ctx.handle, res.data_ptr(), c0s, c1s, bstride, nb, len(blocks), pv.data_ptr(),
+              _item_stride(pv), giants, cur, _stream())
+    OPTIMER.stop(tok, (giants * nb + len(blocks) * nb * 2 + 2 * giants * len(blocks)) * cur * ctx.N * 8)
+    return res
+
+
+def giant_horner(ctx: Context, res: torch.Tensor, giant_offset: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """acc = res[G-1]; acc = rot(acc, giant_offset) + res[g] for g = G-2 .. 0 (all inputs at once)."""
+    G = int(res.shape[1])
+    cur = int(res.shape[3])
+    acc0, acc1 = res[0, G - 1], res[1, G - 1]
+    for g in range(G - 2, -1, -1):
+        n0 = torch.empty_like(acc0)
+        n1 = torch.empty_like(acc1)
+        rotate_batch(ctx, acc0, acc1, cur, giant_offset, n0, n1, post0=res[0, g], post1=res[1, g])
+        acc0, acc1 = n0, n1
+    return acc0, acc1
+
+
+def hoisted_mac_sum(cipher: Cipher, baby_offsets, plaintexts: Plaintext, giant_offset: int, giant_count: int, ctx,
+                    strategy: str = "normal", baby_anchor_step: int = -1, baby_rotations=None) -> Cipher:
+    """sum_g rot(sum_b pt[g B + b] baby[b], g giant_offset) via Horner; scale degree adds the plaintext's."""
+    ctx = _ctx(ctx)
+    if baby_rotations is None:
+        baby_rotations = prepare_hoisted_baby_rotations(cipher, baby_offsets, ctx, strategy, baby_anchor_step)
+    block = baby_rotations[0]
+    res = bsgs_partial_sums(ctx, [block], plaintexts, int(giant_count))
+    acc0, acc1 = giant_horner(ctx, res, int(giant_offset))
+    sf = None
+    if block.state.scaling_factor is not None and plaintexts.state.scaling_factor is not None:
+        sf = float(block.state.scaling_factor) * float(plaintexts.state.scaling_factor)
+    state = CipherState(int(block.state.cur_limbs),
+                        int(block.state.scale_degree) + int(plaintexts.state.scale_degree), sf)
+    return Cipher([acc0, acc1], state, cipher.slots, False, 1, ctx)
+
+
+def homo_mul_pt(a: Cipher, pt: Plaintext, ctx) -> Cipher:
+    ctx = _ctx(ctx)
+    cur = int(a.state.cur_limbs)
+    if int(pt.state.cur_limbs) < cur:
+        raise ValueError("homo_mul_pt: plaintext has fewer limbs than the ciphertext")
+    sf = None
+    if a.state.scaling_factor is not None and pt.state.scaling_factor is not None:
+        sf = float(a.state.scaling_factor) * float(pt.state.scaling_factor)
+    state = CipherState(cur, int(a.state.scale_degree) + int(pt.state.scale_degree), sf)
+    out = _new_cipher(ctx, a.batch_size, cur, state, a.slots)
+    p = pt.cv[0][:1].expand(a.batch_size, -1, -1) if pt.cv[0].shape[0] == 1 else pt.cv[0]
+    for c in range(2):
+        _lib.call("holmes_elementwise", ctx.handle, 2, a.cv[c].data_ptr(), p.data_ptr(), out.cv[c].data_ptr(),
+                  a.batch_size, cur, _item_stride(a.cv[c]), int(p.stride(0)), _item_stride(out.cv[c]), _stream())
+    return out
+
+
+def homo_mul_no_relin(a: Cipher, b: Cipher, ctx) -> Cipher:
+    ctx = _ctx(ctx)
+    if int(a.state.cur_limbs) != int(b.state.cur_limbs):
+        raise ValueError("homo_mul: limb mismatch")
+    cur = int(a.state.cur_limbs)
+    n = a.batch_size
+    shape = (n, cur, ctx.N)
+    d0 = torch.empty(shape, dtype=torch.uint64, device=ctx.device)
+    d1 = torch.empty_like(d0)
+    d2 = torch.empty_like(d0)
+    t = torch.empty_like(d0)
+    _ew(ctx, 2, a.cv[0], b.cv[0], d0, cur)
+    _ew(ctx, 2, a.cv[0], b.cv[1], d1, cur)
+    _ew(ctx, 2, a.cv[1], b.cv[0], t, cur)
+    _ew(ctx, 0, d1, t, d1, cur)
+    _ew(ctx, 2, a.cv[1], b.cv[1], d2, cur)
+    sf = None
+    if a.state.scaling_factor is not None and b.state.scaling_factor is not None:
+        sf = float(a.state.scaling_factor) * float(b.state.scaling_factor)
+    state = CipherState(cur, int(a.state.scale_degree) + int(b.state.scale_degree), sf)
+    return Cipher([d0, d1, d2], state, a.slots, False, n, ctx)
+
+
+def homo_relinearize(a: Cipher, ctx) -> Cipher:
+    ctx = _ctx(ctx)
+    if len(a.cv) != 3:
+        raise ValueError("homo_relinearize expects a three-component ciphertext")
+    cur = int(a.state.cur_limbs)
+    n = a.batch_size
+    out = _new_cipher(ctx, n, cur, a.state, a.slots)
+    digits, dig_item = _modup(ctx, a.cv[2], cur, n)
+    _keyswitch(ctx, digits, dig_item, cur, 1, ctx.switch_key(0, cur), a.cv[0], a.cv[1], _item_stride(a.cv[0]),
+               out.cv[0], out.cv[1], n)
+    return out
+
+
+def homo_mul_relin(a: Cipher, b: Cipher, ctx) -> Cipher:
+    return homo_relinearize(homo_mul_no_relin(a, b, ctx), ctx)
+
+
+def homo_mul_relin_rescale_postop(a: Cipher, b: Cipher, ctx) -> Cipher:
+    return rescale(homo_mul_relin(a, b, ctx), ctx)
+
+
+# ----------------------------------------------------------------------------------------------------- constants
+
+
+class PackedRaw:
+    """Slot values already packed: a tensor ``[rows][slots]`` (or ``[slots]``), real or complex."""
+
+    def __init__(self, tensor) -> None:
+        self.tensor = tensor
+
+    def packed(self, slots: int, context) -> torch.Tensor:
+        del context
+        return self.tensor
+
+
+class UnpackedRaw:
+    """A raw source plus the packer that turns it into ``[rows][slots]`` slot values."""
+
+    def __init__(self, source, packer) -> None:
+        self.source = source
+        self.packer = packer
+
+    def packed(self, slots: int, context) -> torch.Tensor:
+        return self.packer(self.source, int(slots), context)
+
+
+class ConstantBundle:
+    """Named plaintext constants with an optional cache of the FFT'd values ("middle") and/or the final
+    NTT plaintexts ("plain"), per ``cache_mode`` in {"none", "middle", "plain", "both"}."""
+
+    def __init__(self, vectors: dict, cache_mode: str = "none") -> None:
+        if cache_mode not in ("none", "middle", "plain", "both"):
+            raise ValueError(f"unknown cache_mode {cache_mode!r}")
+        self.vectors = dict(vectors)
+        self.cache_mode = cache_mode
+        self._middle: dict = {}
+        self._plain: dict = {}
+        self._stats = {"middle_hits": 0, "middle_misses": 0, "plain_hits": 0, "plain_misses": 0}
+
+    def _encoded_middle(self, name: str, *, slots: int, context) -> torch.Tensor:
+        ctx = _ctx(context)
+        key = (name, int(slots))
+        mid = self._middle.get(key)
+        if mid is not None:
+            self._stats["middle_hits"] += 1
+            return mid
+        self._stats["middle_misses"] += 1
+        raw = self.vectors[name].packed(int(slots), ctx)
+        if not torch.is_tensor(raw):
+            raw = torch.from_numpy(np.asarray(raw))
+        raw = raw.reshape(-1, int(slots))
+        mid = fft_special_inv_rows(ctx, raw, int(slots))
+        if self.cache_mode in ("middle", "both"):
+            self._middle[key] = mid
+        return mid
+
+    def plaintext(self, name: str, *, state: CipherState, slots: int, context, is_ext: bool = False,
+                  cache: bool = False) -> Plaintext:
+        del is_ext
+        ctx = _ctx(context)
+        key = (name, int(slots), int(state.cur_limbs), float(state.scaling_factor or ctx.scale))
+        hit = self._plain.get(key)
+        if hit is not None:
+            self._stats["plain_hits"] += 1
+            return hit
+        self._stats["plain_misses"] += 1
+        mid = self._encoded_middle(name, slots=slots, context=ctx)
+        scale = float(state.scaling_factor) if state.scaling_factor is not None else ctx.scale_at(state.cur_limbs)
+        pv = encode_rows(ctx, mid, int(state.cur_limbs), scale, int(slots), already_transformed=True)
+        pt = Plaintext([pv], CipherState(int(state.cur_limbs), int(state.scale_degree), scale), int(slots), False,
+                       int(pv.shape[0]), ctx)
+        if self.cache_mode in ("plain", "both") or (cache and self.cache_mode != "none"):
+            self._plain[key] = pt
+        return pt
+
+    def cache_info(self) -> dict:
+        mb = sum(int(t.numel()) * t.element_size() for t in self._middle.values())
+        pb = sum(int(p.cv[0].numel()) * 8 for p in self._plain.values())
+        return {"middle_entries": len(self._middle), "plain_entries": len(self._plain), "middle_bytes": mb,
+                "plain_bytes": pb, "total_bytes": mb + pb, **self._stats}
+
+    def clear_cache(self) -> None:
+        self._middle.clear()
+        self._plain.clear()

@@ -1,0 +1,139 @@
+/*
+ * holmes_cuda.h -- C ABI of libholmes_cuda, the B200 (sm_100a) RNS-CKKS engine under Holmes's
+ * linear / key-switch hot path.
+ *
+ * Conventions (shared by every entry point):
+ *   - every function returns 0 on success, a negative argument-error code, or a positive
+ *     cudaError_t, like the reference's C ABIs (bench/cmp/kernels/holmes_mac.cu:359-402);
+ *   - buffers are caller-owned device pointers; `stream` is a cudaStream_t (NULL = legacy stream);
+ *   - residue arrays are uint64 words laid out [items][limbs][N] (limb stride N), the layout of
+ *     EasyFHE's Cipher.cv components [batch][limbs_alloc][N] (llama3fhe/parallel/wire.py:81-120);
+ *   - moduli are indexed 0..L-1 for the Q limbs and L..L+K-1 for the special limbs;
+ *   - NTT-domain words use the reference's root order (bench/cmp/kernels/holmes_encode.cu:65-71).
+ * No function allocates device memory except holmes_ctx_create (its tables) and
+ * holmes_ctx_create's secret upload; scratch buffers are passed in.
+ */
+#ifndef HOLMES_CUDA_H
+#define HOLMES_CUDA_H
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct holmes_params {
+  int log_n;           /* ring degree 2^log_n, 10..16 */
+  int limbs;           /* L: Q limbs at the top level (depth + 1) */
+  int dnum;            /* key-switch digits; alpha = ceil(L / dnum) limbs per digit */
+  int dcrt_bits;       /* bits of Q limbs 1..L-1 */
+  int first_mod_bits;  /* bits of Q limb 0 */
+  int special_bits;    /* bits of the special primes */
+  int special_limbs;   /* K; 0 = alpha */
+  int hamming;         /* secret hamming weight; 0 = uniform ternary */
+  uint64_t seed;       /* key / encryption randomness seed */
+} holmes_params;
+
+/* ---- context: replaces EasyFHE's generate_client_context / CKKSContextSpec
+ *      (llama3fhe/backend.py:556-596 create_sim_context) */
+int holmes_ctx_create(const holmes_params* params, void** ctx_out);
+int holmes_ctx_destroy(void* ctx);
+/* moduli[L + K] (host) */
+int holmes_ctx_moduli(void* ctx, uint64_t* moduli_out);
+/* dims[6] = {log_n, L, K, alpha, dnum, beta_max} (host) */
+int holmes_ctx_dims(void* ctx, int* dims_out);
+/* device pointer of the secret key [L + K][N] (NTT form); simulation contexts hold the client key */
+int holmes_ctx_secret(void* ctx, void** secret_out);
+/* automorphism index of a slot rotation (negative r as N/2 + r, keys.py:91-102); M - 1 = conjugation */
+int holmes_galois(void* ctx, long long rotation, uint64_t* galois_out);
+/* words of one switching key holding Q limbs < cap: 2 * beta(cap) * (cap + K) * N (keys.py:105-118) */
+int holmes_key_words(void* ctx, int cap, long long* words_out);
+
+/* ---- keys and client (EasyFHE generate_client_context keygen, client.encrypt / decrypt,
+ *      llama3fhe/backend.py:293-396) */
+/* switching key for X -> X^galois (galois > 1) or relinearisation (galois == 0):
+ * key[2][beta(cap)][cap + K][N] = (b, a) */
+int holmes_keygen(void* ctx, uint64_t galois, int cap, uint64_t* key, void* stream);
+/* secret-key encryption of the NTT plaintext m[cur][N]: c1 = a, c0 = e - a s + m */
+int holmes_encrypt(void* ctx, const uint64_t* m, int cur, uint64_t counter, uint64_t* c0, uint64_t* c1, void* stream);
+/* coefficients (not centred) of c0 + c1 s, [cur][N] */
+int holmes_decrypt(void* ctx, const uint64_t* c0, const uint64_t* c1, int cur, uint64_t* coef_out, void* stream);
+
+/* ---- transforms (EasyFHE NttImpl / encode; holmes_encode.cu:108-285) */
+/* in-place forward (inverse = 0) or inverse NTT of [items][limbs][N], limb l with modulus first_mod + l */
+int holmes_ntt(void* ctx, uint64_t* data, int items, int limbs, long long item_stride, int first_mod, int inverse,
+               void* stream);
+/* encode rows of `slots` complex values z[rows][slots][2] (overwritten by the inverse special FFT) at `scale`
+ * into NTT plaintexts out[rows][cur][N]; *flag (device int) is set to 1 if a value reaches 2^61 */
+int holmes_encode(void* ctx, double* z, long long row_stride, int rows, int slots, double scale, int cur, uint64_t* out,
+                  long long out_row_stride, int* flag, void* stream);
+/* the two halves of holmes_encode: the inverse special FFT in place (EasyFHE cv_pre_encode_stage1), and the
+ * rounding / reduction / NTT of already transformed rows (cv_encode, holmes_encode.cu:115-226) */
+int holmes_fft_special_inv(void* ctx, double* z, long long row_stride, int rows, int slots, void* stream);
+int holmes_encode_fft(void* ctx, const double* u, long long row_stride, int rows, int slots, double scale, int cur,
+                      uint64_t* out, long long out_row_stride, int* flag, void* stream);
+/* diagonal rows of one BSGS chunk (weight.py:122-154 _cpu_packer / gpu_packer.py:48-200):
+ * out[giant_count * baby][slots][2] complex; weight [dim][dim] float64 or complex128 (weight_complex = 1) */
+int holmes_pack_diagonals(const double* weight, int weight_complex, int dim, int lanes, int baby, int giant_base,
+                          int giant_count, int lane_shift, int slots, double* out, long long row_stride, void* stream);
+
+/* ---- ciphertext arithmetic (fhe.homo_add / homo_sub / homo_mul_pt / homo_mul_i / rescale,
+ *      llama3fhe/operators/primitives.py:21-190) */
+/* op: 0 add, 1 sub, 2 multiply, 3 negate (b unused); limb l uses modulus l */
+int holmes_elementwise(void* ctx, int op, const uint64_t* a, const uint64_t* b, uint64_t* out, int items, int limbs,
+                       long long a_item, long long b_item, long long out_item, void* stream);
+/* multiply by X^(N/2) (slot-wise i) */
+int holmes_mul_i(void* ctx, const uint64_t* a, uint64_t* out, int items, int limbs, long long a_item, long long out_item,
+                 void* stream);
+/* NTT-domain automorphism X -> X^galois */
+int holmes_automorph(void* ctx, const uint64_t* a, uint64_t* out, uint64_t galois, int items, int limbs,
+                     long long a_item, long long out_item, void* stream);
+/* multiply limb l by consts[l] (device array of canonical residues) */
+int holmes_mul_const(void* ctx, const uint64_t* a, const uint64_t* consts, uint64_t* out, int items, int limbs,
+                     long long a_item, long long out_item, void* stream);
+/* divide by the last limb with centred rounding: in[comps][cur][N] -> out[comps][cur - 1][N];
+ * scratch >= comps * N words */
+int holmes_rescale(void* ctx, const uint64_t* in, long long in_stride, uint64_t* out, long long out_stride, int cur,
+                   int comps, uint64_t* scratch, void* stream);
+
+/* ---- hybrid key switch (EasyFHE cv_modup / cv_innerproduct / cv_moddown, bench/cmp/report.py:23-46;
+ *      fhe.homo_rotate, prepare_hoisted_baby_rotations, homo_relinearize) */
+/* digits[items][beta(cur)][cur + K][N] = ModUp(c1[items][cur][N]) (item strides c1_item / digit_item words);
+ * scratch >= items * cur * N words */
+int holmes_modup(void* ctx, const uint64_t* c1, long long c1_item, int cur, int items, uint64_t* digits,
+                 long long digit_item, uint64_t* scratch, void* stream);
+/* for `items` ciphertexts sharing one key:
+ *   out0 = perm(add0) + ModDown(sum_j perm(digit_j) key_b[j]) + post0
+ *   out1 = perm(add1) + ModDown(sum_j perm(digit_j) key_a[j]) + post1
+ * perm = automorphism X -> X^galois (galois <= 1: identity); every addend may be NULL;
+ * scratch >= items * 2 * K * N words */
+int holmes_keyswitch(void* ctx, const uint64_t* digits, long long digit_item, int cur, const uint64_t* key, int key_cap,
+                     uint64_t galois, const uint64_t* add0, const uint64_t* add1, long long add_item,
+                     const uint64_t* post0, const uint64_t* post1, long long post_item, uint64_t* out0,
+                     uint64_t* out1, long long out_item, int items, uint64_t* scratch, void* stream);
+
+/* ---- BSGS plaintext multiply-accumulate (fhe.hoisted_mac_sum baby step, holmes_multi_mac.py:148-194):
+ * res[2][groups][inputs][limbs][N] = sum_b pts[g * nb + b][limb] * baby_i[b][c][limb] (mod q_limb);
+ * c0s / c1s: host arrays of `inputs` (<= 32) device pointers to baby bases [nb][>= limbs][N] (item stride bstride) */
+int holmes_bsgs_mac(void* ctx, uint64_t* res, const uint64_t* const* c0s, const uint64_t* const* c1s, long long bstride,
+                    int nb, int inputs, const uint64_t* pts, long long pstride, int groups, int limbs, void* stream);
+
+/* ---- collectives: mod-q sum of nsrc (<= 16) equally shaped buffers (peer-mapped partials included);
+ *      the owner-side reduce of parallel/decode/decode_collectives.py:59-195 and
+ *      operators/attention/distributed/distributed_output.py:801-830 */
+int holmes_modsum(void* ctx, const uint64_t* const* srcs, int nsrc, uint64_t* out, int items, int limbs,
+                  long long item_stride, void* stream);
+
+/* kernels launched by this library since it was loaded (all streams, all contexts) */
+int holmes_launch_count(unsigned long long* count_out);
+
+/* ---- drop-in for the reference's own ctypes binding (bench/cmp/kernels/holmes_mac.cu:359-402, bound in
+ *      bench/cmp/holmes_multi_mac.py:33-54): same signature, arguments and return codes; N = 2^16;
+ *      `ti` is accepted from the reference's tile set and used only as a hint. */
+int holmes_mac_multi(uint64_t* res, const uint64_t* const* c0s, const uint64_t* const* c1s, long long bstride, int nb,
+                     int inputs, const uint64_t* pts, long long pstride, int groups, int ti, int limbs,
+                     const uint64_t* primes, const uint64_t* ratios, const uint64_t* ks, void* stream_ptr);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,300 @@
+"""CUDA path vs the CPU oracle, residue for residue (bit-exact), through the C ABI.
+
+Small rings (N = 2^10 .. 2^13, single-CTA NTT) and cluster rings (N = 2^14 .. 2^16, DSMEM NTT) are both
+covered.  Decoded values are additionally checked against NumPy at the tolerances of the reference's own
+GPU tests (tests/test_linear.py:280-340: 2e-8 relative to the weight scale)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import packing
+from tests.gpu_helpers import dev, host, make_pair, residues
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def pair():
+    o, client, ctx = make_pair(log_n=10, limbs=5, dnum=2, dcrt=40, first=50, special=50)
+    yield o, client, ctx
+    ctx.close()
+
+
+def _lib():
+    from holmes_b200 import _lib
+
+    return _lib
+
+
+def test_context_tables_match_oracle(pair):
+    import ctypes
+
+    o, _, ctx = pair
+    assert ctx.moduli == o.pr.q
+    ptr = ctypes.c_void_p()
+    _lib().call("holmes_ctx_secret", ctx.handle, ctypes.byref(ptr))
+    n = (ctx.L + ctx.K) * ctx.N
+    buf = torch.empty(n, dtype=torch.uint64, device=ctx.device)
+    torch.cuda.synchronize()
+    _copy_ptr(ptr.value, buf, n * 8)
+    np.testing.assert_array_equal(host(buf).reshape(ctx.L + ctx.K, ctx.N), o.secret)
+
+
+def _copy_ptr(src_ptr: int, dst: torch.Tensor, nbytes: int) -> None:
+    import ctypes
+
+    cudart = ctypes.CDLL("libcudart.so.12") if _has("libcudart.so.12") else ctypes.CDLL("libcudart.so")
+    cudart.cudaMemcpy.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int]
+    assert cudart.cudaMemcpy(ctypes.c_void_p(dst.data_ptr()), ctypes.c_void_p(src_ptr), nbytes, 3) == 0
+
+
+def _has(name: str) -> bool:
+    import ctypes
+
+    try:
+        ctypes.CDLL(name)
+        return True
+    except OSError:
+        return False
+
+
+@pytest.mark.parametrize("log_n", [10, 12, 13, 14, 15, 16])
+def test_ntt_forward_inverse_bitexact(log_n):
+    o, _, ctx = make_pair(log_n=log_n, limbs=3, dnum=1, dcrt=59, first=60, special=60, K=1)
+    rng = np.random.default_rng(log_n)
+    items, limbs = 3, 3
+    a = np.stack([residues(o.pr.q, limbs, o.pr.n, rng) for _ in range(items)])
+    t = dev(a)
+    _lib().call("holmes_ntt", ctx.handle, t.data_ptr(), items, limbs, limbs * o.pr.n, 0, 0, 0)
+    got = host(t)
+    for i in range(items):
+        np.testing.assert_array_equal(got[i], o.ntt(a[i], range(limbs)))
+    _lib().call("holmes_ntt", ctx.handle, t.data_ptr(), items, limbs, limbs * o.pr.n, 0, 1, 0)
+    np.testing.assert_array_equal(host(t), a)
+    # special-prime moduli (index L .. L + K - 1)
+    b = residues(o.pr.q, 1, o.pr.n, rng, limb_ids=[3])
+    tb = dev(b)
+    _lib().call("holmes_ntt", ctx.handle, tb.data_ptr(), 1, 1, o.pr.n, 3, 0, 0)
+    np.testing.assert_array_equal(host(tb), o.ntt(b, [3]))
+    ctx.close()
+
+
+def test_keys_bitexact(pair):
+    o, _, ctx = pair
+    for galois, cap in ((5, ctx.L), (pow(5, 7, 2 * ctx.N), 3), (2 * ctx.N - 1, ctx.L), (0, ctx.L)):
+        key = torch.empty(ctx.key_words(cap), dtype=torch.uint64, device=ctx.device)
+        _lib().call("holmes_keygen", ctx.handle, galois, cap, key.data_ptr(), 0)
+        kb, ka = o.relin_key(cap) if galois == 0 else o.rotation_key(galois, cap)
+        got = host(key).reshape(2, *kb.shape)
+        np.testing.assert_array_equal(got[1], ka)
+        np.testing.assert_array_equal(got[0], kb)
+
+
+def test_encrypt_bitexact_and_decrypts(pair):
+    o, client, ctx = pair
+    rng = np.random.default_rng(7)
+    z = rng.normal(size=ctx.max_slots) + 1j * rng.normal(size=ctx.max_slots)
+    for cur in (ctx.L, 2):
+        ct = client.encrypt(z, cur_limbs=cur, counter=11)
+        r0, r1 = o.encrypt(z, cur, counter=11)
+        np.testing.assert_array_equal(host(ct.cv[0][0]), r0)
+        np.testing.assert_array_equal(host(ct.cv[1][0]), r1)
+        assert np.abs(client.decrypt(ct) - z).max() < 1e-6
+
+
+@pytest.mark.parametrize("slots", [512, 64, 4])
+def test_encode_bitexact(pair, slots):
+    o, _, ctx = pair
+    from holmes_b200 import fhe as F
+
+    rng = np.random.default_rng(slots)
+    rows = rng.normal(size=(3, slots)) + 1j * rng.normal(size=(3, slots))
+    pt = F.encode_rows(ctx, torch.from_numpy(rows).to(ctx.device), 4, ctx.scale, slots)
+    got = host(pt)
+    for r in range(3):
+        np.testing.assert_array_equal(got[r], o.encode(rows[r], 4, ctx.scale, slots))
+
+
+def test_encode_range_error_is_raised(pair):
+    _, _, ctx = pair
+    from holmes_b200 import fhe as F
+
+    big = np.full((1, ctx.max_slots), 1e9, dtype=np.complex128)
+    F.encode_rows(ctx, torch.from_numpy(big).to(ctx.device), 2, ctx.scale, ctx.max_slots)
+    with pytest.raises(ValueError):
+        ctx.check_encode_range()
+
+
+def _cipher(o, client, z, cur, counter):
+    ct = client.encrypt(z, cur_limbs=cur, counter=counter)
+    return ct, o.encrypt(z, cur, counter=counter)
+
+
+@pytest.mark.parametrize("cur", [5, 3, 1])
+def test_rotation_and_conjugation_bitexact(pair, cur):
+    o, client, ctx = pair
+    from holmes_b200 import fhe as F
+
+    rng = np.random.default_rng(cur)
+    z = rng.normal(size=ctx.max_slots) * 0.5
+    ct, ref = _cipher(o, client, z, cur, 3)
+    for r in (1, 7, -5, ctx.max_slots - 1, 2 * ctx.N - 1):
+        out = F.homo_rotate(ct, r, ctx)
+        e0, e1 = o.rotate(ref, r)
+        np.testing.assert_array_equal(host(out.cv[0][0]), e0)
+        np.testing.assert_array_equal(host(out.cv[1][0]), e1)
+    want = np.roll(z, -7)
+    assert np.abs(client.decrypt(F.homo_rotate(ct, 7, ctx)) - want).max() < 1e-5
+
+
+def test_hoisted_babies_bitexact(pair):
+    o, client, ctx = pair
+    from holmes_b200 import fhe as F
+
+    z = np.random.default_rng(4).normal(size=ctx.max_slots)
+    ct, ref = _cipher(o, client, z, 4, 5)
+    offsets = [0, 3, 6, 9, 12]
+    (block,) = F.prepare_hoisted_baby_rotations(ct, offsets, ctx)
+    expect = o.hoisted_rotations(ref, offsets)
+    for b in range(len(offsets)):
+        np.testing.assert_array_equal(host(block.cv[0][b]), expect[b][0])
+        np.testing.assert_array_equal(host(block.cv[1][b]), expect[b][1])
+
+
+def test_elementwise_rescale_mul_i_relin_bitexact(pair):
+    o, client, ctx = pair
+    from holmes_b200 import fhe as F
+
+    rng = np.random.default_rng(9)
+    za = rng.normal(size=ctx.max_slots) * 0.5
+    zb = rng.normal(size=ctx.max_slots) * 0.5
+    a, ra = _cipher(o, client, za, 5, 21)
+    b, rb = _cipher(o, client, zb, 5, 22)
+    ids = range(5)
+    s = F.homo_add(a, b, ctx)
+    np.testing.assert_array_equal(host(s.cv[0][0]), o.add(ra[0], rb[0], ids))
+    d = F.homo_sub(a, b, ctx)
+    np.testing.assert_array_equal(host(d.cv[1][0]), o.sub(ra[1], rb[1], ids))
+    mi = F.homo_mul_i(a, ctx)
+    e = o.mul_i(ra)
+    np.testing.assert_array_equal(host(mi.cv[0][0]), e[0])
+    np.testing.assert_array_equal(host(mi.cv[1][0]), e[1])
+    rs = F.rescale(a, ctx)
+    e = o.rescale(ra)
+    np.testing.assert_array_equal(host(rs.cv[0][0]), e[0])
+    np.testing.assert_array_equal(host(rs.cv[1][0]), e[1])
+    prod = F.homo_mul_relin(a, b, ctx)
+    e = o.mul_relin(ra, rb)
+    np.testing.assert_array_equal(host(prod.cv[0][0]), e[0])
+    np.testing.assert_array_equal(host(prod.cv[1][0]), e[1])
+    got = client.decrypt(F.rescale(prod, ctx))
+    assert np.abs(got - za * zb).max() < 1e-4
+
+
+def test_bsgs_mac_bitexact(pair):
+    o, _, ctx = pair
+    rng = np.random.default_rng(12)
+    nb, G, inputs, cur = 5, 3, 3, 4
+    pts = np.stack([residues(o.pr.q, cur, o.pr.n, rng) for _ in range(G * nb)])
+    babies = [[(residues(o.pr.q, cur, o.pr.n, rng), residues(o.pr.q, cur, o.pr.n, rng)) for _ in range(nb)]
+              for _ in range(inputs)]
+    from holmes_b200 import _lib as L
+
+    store = [torch.stack([torch.stack([dev(b[c]) for b in babies[i]]) for c in range(2)]) for i in range(inputs)]
+    res = torch.empty((2, G, inputs, cur, ctx.N), dtype=torch.uint64, device=ctx.device)
+    pt = dev(pts)
+    c0s = L.ptr_array([s[0].data_ptr() for s in store])
+    c1s = L.ptr_array([s[1].data_ptr() for s in store])
+    L.call("holmes_bsgs_mac", ctx.handle, res.data_ptr(), c0s, c1s, cur * ctx.N, nb, inputs, pt.data_ptr(),
+           cur * ctx.N, G, cur, 0)
+    got = host(res)
+    for i in range(inputs):
+        e = o.bsgs_mac(pts, babies[i], G)
+        for c in range(2):
+            np.testing.assert_array_equal(got[c, :, i], e[c])
+
+
+def _oracle_linear(o, ref_inputs, weight, plan, cur, scale):
+    """Per-input restatement of LinearOperator.apply (reference: operator.py:203-467)."""
+    outs = []
+    for ref in ref_inputs:
+        babies = o.hoisted_rotations(ref, plan.baby_offsets)
+        acc = None
+        for chunk in plan.chunks:
+            rows = packing.diagonal_rows(weight, dimension=plan.dimension, token_lanes=plan.token_lanes,
+                                         baby_steps=plan.baby_steps, giant_base=chunk.giant_base,
+                                         giant_count=chunk.giant_count, lane_shift=plan.lane_shift)
+            pts = np.stack([o.encode(r, cur, scale) for r in rows])
+            part = o.bsgs_mac(pts, babies, chunk.giant_count)
+            res = o.giant_horner(part, plan.giant_offset)
+            if chunk.giant_base:
+                res = o.rotate(res, chunk.giant_base * plan.giant_offset)
+            acc = res if acc is None else (o.add(acc[0], res[0], range(cur)), o.add(acc[1], res[1], range(cur)))
+        outs.append(o.rescale(acc))
+    return outs
+
+
+@pytest.mark.parametrize("complex_weight", [False, True])
+def test_linear_operator_bitexact_and_decodes(complex_weight):
+    from holmes_b200 import linear as LN
+
+    o, client, ctx = make_pair(log_n=11, limbs=4, dnum=2, dcrt=45, first=55, special=55)
+    session = LN.Session(client, ctx)
+    dim, lanes = 64, 16            # slots = 1024 = dim * lanes
+    cfg = LN.LinearOperatorConfig(baby_steps=8, baby_anchor_step=8, max_plaintext_rows=16)
+    plan = cfg.plan(dimension=dim, token_lanes=lanes)
+    rng = np.random.default_rng(26081431)
+    w = rng.normal(scale=0.02, size=(dim, dim))
+    if complex_weight:
+        w = w + 1j * rng.normal(scale=0.02, size=(dim, dim))
+    xs = rng.normal(size=(3, lanes, dim))
+    cur = ctx.L
+    cts, refs = [], []
+    for i, x in enumerate(xs):
+        carrier = x.T.reshape(-1)            # slot(d, t) = d * lanes + t
+        ct, ref = _cipher(o, client, carrier, cur, 100 + i)
+        cts.append(ct)
+        refs.append(ref)
+    with LN.LinearOperator(crypto_context=session, token_lanes=lanes, config=cfg) as op, \
+            LN.LinearWeight(w, dtype=w.dtype, crypto_context=session) as lw:
+        outs, profile = op.apply(cts, lw)
+        again, _ = op.apply(cts, lw)
+        assert op.cache_info()["baby_hits"] == 3
+    expect = _oracle_linear(o, refs, w, plan, cur, ctx.scale)
+    for got, e, x in zip(outs, expect, xs):
+        np.testing.assert_array_equal(host(got.cv[0][0]), e[0])
+        np.testing.assert_array_equal(host(got.cv[1][0]), e[1])
+        dec = client.decrypt(got).reshape(dim, lanes).T
+        np.testing.assert_allclose(dec, x @ w.T, atol=2e-8 * 50, rtol=2e-6)
+    for a, b in zip(outs, again):
+        np.testing.assert_array_equal(host(a.cv[0]), host(b.cv[0]))
+    assert profile["online"] > 0
+    ctx.close()
+
+
+def test_full_ring_rotation_round_trip_and_linearity():
+    """N = 2^16 with the reference's production primes (59/60-bit, dnum 5 at 13 limbs): rotation by r then -r and
+    conjugation twice return the message; rotation is linear (size-independent properties)."""
+    from holmes_b200 import fhe as F
+
+    o, client, ctx = make_pair(log_n=16, limbs=13, dnum=2, dcrt=59, first=60, special=60, K=7, hamming=192)
+    rng = np.random.default_rng(0)
+    za = rng.normal(size=ctx.max_slots) * 0.1
+    zb = rng.normal(size=ctx.max_slots) * 0.1
+    a = client.encrypt(za, counter=1)
+    b = client.encrypt(zb, counter=2)
+    r = F.homo_rotate(F.homo_rotate(a, 513, ctx), -513, ctx)
+    assert np.abs(client.decrypt(r) - za).max() < 1e-9
+    c = F.homo_rotate(F.homo_rotate(a, 2 * ctx.N - 1, ctx), 2 * ctx.N - 1, ctx)
+    assert np.abs(client.decrypt(c) - za).max() < 1e-9
+    lhs = F.homo_rotate(F.homo_add(a, b, ctx), 4096, ctx)
+    rhs = F.homo_add(F.homo_rotate(a, 4096, ctx), F.homo_rotate(b, 4096, ctx), ctx)
+    assert np.abs(client.decrypt(lhs) - client.decrypt(rhs)).max() < 1e-9
+    assert np.abs(client.decrypt(lhs) - np.roll(za + zb, -4096)).max() < 1e-9
+    # one rotation against the oracle at full size
+    ra = o.encrypt(za, ctx.L, counter=1)
+    e0, e1 = o.rotate(ra, 513)
+    g = F.homo_rotate(a, 513, ctx)
+    np.testing.assert_array_equal(host(g.cv[0][0]), e0)
+    np.testing.assert_array_equal(host(g.cv[1][0]), e1)
+    ctx.close()
