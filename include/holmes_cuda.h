@@ -95,6 +95,16 @@ int holmes_mul_const(void* ctx, const uint64_t* a, const uint64_t* consts, uint6
 int holmes_rescale(void* ctx, const uint64_t* in, long long in_stride, uint64_t* out, long long out_stride, int cur,
                    int comps, uint64_t* scratch, void* stream);
 
+/* holmes_rescale without caller scratch, for callers that cannot allocate device memory (a runtime that
+ * owns the whole pool, or a loop where cudaMalloc's device synchronisation is unacceptable).  No
+ * counterpart in the reference.  Scratch comes from a 2 MiB array compiled into the library (held by every
+ * GPU that loads it): comps * N must not exceed 4 * 2^16 words (-6 otherwise), and the calling thread's
+ * current device must be the context's (-7 otherwise).  The first call on a device looks up the array's
+ * device address, so make it before any stream capture.  Calls that overlap on the GPU race on the shared
+ * array; nothing needs clearing between calls. */
+int holmes_rescale_noalloc(void* ctx, const uint64_t* in, long long in_stride, uint64_t* out, long long out_stride,
+                           int cur, int comps, void* stream);
+
 /* ---- hybrid key switch (EasyFHE cv_modup / cv_innerproduct / cv_moddown, bench/cmp/report.py:23-46;
  *      fhe.homo_rotate, prepare_hoisted_baby_rotations, homo_relinearize) */
 /* digits[items][beta(cur)][cur + K][N] = ModUp(c1[items][cur][N]) (item strides c1_item / digit_item words);
