@@ -10,7 +10,7 @@ import ctypes
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "lib", "libholmes_cuda.so")
+LIB_PATH = os.environ.get("HOLMES_LIB", os.path.join(HERE, "lib", "libholmes_cuda.so"))
 
 _lib = None
 

@@ -50,19 +50,29 @@ def _compile(src: str, force: bool, extra: list[str]) -> str:
     return obj
 
 
-def build(force: bool = False, verbose_ptxas: bool = False) -> str:
-    os.makedirs(OBJ, exist_ok=True)
+def build(force: bool = False, verbose_ptxas: bool = False, defines=(), out: str | None = None) -> str:
+    """Compile every source and link ``out`` (default ``lib/libholmes_cuda.so``); ``defines`` are extra -D flags
+    for a variant build, which then gets its own object directory."""
+    global OBJ
+    obj_dir = OBJ if not defines else OBJ + "_" + "_".join(d.replace("=", "") for d in defines)
+    target = LIB if out is None else out
+    os.makedirs(obj_dir, exist_ok=True)
     extra = ["-Xptxas", "-v"] if verbose_ptxas else []
-    with cf.ThreadPoolExecutor(max_workers=len(SOURCES)) as ex:
-        objs = list(ex.map(lambda s: _compile(s, force, extra), SOURCES))
-    if force or _stale(LIB, objs):
-        tmp = LIB + f".{os.getpid()}.tmp"
+    extra += [f"-D{d}" for d in defines]
+    saved, OBJ = OBJ, obj_dir
+    try:
+        with cf.ThreadPoolExecutor(max_workers=len(SOURCES)) as ex:
+            objs = list(ex.map(lambda s: _compile(s, force, extra), SOURCES))
+    finally:
+        OBJ = saved
+    if force or _stale(target, objs):
+        tmp = target + f".{os.getpid()}.tmp"
         cmd = [NVCC, *ARCH, "-shared", "-o", tmp, *objs, "-lcudart"]
         res = subprocess.run(cmd, capture_output=True, text=True)
         if res.returncode != 0:
             raise RuntimeError(f"link failed:\n{res.stdout}\n{res.stderr}")
-        os.replace(tmp, LIB)
-    return LIB
+        os.replace(tmp, target)
+    return target
 
 
 if __name__ == "__main__":

@@ -1,5 +1,7 @@
 // Kernels that are not NTT-shaped: elementwise RNS arithmetic, the BSGS plaintext multiply-accumulate,
 // the CKKS special FFT of the encoder, diagonal packing, and the mod-q sum of peer partials.
+#include <cstdlib>
+
 #include "ops.h"
 
 namespace holmes {
@@ -170,6 +172,158 @@ __global__ void __launch_bounds__(256) k_bsgs_mac(u64* __restrict__ res, InPtrs 
   }
 }
 
+// ---------------------------------------------------------------------------------------------------------
+// k_bsgs_mac2: the same result with radix-2^30 partial products.
+//
+// Every residue a < 2^60 splits as a = a1 2^30 + a0 with a0, a1 < 2^30, so each of the four partial products
+// a0 b0, a0 b1, a1 b0, a1 b1 is below 2^60 and is one 32 x 32 -> 64-bit multiply-add into a 64-bit sum; 16 of
+// them (plus a carried value below 2^30) still fit in 64 bits.  A thread keeps, per output, the four sums
+// S00, SA (a0 b1), SB (a1 b0), S11 and every 16 baby steps folds
+//     V = S00 + (SA + SB) 2^30 + S11 2^60  (< 16 q^2 + q),
+// reduces V mod q with the 128-bit Barrett step (common.cuh) and restarts the sums from the two 30-bit
+// halves of the residue.  That is 4 multiply-adds per product plus a fold amortised over 16 steps,
+// instead of a full 64 x 64 -> 128-bit product and a 128-bit add.
+//
+// Block: 256 threads = 8 warps over 32 consecutive words of one limb; warp w takes input i0 + w/2 and the
+// giant half w % 2 (4 giants) of an 8-giant group, both ciphertext components.  The plaintext words of the
+// 8 giants are staged in shared memory 16 baby steps at a time (cp.async, double-buffered) and split into
+// (a0 | a1 << 32) once per block, so each is fetched from HBM once per 4 inputs and split once.
+constexpr int kMacSB = 16;      // baby steps per stage
+constexpr int kMacGG = 8;       // giants per block
+constexpr int kMacIW = 4;       // inputs per block
+constexpr int kMacStageWords = kMacGG * kMacSB * 32;
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::); }
+
+struct Split4 {
+  u64 s00, sa, sb, s11;
+};
+__device__ __forceinline__ void mad_split(Split4& acc, u32 a0, u32 a1, u64 bp) {
+  const u32 b0 = (u32)bp, b1 = (u32)(bp >> 32);
+  acc.s00 += (u64)a0 * b0;
+  acc.sa += (u64)a0 * b1;
+  acc.sb += (u64)a1 * b0;
+  acc.s11 += (u64)a1 * b1;
+}
+__device__ __forceinline__ u64 fold_split(const Split4& acc, const Mod& m) {
+  // V = s00 + (sa << 30) + (sb << 30) + (s11 << 60) as 128 bits
+  u64 lo = acc.s00, hi = 0;
+  const u64 a_lo = acc.sa << 30, a_hi = acc.sa >> 34;
+  const u64 b_lo = acc.sb << 30, b_hi = acc.sb >> 34;
+  const u64 c_lo = acc.s11 << 60, c_hi = acc.s11 >> 4;
+  asm("add.cc.u64 %0, %0, %2;\n\taddc.u64 %1, %1, %3;" : "+l"(lo), "+l"(hi) : "l"(a_lo), "l"(a_hi));
+  asm("add.cc.u64 %0, %0, %2;\n\taddc.u64 %1, %1, %3;" : "+l"(lo), "+l"(hi) : "l"(b_lo), "l"(b_hi));
+  asm("add.cc.u64 %0, %0, %2;\n\taddc.u64 %1, %1, %3;" : "+l"(lo), "+l"(hi) : "l"(c_lo), "l"(c_hi));
+  return reduce128(hi, lo, m);
+}
+__device__ __forceinline__ void restart_split(Split4& acc, u64 r) {
+  acc.s00 = r & ((1ull << 30) - 1);
+  acc.sa = r >> 30;
+  acc.sb = 0;
+  acc.s11 = 0;
+}
+
+__global__ void __launch_bounds__(256, 2) k_bsgs_mac2(u64* __restrict__ res, InPtrs in, long long bstride, int nb,
+                                                      int inputs, int G, const u64* __restrict__ pts, long long pstride,
+                                                      int limbs, ModSrc ms, int log_n) {
+  extern __shared__ __align__(16) u64 mac_smem[];
+  u64(*stage)[kMacStageWords] = reinterpret_cast<u64(*)[kMacStageWords]>(mac_smem);
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int itiles = (inputs + kMacIW - 1) / kMacIW;
+  const int j0 = (blockIdx.x / itiles) * 32;
+  const int i = (blockIdx.x % itiles) * kMacIW + (w >> 1);
+  const int half = w & 1;
+  const int limb = blockIdx.y, g0 = blockIdx.z * kMacGG;
+  const Mod m = ms.get(limb);
+  const size_t lpos = ((size_t)limb << log_n) + j0;
+  const bool active = i < inputs;
+  const u64* __restrict__ b0p = in.c0[active ? i : 0] + lpos + lane;
+  const u64* __restrict__ b1p = in.c1[active ? i : 0] + lpos + lane;
+
+  // staging: 8 giants x 16 steps x 32 words = 2048 16-byte chunks; thread t copies chunks t + 256 k
+  auto issue_stage = [&](int s, int buf) {
+#pragma unroll
+    for (int k = 0; k < kMacStageWords / 2 / 256; ++k) {
+      const int chunk = threadIdx.x + 256 * k;
+      const int g = chunk / (kMacSB * 16), r = chunk % (kMacSB * 16);
+      const int bb = r / 16, c = r % 16;
+      const int b = s * kMacSB + bb;
+      if (b < nb) {
+        const int gg = g0 + g < G ? g0 + g : g0;
+        cp_async16(&stage[buf][(g * kMacSB + bb) * 32 + 2 * c], pts + ((size_t)gg * nb + b) * pstride + lpos + 2 * c);
+      }
+    }
+    asm volatile("cp.async.commit_group;\n" ::);
+  };
+  auto split_stage = [&](int buf) {
+#pragma unroll
+    for (int k = 0; k < kMacStageWords / 2 / 256; ++k) {
+      const int chunk = threadIdx.x + 256 * k;
+      u64* p = &stage[buf][chunk * 2];
+      const u64 x = p[0], y = p[1];
+      p[0] = (x & ((1ull << 30) - 1)) | ((x >> 30) << 32);
+      p[1] = (y & ((1ull << 30) - 1)) | ((y >> 30) << 32);
+    }
+  };
+
+  Split4 acc[2][4];
+#pragma unroll
+  for (int c = 0; c < 2; ++c)
+#pragma unroll
+    for (int g = 0; g < 4; ++g) acc[c][g] = Split4{0, 0, 0, 0};
+
+  const int nstages = (nb + kMacSB - 1) / kMacSB;
+  issue_stage(0, 0);
+  for (int s = 0; s < nstages; ++s) {
+    const int buf = s & 1;
+    cp_async_wait_all();
+    split_stage(buf);
+    __syncthreads();
+    if (s + 1 < nstages) issue_stage(s + 1, buf ^ 1);
+    const int steps = nb - s * kMacSB < kMacSB ? nb - s * kMacSB : kMacSB;
+    if (active) {
+      const u64* sp = &stage[buf][(half * 4) * kMacSB * 32 + lane];
+      u64 n0 = b0p[(size_t)(s * kMacSB) * bstride], n1 = b1p[(size_t)(s * kMacSB) * bstride];
+      for (int bb = 0; bb < steps; ++bb) {
+        const u64 v0 = n0, v1 = n1;
+        if (bb + 1 < steps) {
+          n0 = b0p[(size_t)(s * kMacSB + bb + 1) * bstride];
+          n1 = b1p[(size_t)(s * kMacSB + bb + 1) * bstride];
+        }
+        const u32 x0 = (u32)(v0 & ((1ull << 30) - 1)), x1 = (u32)(v0 >> 30);
+        const u32 y0 = (u32)(v1 & ((1ull << 30) - 1)), y1 = (u32)(v1 >> 30);
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const u64 bp = sp[(g * kMacSB + bb) * 32];
+          mad_split(acc[0][g], x0, x1, bp);
+          mad_split(acc[1][g], y0, y1, bp);
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int g = 0; g < 4; ++g) restart_split(acc[c][g], fold_split(acc[c][g], m));
+    }
+    __syncthreads();  // the buffer is refilled by the next stage's copies
+  }
+  if (!active) return;
+  const size_t is = (size_t)limbs << log_n, gs = (size_t)inputs * is;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    const int gg = g0 + half * 4 + g;
+    if (gg >= G) break;
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const u64 r = (acc[c][g].sa << 30) | acc[c][g].s00;  // restart_split left the canonical residue here
+      res[((size_t)c * G + gg) * gs + (size_t)i * is + lpos + lane] = r;
+    }
+  }
+}
+
 int bsgs_mac(ModSrc ms, u64* res, const u64* const* c0s, const u64* const* c1s,
              long long bstride, int nb, int inputs, const u64* pts, long long pstride, int groups, int limbs, int n,
              cudaStream_t st) {
@@ -184,10 +338,20 @@ int bsgs_mac(ModSrc ms, u64* res, const u64* const* c0s, const u64* const* c1s,
     in.c0[i] = c0s[i < inputs ? i : 0];
     in.c1[i] = c1s[i < inputs ? i : 0];
   }
-  constexpr int TG = 8;
-  dim3 grid((unsigned)((n / 32) * ((inputs + 7) / 8)), (unsigned)limbs, (unsigned)((groups + TG - 1) / TG));
+  if (getenv("HOLMES_MAC_V1")) {  // the first-generation kernel, kept for A/B timing
+    constexpr int TG = 8;
+    dim3 grid((unsigned)((n / 32) * ((inputs + 7) / 8)), (unsigned)limbs, (unsigned)((groups + TG - 1) / TG));
+    count_launch();
+    k_bsgs_mac<TG><<<grid, 256, 0, st>>>(res, in, bstride, nb, inputs, groups, pts, pstride, limbs, ms, log_n);
+    return (int)cudaGetLastError();
+  }
+  const int smem = 2 * kMacStageWords * 8;
+  cudaError_t e = cudaFuncSetAttribute(k_bsgs_mac2, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return (int)e;
+  dim3 grid((unsigned)((n / 32) * ((inputs + kMacIW - 1) / kMacIW)), (unsigned)limbs,
+            (unsigned)((groups + kMacGG - 1) / kMacGG));
   count_launch();
-  k_bsgs_mac<TG><<<grid, 256, 0, st>>>(res, in, bstride, nb, inputs, groups, pts, pstride, limbs, ms, log_n);
+  k_bsgs_mac2<<<grid, 256, smem, st>>>(res, in, bstride, nb, inputs, groups, pts, pstride, limbs, ms, log_n);
   return (int)cudaGetLastError();
 }
 

@@ -50,12 +50,12 @@ struct StPlain {
 };
 
 template <int LOGN>
-__global__ void __launch_bounds__(NttGeom<LOGN>::THREADS) k_fwd_plain(NttTables T, PolyMap pm, LdPlain ld, StPlain st) {
+__global__ void HOLMES_NTT_BOUNDS(LOGN) k_fwd_plain(NttTables T, PolyMap pm, LdPlain ld, StPlain st) {
   const int p = blockIdx.x / NttGeom<LOGN>::CL;
   ntt_forward_body<LOGN>(p, pm.mod(p), T, ld, st);
 }
 template <int LOGN>
-__global__ void __launch_bounds__(NttGeom<LOGN>::THREADS) k_inv_plain(NttTables T, PolyMap pm, const Tw* scale,
+__global__ void HOLMES_NTT_BOUNDS(LOGN) k_inv_plain(NttTables T, PolyMap pm, const Tw* scale,
                                                                        int scale_by_limb, LdPlain ld, StPlain st) {
   const int p = blockIdx.x / NttGeom<LOGN>::CL;
   const int mi = pm.mod(p);
@@ -88,8 +88,8 @@ struct LdConv {
   int w, lo, cur, ntgt, L, T, log_n;
   struct S {
     const u64* y;
+    const u64* h;  // hat constants of the target modulus, stride T (read through the cache at use)
     Mod m;
-    u64 h[MAXA];
   };
   __device__ int target(int p) const {
     const int r = p % ntgt;
@@ -100,16 +100,14 @@ struct LdConv {
     const int mi = t < cur ? t : L + t - cur;
     S s;
     s.y = y + (p / ntgt) * y_item;
+    s.h = hat + mi;
     s.m = mods[mi];
-#pragma unroll
-    for (int a = 0; a < MAXA; ++a) s.h[a] = a < w ? hat[a * T + mi] : 0;
     return s;
   }
   __device__ u64 load(const S& s, int n) const {
     U128 acc{0, 0};
-#pragma unroll
-    for (int a = 0; a < MAXA; ++a)
-      if (a < w) mac128(acc, s.y[((size_t)a << log_n) + n], s.h[a]);
+#pragma unroll 4
+    for (int a = 0; a < w; ++a) mac128(acc, s.y[((size_t)a << log_n) + n], __ldg(s.h + a * T));
     return reduce128(acc, s.m);
   }
 };
@@ -127,7 +125,7 @@ struct StDigit {
 };
 
 template <int LOGN>
-__global__ void __launch_bounds__(NttGeom<LOGN>::THREADS) k_modup_ntt(NttTables T, LdConv ld, StDigit st) {
+__global__ void HOLMES_NTT_BOUNDS(LOGN) k_modup_ntt(NttTables T, LdConv ld, StDigit st) {
   const int p = blockIdx.x / NttGeom<LOGN>::CL;
   const int t = ld.target(p);
   const int mi = t < ld.cur ? t : ld.L + t - ld.cur;
@@ -225,7 +223,7 @@ struct StScratch {
   __device__ void store(const S& s, int n, u64 v) const { s.p[n] = v; }
 };
 template <int LOGN>
-__global__ void __launch_bounds__(NttGeom<LOGN>::THREADS) k_ks_p(NttTables T, const Tw* md_scale, LdKsP ld,
+__global__ void HOLMES_NTT_BOUNDS(LOGN) k_ks_p(NttTables T, const Tw* md_scale, LdKsP ld,
                                                                   StScratch st) {
   const int p = blockIdx.x / NttGeom<LOGN>::CL;
   const int k = (p % (2 * ld.K)) % ld.K;
@@ -240,23 +238,21 @@ struct LdKsQ {
   int cur, K, L, log_n;
   struct S {
     const u64* y;
+    const u64* h;  // (P/p_k) mod q_i for k < K, stride L (read through the cache at use)
     Mod m;
-    u64 h[MAXA];
   };
   __device__ S prep(int p) const {
     const int item = p / (2 * cur), r = p % (2 * cur), c = r / cur, i = r % cur;
     S s;
     s.y = scratch + (((size_t)item * 2 + c) * K << log_n);
+    s.h = md_hat + i;
     s.m = mods[i];
-#pragma unroll
-    for (int k = 0; k < MAXA; ++k) s.h[k] = k < K ? md_hat[k * L + i] : 0;
     return s;
   }
   __device__ u64 load(const S& s, int n) const {
     U128 acc{0, 0};
-#pragma unroll
-    for (int k = 0; k < MAXA; ++k)
-      if (k < K) mac128(acc, s.y[((size_t)k << log_n) + n], s.h[k]);
+#pragma unroll 4
+    for (int k = 0; k < K; ++k) mac128(acc, s.y[((size_t)k << log_n) + n], __ldg(s.h + k * L));
     return reduce128(acc, s.m);
   }
 };
@@ -314,7 +310,7 @@ struct StKsQ {
   }
 };
 template <int LOGN>
-__global__ void __launch_bounds__(NttGeom<LOGN>::THREADS) k_ks_q(NttTables T, LdKsQ ld, StKsQ st) {
+__global__ void HOLMES_NTT_BOUNDS(LOGN) k_ks_q(NttTables T, LdKsQ ld, StKsQ st) {
   const int p = blockIdx.x / NttGeom<LOGN>::CL;
   ntt_forward_body<LOGN>(p, (p % (2 * ld.cur)) % ld.cur, T, ld, st);
 }
@@ -411,7 +407,7 @@ struct StRescale {
   __device__ void store(const S& s, int n, u64 v) const { s.o[n] = shoup(sub_mod(s.a[n], v, s.q), s.t, s.q); }
 };
 template <int LOGN>
-__global__ void __launch_bounds__(NttGeom<LOGN>::THREADS) k_rescale(NttTables T, LdRescale ld, StRescale st) {
+__global__ void HOLMES_NTT_BOUNDS(LOGN) k_rescale(NttTables T, LdRescale ld, StRescale st) {
   const int p = blockIdx.x / NttGeom<LOGN>::CL;
   ntt_forward_body<LOGN>(p, p % (ld.cur - 1), T, ld, st);
 }
@@ -486,7 +482,7 @@ struct LdEncode {
   }
 };
 template <int LOGN>
-__global__ void __launch_bounds__(NttGeom<LOGN>::THREADS) k_encode(NttTables T, LdEncode ld, StPlain st) {
+__global__ void HOLMES_NTT_BOUNDS(LOGN) k_encode(NttTables T, LdEncode ld, StPlain st) {
   const int p = blockIdx.x / NttGeom<LOGN>::CL;
   ntt_forward_body<LOGN>(p, p % ld.cur, T, ld, st);
 }
@@ -529,7 +525,7 @@ struct LdDecrypt {
   __device__ u64 load(const S& s, int n) const { return add_mod(s.a[n], mul_mod(s.b[n], s.sk[n], s.m), s.m.q); }
 };
 template <int LOGN>
-__global__ void __launch_bounds__(NttGeom<LOGN>::THREADS) k_decrypt(NttTables T, const Tw* ninv, LdDecrypt ld,
+__global__ void HOLMES_NTT_BOUNDS(LOGN) k_decrypt(NttTables T, const Tw* ninv, LdDecrypt ld,
                                                                      StScratch st) {
   const int p = blockIdx.x / NttGeom<LOGN>::CL;
   ntt_inverse_body<LOGN>(p, p, ninv[p], T, ld, st);
@@ -557,7 +553,7 @@ struct LdSigned {
   __device__ u64 load(const S& s, int n) const { return signed_residue(v[n], s.m); }
 };
 template <int LOGN>
-__global__ void __launch_bounds__(NttGeom<LOGN>::THREADS) k_secret(NttTables T, LdSigned ld, StScratch st) {
+__global__ void HOLMES_NTT_BOUNDS(LOGN) k_secret(NttTables T, LdSigned ld, StScratch st) {
   const int p = blockIdx.x / NttGeom<LOGN>::CL;
   ntt_forward_body<LOGN>(p, p, T, ld, st);
 }
@@ -646,7 +642,7 @@ struct StKey {
   }
 };
 template <int LOGN>
-__global__ void __launch_bounds__(NttGeom<LOGN>::THREADS) k_keygen(NttTables T, LdError ld, StKey st) {
+__global__ void HOLMES_NTT_BOUNDS(LOGN) k_keygen(NttTables T, LdError ld, StKey st) {
   const int p = blockIdx.x / NttGeom<LOGN>::CL;
   ntt_forward_body<LOGN>(p, st.pm.mod(p), T, ld, st);
 }
@@ -704,7 +700,7 @@ struct StEnc {
   }
 };
 template <int LOGN>
-__global__ void __launch_bounds__(NttGeom<LOGN>::THREADS) k_encrypt(NttTables T, LdError ld, StEnc st) {
+__global__ void HOLMES_NTT_BOUNDS(LOGN) k_encrypt(NttTables T, LdError ld, StEnc st) {
   const int p = blockIdx.x / NttGeom<LOGN>::CL;
   ntt_forward_body<LOGN>(p, p, T, ld, st);
 }
