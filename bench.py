@@ -156,8 +156,11 @@ def run_engine(args) -> None:
         from datetime import timedelta
 
         dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+    from holmes_b200 import collectives as C
+
     n_inputs = args.inputs
-    mine = list(range(rank * n_inputs // world, (rank + 1) * n_inputs // world))
+    mine = list(C.token_shard(n_inputs, world, rank))
+    chunked = args.parallelism == "chunk" and world > 1
     cur = args.limbs
     spec, cfg, rots = spec_for(cur)
     client, ctx = F.generate_client_context(spec, f"cuda:{local}")
@@ -166,16 +169,31 @@ def run_engine(args) -> None:
     level = ctx.L - cur
     weight = make_weight()
     carriers = make_inputs(n_inputs)
-    cts = [session.encrypt(carriers[i], level=level, counter=i) for i in mine]
+    # chunk sharding: every rank holds all inputs and MACs its BSGS chunks; token sharding: its own inputs
+    held = list(range(n_inputs)) if chunked else mine
+    cts = [session.encrypt(carriers[i], level=level, counter=i) for i in held]
     op = LN.LinearOperator(crypto_context=session, token_lanes=LANES, config=cfg)
     lw = LN.LinearWeight(weight, dtype=np.complex128, crypto_context=session)
     lw.prepare(cfg)
+    my_chunks = C.chunk_shard(len(op.plan(DIM).chunks), world, rank)
     torch.cuda.synchronize()
 
     def step():
         op.clear_baby_cache()
-        outs, _ = op.apply(cts, lw)
-        return outs
+        return page(op, cts, lw)
+
+    def page(op_, cts_, lw_):
+        if not chunked:
+            outs, _ = op_.apply(cts_, lw_)
+            return outs
+        parts, _ = op_.apply(cts_, lw_, chunk_indices=my_chunks, rescale=False)
+        p0 = torch.cat([p.cv[0] for p in parts])
+        p1 = torch.cat([p.cv[1] for p in parts])
+        s0 = C.modular_reduce_scatter(ctx, p0, world)
+        s1 = C.modular_reduce_scatter(ctx, p1, world)
+        batch = F.Cipher([s0, s1], parts[0].state, parts[0].slots, False, len(mine), ctx)
+        res = F.rescale(batch, ctx)
+        return [res.cipher_like([res.cv[0][i:i + 1], res.cv[1][i:i + 1]], batch_size=1) for i in range(len(mine))]
 
     for _ in range(args.warmup):
         step()
@@ -191,11 +209,13 @@ def run_engine(args) -> None:
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("timed")
     start.record()
     for _ in range(args.steps):
         outs = step()
     end.record()
     torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
     F.OPTIMER.enabled = False
     count1 = _lib.ctypes.c_ulonglong()
     _lib.call("holmes_launch_count", _lib.ctypes.byref(count1))
@@ -222,7 +242,7 @@ def run_engine(args) -> None:
         w_dev = host_w.to(ctx.device, non_blocking=True)
         with LN.LinearWeight(w_dev, dtype=np.complex128, crypto_context=session) as lw2:
             with LN.LinearOperator(crypto_context=session, token_lanes=LANES, config=cfg) as op2:
-                res, _ = op2.apply(dev_in, lw2)
+                res = page(op2, dev_in, lw2)
         back = [torch.stack([r.cv[0][0], r.cv[1][0]]).to("cpu", non_blocking=True) for r in res]
         out_bytes = sum(b.numel() * 8 for b in back)
         return back
@@ -266,7 +286,7 @@ def run_engine(args) -> None:
                         "avg_launch_ms": round(d["ms"] / d["launches"], 4),
                         "share_of_step": round(d["ms"] / args.steps / ms, 4)}
         cpu = None
-        if args.cpu_baseline:
+        if args.cpu_baseline and world == 1:
             cpu = cpu_baseline(sample=args.cpu_sample)
         line = {
             "metric": METRIC, "value": round(ms / 1e3, 5), "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -275,7 +295,8 @@ def run_engine(args) -> None:
             "config": {"workload": f"QKV-shaped linear page: {n_inputs} ciphertexts x one 4096x4096 complex page, "
                                    f"N=2^16, {cur}/{DEPTH + 1} limbs, dnum {DNUM} (alpha {ctx.alpha}, K {ctx.K}), "
                                    f"baby 64, 8 chunks x 8 giants, lanes 8, rescale",
-                       "parallelism": f"token-sharded x{world}", "inputs_per_rank": len(mine),
+                       "parallelism": (f"chunk-sharded x{world} + modular reduce-scatter" if chunked
+                                       else f"token-sharded x{world}"), "inputs_per_rank": len(mine),
                        "l2": "working set (plaintext chunks 3.4 GB, baby basis 13.6 GB) >> 126 MB L2",
                        "keys": f"{len(rots)} rotation keys capped at {cur} limbs"},
             "roofline": roofline, "kernels": {k: {"launches": v["launches"], "ms_per_step": round(v["ms"] / args.steps, 3)}
@@ -366,19 +387,91 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_kernel(args) -> None:
+    """One bench-shaped launch of one kernel family (N = 2^16, 13 limbs, 16 ciphertexts), after one warm-up
+    launch, for profiler captures: ``mac`` (one chunk: 8 giants x 64 babies), ``keyswitch`` (k_ks_p + k_ks_q of
+    one baby rotation), ``modup``, ``ntt`` (forward NTT of 16 x 13 polynomials), ``encode`` (one chunk's 512 rows).
+    Memory on the device stays below 20 GB."""
+    import torch
+
+    from holmes_b200 import _lib as L
+    from holmes_b200 import fhe as F
+
+    spec, _, _ = spec_for(CUR_LIMBS)
+    _, ctx = F.generate_client_context(spec)
+    N, cur, I = ctx.N, CUR_LIMBS, INPUTS
+
+    def rand(items, limbs):
+        out = torch.empty((items, limbs, N), dtype=torch.uint64, device=ctx.device)
+        for li in range(limbs):
+            r = torch.randint(0, 2 ** 62, (items, N), device=ctx.device, dtype=torch.int64)
+            out[:, li] = (r % ctx.moduli[li]).to(torch.uint64)
+        return out
+
+    if args.kernel == "mac":
+        nb, G = 64, 8
+        pts = rand(G * nb, cur)
+        bab = rand(2 * nb * I, cur).reshape(2, nb, I, cur, N)
+        res = torch.empty((2, G, I, cur, N), dtype=torch.uint64, device=ctx.device)
+        c0s = L.ptr_array([bab[0, :, i].data_ptr() for i in range(I)])
+        c1s = L.ptr_array([bab[1, :, i].data_ptr() for i in range(I)])
+
+        def fn():
+            L.call("holmes_bsgs_mac", ctx.handle, res.data_ptr(), c0s, c1s, I * cur * N, nb, I, pts.data_ptr(),
+                   cur * N, G, cur, 0)
+    elif args.kernel in ("keyswitch", "modup"):
+        c0, c1 = rand(I, cur), rand(I, cur)
+        o0, o1 = torch.empty_like(c0), torch.empty_like(c1)
+        g = ctx.galois(LANES)
+        key = ctx.switch_key(g, cur)
+        digits, dig_item = F._modup(ctx, c1, cur, I)
+
+        def fn():
+            if args.kernel == "modup":
+                F._modup(ctx, c1, cur, I)
+            else:
+                F._keyswitch(ctx, digits, dig_item, cur, g, key, c0, None, F._item_stride(c0), o0, o1, I)
+    elif args.kernel == "ntt":
+        x = rand(I, cur)
+
+        def fn():
+            L.call("holmes_ntt", ctx.handle, x.data_ptr(), I, cur, cur * N, 0, 0, 0)
+    elif args.kernel == "encode":
+        rows = torch.randn((512, ctx.max_slots), dtype=torch.complex128, device=ctx.device) * 0.02
+        mid = F.fft_special_inv_rows(ctx, rows, ctx.max_slots)
+
+        def fn():
+            F.encode_rows(ctx, mid, cur, ctx.scale, ctx.max_slots, already_transformed=True)
+    else:
+        raise SystemExit(f"unknown kernel family {args.kernel}")
+    fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    fn()
+    b.record()
+    torch.cuda.synchronize()
+    print(json.dumps({"kernel": args.kernel, "ms": round(a.elapsed_time(b), 3)}), flush=True)
+    ctx.close()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
+    ap.add_argument("--kernel", default=None, help="profile one kernel family (see run_kernel)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("holmes", "reference"), default="holmes")
     ap.add_argument("--inputs", type=int, default=INPUTS)
     ap.add_argument("--limbs", type=int, default=CUR_LIMBS)
+    ap.add_argument("--parallelism", choices=("token", "chunk"), default="token")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--cpu-sample", default="small")
     ap.add_argument("--no-check", dest="check", action="store_false")
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.kernel:
+        run_kernel(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_engine(args)

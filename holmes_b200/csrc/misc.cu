@@ -202,12 +202,16 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 struct Split4 {
   u64 s00, sa, sb, s11;
 };
+// acc += a * b for 32-bit a, b and a 64-bit accumulator: one wide multiply-add
+__device__ __forceinline__ void mad_wide(u64& acc, u32 a, u32 b) {
+  asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(acc) : "r"(a), "r"(b));
+}
 __device__ __forceinline__ void mad_split(Split4& acc, u32 a0, u32 a1, u64 bp) {
   const u32 b0 = (u32)bp, b1 = (u32)(bp >> 32);
-  acc.s00 += (u64)a0 * b0;
-  acc.sa += (u64)a0 * b1;
-  acc.sb += (u64)a1 * b0;
-  acc.s11 += (u64)a1 * b1;
+  mad_wide(acc.s00, a0, b0);
+  mad_wide(acc.sa, a0, b1);
+  mad_wide(acc.sb, a1, b0);
+  mad_wide(acc.s11, a1, b1);
 }
 __device__ __forceinline__ u64 fold_split(const Split4& acc, const Mod& m) {
   // V = s00 + (sa << 30) + (sb << 30) + (s11 << 60) as 128 bits

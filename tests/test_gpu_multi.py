@@ -1,0 +1,66 @@
+"""Two GPUs over NCCL: the modular reduce-scatter of partial sums (raw limbs over all_to_all, owner-side mod-q sum
+with holmes_modsum) equals the oracle's sum.  Skipped with fewer than two GPUs."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, out_dir):
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from holmes_b200 import collectives as C
+    from tests.gpu_helpers import make_pair
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        _, _, ctx = make_pair(log_n=12, limbs=4, dnum=2, dcrt=45, first=55, special=55)
+        rng = np.random.default_rng(7 + rank)
+        items, limbs, n = 4, 4, ctx.N
+        parts = np.stack([rng.integers(0, ctx.moduli[l], (items, n), dtype=np.uint64) for l in range(limbs)], axis=1)
+        np.save(os.path.join(out_dir, f"p{rank}.npy"), parts)
+        got = C.modular_reduce_scatter(ctx, torch.from_numpy(parts).cuda(), world)
+        torch.cuda.synchronize()
+        np.save(os.path.join(out_dir, f"s{rank}.npy"), got.cpu().numpy())
+        np.save(os.path.join(out_dir, "q.npy"), np.array(ctx.moduli[:limbs], dtype=np.uint64))
+        dist.barrier()
+        ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_modular_reduce_scatter_two_gpus(tmp_path):
+    import torch.multiprocessing as mp
+
+    from holmes_b200 import collectives as C
+
+    world = 2
+    mp.spawn(_worker, args=(world, _port(), str(tmp_path)), nprocs=world, join=True)
+    parts = [np.load(tmp_path / f"p{r}.npy") for r in range(world)]
+    q = [int(v) for v in np.load(tmp_path / "q.npy")]
+    for r in range(world):
+        got = np.load(tmp_path / f"s{r}.npy")
+        owned = list(C.token_shard(4, world, r))
+        want = sum(p[owned].astype(object) for p in parts)
+        for li, ql in enumerate(q):
+            assert np.array_equal(got[:, li].astype(object), want[:, li] % ql)
