@@ -42,6 +42,19 @@ CUR_LIMBS = 13
 DIM, LANES, INPUTS = 4096, 8, 16
 
 
+def measured_traffic(family: str):
+    """DRAM bytes per launch of a kernel family from the committed ncu summary (profiles/traffic.txt), or None."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.txt"), encoding="utf-8") as f:
+            for line in f:
+                parts = line.split()
+                if len(parts) >= 2 and not line.startswith("#") and parts[0] == family:
+                    return int(parts[1])
+    except OSError:
+        pass
+    return None
+
+
 def peaks():
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json"), encoding="utf-8") as f:
@@ -281,7 +294,8 @@ def run_engine(args) -> None:
             per_launch_s = d["ms"] / 1e3 / d["launches"]
             achieved = d["bytes"] / d["launches"] / per_launch_s / 1e9
             roofline = {"bound": "hbm", "kernel": name, "achieved": round(achieved, 1), "peak": hbm,
-                        "peak_kind": kind, "unit": "GB/s", "frac": round(achieved / hbm, 4), "traffic": None,
+                        "peak_kind": kind, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                        "traffic": measured_traffic(name),
                         "algorithmic_bytes_per_launch": d["bytes"] // d["launches"],
                         "avg_launch_ms": round(d["ms"] / d["launches"], 4),
                         "share_of_step": round(d["ms"] / args.steps / ms, 4)}
