@@ -44,7 +44,9 @@ SIGNATURES = {
     "holmes_automorph": [p, p, p, u64, i32, i32, i64, i64, p],
     "holmes_mul_const": [p, p, p, p, i32, i32, i64, i64, p],
     "holmes_rescale": [p, p, i64, p, i64, i32, i32, p, p],
-    "holmes_rescale_noalloc": [p, p, i64, p, i64, i32, i32, p],
+    "holmes_modraise": [p, p, i64, p, i64, i32, i32, p, p],
+    "holmes_add_const": [p, p, p, p, i32, i32, i64, i64, p],
+    "holmes_rescale_noalloc":[p, p, i64, p, i64, i32, i32, p],
     "holmes_modup": [p, p, i64, i32, i32, p, i64, p, p],
     "holmes_keyswitch": [p, p, i64, i32, p, i32, u64, p, p, i64, p, p, i64, p, p, i64, i32, p, p],
     "holmes_bsgs_mac": [p, p, p, p, i64, i32, i32, p, i64, i32, i32, p],

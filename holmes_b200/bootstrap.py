@@ -1,0 +1,480 @@
+"""CKKS bootstrapping over libholmes_cuda (full-slot, "modraise first").
+
+The reference runs EasyFHE's OpenFHE-style bootstrap (``easyfhe.bs.openfhe``: ``BootstrapSpec``, ``generate``,
+``bootstrap``, ``requirements``; used by ``llama3fhe/operators/nonlinear/bootstrap.py:119-159, 249-294, 626-711``)
+in the pass order ModRaise -> CoeffsToSlots -> conjugate / real / imaginary -> EvalMod x 2 -> recombine ->
+SlotsToCoeffs (``bench/cmp/holmes_batch_bs.py:65-118``).  This module implements that pipeline from the
+published algorithm (Cheon-Han-Kim-Kim-Song 2018; cosine + double-angle EvalMod, Han-Ki 2020):
+
+* **ModRaise** -- the ciphertext is scaled by 2^-cf (one level) and brought to q0; ``holmes_modraise`` reads it as
+  centred integers modulo q_0..q_{raise-1}.  It now decrypts to t = m' + q0 I with |I| <= ``k_bound``.
+* **CoeffsToSlots** -- the special inverse FFT (without its bit reversal and 1/n) factored into log2(n) butterfly
+  stages with diagonals {0, +-len/2}, grouped into ``level_budget[0]`` levels; each level is one hoisted set of
+  rotations (one ModUp, one key switch per diagonal), one multi-diagonal MAC and one rescale.  The constant
+  Delta / (2 n q0 B) is spread evenly over the levels so no plaintext diagonal loses precision.
+* **EvalMod** -- the real and imaginary parts (one conjugation) are each mapped to sin(2 pi v) with
+  v = t_j / q0: cos(2 pi B w / 2^r) as a Chebyshev series on w = (v - 1/4) / B in [-1, 1], then r double-angle
+  steps c <- 2 c^2 - 1.
+* **SlotsToCoeffs** -- the forward special FFT stages with q0 2^cf / (2 pi Delta) spread over
+  ``level_budget[1]`` levels.
+
+Scales follow the reference's FIXEDMANUAL policy (``llama3fhe/config.py:15-25``): every ciphertext carries the
+nominal scale Delta = 2^dcrt_bits at every level; plaintext constants are encoded at the scale of the limb the
+next rescale drops, so a multiply-then-rescale returns to Delta.
+
+EasyFHE's constants, level split and EvalMod polynomial are not available, so residues are not comparable to the
+reference's; the result is checked at the decoded level (``tests/test_gpu_bootstrap.py``).
+"""
+from __future__ import annotations
+
+import math
+import time
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from . import _lib
+from . import fhe as F
+
+# --------------------------------------------------------------------------------------------------------- spec
+
+
+@dataclass(frozen=True)
+class BootstrapSpec:
+    log_slots: int = 15
+    level_budget: tuple = (4, 4)
+    output_levels: int = 24
+    strategy: str = "double_hoist"
+    mode: str = "modraise_first"
+    dim1: tuple | None = None
+    baby_step: tuple | None = None
+    # engine parameters
+    k_bound: int = 24            # bound on |I| in t = m' + q0 I after ModRaise (sparse secret)
+    cheb_degree: int = 63        # Chebyshev degree of the cosine
+    double_angles: int = 3       # r
+    correction_bits: int | None = None   # cf; default makes q0 2^cf / Delta ~ 2^10
+
+    def __post_init__(self) -> None:
+        if self.mode != "modraise_first":
+            raise ValueError(f"unsupported bootstrap mode {self.mode!r}")
+        if len(tuple(self.level_budget)) != 2 or min(self.level_budget) < 1:
+            raise ValueError("level_budget must be two positive integers")
+
+    @property
+    def evalmod_depth(self) -> int:
+        return int(math.ceil(math.log2(self.cheb_degree + 1))) + 1 + int(self.double_angles)
+
+    @property
+    def depth(self) -> int:
+        return int(self.level_budget[0]) + self.evalmod_depth + int(self.level_budget[1])
+
+
+@dataclass(frozen=True)
+class Requirements:
+    rotations: tuple
+    depth: int
+
+
+# --------------------------------------------------------------------------------------------------------- matrices
+
+
+def _rot_group(n: int, M: int) -> np.ndarray:
+    out = np.empty(n // 2 if n >= 2 else 1, dtype=np.int64)
+    r = 1
+    for j in range(out.size):
+        out[j] = r
+        r = (r * 5) % M
+    return out
+
+
+def _stage(n: int, length: int, M: int, inverse: bool) -> dict:
+    """One butterfly stage of the special FFT as {offset: diagonal} with out[p] = sum_r d_r[p] v[p + r]."""
+    half = length // 2
+    lenq = 4 * length
+    rot = _rot_group(max(length, 2), M)[:half]
+    p = np.arange(n)
+    j = p % length
+    lower = j < half
+    jj = np.where(lower, j, j - half)
+    if inverse:
+        k = (lenq - (rot[jj] % lenq)) * (M // lenq)
+    else:
+        k = (rot[jj] % lenq) * (M // lenq)
+    w = np.exp(2j * np.pi * k / M)
+    d0 = np.where(lower, 1.0 + 0j, -w)
+    if inverse:
+        dp = np.where(lower, 1.0 + 0j, 0j)
+        dm = np.where(lower, 0j, w)
+    else:
+        dp = np.where(lower, w, 0j)
+        dm = np.where(lower, 0j, 1.0 + 0j)
+    out = {0: d0}
+    for r, d in ((half % n, dp), ((-half) % n, dm)):  # +len/2 and -len/2 coincide when len = n
+        out[r] = out.get(r, 0) + d
+    return out
+
+
+def _compose(a: dict, b: dict, n: int) -> dict:
+    """Diagonals of A o B (apply B first): (A B)_{r+s} += A_r * rot(B_s, r)."""
+    out: dict = {}
+    for r, da in a.items():
+        for s, db in b.items():
+            key = (r + s) % n
+            term = da * np.roll(db, -r)
+            out[key] = out.get(key, 0) + term
+    return {k: v for k, v in out.items() if np.abs(v).max() > 0}
+
+
+def fft_levels(n: int, M: int, budget: int, inverse: bool) -> list[dict]:
+    """CoeffsToSlots (inverse=True: stages len = n .. 2) or SlotsToCoeffs (len = 2 .. n) grouped into ``budget``
+    levels, each the product of consecutive stages."""
+    lengths = [n >> i for i in range(int(math.log2(n)))] if inverse else [2 << i for i in range(int(math.log2(n)))]
+    stages = [_stage(n, ln, M, inverse) for ln in lengths]
+    groups = np.array_split(np.arange(len(stages)), budget)
+    levels = []
+    for g in groups:
+        mat = {0: np.ones(n, dtype=np.complex128)}
+        for idx in g:
+            mat = _compose(stages[idx], mat, n)
+        levels.append(mat)
+    return levels
+
+
+def apply_levels_numpy(levels: list[dict], v: np.ndarray, scales=None) -> np.ndarray:
+    """Plaintext application of grouped levels (host reference for the homomorphic transform)."""
+    out = np.asarray(v, dtype=np.complex128)
+    for i, mat in enumerate(levels):
+        acc = np.zeros_like(out)
+        for r, d in mat.items():
+            acc += d * np.roll(out, -r)
+        out = acc * (1.0 if scales is None else scales[i])
+    return out
+
+
+def chebyshev_cos(B: float, r: int, degree: int) -> np.ndarray:
+    """Chebyshev coefficients of cos(2 pi B w / 2^r) on w in [-1, 1]."""
+    f = lambda w: np.cos(2 * np.pi * B * w / (1 << r))  # noqa: E731
+    return np.polynomial.chebyshev.chebinterpolate(f, degree)
+
+
+# --------------------------------------------------------------------------------------------------------- program
+
+
+@dataclass
+class BootstrapProgram:
+    spec: BootstrapSpec
+    context: object
+    n: int
+    raise_to_limbs: int
+    output_limbs: int
+    cf: int
+    B: float
+    c2s: list
+    s2c: list
+    c2s_scale: float
+    s2c_scale: float
+    cheb: np.ndarray
+    rotations: tuple
+    _plain: dict = field(default_factory=dict)
+    setup_seconds: float = 0.0
+
+    @property
+    def output_state(self) -> F.CipherState:
+        return F.CipherState(self.output_limbs, 1, self.context.scale)
+
+    def diagonal_plaintexts(self, which: str, level: int, cur: int):
+        """Encoded diagonals of one transform level at ``cur`` limbs, scale q_{cur-1} (cached)."""
+        key = (which, level, cur)
+        hit = self._plain.get(key)
+        if hit is not None:
+            return hit
+        ctx = self.context
+        mats = self.c2s if which == "c2s" else self.s2c
+        factor = self.c2s_scale if which == "c2s" else self.s2c_scale
+        mat = mats[level]
+        offsets = sorted(mat)
+        rows = np.stack([mat[r] * factor for r in offsets])
+        scale = float(ctx.q(cur - 1))
+        pv = F.encode_rows(ctx, torch.from_numpy(rows).to(ctx.device), cur, scale, self.n)
+        ctx.check_encode_range()
+        pt = F.Plaintext([pv], F.CipherState(cur, 1, scale), self.n, False, len(offsets), ctx)
+        self._plain[key] = (offsets, pt)
+        return self._plain[key]
+
+
+def requirements(specs, log_n: int) -> Requirements:
+    rots: set = set()
+    depth = 0
+    for spec in specs:
+        n = 1 << int(spec.log_slots)
+        M = 2 << int(log_n)
+        for inverse, budget in ((True, spec.level_budget[0]), (False, spec.level_budget[1])):
+            for mat in fft_levels(n, M, int(budget), inverse):
+                rots.update(int(r) for r in mat if int(r))
+        rots.add(M - 1)
+        depth = max(depth, spec.depth)
+    return Requirements(tuple(sorted(rots)), depth)
+
+
+def generate(context, spec: BootstrapSpec) -> BootstrapProgram:
+    """Precompute one bootstrap program for ``context`` (``bs.generate``)."""
+    start = time.perf_counter()
+    ctx = context
+    n = 1 << int(spec.log_slots)
+    if n != ctx.N // 2:
+        raise ValueError(f"only full-slot bootstrapping is implemented (slots {ctx.N // 2}, got {n})")
+    raise_to = ctx.L
+    out_limbs = raise_to - spec.depth
+    if out_limbs < 2:
+        raise ValueError(f"bootstrap depth {spec.depth} leaves {out_limbs} limbs of {raise_to}")
+    q0 = ctx.q(0)
+    delta = ctx.scale
+    cf = spec.correction_bits
+    if cf is None:
+        cf = max(0, int(round(10 - math.log2(q0 / delta))))
+    B = float(spec.k_bound + 1)
+    c2s = fft_levels(n, ctx.M, int(spec.level_budget[0]), True)
+    s2c = fft_levels(n, ctx.M, int(spec.level_budget[1]), False)
+    c2s_total = delta / (2.0 * n * q0 * B)
+    s2c_total = q0 * (2.0 ** cf) / (2.0 * math.pi * delta)
+    cheb = chebyshev_cos(B, int(spec.double_angles), int(spec.cheb_degree))
+    req = requirements([spec], ctx.logN)
+    prog = BootstrapProgram(spec=spec, context=ctx, n=n, raise_to_limbs=raise_to, output_limbs=out_limbs, cf=cf, B=B,
+                            c2s=c2s, s2c=s2c, c2s_scale=c2s_total ** (1.0 / len(c2s)),
+                            s2c_scale=s2c_total ** (1.0 / len(s2c)), cheb=cheb, rotations=req.rotations)
+    prog.setup_seconds = time.perf_counter() - start
+    return prog
+
+
+# --------------------------------------------------------------------------------------------------------- helpers
+# Every helper keeps the FIXEDMANUAL invariant: the result carries the nominal scale Delta.
+
+
+def _residues(ctx, value: float, scale: float, limbs: int) -> torch.Tensor:
+    """round(value * scale) as residues of the first ``limbs`` moduli (device tensor)."""
+    v = int(round(float(value) * float(scale)))
+    return torch.tensor([v % ctx.q(i) for i in range(limbs)], dtype=torch.uint64, device=ctx.device)
+
+
+def _nominal(ct: F.Cipher) -> F.Cipher:
+    ct.state = F.CipherState(int(ct.state.cur_limbs), 1, float(ct.context.scale))
+    return ct
+
+
+def _stream():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def mul_scalar_rescale(ct: F.Cipher, value: float) -> F.Cipher:
+    ctx = ct.context
+    cur = int(ct.state.cur_limbs)
+    k = _residues(ctx, value, float(ctx.q(cur - 1)), cur)
+    out = F._new_cipher(ctx, ct.batch_size, cur, F.CipherState(cur, 2, None), ct.slots)
+    for c in range(2):
+        _lib.call("holmes_mul_const", ctx.handle, ct.cv[c].data_ptr(), k.data_ptr(), out.cv[c].data_ptr(),
+                  ct.batch_size, cur, F._item_stride(ct.cv[c]), F._item_stride(out.cv[c]), _stream())
+    return _nominal(F.rescale(out, ctx))
+
+
+def add_scalar(ct: F.Cipher, value: float) -> F.Cipher:
+    ctx = ct.context
+    cur = int(ct.state.cur_limbs)
+    k = _residues(ctx, value, float(ctx.scale), cur)
+    out = F.Cipher([torch.empty_like(ct.cv[0][:, :cur]), ct.cv[1][:, :cur].clone()], ct.state, ct.slots, False,
+                   ct.batch_size, ctx)
+    _lib.call("holmes_add_const", ctx.handle, ct.cv[0].data_ptr(), k.data_ptr(), out.cv[0].data_ptr(), ct.batch_size,
+              cur, F._item_stride(ct.cv[0]), F._item_stride(out.cv[0]), _stream())
+    return out
+
+
+def drop_to(ct: F.Cipher, limbs: int) -> F.Cipher:
+    if int(ct.state.cur_limbs) == limbs:
+        return ct
+    return F.align_to(ct, ct.state.replace(cur_limbs=int(limbs)), ct.context)
+
+
+def mul_rescale(a: F.Cipher, b: F.Cipher) -> F.Cipher:
+    lim = min(int(a.state.cur_limbs), int(b.state.cur_limbs))
+    a, b = drop_to(a, lim), drop_to(b, lim)
+    return _nominal(F.rescale(F.homo_mul_relin(a, b, a.context), a.context))
+
+
+def add(a: F.Cipher, b: F.Cipher) -> F.Cipher:
+    lim = min(int(a.state.cur_limbs), int(b.state.cur_limbs))
+    return F.homo_add(_nominal(drop_to(a, lim)), _nominal(drop_to(b, lim)), a.context)
+
+
+def sub(a: F.Cipher, b: F.Cipher) -> F.Cipher:
+    lim = min(int(a.state.cur_limbs), int(b.state.cur_limbs))
+    return F.homo_sub(_nominal(drop_to(a, lim)), _nominal(drop_to(b, lim)), a.context)
+
+
+def linear_level(ct: F.Cipher, offsets, pt: F.Plaintext) -> F.Cipher:
+    """sum_r diag_r * rot(ct, r): hoisted rotations (one ModUp), one multi-diagonal MAC, one rescale."""
+    ctx = ct.context
+    cur = int(ct.state.cur_limbs)
+    items = ct.batch_size
+    nb = len(offsets)
+    store = torch.empty((2, nb, items, cur, ctx.N), dtype=torch.uint64, device=ctx.device)
+    digits = dig_item = None
+    for b, off in enumerate(offsets):
+        g = ctx.galois(int(off))
+        if g == 1:
+            store[0, b].copy_(ct.cv[0][:, :cur])
+            store[1, b].copy_(ct.cv[1][:, :cur])
+            continue
+        if digits is None:
+            digits, dig_item = F._modup(ctx, ct.cv[1], cur, items)
+        F._keyswitch(ctx, digits, dig_item, cur, g, ctx.switch_key(g, cur), ct.cv[0], None, F._item_stride(ct.cv[0]),
+                     store[0, b], store[1, b], items)
+    blocks = [F.Cipher([store[0, :, i], store[1, :, i]], ct.state, ct.slots, False, nb, ctx) for i in range(items)]
+    res = F.bsgs_partial_sums(ctx, blocks, pt, 1)          # [2][1][items][cur][N]
+    out = F.Cipher([res[0, 0], res[1, 0]], F.CipherState(cur, 2, None), ct.slots, False, items, ctx)
+    return _nominal(F.rescale(out, ctx))
+
+
+def _chebyshev(w: F.Cipher, coeffs: np.ndarray) -> F.Cipher:
+    """sum_k c_k T_k(w) with T_2k = 2 T_k^2 - 1, T_2k+1 = 2 T_k T_k+1 - T_1."""
+    d = len(coeffs) - 1
+    T: dict = {1: w}
+
+    def get(k: int) -> F.Cipher:
+        if k in T:
+            return T[k]
+        if k % 2 == 0:
+            a = get(k // 2)
+            sq = mul_rescale(a, a)
+            T[k] = add_scalar(F.homo_add(sq, sq, sq.context), -1.0)
+        else:
+            a, b = get(k // 2), get(k // 2 + 1)
+            pr = mul_rescale(a, b)
+            T[k] = sub(F.homo_add(pr, pr, pr.context), T[1])
+        return T[k]
+
+    terms = []
+    for k in range(1, d + 1):
+        if abs(coeffs[k]) < 1e-18:
+            continue
+        terms.append(mul_scalar_rescale(get(k), float(coeffs[k])))
+    lim = min(int(t.state.cur_limbs) for t in terms)
+    acc = drop_to(terms[0], lim)
+    for t in terms[1:]:
+        acc = add(acc, t)
+    return add_scalar(acc, float(coeffs[0]))
+
+
+def eval_mod(x: F.Cipher, program: BootstrapProgram) -> F.Cipher:
+    """x holds v / B (v = t_j / q0); returns sin(2 pi v)."""
+    w = add_scalar(x, -0.25 / program.B)
+    c = _chebyshev(w, program.cheb)
+    for _ in range(int(program.spec.double_angles)):
+        sq = mul_rescale(c, c)
+        c = add_scalar(F.homo_add(sq, sq, sq.context), -1.0)
+    return c
+
+
+def bootstrap(ct: F.Cipher, ctx, program: BootstrapProgram) -> F.Cipher:
+    """Refresh ``ct`` (>= 2 limbs, scale degree 1) to ``program.output_limbs`` limbs (``bs.bootstrap``)."""
+    ctx = F._ctx(ctx)
+    if int(ct.state.cur_limbs) < 2:
+        raise ValueError("bootstrap input needs at least two limbs")
+    if int(ct.state.scale_degree) != 1 or ct.is_ext:
+        raise ValueError("bootstrap input must be a non-extended degree-1 ciphertext")
+    if int(ct.slots) != program.n:
+        raise ValueError(f"bootstrap program is for {program.n} slots, ciphertext has {ct.slots}")
+    x = _nominal(drop_to(ct, 2).deep_copy() if int(ct.state.cur_limbs) > 2 else ct.deep_copy())
+    x = mul_scalar_rescale(x, 2.0 ** (-program.cf))                    # -> q0 alone
+    raise_to = program.raise_to_limbs
+    items = x.batch_size
+    raised = F._new_cipher(ctx, items, raise_to, F.CipherState(raise_to, 1, ctx.scale), x.slots)
+    scratch = ctx.workspace("modraise", items * ctx.N)
+    for c in range(2):
+        _lib.call("holmes_modraise", ctx.handle, x.cv[c].data_ptr(), F._item_stride(x.cv[c]), raised.cv[c].data_ptr(),
+                  F._item_stride(raised.cv[c]), raise_to, items, scratch.data_ptr(), _stream())
+    y = raised
+    for lvl in range(len(program.c2s)):
+        offsets, pt = program.diagonal_plaintexts("c2s", lvl, int(y.state.cur_limbs))
+        y = linear_level(y, offsets, pt)
+    conj = F.homo_rotate(y, ctx.M - 1, ctx)
+    re = F.homo_add(y, conj, ctx)
+    im = F.homo_mul_i(F.homo_sub(conj, y, ctx), ctx)
+    re = eval_mod(re, program)
+    im = eval_mod(im, program)
+    z = add(re, F.homo_mul_i(im, ctx))
+    for lvl in range(len(program.s2c)):
+        offsets, pt = program.diagonal_plaintexts("s2c", lvl, int(z.state.cur_limbs))
+        z = linear_level(z, offsets, pt)
+    return _nominal(drop_to(z, program.output_limbs))
+
+
+# --------------------------------------------------------------------------------------------------------- operator
+
+
+@dataclass(frozen=True)
+class BootstrapConfig:
+    """Reference: ``llama3fhe/operators/nonlinear/bootstrap.py:47-159`` (full-slot program)."""
+
+    log_slots: int = 15
+    level_budget: tuple = (4, 4)
+    output_levels: int = 24
+    iterations: int = 1
+    precision_bits: int = 8
+    mode: str = "modraise_first"
+    strategy: str = "double_hoist"
+    k_bound: int = 24
+    cheb_degree: int = 63
+    double_angles: int = 3
+
+    def spec(self) -> BootstrapSpec:
+        return BootstrapSpec(log_slots=self.log_slots, level_budget=tuple(self.level_budget),
+                             output_levels=self.output_levels, strategy=self.strategy, mode=self.mode,
+                             k_bound=self.k_bound, cheb_degree=self.cheb_degree, double_angles=self.double_angles)
+
+
+@dataclass
+class BootstrapOperator:
+    """Prepared bootstrap program (reference: ``BootstrapOperator.prepare / refresh / refresh_many``)."""
+
+    crypto_context: object
+    config: BootstrapConfig
+    program: BootstrapProgram
+    setup_seconds: float
+    calls: int = 0
+    batch_calls: int = 0
+
+    @classmethod
+    def prepare(cls, crypto_context, config: BootstrapConfig) -> "BootstrapOperator":
+        start = time.perf_counter()
+        ctx = crypto_context.context
+        program = generate(ctx, config.spec())
+        ctx.generate_rotation_keys(program.rotations, ctx.L)
+        ctx.switch_key(0, ctx.L)
+        return cls(crypto_context, config, program, time.perf_counter() - start)
+
+    @staticmethod
+    def required_rotations(*, log_n: int, log_slots: int = 15, level_budget: tuple = (4, 4), **_) -> tuple:
+        return requirements([BootstrapSpec(log_slots=log_slots, level_budget=tuple(level_budget))], log_n).rotations
+
+    def refresh(self, cipher, **_) -> F.Cipher:
+        if int(self.config.iterations) != 1:
+            raise NotImplementedError("the two-pass (Meta-BTS) correction is not implemented")
+        self.calls += 1
+        return bootstrap(cipher, self.crypto_context.context, self.program)
+
+    def refresh_many(self, ciphers, **kw) -> list:
+        """All ciphertexts of one state in one batched pass (every step runs on the batch)."""
+        ciphers = list(ciphers)
+        if not ciphers:
+            return []
+        if len(ciphers) == 1 or any(c.state != ciphers[0].state for c in ciphers):
+            return [self.refresh(c, **kw) for c in ciphers]
+        ctx = self.crypto_context.context
+        cur = int(ciphers[0].state.cur_limbs)
+        c0 = torch.stack([c.cv[0][0, :cur] for c in ciphers])
+        c1 = torch.stack([c.cv[1][0, :cur] for c in ciphers])
+        batch = F.Cipher([c0, c1], ciphers[0].state, ciphers[0].slots, False, len(ciphers), ctx)
+        out = bootstrap(batch, ctx, self.program)
+        self.calls += len(ciphers)
+        self.batch_calls += 1
+        return [out.cipher_like([out.cv[0][i:i + 1], out.cv[1][i:i + 1]], batch_size=1) for i in range(len(ciphers))]

@@ -169,6 +169,18 @@ int holmes_rescale(void* ctx, const uint64_t* in, long long in_stride, uint64_t*
   return rescale(*C(ctx), in, in_stride, out, out_stride, cur, comps, scratch, S(stream));
 }
 
+int holmes_modraise(void* ctx, const uint64_t* in, long long in_stride, uint64_t* out, long long out_stride, int raise,
+                    int comps, uint64_t* scratch, void* stream) {
+  if (!ctx || !in || !out || !scratch) return -1;
+  return modraise(*C(ctx), in, in_stride, out, out_stride, raise, comps, scratch, S(stream));
+}
+
+int holmes_add_const(void* ctx, const uint64_t* a, const uint64_t* consts, uint64_t* out, int items, int limbs,
+                     long long a_item, long long out_item, void* stream) {
+  if (!ctx || !a || !consts || !out) return -1;
+  return add_const(*C(ctx), a, consts, out, items, limbs, a_item, out_item, S(stream));
+}
+
 int holmes_modup(void* ctx, const uint64_t* c1, long long c1_item, int cur, int items, uint64_t* digits,
                  long long digit_item, uint64_t* scratch, void* stream) {
   if (!ctx || !c1 || !digits || !scratch) return -1;

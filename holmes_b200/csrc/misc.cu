@@ -115,6 +115,25 @@ int mul_const(const HolmesCtx& c, const u64* a, const u64* consts, u64* out, int
   return (int)cudaGetLastError();
 }
 
+__global__ void k_add_const(const u64* __restrict__ a, const u64* __restrict__ k, u64* __restrict__ o, int items,
+                            int limbs, long long ai, long long oi, int log_n, const Mod* __restrict__ mods) {
+  const size_t per_item = (size_t)limbs << log_n;
+  const size_t total = (size_t)items * per_item;
+  for (size_t w = blockIdx.x * (size_t)blockDim.x + threadIdx.x; w < total; w += (size_t)gridDim.x * blockDim.x) {
+    const int item = (int)(w / per_item);
+    const size_t r = w - (size_t)item * per_item;
+    const int limb = (int)(r >> log_n);
+    o[item * oi + r] = add_mod(a[item * ai + r], k[limb], mods[limb].q);
+  }
+}
+int add_const(const HolmesCtx& c, const u64* a, const u64* consts, u64* out, int items, int limbs, long long a_item,
+              long long o_item, cudaStream_t st) {
+  if (limbs < 1 || limbs > c.T || items < 1) return -2;
+  const size_t work = (size_t)items * limbs * c.n;
+  k_add_const<<<grid_for(work, 256), 256, 0, st>>>(a, consts, out, items, limbs, a_item, o_item, c.log_n, c.d_mod);
+  return (int)cudaGetLastError();
+}
+
 // --------------------------------------------------------------------------------------------- BSGS MAC
 // res[c][g][i][limb][j] = sum_b pts[g nb + b][limb][j] * baby_i[b][c][limb][j]  (mod q_limb)
 // (semantics of the reference's mac_multi, bench/cmp/kernels/holmes_mac.cu:1-13, 116-190).

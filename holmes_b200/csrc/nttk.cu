@@ -448,6 +448,72 @@ int rescale(const HolmesCtx& c, const u64* in, long long in_stride, u64* out, lo
   }
 }
 
+// --------------------------------------------------------------------------------------------- mod raise
+// Bootstrapping's first step: a ciphertext modulo q0 alone is read as integer coefficients in
+// (-q0/2, q0/2] and re-expressed modulo q_0 .. q_{raise-1}: iNTT of limb 0, centred lift fused into the NTT
+// load of every raised limb.
+struct LdLift {
+  const u64* x;  // scratch [comps][N]: coefficients mod q0
+  const Mod* mods;
+  u64 q0;
+  int raise, log_n;
+  struct S {
+    const u64* x;
+    Mod m;
+    u64 q0m;
+  };
+  __device__ S prep(int p) const {
+    S s;
+    s.x = x + ((size_t)(p / raise) << log_n);
+    s.m = mods[p % raise];
+    s.q0m = reduce128(0, q0, s.m);
+    return s;
+  }
+  __device__ u64 load(const S& s, int n) const {
+    const u64 v = s.x[n];
+    const u64 r = reduce128(0, v, s.m);
+    return v > (q0 >> 1) ? sub_mod(r, s.q0m, s.m.q) : r;
+  }
+};
+template <int LOGN>
+__global__ void HOLMES_NTT_BOUNDS(LOGN) k_modraise(NttTables T, LdLift ld, StPlain st) {
+  const int p = blockIdx.x / NttGeom<LOGN>::CL;
+  ntt_forward_body<LOGN>(p, p % ld.raise, T, ld, st);
+}
+
+int modraise(const HolmesCtx& c, const u64* in, long long in_stride, u64* out, long long out_stride, int raise,
+             int comps, u64* scratch, cudaStream_t st) {
+  if (raise < 2 || raise > c.L || comps < 1) return -2;
+  const int N = c.n;
+  {
+    NttTables T{c.d_itw, c.d_mod};
+    PolyMap pin = poly_map(1, in_stride, N, 0);
+    PolyMap pout = poly_map(1, N, N, 0);
+    LdPlain ld{in, pin};
+    StPlain sp{scratch, pout};
+#define L_(LG)                                                                                                 \
+  {                                                                                                            \
+    using G = NttGeom<LG>;                                                                                     \
+    cudaError_t e = launch_ntt(k_inv_plain<LG>, G::LOGCL, G::THREADS, G::SMEM, comps, st, T, pin, c.d_ninv, 0, \
+                               ld, sp);                                                                        \
+    if (e != cudaSuccess) return (int)e;                                                                       \
+    break;                                                                                                     \
+  }
+    HOLMES_LOGN_SWITCH(c.log_n, L_)
+#undef L_
+  }
+  NttTables T{c.d_tw, c.d_mod};
+  LdLift ld{scratch, c.d_mod, c.q[0], raise, c.log_n};
+  StPlain sp{out, poly_map(raise, out_stride, N, 0)};
+#define L_(LG)                                                                                         \
+  {                                                                                                    \
+    using G = NttGeom<LG>;                                                                             \
+    return (int)launch_ntt(k_modraise<LG>, G::LOGCL, G::THREADS, G::SMEM, comps * raise, st, T, ld, sp); \
+  }
+  HOLMES_LOGN_SWITCH(c.log_n, L_)
+#undef L_
+}
+
 // --------------------------------------------------------------------------------------------- encode
 // Coefficient n of a row: Re(u[n / gap]) for n < N/2, Im(u[(n - N/2) / gap]) above, 0 off the gap grid;
 // rounded with llround(v * scale) (bench/cmp/kernels/holmes_encode.cu:136-159) and reduced mod q_i.

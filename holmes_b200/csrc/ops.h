@@ -72,6 +72,14 @@ int ks_apply(const HolmesCtx& c, const KsArgs& a, cudaStream_t st);
 int rescale(const HolmesCtx& c, const u64* in, long long in_stride, u64* out, long long out_stride, int cur, int comps,
             u64* scratch, cudaStream_t st);
 
+// Mod raise: [comps][1][N] modulo q0 (item stride in_stride) -> [comps][raise][N] (centred lift), scratch >= comps * N.
+int modraise(const HolmesCtx& c, const u64* in, long long in_stride, u64* out, long long out_stride, int raise,
+             int comps, u64* scratch, cudaStream_t st);
+
+// out[item][l][n] = a[item][l][n] + consts[l] (a constant polynomial added in the NTT domain)
+int add_const(const HolmesCtx& c, const u64* a, const u64* consts, u64* out, int items, int limbs, long long a_item,
+              long long o_item, cudaStream_t st);
+
 // Rows of slot vectors after the special inverse FFT ([rows][slots] complex, interleaved doubles) ->
 // [rows][cur][N] NTT plaintexts at `scale`.  Out-of-range values set *flag = 1.
 int encode_rows(const HolmesCtx& c, const double* u, long long row_stride, int rows, int slots, double scale, int cur,

@@ -95,6 +95,16 @@ int holmes_mul_const(void* ctx, const uint64_t* a, const uint64_t* consts, uint6
 int holmes_rescale(void* ctx, const uint64_t* in, long long in_stride, uint64_t* out, long long out_stride, int cur,
                    int comps, uint64_t* scratch, void* stream);
 
+/* bootstrapping's ModRaise (EasyFHE bs.openfhe raise_ciphertext, bench/cmp/holmes_batch_bs.py:65-90): in[comps][1][N]
+ * modulo q0 (NTT) is read as centred integers and written modulo q_0..q_{raise-1}: out[comps][raise][N];
+ * scratch >= comps * N words */
+int holmes_modraise(void* ctx, const uint64_t* in, long long in_stride, uint64_t* out, long long out_stride, int raise,
+                    int comps, uint64_t* scratch, void* stream);
+/* add consts[l] (device, canonical residues) to every NTT word of limb l: a constant polynomial
+ * (fhe.homo_add_scalar, operators/nonlinear/polynomial.py) */
+int holmes_add_const(void* ctx, const uint64_t* a, const uint64_t* consts, uint64_t* out, int items, int limbs,
+                     long long a_item, long long out_item, void* stream);
+
 /* holmes_rescale without caller scratch, for callers that cannot allocate device memory (a runtime that
  * owns the whole pool, or a loop where cudaMalloc's device synchronisation is unacceptable).  No
  * counterpart in the reference.  Scratch comes from a 2 MiB array compiled into the library (held by every

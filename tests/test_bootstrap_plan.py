@@ -1,0 +1,63 @@
+"""Bootstrapping host logic on CPU: the level-grouped butterfly factorisation of CoeffsToSlots / SlotsToCoeffs
+against the oracle's special FFT, the Chebyshev cosine, and the key / depth requirements."""
+import numpy as np
+import pytest
+
+from holmes_b200 import bootstrap as BS
+from oracle.oracle import Oracle, OracleParams, _p, lib
+
+
+def _bitrev(v):
+    n = v.size
+    bits = n.bit_length() - 1
+    idx = np.array([int(format(i, f"0{bits}b")[::-1], 2) for i in range(n)])
+    return v[idx]
+
+
+@pytest.mark.parametrize(("log_n", "budget"), [(10, 3), (12, 3), (12, 4), (13, 5)])
+def test_transform_levels_match_special_fft(log_n, budget):
+    o = Oracle(OracleParams(log_n=log_n, limbs=2, dnum=1, dcrt_bits=40, first_mod_bits=50, special_bits=50))
+    n, M = o.pr.n // 2, 2 * o.pr.n
+    rng = np.random.default_rng(log_n)
+    v = rng.normal(size=n) + 1j * rng.normal(size=n)
+    # oracle special inverse FFT (with bit reversal and 1/n)
+    re, im = np.ascontiguousarray(v.real), np.ascontiguousarray(v.imag)
+    lib().orc_fft_special_inv(_p(re), _p(im), n, M, _p(o.rot_group), _p(o.ksi_re), _p(o.ksi_im))
+    inv = re + 1j * im
+    c2s = BS.fft_levels(n, M, budget, inverse=True)
+    assert len(c2s) == budget
+    np.testing.assert_allclose(BS.apply_levels_numpy(c2s, v), n * _bitrev(inv), atol=1e-8 * n)
+    # forward: butterflies after bit reversal
+    re, im = np.ascontiguousarray(v.real), np.ascontiguousarray(v.imag)
+    lib().orc_fft_special(_p(re), _p(im), n, M, _p(o.rot_group), _p(o.ksi_re), _p(o.ksi_im))
+    fwd = re + 1j * im
+    s2c = BS.fft_levels(n, M, budget, inverse=False)
+    np.testing.assert_allclose(BS.apply_levels_numpy(s2c, _bitrev(v)), fwd, atol=1e-8 * n)
+    # diagonal counts: a level of s stages has at most 2^(s+1) - 1 diagonals
+    stages = int(np.log2(n))
+    for lvl in c2s + s2c:
+        assert len(lvl) <= 2 ** (int(np.ceil(stages / budget)) + 1) - 1
+
+
+def test_chebyshev_cosine_accuracy():
+    B, r = 13.0, 3
+    c = BS.chebyshev_cos(B, r, 63)
+    w = np.linspace(-1, 1, 2001)
+    got = np.polynomial.chebyshev.chebval(w, c)
+    assert np.abs(got - np.cos(2 * np.pi * B * w / 2 ** r)).max() < 1e-12
+    # r double angles of cos(2 pi (v - 1/4) / 2^r) give sin(2 pi v)
+    v = np.linspace(-12.4, 12.4, 997)
+    x = np.polynomial.chebyshev.chebval((v - 0.25) / B, c)
+    for _ in range(r):
+        x = 2 * x * x - 1
+    assert np.abs(x - np.sin(2 * np.pi * v)).max() < 1e-9
+
+
+def test_requirements_and_depth():
+    spec = BS.BootstrapSpec(log_slots=11, level_budget=(3, 3), k_bound=12)
+    req = BS.requirements([spec], log_n=12)
+    assert spec.depth == 3 + 10 + 3 == req.depth
+    assert (2 << 12) - 1 in req.rotations
+    assert all(0 < r < (1 << 11) or r == (2 << 12) - 1 for r in req.rotations)
+    with pytest.raises(ValueError):
+        BS.BootstrapSpec(mode="slots_first")

@@ -1,0 +1,68 @@
+"""CKKS bootstrapping on the GPU: residue-for-residue against the CPU restatement (oracle/bootstrap_oracle.py),
+decoded against the input message, and batched refresh (refresh_many) identical to one-at-a-time refresh.
+
+Ring N = 2^12 (2^11 slots), 20 limbs of 59/60-bit primes (the reference's production prime sizes), level budget
+(3, 3): depth 3 + 10 + 3 = 16, so 4 limbs remain."""
+import numpy as np
+import pytest
+
+from tests.gpu_helpers import host, make_pair
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def boot():
+    from holmes_b200 import bootstrap as BS
+    from holmes_b200 import linear as LN
+
+    o, client, ctx = make_pair(log_n=12, limbs=20, dnum=4, dcrt=59, first=60, special=60, hamming=64, seed=1)
+    session = LN.Session(client, ctx)
+    cfg = BS.BootstrapConfig(log_slots=11, level_budget=(3, 3), k_bound=12)
+    op = BS.BootstrapOperator.prepare(session, cfg)
+    yield o, client, ctx, op
+    ctx.close()
+
+
+def test_bootstrap_decodes_to_the_message(boot):
+    _, client, ctx, op = boot
+    rng = np.random.default_rng(0)
+    z = (rng.normal(size=ctx.max_slots) + 1j * rng.normal(size=ctx.max_slots)) * 0.5
+    ct = client.encrypt(z, cur_limbs=3, counter=5)
+    out = op.refresh(ct)
+    assert int(out.state.cur_limbs) == op.program.output_limbs == ctx.L - 16
+    err = np.abs(client.decrypt(out) - z).max()
+    assert err < 1e-4, err
+
+
+def test_bootstrap_bitexact_vs_oracle(boot):
+    from oracle.bootstrap_oracle import OracleBootstrap
+
+    o, client, ctx, op = boot
+    rng = np.random.default_rng(1)
+    z = rng.normal(size=ctx.max_slots) * 0.3
+    ct = client.encrypt(z, cur_limbs=2, counter=9)
+    ref = o.encrypt(z, 2, counter=9)
+    got = op.refresh(ct)
+    e0, e1 = OracleBootstrap(o, op.program).bootstrap(ref)
+    np.testing.assert_array_equal(host(got.cv[0][0]), e0)
+    np.testing.assert_array_equal(host(got.cv[1][0]), e1)
+
+
+def test_refresh_many_matches_single(boot):
+    _, client, ctx, op = boot
+    rng = np.random.default_rng(2)
+    cts = [client.encrypt(rng.normal(size=ctx.max_slots) * 0.4, cur_limbs=3, counter=20 + i) for i in range(3)]
+    many = op.refresh_many(cts)
+    for ct, m in zip(cts, many):
+        one = op.refresh(ct)
+        np.testing.assert_array_equal(host(m.cv[0][0]), host(one.cv[0][0]))
+        np.testing.assert_array_equal(host(m.cv[1][0]), host(one.cv[1][0]))
+    assert op.batch_calls >= 1
+
+
+def test_bootstrap_rejects_bad_input(boot):
+    _, client, ctx, op = boot
+    ct = client.encrypt(np.zeros(ctx.max_slots), cur_limbs=1, counter=30)
+    with pytest.raises(ValueError):
+        op.refresh(ct)
