@@ -469,8 +469,51 @@ def run_kernel(args) -> None:
     ctx.close()
 
 
+def run_bootstrap(args) -> None:
+    """Production-size bootstrap: N = 2^16, 38 limbs (59/60-bit, dnum 5), level budget (5, 5) -> 18 limbs left
+    (llama3fhe/parallel/presets.py:25-60), a batch of ``--boot-batch`` ciphertexts refreshed together
+    (BootstrapOperator.refresh_many, the pair-refresh call of parallel/prefill/stations.py:102-174)."""
+    import torch
+
+    from holmes_b200 import bootstrap as BS
+    from holmes_b200 import fhe as F
+    from holmes_b200 import linear as LN
+
+    spec = F.CKKSContextSpec(depth=DEPTH, log_n=LOG_N, dnum=DNUM, dcrt_bits=DCRT, first_mod=FIRST, special_bits=60,
+                             hamming_weight=192, seed=0, auto_load_keys=False)
+    client, ctx = F.generate_client_context(spec)
+    session = LN.Session(client, ctx)
+    t0 = time.perf_counter()
+    op = BS.BootstrapOperator.prepare(session, BS.BootstrapConfig(log_slots=15, level_budget=(5, 5)))
+    torch.cuda.synchronize()
+    setup = time.perf_counter() - t0
+    rng = np.random.default_rng(0)
+    zs = [(rng.normal(size=ctx.max_slots) + 1j * rng.normal(size=ctx.max_slots)) * 0.5 for _ in range(args.boot_batch)]
+    cts = [client.encrypt(z, cur_limbs=3, counter=i) for i, z in enumerate(zs)]
+    for _ in range(max(1, args.warmup)):
+        op.refresh_many(cts)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        outs = op.refresh_many(cts)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    err = max(float(np.abs(client.decrypt(o) - z).max()) for o, z in zip(outs, zs))
+    print(json.dumps({"metric": "CKKS bootstrap latency per ciphertext (full slots, N=2^16, 38 -> 18 limbs)",
+                      "value": round(ms / 1e3 / len(cts), 5), "unit": "s", "batch": len(cts),
+                      "ms_per_batch": round(ms, 2), "steps": args.steps, "higher_is_better": False,
+                      "max_abs_err": err, "setup_s": round(setup, 1), "rotation_keys": len(op.program.rotations),
+                      "key_gb": round(ctx.key_bytes / 1e9, 1), "depth": op.program.spec.depth,
+                      "output_limbs": op.program.output_limbs}), flush=True)
+    ctx.close()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
+    ap.add_argument("--workload", choices=("linear", "bootstrap"), default="linear")
+    ap.add_argument("--boot-batch", type=int, default=8)
     ap.add_argument("--kernel", default=None, help="profile one kernel family (see run_kernel)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=3)
@@ -485,6 +528,8 @@ def main() -> None:
     args = ap.parse_args()
     if args.kernel:
         run_kernel(args)
+    elif args.workload == "bootstrap":
+        run_bootstrap(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -248,39 +248,58 @@ def generate(context, spec: BootstrapSpec) -> BootstrapProgram:
 
 
 # --------------------------------------------------------------------------------------------------------- helpers
-# Every helper keeps the FIXEDMANUAL invariant: the result carries the nominal scale Delta.
-
-
-def _residues(ctx, value: float, scale: float, limbs: int) -> torch.Tensor:
-    """round(value * scale) as residues of the first ``limbs`` moduli (device tensor)."""
-    v = int(round(float(value) * float(scale)))
-    return torch.tensor([v % ctx.q(i) for i in range(limbs)], dtype=torch.uint64, device=ctx.device)
-
-
-def _nominal(ct: F.Cipher) -> F.Cipher:
-    ct.state = F.CipherState(int(ct.state.cur_limbs), 1, float(ct.context.scale))
-    return ct
+# Exact scales.  A ciphertext's state.scaling_factor is always its true scale.  Inside EvalMod every ciphertext at
+# l limbs carries the canonical scale S[l], S[l-1] = S[l]^2 / q_{l-1}: a product of two level-l ciphertexts lands
+# on S[l-1] by itself, and level drops and scalar products multiply by an integer chosen to land on S exactly.
+# (Treating every scale as the nominal 2^59 would be off by the primes' distance from 2^59, about 2^-32 at
+# N = 2^16, and EvalMod multiplies that by the q0 * I overflow term it removes.)
 
 
 def _stream():
     return torch.cuda.current_stream().cuda_stream
 
 
-def mul_scalar_rescale(ct: F.Cipher, value: float) -> F.Cipher:
+def scale_table(top_limbs: int, top_scale: float, ctx) -> dict:
+    S = {int(top_limbs): float(top_scale)}
+    for lv in range(int(top_limbs), 1, -1):
+        S[lv - 1] = S[lv] * S[lv] / float(ctx.q(lv - 1))
+    return S
+
+
+def int_mul_rescale(ct: F.Cipher, k: int, new_scale: float) -> F.Cipher:
+    """ct * k (an integer) then rescale; the result is declared at ``new_scale``."""
     ctx = ct.context
     cur = int(ct.state.cur_limbs)
-    k = _residues(ctx, value, float(ctx.q(cur - 1)), cur)
+    res = torch.tensor([int(k) % ctx.q(i) for i in range(cur)], dtype=torch.uint64, device=ctx.device)
     out = F._new_cipher(ctx, ct.batch_size, cur, F.CipherState(cur, 2, None), ct.slots)
     for c in range(2):
-        _lib.call("holmes_mul_const", ctx.handle, ct.cv[c].data_ptr(), k.data_ptr(), out.cv[c].data_ptr(),
+        _lib.call("holmes_mul_const", ctx.handle, ct.cv[c].data_ptr(), res.data_ptr(), out.cv[c].data_ptr(),
                   ct.batch_size, cur, F._item_stride(ct.cv[c]), F._item_stride(out.cv[c]), _stream())
-    return _nominal(F.rescale(out, ctx))
+    r = F.rescale(out, ctx)
+    r.state = F.CipherState(cur - 1, 1, float(new_scale))
+    return r
+
+
+def mul_scalar_to(ct: F.Cipher, value: float, target: float) -> F.Cipher:
+    """value * ct at one limb fewer, landing on scale ``target``."""
+    q = float(ct.context.q(int(ct.state.cur_limbs) - 1))
+    k = int(round(float(value) * target * q / float(ct.state.scaling_factor)))
+    return int_mul_rescale(ct, k, target)
+
+
+def adjust(ct: F.Cipher, limbs: int, S: dict) -> F.Cipher:
+    """Drop ``ct`` to ``limbs`` limbs, landing on the canonical scale S[limbs]."""
+    while int(ct.state.cur_limbs) > int(limbs):
+        cur = int(ct.state.cur_limbs)
+        ct = mul_scalar_to(ct, 1.0, S[cur - 1])
+    return ct
 
 
 def add_scalar(ct: F.Cipher, value: float) -> F.Cipher:
     ctx = ct.context
     cur = int(ct.state.cur_limbs)
-    k = _residues(ctx, value, float(ctx.scale), cur)
+    v = int(round(float(value) * float(ct.state.scaling_factor)))
+    k = torch.tensor([v % ctx.q(i) for i in range(cur)], dtype=torch.uint64, device=ctx.device)
     out = F.Cipher([torch.empty_like(ct.cv[0][:, :cur]), ct.cv[1][:, :cur].clone()], ct.state, ct.slots, False,
                    ct.batch_size, ctx)
     _lib.call("holmes_add_const", ctx.handle, ct.cv[0].data_ptr(), k.data_ptr(), out.cv[0].data_ptr(), ct.batch_size,
@@ -289,29 +308,35 @@ def add_scalar(ct: F.Cipher, value: float) -> F.Cipher:
 
 
 def drop_to(ct: F.Cipher, limbs: int) -> F.Cipher:
+    """Modulus-only drop (the scale is kept)."""
     if int(ct.state.cur_limbs) == limbs:
         return ct
     return F.align_to(ct, ct.state.replace(cur_limbs=int(limbs)), ct.context)
 
 
-def mul_rescale(a: F.Cipher, b: F.Cipher) -> F.Cipher:
+def mul_rescale(a: F.Cipher, b: F.Cipher, S: dict) -> F.Cipher:
     lim = min(int(a.state.cur_limbs), int(b.state.cur_limbs))
-    a, b = drop_to(a, lim), drop_to(b, lim)
-    return _nominal(F.rescale(F.homo_mul_relin(a, b, a.context), a.context))
+    a, b = adjust(a, lim, S), adjust(b, lim, S)
+    return F.rescale(F.homo_mul_relin(a, b, a.context), a.context)
 
 
-def add(a: F.Cipher, b: F.Cipher) -> F.Cipher:
+def double(a: F.Cipher) -> F.Cipher:
+    return F.homo_add(a, a, a.context)
+
+
+def add(a: F.Cipher, b: F.Cipher, S: dict) -> F.Cipher:
     lim = min(int(a.state.cur_limbs), int(b.state.cur_limbs))
-    return F.homo_add(_nominal(drop_to(a, lim)), _nominal(drop_to(b, lim)), a.context)
+    return F.homo_add(adjust(a, lim, S), adjust(b, lim, S), a.context)
 
 
-def sub(a: F.Cipher, b: F.Cipher) -> F.Cipher:
+def sub(a: F.Cipher, b: F.Cipher, S: dict) -> F.Cipher:
     lim = min(int(a.state.cur_limbs), int(b.state.cur_limbs))
-    return F.homo_sub(_nominal(drop_to(a, lim)), _nominal(drop_to(b, lim)), a.context)
+    return F.homo_sub(adjust(a, lim, S), adjust(b, lim, S), a.context)
 
 
 def linear_level(ct: F.Cipher, offsets, pt: F.Plaintext) -> F.Cipher:
-    """sum_r diag_r * rot(ct, r): hoisted rotations (one ModUp), one multi-diagonal MAC, one rescale."""
+    """sum_r diag_r * rot(ct, r): hoisted rotations (one ModUp), one multi-diagonal MAC, one rescale.  The diagonals
+    are encoded at the scale of the limb the rescale drops, so the scale is unchanged."""
     ctx = ct.context
     cur = int(ct.state.cur_limbs)
     items = ct.batch_size
@@ -330,47 +355,53 @@ def linear_level(ct: F.Cipher, offsets, pt: F.Plaintext) -> F.Cipher:
                      store[0, b], store[1, b], items)
     blocks = [F.Cipher([store[0, :, i], store[1, :, i]], ct.state, ct.slots, False, nb, ctx) for i in range(items)]
     res = F.bsgs_partial_sums(ctx, blocks, pt, 1)          # [2][1][items][cur][N]
-    out = F.Cipher([res[0, 0], res[1, 0]], F.CipherState(cur, 2, None), ct.slots, False, items, ctx)
-    return _nominal(F.rescale(out, ctx))
+    out = F.Cipher([res[0, 0], res[1, 0]], F.CipherState(cur, 2, float(ct.state.scaling_factor) * float(ctx.q(cur - 1))),
+                   ct.slots, False, items, ctx)
+    return F.rescale(out, ctx)
 
 
-def _chebyshev(w: F.Cipher, coeffs: np.ndarray) -> F.Cipher:
-    """sum_k c_k T_k(w) with T_2k = 2 T_k^2 - 1, T_2k+1 = 2 T_k T_k+1 - T_1."""
+def _chebyshev(w: F.Cipher, coeffs: np.ndarray, S: dict) -> F.Cipher:
+    """sum_k c_k T_k(w) with T_2k = 2 T_k^2 - 1, T_2k+1 = 2 T_k T_k+1 - T_1 (canonical scales throughout)."""
     d = len(coeffs) - 1
     T: dict = {1: w}
+    low: dict = {}
+
+    def t1_at(limbs: int) -> F.Cipher:
+        if limbs not in low:
+            low[limbs] = adjust(w, limbs, S)
+        return low[limbs]
 
     def get(k: int) -> F.Cipher:
         if k in T:
             return T[k]
         if k % 2 == 0:
             a = get(k // 2)
-            sq = mul_rescale(a, a)
-            T[k] = add_scalar(F.homo_add(sq, sq, sq.context), -1.0)
+            T[k] = add_scalar(double(mul_rescale(a, a, S)), -1.0)
         else:
-            a, b = get(k // 2), get(k // 2 + 1)
-            pr = mul_rescale(a, b)
-            T[k] = sub(F.homo_add(pr, pr, pr.context), T[1])
+            p = double(mul_rescale(get(k // 2), get(k // 2 + 1), S))
+            T[k] = F.homo_sub(p, t1_at(int(p.state.cur_limbs)), p.context)
         return T[k]
 
     terms = []
     for k in range(1, d + 1):
         if abs(coeffs[k]) < 1e-18:
             continue
-        terms.append(mul_scalar_rescale(get(k), float(coeffs[k])))
+        tk = get(k)
+        terms.append(mul_scalar_to(tk, float(coeffs[k]), S[int(tk.state.cur_limbs) - 1]))
     lim = min(int(t.state.cur_limbs) for t in terms)
-    acc = drop_to(terms[0], lim)
+    acc = adjust(terms[0], lim, S)
     for t in terms[1:]:
-        acc = add(acc, t)
+        acc = F.homo_add(acc, adjust(t, lim, S), acc.context)
     return add_scalar(acc, float(coeffs[0]))
 
 
 def eval_mod(x: F.Cipher, program: BootstrapProgram) -> F.Cipher:
     """x holds v / B (v = t_j / q0); returns sin(2 pi v)."""
+    S = scale_table(int(x.state.cur_limbs), float(x.state.scaling_factor), x.context)
     w = add_scalar(x, -0.25 / program.B)
-    c = _chebyshev(w, program.cheb)
+    c = _chebyshev(w, program.cheb, S)
     for _ in range(int(program.spec.double_angles)):
-        sq = mul_rescale(c, c)
-        c = add_scalar(F.homo_add(sq, sq, sq.context), -1.0)
+        c = add_scalar(double(mul_rescale(c, c, S)), -1.0)
     return c
 
 
@@ -383,11 +414,14 @@ def bootstrap(ct: F.Cipher, ctx, program: BootstrapProgram) -> F.Cipher:
         raise ValueError("bootstrap input must be a non-extended degree-1 ciphertext")
     if int(ct.slots) != program.n:
         raise ValueError(f"bootstrap program is for {program.n} slots, ciphertext has {ct.slots}")
-    x = _nominal(drop_to(ct, 2).deep_copy() if int(ct.state.cur_limbs) > 2 else ct.deep_copy())
-    x = mul_scalar_rescale(x, 2.0 ** (-program.cf))                    # -> q0 alone
+    s_in = float(ct.state.scaling_factor if ct.state.scaling_factor is not None else ctx.scale)
+    x = drop_to(ct, 2).deep_copy() if int(ct.state.cur_limbs) > 2 else ct.deep_copy()
+    x.state = F.CipherState(2, 1, s_in)
+    k_pre = int(round(2.0 ** (-program.cf) * float(ctx.q(1))))
+    x = int_mul_rescale(x, k_pre, s_in)                 # polynomial * k_pre / q1 ~ 2^-cf, now modulo q0 alone
     raise_to = program.raise_to_limbs
     items = x.batch_size
-    raised = F._new_cipher(ctx, items, raise_to, F.CipherState(raise_to, 1, ctx.scale), x.slots)
+    raised = F._new_cipher(ctx, items, raise_to, F.CipherState(raise_to, 1, float(ctx.scale)), x.slots)
     scratch = ctx.workspace("modraise", items * ctx.N)
     for c in range(2):
         _lib.call("holmes_modraise", ctx.handle, x.cv[c].data_ptr(), F._item_stride(x.cv[c]), raised.cv[c].data_ptr(),
@@ -401,11 +435,15 @@ def bootstrap(ct: F.Cipher, ctx, program: BootstrapProgram) -> F.Cipher:
     im = F.homo_mul_i(F.homo_sub(conj, y, ctx), ctx)
     re = eval_mod(re, program)
     im = eval_mod(im, program)
-    z = add(re, F.homo_mul_i(im, ctx))
+    z = F.homo_add(re, F.homo_mul_i(im, ctx), ctx)
     for lvl in range(len(program.s2c)):
         offsets, pt = program.diagonal_plaintexts("s2c", lvl, int(z.state.cur_limbs))
         z = linear_level(z, offsets, pt)
-    return _nominal(drop_to(z, program.output_limbs))
+    z = drop_to(z, program.output_limbs)
+    # S2C's constant assumed the message at the nominal scale: declare the scale at which z holds the input values
+    m_scale = s_in * k_pre * 2.0 ** program.cf / float(ctx.q(1))
+    z.state = F.CipherState(int(z.state.cur_limbs), 1, float(z.state.scaling_factor) * float(ctx.scale) / m_scale)
+    return z
 
 
 # --------------------------------------------------------------------------------------------------------- operator

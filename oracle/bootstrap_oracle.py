@@ -3,7 +3,8 @@
 Same pass order as the reference's batched bootstrap (``bench/cmp/holmes_batch_bs.py:65-118``: ModRaise ->
 CoeffsToSlots -> conjugate / real / imaginary -> EvalMod x 2 -> recombine -> SlotsToCoeffs) and as
 ``holmes_b200.bootstrap``, on the oracle's exact CPU primitives (``oracle/oracle.py``), so the GPU result can be
-compared residue for residue.  The transform diagonals and the Chebyshev coefficients are the host-side plan of
+compared residue for residue; scales are tracked exactly, with the same floating-point
+steps as the GPU path, so the integer constants agree.  The transform diagonals and the Chebyshev coefficients are the host-side plan of
 ``holmes_b200.bootstrap`` (``fft_levels`` / ``chebyshev_cos``), which ``tests/test_bootstrap_plan.py`` checks
 against the oracle's special FFT.  EasyFHE's own bootstrap constants are not available: parity with the
 reference binary is unpinned here; the decoded result is checked against the input message.
@@ -24,87 +25,112 @@ class OracleBootstrap:
         self.prog = program
         self.delta = float(2.0 ** self.pr.scale_bits)
 
-    # -- FIXEDMANUAL helpers (nominal scale Delta after every rescale)
+    # -- exact scales: a ciphertext is (c0, c1, scale); inside EvalMod the scale at l limbs is the canonical
+    #    S[l], S[l-1] = S[l]^2 / q_{l-1}, reached by integer multiplies before each rescale
     def _ids(self, cur):
         return list(range(cur))
 
-    def _res(self, value, scale, cur):
-        v = int(round(float(value) * float(scale)))
-        return [v % self.pr.q[i] for i in range(cur)]
+    def scale_table(self, top, s_top):
+        S = {top: float(s_top)}
+        for lv in range(top, 1, -1):
+            S[lv - 1] = S[lv] * S[lv] / float(self.pr.q[lv - 1])
+        return S
 
-    def mul_scalar_rescale(self, ct, value):
-        cur = ct[0].shape[0]
-        k = self._res(value, float(self.pr.q[cur - 1]), cur)
+    def int_mul_rescale(self, ct, k, new_scale):
+        c0, c1, _ = ct
+        cur = c0.shape[0]
+        r = [int(k) % self.pr.q[i] for i in range(cur)]
         o = self.o
-        return o.rescale((o.mul_scalar(ct[0], k, self._ids(cur)), o.mul_scalar(ct[1], k, self._ids(cur))))
+        d0, d1 = o.rescale((o.mul_scalar(c0, r, self._ids(cur)), o.mul_scalar(c1, r, self._ids(cur))))
+        return d0, d1, float(new_scale)
+
+    def mul_scalar_to(self, ct, value, target):
+        q = float(self.pr.q[ct[0].shape[0] - 1])
+        return self.int_mul_rescale(ct, int(round(float(value) * target * q / float(ct[2]))), target)
+
+    def adjust(self, ct, lim, S):
+        while ct[0].shape[0] > lim:
+            ct = self.mul_scalar_to(ct, 1.0, S[ct[0].shape[0] - 1])
+        return ct
 
     def add_scalar(self, ct, value):
-        cur = ct[0].shape[0]
-        k = self._res(value, self.delta, cur)
-        c0 = ct[0].copy()
+        c0, c1, sf = ct
+        cur = c0.shape[0]
+        v = int(round(float(value) * float(sf)))
+        out = c0.copy()
         for i in range(cur):
-            c0[i] = ((c0[i].astype(object) + k[i]) % self.pr.q[i]).astype(np.uint64)
-        return c0, ct[1].copy()
+            out[i] = ((out[i].astype(object) + v % self.pr.q[i]) % self.pr.q[i]).astype(np.uint64)
+        return out, c1.copy(), sf
 
     @staticmethod
     def drop(ct, lim):
-        return ct[0][:lim].copy(), ct[1][:lim].copy()
+        return ct[0][:lim].copy(), ct[1][:lim].copy(), ct[2]
 
-    def mul_rescale(self, a, b):
-        lim = min(a[0].shape[0], b[0].shape[0])
-        return self.o.rescale(self.o.mul_relin(self.drop(a, lim), self.drop(b, lim)))
+    def _add(self, a, b, sub=False):
+        f = self.o.sub if sub else self.o.add
+        lim = a[0].shape[0]
+        return f(a[0], b[0], self._ids(lim)), f(a[1], b[1], self._ids(lim)), a[2]
 
-    def add(self, a, b):
+    def mul_rescale(self, a, b, S):
         lim = min(a[0].shape[0], b[0].shape[0])
-        a, b = self.drop(a, lim), self.drop(b, lim)
-        return self.o.add(a[0], b[0], self._ids(lim)), self.o.add(a[1], b[1], self._ids(lim))
-
-    def sub(self, a, b):
-        lim = min(a[0].shape[0], b[0].shape[0])
-        a, b = self.drop(a, lim), self.drop(b, lim)
-        return self.o.sub(a[0], b[0], self._ids(lim)), self.o.sub(a[1], b[1], self._ids(lim))
+        a, b = self.adjust(a, lim, S), self.adjust(b, lim, S)
+        d0, d1 = self.o.rescale(self.o.mul_relin(a[:2], b[:2]))
+        return d0, d1, float(a[2]) * float(b[2]) / self.pr.q[lim - 1]
 
     def linear(self, ct, mat, factor):
         o = self.o
-        cur = ct[0].shape[0]
+        c0, c1, sf = ct
+        cur = c0.shape[0]
         offs = sorted(mat)
-        rots = o.hoisted_rotations(ct, offs)
+        rots = o.hoisted_rotations((c0, c1), offs)
         acc = None
-        for r, (c0, c1) in zip(offs, rots):
+        for r, (r0, r1) in zip(offs, rots):
             pt = o.encode(mat[r] * factor, cur, float(self.pr.q[cur - 1]))
-            t = (o.mul(c0, pt, self._ids(cur)), o.mul(c1, pt, self._ids(cur)))
+            t = (o.mul(r0, pt, self._ids(cur)), o.mul(r1, pt, self._ids(cur)))
             acc = t if acc is None else (o.add(acc[0], t[0], self._ids(cur)), o.add(acc[1], t[1], self._ids(cur)))
-        return o.rescale(acc)
+        d0, d1 = o.rescale(acc)
+        return d0, d1, float(sf) * float(self.pr.q[cur - 1]) / self.pr.q[cur - 1]
 
-    def chebyshev(self, w):
+    def chebyshev(self, w, S):
         coeffs = self.prog.cheb
         T = {1: w}
+        low = {}
+
+        def t1_at(lim):
+            if lim not in low:
+                low[lim] = self.adjust(w, lim, S)
+            return low[lim]
 
         def get(k):
             if k in T:
                 return T[k]
             if k % 2 == 0:
                 a = get(k // 2)
-                s = self.mul_rescale(a, a)
-                T[k] = self.add_scalar(self.add(s, s), -1.0)
+                s = self.mul_rescale(a, a, S)
+                T[k] = self.add_scalar(self._add(s, s), -1.0)
             else:
-                a, b = get(k // 2), get(k // 2 + 1)
-                p = self.mul_rescale(a, b)
-                T[k] = self.sub(self.add(p, p), T[1])
+                p = self.mul_rescale(get(k // 2), get(k // 2 + 1), S)
+                T[k] = self._add(self._add(p, p), t1_at(p[0].shape[0]), sub=True)
             return T[k]
 
-        terms = [self.mul_scalar_rescale(get(k), float(coeffs[k])) for k in range(1, len(coeffs))
-                 if abs(coeffs[k]) >= 1e-18]
-        acc = self.drop(terms[0], min(t[0].shape[0] for t in terms))
+        terms = []
+        for k in range(1, len(coeffs)):
+            if abs(coeffs[k]) < 1e-18:
+                continue
+            tk = get(k)
+            terms.append(self.mul_scalar_to(tk, float(coeffs[k]), S[tk[0].shape[0] - 1]))
+        lim = min(t[0].shape[0] for t in terms)
+        acc = self.adjust(terms[0], lim, S)
         for t in terms[1:]:
-            acc = self.add(acc, t)
+            acc = self._add(acc, self.adjust(t, lim, S))
         return self.add_scalar(acc, float(coeffs[0]))
 
     def eval_mod(self, x):
-        c = self.chebyshev(self.add_scalar(x, -0.25 / self.prog.B))
+        S = self.scale_table(x[0].shape[0], x[2])
+        c = self.chebyshev(self.add_scalar(x, -0.25 / self.prog.B), S)
         for _ in range(int(self.prog.spec.double_angles)):
-            s = self.mul_rescale(c, c)
-            c = self.add_scalar(self.add(s, s), -1.0)
+            s = self.mul_rescale(c, c, S)
+            c = self.add_scalar(self._add(s, s), -1.0)
         return c
 
     def modraise(self, ct, raise_to):
@@ -115,24 +141,32 @@ class OracleBootstrap:
             v = np.where(v > q0 // 2, v - q0, v)
             rows = np.stack([np.array([int(a) % self.pr.q[i] for a in v], dtype=np.uint64) for i in range(raise_to)])
             out.append(o.ntt(rows, self._ids(raise_to)))
-        return tuple(out)
+        return out[0], out[1], self.delta
 
-    def bootstrap(self, ct):
+    def bootstrap(self, ct, s_in=None):
+        """Refresh ``ct`` = (c0, c1) at scale ``s_in`` (default 2^scale_bits); returns (c0, c1, scale)."""
         o, prog = self.o, self.prog
-        x = self.drop(ct, 2) if ct[0].shape[0] > 2 else (ct[0].copy(), ct[1].copy())
-        x = self.mul_scalar_rescale(x, 2.0 ** (-prog.cf))
+        s_in = self.delta if s_in is None else float(s_in)
+        x = (ct[0][:2].copy(), ct[1][:2].copy(), s_in)
+        k_pre = int(round(2.0 ** (-prog.cf) * float(self.pr.q[1])))
+        x = self.int_mul_rescale(x, k_pre, s_in)
         y = self.modraise(x, prog.raise_to_limbs)
         for lvl in prog.c2s:
             y = self.linear(y, lvl, prog.c2s_scale)
         cur = y[0].shape[0]
-        cj = o.rotate(y, 2 * self.pr.n - 1)          # conjugation: rotation index M - 1
-        re = (o.add(y[0], cj[0], self._ids(cur)), o.add(y[1], cj[1], self._ids(cur)))
-        im = o.mul_i((o.sub(cj[0], y[0], self._ids(cur)), o.sub(cj[1], y[1], self._ids(cur))))
-        re, im = self.eval_mod(re), self.eval_mod(im)
-        z = self.add(re, o.mul_i(im))
+        c0, c1 = o.rotate(y[:2], 2 * self.pr.n - 1)          # conjugation: rotation index M - 1
+        cj = (c0, c1, y[2])
+        re = self._add(y, cj)
+        d = self._add(cj, y, sub=True)
+        i0, i1 = o.mul_i(d[:2])
+        re, im = self.eval_mod(re), self.eval_mod((i0, i1, d[2]))
+        j0, j1 = o.mul_i(im[:2])
+        z = self._add(re, (j0, j1, im[2]))
         for lvl in prog.s2c:
             z = self.linear(z, lvl, prog.s2c_scale)
-        return self.drop(z, prog.output_limbs)
+        z = self.drop(z, prog.output_limbs)
+        m_scale = s_in * k_pre * 2.0 ** prog.cf / float(self.pr.q[1])
+        return z[0], z[1], float(z[2]) * self.delta / m_scale
 
 
 __all__ = ["OracleBootstrap"]

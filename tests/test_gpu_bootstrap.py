@@ -32,7 +32,7 @@ def test_bootstrap_decodes_to_the_message(boot):
     out = op.refresh(ct)
     assert int(out.state.cur_limbs) == op.program.output_limbs == ctx.L - 16
     err = np.abs(client.decrypt(out) - z).max()
-    assert err < 1e-4, err
+    assert err < 1e-6, err
 
 
 def test_bootstrap_bitexact_vs_oracle(boot):
@@ -44,9 +44,10 @@ def test_bootstrap_bitexact_vs_oracle(boot):
     ct = client.encrypt(z, cur_limbs=2, counter=9)
     ref = o.encrypt(z, 2, counter=9)
     got = op.refresh(ct)
-    e0, e1 = OracleBootstrap(o, op.program).bootstrap(ref)
+    e0, e1, esf = OracleBootstrap(o, op.program).bootstrap(ref, s_in=float(ct.state.scaling_factor))
     np.testing.assert_array_equal(host(got.cv[0][0]), e0)
     np.testing.assert_array_equal(host(got.cv[1][0]), e1)
+    assert float(got.state.scaling_factor) == esf
 
 
 def test_refresh_many_matches_single(boot):
