@@ -405,7 +405,8 @@ def run_kernel(args) -> None:
     """One bench-shaped launch of one kernel family (N = 2^16, 13 limbs, 16 ciphertexts), after one warm-up
     launch, for profiler captures: ``mac`` (one chunk: 8 giants x 64 babies), ``keyswitch`` (k_ks_p + k_ks_q of
     one baby rotation), ``modup``, ``ntt`` (forward NTT of 16 x 13 polynomials), ``encode`` (one chunk's 512 rows).
-    Memory on the device stays below 20 GB."""
+    ``--inputs`` / ``--limbs`` shrink the case (multi-pass captures want a few GB on the device); at the bench
+    shape memory on the device stays below 20 GB."""
     import torch
 
     from holmes_b200 import _lib as L
@@ -413,7 +414,7 @@ def run_kernel(args) -> None:
 
     spec, _, _ = spec_for(CUR_LIMBS)
     _, ctx = F.generate_client_context(spec)
-    N, cur, I = ctx.N, CUR_LIMBS, INPUTS
+    N, cur, I = ctx.N, int(args.limbs), int(args.inputs)
 
     def rand(items, limbs):
         out = torch.empty((items, limbs, N), dtype=torch.uint64, device=ctx.device)

@@ -347,6 +347,217 @@ __global__ void __launch_bounds__(256, 2) k_bsgs_mac2(u64* __restrict__ res, InP
   }
 }
 
+// ---------------------------------------------------------------------------------------------------------
+// k_bsgs_mac3: k_bsgs_mac2's arithmetic with the baby words staged as well.
+//
+// Measured on B200: the 32 x 32 -> 64-bit wide multiply-add (and mul.hi) issues at quarter rate, about 32 per
+// clock per SM, so a product (four of them) costs 16 cycles of a warp's multiply pipe and the multiply-add
+// ceiling is 8 products per clock per SM.  Three things keep the kernel near it:
+//   * the baby words of the block's IW inputs join the plaintext words of its 8 giants in a 3-deep cp.async
+//     ring of 8-step stages, so two stages of multiply-adds are in flight while one is consumed (k_bsgs_mac2
+//     read the babies straight from HBM one step ahead and every warp waited on them);
+//   * each thread splits the words it copied into (low 30 bits, high 30 bits) pairs in place once they land;
+//     a product of two such pairs is then four fused wide multiply-adds, whereas splitting a 64-bit word in
+//     registers right before the multiply costs the compiler about eight extra instructions per product;
+//   * the sums are folded lazily (any representative below 16 q) except at the last fold.
+// Tiles: IW inputs x 8 giants per block, GPT giants per thread (HOLMES_MAC_TILE="IWxGPT" selects one for A/B
+// timing; 4x4 is the default, 11.7 ms per 512-row chunk of 16 ciphertexts at 13 limbs).
+constexpr int kM3SB = 8;   // baby steps per stage
+constexpr int kM3NS = 3;   // stages in the ring
+
+// V = S00 + (SA + SB) 2^30 + S11 2^60 < 16 q^2 + 16 q reduced to [0, 16 q); the restart splits it into
+// S00 < 2^30 and SA < 2^34, and 16 more products keep every sum below 2^64.
+__device__ __forceinline__ u64 fold_split_lazy(const Split4& acc, const Mod& m) {
+  u64 lo = acc.s00, hi = 0;
+  const u64 a_lo = acc.sa << 30, a_hi = acc.sa >> 34;
+  const u64 b_lo = acc.sb << 30, b_hi = acc.sb >> 34;
+  const u64 c_lo = acc.s11 << 60, c_hi = acc.s11 >> 4;
+  asm("add.cc.u64 %0, %0, %2;\n\taddc.u64 %1, %1, %3;" : "+l"(lo), "+l"(hi) : "l"(a_lo), "l"(a_hi));
+  asm("add.cc.u64 %0, %0, %2;\n\taddc.u64 %1, %1, %3;" : "+l"(lo), "+l"(hi) : "l"(b_lo), "l"(b_hi));
+  asm("add.cc.u64 %0, %0, %2;\n\taddc.u64 %1, %1, %3;" : "+l"(lo), "+l"(hi) : "l"(c_lo), "l"(c_hi));
+  return reduce128_lazy(hi, lo, m);
+}
+// Tile of k_bsgs_mac3: IW inputs per block, GPT of the 8 giants per thread (both components), so
+// 8 / GPT warps per input and IW * 8 / GPT warps per block.
+template <int GPT>
+struct MacAcc {
+  u64 s00[2 * GPT], sa[2 * GPT], sb[2 * GPT], s11[2 * GPT];  // index c * GPT + g
+};
+// one baby step on words pre-split into (low 30 bits, high 30 bits) pairs: every 32 x 32 -> 64-bit
+// product is one fused wide multiply-add into a 64-bit sum
+template <int GPT>
+__device__ __forceinline__ void m3_step(MacAcc<GPT>& A, const uint2* bb, const uint2* pt, int st) {
+  const uint2 x = bb[st * 32], y = bb[(kM3SB + st) * 32];
+#pragma unroll
+  for (int g = 0; g < GPT; ++g) {
+    const uint2 p = pt[(g * kM3SB + st) * 32];
+    A.s00[g] += (u64)x.x * p.x;
+    A.sa[g] += (u64)x.x * p.y;
+    A.sb[g] += (u64)x.y * p.x;
+    A.s11[g] += (u64)x.y * p.y;
+    A.s00[GPT + g] += (u64)y.x * p.x;
+    A.sa[GPT + g] += (u64)y.x * p.y;
+    A.sb[GPT + g] += (u64)y.y * p.x;
+    A.s11[GPT + g] += (u64)y.y * p.y;
+  }
+}
+template <bool CANON, int GPT>
+__device__ __forceinline__ void m3_fold(MacAcc<GPT>& A, const Mod& m) {
+#pragma unroll
+  for (int k = 0; k < 2 * GPT; ++k) {
+    const Split4 s{A.s00[k], A.sa[k], A.sb[k], A.s11[k]};
+    const u64 r = CANON ? fold_split(s, m) : fold_split_lazy(s, m);
+    A.s00[k] = r & ((1ull << 30) - 1);
+    A.sa[k] = r >> 30;
+    A.sb[k] = 0;
+    A.s11[k] = 0;
+  }
+}
+// the words w at p, p + 1 become the pairs (w mod 2^30, w >> 30) in place
+__device__ __forceinline__ void split_words(u64* p) {
+  const ulonglong2 v = *reinterpret_cast<const ulonglong2*>(p);
+  ulonglong2 o;
+  o.x = (v.x & ((1ull << 30) - 1)) | ((v.x >> 30) << 32);
+  o.y = (v.y & ((1ull << 30) - 1)) | ((v.y >> 30) << 32);
+  *reinterpret_cast<ulonglong2*>(p) = o;
+}
+
+template <int IW, int GPT>
+struct M3Geom {
+  static constexpr int THREADS = IW * (kMacGG / GPT) * 32;
+  static constexpr int PT_WORDS = kMacGG * kM3SB * 32;
+  static constexpr int BB_WORDS = IW * 2 * kM3SB * 32;
+  static constexpr int STAGE_WORDS = PT_WORDS + BB_WORDS;
+  static constexpr int SMEM = kM3NS * STAGE_WORDS * 8;
+  static constexpr int MINB = (228 * 1024) / (SMEM + 1024) < 4 ? (228 * 1024) / (SMEM + 1024) : 4;
+};
+
+template <int IW, int GPT>
+__global__ void __launch_bounds__(M3Geom<IW, GPT>::THREADS, M3Geom<IW, GPT>::MINB)
+    k_bsgs_mac3(u64* __restrict__ res, InPtrs in, long long bstride, int nb, int inputs, int G,
+                const u64* __restrict__ pts, long long pstride, int limbs, ModSrc ms, int log_n) {
+  using Geo = M3Geom<IW, GPT>;
+  constexpr int WPI = kMacGG / GPT;  // warps per input
+  extern __shared__ __align__(16) u64 mac_smem[];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int itiles = (inputs + IW - 1) / IW;
+  const int j0 = (blockIdx.x / itiles) * 32;
+  const int i0 = (blockIdx.x % itiles) * IW;
+  const int iw = w / WPI, gq = w % WPI;
+  const int limb = blockIdx.y, g0 = blockIdx.z * kMacGG;
+  const Mod m = ms.get(limb);
+  const size_t lpos = ((size_t)limb << log_n) + j0;
+  const bool active = i0 + iw < inputs;
+  const int nstages = (nb + kM3SB - 1) / kM3SB;
+
+  // Stage s -> ring slot s % kM3NS.  16-byte chunk c of a region holds its words 2c, 2c + 1: plaintext chunk
+  // c is giant c / 128, step (c / 16) % 8, words 2 (c % 16) .. +1 of the 32; baby chunk c is input c / 256,
+  // component (c / 128) % 2, step (c / 16) % 8.  Thread t copies (and later splits) chunks t + THREADS k; their
+  // stage-0 sources are computed once, stage s adds s * 8 rows.
+  constexpr int PCH = Geo::PT_WORDS / 2 / Geo::THREADS, BCH = Geo::BB_WORDS / 2 / Geo::THREADS;
+  const u64* psrc[PCH];
+  int pstep[PCH];
+  const u64* bsrc[BCH];
+  int bstep[BCH];
+#pragma unroll
+  for (int k = 0; k < PCH; ++k) {
+    const int c = threadIdx.x + Geo::THREADS * k;
+    const int g = c / (kM3SB * 16), st = (c / 16) % kM3SB;
+    const int gg = g0 + g < G ? g0 + g : g0;
+    psrc[k] = pts + ((size_t)gg * nb + st) * pstride + lpos + 2 * (c % 16);
+    pstep[k] = st;
+  }
+#pragma unroll
+  for (int k = 0; k < BCH; ++k) {
+    const int c = threadIdx.x + Geo::THREADS * k;
+    const int ii = c / (2 * kM3SB * 16), comp = (c / (kM3SB * 16)) % 2, st = (c / 16) % kM3SB;
+    const bool ok = i0 + ii < inputs;
+    bsrc[k] = ok ? (comp ? in.c1[i0 + ii] : in.c0[i0 + ii]) + (size_t)st * bstride + lpos + 2 * (c % 16) : nullptr;
+    bstep[k] = st;
+  }
+  auto issue_stage = [&](int s) {
+    if (s < nstages) {
+      u64* pt = mac_smem + (size_t)(s % kM3NS) * Geo::STAGE_WORDS;
+      u64* bb = pt + Geo::PT_WORDS;
+      const size_t po = (size_t)s * kM3SB * pstride, bo = (size_t)s * kM3SB * bstride;
+      const int left = nb - s * kM3SB;
+#pragma unroll
+      for (int k = 0; k < PCH; ++k)
+        if (pstep[k] < left) cp_async16(pt + 2 * (threadIdx.x + Geo::THREADS * k), psrc[k] + po);
+#pragma unroll
+      for (int k = 0; k < BCH; ++k)
+        if (bsrc[k] && bstep[k] < left) cp_async16(bb + 2 * (threadIdx.x + Geo::THREADS * k), bsrc[k] + bo);
+    }
+    asm volatile("cp.async.commit_group;\n" ::);  // an empty group past the end keeps the wait count uniform
+  };
+
+  MacAcc<GPT> A;
+#pragma unroll
+  for (int k = 0; k < 2 * GPT; ++k) A.s00[k] = A.sa[k] = A.sb[k] = A.s11[k] = 0;
+
+#pragma unroll
+  for (int s = 0; s < kM3NS - 1; ++s) issue_stage(s);
+  for (int s = 0; s < nstages; ++s) {
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(kM3NS - 2));
+    {  // this thread's copies of stage s have landed: split them in place
+      u64* pt = mac_smem + (size_t)(s % kM3NS) * Geo::STAGE_WORDS;
+      u64* bb = pt + Geo::PT_WORDS;
+      const int left = nb - s * kM3SB;
+#pragma unroll
+      for (int k = 0; k < PCH; ++k)
+        if (pstep[k] < left) split_words(pt + 2 * (threadIdx.x + Geo::THREADS * k));
+#pragma unroll
+      for (int k = 0; k < BCH; ++k)
+        if (bsrc[k] && bstep[k] < left) split_words(bb + 2 * (threadIdx.x + Geo::THREADS * k));
+    }
+    __syncthreads();  // stage s is split and visible to every thread; slot (s - 1) % kM3NS is no longer read
+    issue_stage(s + kM3NS - 1);
+    const int steps = nb - s * kM3SB < kM3SB ? nb - s * kM3SB : kM3SB;
+    if (active) {
+      const u64* base = mac_smem + (size_t)(s % kM3NS) * Geo::STAGE_WORDS;
+      const uint2* pt = reinterpret_cast<const uint2*>(base) + (gq * GPT) * kM3SB * 32 + lane;
+      const uint2* bb = reinterpret_cast<const uint2*>(base + Geo::PT_WORDS) + (iw * 2) * kM3SB * 32 + lane;
+      if (steps == kM3SB) {
+#pragma unroll
+        for (int st = 0; st < kM3SB; ++st) m3_step<GPT>(A, bb, pt, st);
+      } else {
+        for (int st = 0; st < steps; ++st) m3_step<GPT>(A, bb, pt, st);
+      }
+      // at most 16 products per sum between folds (two 8-step stages); the sums restart from any
+      // representative below 16 q, and only the last fold is made canonical
+      if (s == nstages - 1) m3_fold<true, GPT>(A, m);
+      else if (s & 1) m3_fold<false, GPT>(A, m);
+    }
+  }
+  asm volatile("cp.async.wait_all;\n" ::);
+  if (!active) return;
+  const int i = i0 + iw;
+  const size_t is = (size_t)limbs << log_n, gs = (size_t)inputs * is;
+#pragma unroll
+  for (int g = 0; g < GPT; ++g) {
+    const int gg = g0 + gq * GPT + g;
+    if (gg >= G) break;
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const u64 r = (A.sa[c * GPT + g] << 30) | A.s00[c * GPT + g];  // the last fold left the canonical residue
+      res[((size_t)c * G + gg) * gs + (size_t)i * is + lpos + lane] = r;
+    }
+  }
+}
+
+template <int IW, int GPT>
+static int launch_mac3(u64* res, const InPtrs& in, long long bstride, int nb, int inputs, int groups, const u64* pts,
+                       long long pstride, int limbs, const ModSrc& ms, int log_n, int n, cudaStream_t st) {
+  using Geo = M3Geom<IW, GPT>;
+  cudaError_t e = cudaFuncSetAttribute(k_bsgs_mac3<IW, GPT>, cudaFuncAttributeMaxDynamicSharedMemorySize, Geo::SMEM);
+  if (e != cudaSuccess) return (int)e;
+  dim3 grid((unsigned)((n / 32) * ((inputs + IW - 1) / IW)), (unsigned)limbs, (unsigned)((groups + kMacGG - 1) / kMacGG));
+  count_launch();
+  k_bsgs_mac3<IW, GPT><<<grid, Geo::THREADS, Geo::SMEM, st>>>(res, in, bstride, nb, inputs, groups, pts, pstride,
+                                                               limbs, ms, log_n);
+  return (int)cudaGetLastError();
+}
+
 int bsgs_mac(ModSrc ms, u64* res, const u64* const* c0s, const u64* const* c1s,
              long long bstride, int nb, int inputs, const u64* pts, long long pstride, int groups, int limbs, int n,
              cudaStream_t st) {
@@ -368,14 +579,27 @@ int bsgs_mac(ModSrc ms, u64* res, const u64* const* c0s, const u64* const* c1s,
     k_bsgs_mac<TG><<<grid, 256, 0, st>>>(res, in, bstride, nb, inputs, groups, pts, pstride, limbs, ms, log_n);
     return (int)cudaGetLastError();
   }
-  const int smem = 2 * kMacStageWords * 8;
-  cudaError_t e = cudaFuncSetAttribute(k_bsgs_mac2, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-  if (e != cudaSuccess) return (int)e;
   dim3 grid((unsigned)((n / 32) * ((inputs + kMacIW - 1) / kMacIW)), (unsigned)limbs,
             (unsigned)((groups + kMacGG - 1) / kMacGG));
-  count_launch();
-  k_bsgs_mac2<<<grid, 256, smem, st>>>(res, in, bstride, nb, inputs, groups, pts, pstride, limbs, ms, log_n);
-  return (int)cudaGetLastError();
+  // cp.async moves 16-byte chunks: every staged row must start on a 16-byte boundary
+  bool aligned = ((uintptr_t)pts % 16 == 0) && (pstride % 2 == 0) && (bstride % 2 == 0);
+  for (int i = 0; i < inputs; ++i) aligned = aligned && ((uintptr_t)in.c0[i] % 16 == 0) && ((uintptr_t)in.c1[i] % 16 == 0);
+  if (!aligned || getenv("HOLMES_MAC_V2")) {
+    const int smem = 2 * kMacStageWords * 8;
+    cudaError_t e = cudaFuncSetAttribute(k_bsgs_mac2, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return (int)e;
+    count_launch();
+    k_bsgs_mac2<<<grid, 256, smem, st>>>(res, in, bstride, nb, inputs, groups, pts, pstride, limbs, ms, log_n);
+    return (int)cudaGetLastError();
+  }
+  const char* cfg = getenv("HOLMES_MAC_TILE");  // A/B timing of tile shapes: "IWxGPT"
+  const int c = cfg && cfg[0] && cfg[1] == 'x' ? atoi(cfg) * 10 + atoi(cfg + 2) : 44;
+  switch (c) {
+    case 22: return launch_mac3<2, 2>(res, in, bstride, nb, inputs, groups, pts, pstride, limbs, ms, log_n, n, st);
+    case 24: return launch_mac3<2, 4>(res, in, bstride, nb, inputs, groups, pts, pstride, limbs, ms, log_n, n, st);
+    case 42: return launch_mac3<4, 2>(res, in, bstride, nb, inputs, groups, pts, pstride, limbs, ms, log_n, n, st);
+    default: return launch_mac3<4, 4>(res, in, bstride, nb, inputs, groups, pts, pstride, limbs, ms, log_n, n, st);
+  }
 }
 
 // --------------------------------------------------------------------------------------------- special FFT

@@ -60,22 +60,25 @@ struct NttTables {
 
 // ---------------------------------------------------------------------------------------------------------
 // butterflies
-__device__ __forceinline__ void bf_fwd(u64& x, u64& y, Tw t, u64 q, u64 q2) {
-  if (x >= q2) x -= q2;
-  const u64 v = shoup_lazy(y, t, q);
-  y = x + q2 - v;
+// Butterflies on lazy values below 8q (forward) / 4q (inverse) with the three-product Shoup estimate
+// (shoup_lazy4, common.cuh): its quotient is at most 2 short, so the product lies in [0, 4q), and one
+// conditional subtraction of 4q per butterfly keeps the bounds (8q < 2^63 for q < 2^60).
+__device__ __forceinline__ void bf_fwd(u64& x, u64& y, Tw t, u64 q, u64 q4) {
+  if (x >= q4) x -= q4;
+  const u64 v = shoup_lazy4(y, t, q);
+  y = x + q4 - v;
   x = x + v;
 }
-__device__ __forceinline__ void bf_inv(u64& x, u64& y, Tw t, u64 q, u64 q2) {
+__device__ __forceinline__ void bf_inv(u64& x, u64& y, Tw t, u64 q, u64 q4) {
   u64 u = x + y;
-  if (u >= q2) u -= q2;
-  const u64 d = x + q2 - y;
-  y = shoup_lazy(d, t, q);
+  if (u >= q4) u -= q4;
+  const u64 d = x + q4 - y;
+  y = shoup_lazy4(d, t, q);
   x = u;
 }
-__device__ __forceinline__ u64 canon4(u64 x, u64 q) {
-  const u64 q2 = q << 1;
-  if (x >= q2) x -= q2;
+__device__ __forceinline__ u64 canon8(u64 x, u64 q) {
+  if (x >= (q << 2)) x -= (q << 2);
+  if (x >= (q << 1)) x -= (q << 1);
   if (x >= q) x -= q;
   return x;
 }
@@ -92,7 +95,7 @@ __device__ __forceinline__ void local_pass(u64* sh, int seg0, const Tw* __restri
   constexpr int M = 1 << R;
   constexpr int GROUPS = G::S >> R;
   constexpr int s = LOGN - L0 - R;
-  const u64 q2 = q << 1;
+  const u64 q4 = q << 2;
   for (int gid = threadIdx.x; gid < GROUPS; gid += G::THREADS) {
     const int lo = gid & ((1 << s) - 1);
     const int base = lo | ((gid >> s) << (s + R));
@@ -108,7 +111,7 @@ __device__ __forceinline__ void local_pass(u64* sh, int seg0, const Tw* __restri
 #pragma unroll
         for (int k = 0; k < M; ++k) {
           if (k & h) continue;
-          bf_fwd(x[k], x[k + h], tr[k >> (R - r)], q, q2);
+          bf_fwd(x[k], x[k + h], tr[k >> (R - r)], q, q4);
         }
       }
     } else {
@@ -119,7 +122,7 @@ __device__ __forceinline__ void local_pass(u64* sh, int seg0, const Tw* __restri
 #pragma unroll
         for (int k = 0; k < M; ++k) {
           if (k & h) continue;
-          bf_inv(x[k], x[k + h], tr[k >> (R - r)], q, q2);
+          bf_inv(x[k], x[k + h], tr[k >> (R - r)], q, q4);
         }
       }
     }
@@ -193,7 +196,7 @@ __device__ __forceinline__ void ntt_forward_body(int poly, int mi, const NttTabl
     cluster.sync();
     // cross-segment rounds 0 .. LOGCL-1 on columns j in [rank S/CL, (rank+1) S/CL)
     constexpr int COLS = G::S / G::CL;
-    const u64 q2 = q << 1;
+    const u64 q4 = q << 2;
     // the cross rounds use only the CL - 1 twiddles tw[1 .. CL-1]
     Tw ct[G::CL];
 #pragma unroll
@@ -209,7 +212,7 @@ __device__ __forceinline__ void ntt_forward_body(int poly, int mi, const NttTabl
 #pragma unroll
         for (int r = 0; r < G::CL; ++r) {
           if (r & h) continue;
-          bf_fwd(x[r], x[r + h], ct[(1 << l) + (r >> (G::LOGCL - l))], q, q2);
+          bf_fwd(x[r], x[r + h], ct[(1 << l) + (r >> (G::LOGCL - l))], q, q4);
         }
       }
       // scatter: word r S + j belongs to CTA r, local index j
@@ -227,7 +230,7 @@ __device__ __forceinline__ void ntt_forward_body(int poly, int mi, const NttTabl
   const int seg0 = rank * G::S;
   local_rounds<LOGN, false>(sh, seg0, tw, q);
   const auto ss = st.prep(poly);
-  for (int i = threadIdx.x; i < G::S; i += G::THREADS) st.store(ss, seg0 + i, canon4(sh[swz(i)], q));
+  for (int i = threadIdx.x; i < G::S; i += G::THREADS) st.store(ss, seg0 + i, canon8(sh[swz(i)], q));
 }
 
 // Inverse NTT; `scale` is the final per-polynomial multiplier (N^-1, or N^-1 times a constant).
@@ -253,7 +256,7 @@ __device__ __forceinline__ void ntt_inverse_body(int poly, int mi, Tw scale, con
     cg::cluster_group cluster = cg::this_cluster();
     cluster.sync();
     constexpr int COLS = G::S / G::CL;
-    const u64 q2 = q << 1;
+    const u64 q4 = q << 2;
     Tw ct[G::CL];
 #pragma unroll
     for (int i = 1; i < G::CL; ++i) ct[i] = tw[i];
@@ -268,7 +271,7 @@ __device__ __forceinline__ void ntt_inverse_body(int poly, int mi, Tw scale, con
 #pragma unroll
         for (int r = 0; r < G::CL; ++r) {
           if (r & h) continue;
-          bf_inv(x[r], x[r + h], ct[(1 << l) + (r >> (G::LOGCL - l))], q, q2);
+          bf_inv(x[r], x[r + h], ct[(1 << l) + (r >> (G::LOGCL - l))], q, q4);
         }
       }
 #pragma unroll
