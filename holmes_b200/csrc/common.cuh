@@ -123,6 +123,36 @@ __device__ __forceinline__ u64 reduce128_lazy(u64 hi, u64 lo, const Mod& m) {
 __device__ __forceinline__ u64 mul_mod(u64 a, u64 b, const Mod& m) { return reduce128(__umul64hi(a, b), a * b, m); }
 __device__ __forceinline__ u64 reduce128(const U128& x, const Mod& m) { return reduce128(x.hi, x.lo, m); }
 
+// Radix-2^30 partial-product sums.  A residue below 2^60 splits as a1 2^30 + a0 (a0, a1 < 2^30); the four
+// partial products of two such residues are below 2^60, so up to 16 of each accumulate in one 64-bit word
+// (one fused 32 x 32 -> 64-bit wide multiply-add each).  V = S00 + (SA + SB) 2^30 + S11 2^60.
+struct Split4 {
+  u64 s00, sa, sb, s11;
+};
+__device__ __forceinline__ void split_fold128(const Split4& acc, u64& hi, u64& lo) {
+  lo = acc.s00;
+  hi = 0;
+  const u64 a_lo = acc.sa << 30, a_hi = acc.sa >> 34;
+  const u64 b_lo = acc.sb << 30, b_hi = acc.sb >> 34;
+  const u64 c_lo = acc.s11 << 60, c_hi = acc.s11 >> 4;
+  asm("add.cc.u64 %0, %0, %2;\n\taddc.u64 %1, %1, %3;" : "+l"(lo), "+l"(hi) : "l"(a_lo), "l"(a_hi));
+  asm("add.cc.u64 %0, %0, %2;\n\taddc.u64 %1, %1, %3;" : "+l"(lo), "+l"(hi) : "l"(b_lo), "l"(b_hi));
+  asm("add.cc.u64 %0, %0, %2;\n\taddc.u64 %1, %1, %3;" : "+l"(lo), "+l"(hi) : "l"(c_lo), "l"(c_hi));
+}
+// V mod q, canonical (V < 14 2^k, e.g. 16 products of residues below 2^60 and q)
+__device__ __forceinline__ u64 fold_split(const Split4& acc, const Mod& m) {
+  u64 hi, lo;
+  split_fold128(acc, hi, lo);
+  return reduce128(hi, lo, m);
+}
+// V mod q as a representative in [0, 16 q): restarting the sums from its split (S00 < 2^30, SA < 2^34) leaves
+// room for 16 more products below 2^60 in every sum
+__device__ __forceinline__ u64 fold_split_lazy(const Split4& acc, const Mod& m) {
+  u64 hi, lo;
+  split_fold128(acc, hi, lo);
+  return reduce128_lazy(hi, lo, m);
+}
+
 // bit reversal of the low `bits` bits
 __device__ __forceinline__ u32 brev_bits(u32 v, int bits) { return __brev(v) >> (32 - bits); }
 

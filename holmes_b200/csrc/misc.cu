@@ -218,9 +218,6 @@ __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;\n" ::); }
 
-struct Split4 {
-  u64 s00, sa, sb, s11;
-};
 // acc += a * b for 32-bit a, b and a 64-bit accumulator: one wide multiply-add
 __device__ __forceinline__ void mad_wide(u64& acc, u32 a, u32 b) {
   asm("mad.wide.u32 %0, %1, %2, %0;" : "+l"(acc) : "r"(a), "r"(b));
@@ -231,17 +228,6 @@ __device__ __forceinline__ void mad_split(Split4& acc, u32 a0, u32 a1, u64 bp) {
   mad_wide(acc.sa, a0, b1);
   mad_wide(acc.sb, a1, b0);
   mad_wide(acc.s11, a1, b1);
-}
-__device__ __forceinline__ u64 fold_split(const Split4& acc, const Mod& m) {
-  // V = s00 + (sa << 30) + (sb << 30) + (s11 << 60) as 128 bits
-  u64 lo = acc.s00, hi = 0;
-  const u64 a_lo = acc.sa << 30, a_hi = acc.sa >> 34;
-  const u64 b_lo = acc.sb << 30, b_hi = acc.sb >> 34;
-  const u64 c_lo = acc.s11 << 60, c_hi = acc.s11 >> 4;
-  asm("add.cc.u64 %0, %0, %2;\n\taddc.u64 %1, %1, %3;" : "+l"(lo), "+l"(hi) : "l"(a_lo), "l"(a_hi));
-  asm("add.cc.u64 %0, %0, %2;\n\taddc.u64 %1, %1, %3;" : "+l"(lo), "+l"(hi) : "l"(b_lo), "l"(b_hi));
-  asm("add.cc.u64 %0, %0, %2;\n\taddc.u64 %1, %1, %3;" : "+l"(lo), "+l"(hi) : "l"(c_lo), "l"(c_hi));
-  return reduce128(hi, lo, m);
 }
 __device__ __forceinline__ void restart_split(Split4& acc, u64 r) {
   acc.s00 = r & ((1ull << 30) - 1);
@@ -365,18 +351,6 @@ __global__ void __launch_bounds__(256, 2) k_bsgs_mac2(u64* __restrict__ res, InP
 constexpr int kM3SB = 8;   // baby steps per stage
 constexpr int kM3NS = 3;   // stages in the ring
 
-// V = S00 + (SA + SB) 2^30 + S11 2^60 < 16 q^2 + 16 q reduced to [0, 16 q); the restart splits it into
-// S00 < 2^30 and SA < 2^34, and 16 more products keep every sum below 2^64.
-__device__ __forceinline__ u64 fold_split_lazy(const Split4& acc, const Mod& m) {
-  u64 lo = acc.s00, hi = 0;
-  const u64 a_lo = acc.sa << 30, a_hi = acc.sa >> 34;
-  const u64 b_lo = acc.sb << 30, b_hi = acc.sb >> 34;
-  const u64 c_lo = acc.s11 << 60, c_hi = acc.s11 >> 4;
-  asm("add.cc.u64 %0, %0, %2;\n\taddc.u64 %1, %1, %3;" : "+l"(lo), "+l"(hi) : "l"(a_lo), "l"(a_hi));
-  asm("add.cc.u64 %0, %0, %2;\n\taddc.u64 %1, %1, %3;" : "+l"(lo), "+l"(hi) : "l"(b_lo), "l"(b_hi));
-  asm("add.cc.u64 %0, %0, %2;\n\taddc.u64 %1, %1, %3;" : "+l"(lo), "+l"(hi) : "l"(c_lo), "l"(c_hi));
-  return reduce128_lazy(hi, lo, m);
-}
 // Tile of k_bsgs_mac3: IW inputs per block, GPT of the 8 giants per thread (both components), so
 // 8 / GPT warps per input and IW * 8 / GPT warps per block.
 template <int GPT>

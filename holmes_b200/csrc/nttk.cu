@@ -2,12 +2,15 @@
 // elementwise pre- and post-processing fused into the NTT's global loads and stores.
 //
 //   plain NTT / iNTT              batched [items][limbs][N]
-//   ModUp                         iNTT(c1) * N^-1 (Q_j/q_k)^-1  ->  per digit: base conversion fused
-//                                 into the forward NTT of every target limb
+//   ModUp                         iNTT(c1) * N^-1 (Q_j/q_k)^-1  ->  per digit: base conversion of
+//                                 every target limb (k_conv), then their forward NTTs in place
 //   key switch (hybrid, ModDown)  P limbs: inner product (digits through the automorphism) fused into
-//                                 the iNTT with N^-1 (P/p_k)^-1; Q limbs: base conversion P->q_i fused
-//                                 into the NTT, inner product + subtract + P^-1 + automorphed addend
+//                                 the iNTT with N^-1 (P/p_k)^-1; Q limbs: base conversion P->q_i (k_conv),
+//                                 then the NTT with inner product + subtract + P^-1 + automorphed addend
 //                                 fused into its store
+//   The base conversions run as their own elementwise pass: one thread keeps a coefficient's source
+//   words in registers for every target limb, where the NTT's load phase (fused before) recomputed its
+//   splits per target and stalled on 8 scattered loads per word with few registers to spare.
 //   rescale                       iNTT of the last limb; centred reduction fused into the NTT of the
 //                                 other limbs, (c - v) q_last^-1 fused into its store
 //   encode                        llround(v * scale) and the signed reduction fused into the NTT load
@@ -49,6 +52,105 @@ struct StPlain {
   __device__ void store(const S& s, int n, u64 v) const { s.p[n] = v; }
 };
 
+// --------------------------------------------------------------------------------------------- base conversion
+// out_t[n] = sum_{a < w} y_a[n] H[a][mi(t)] mod q_mi(t) for every target t < ntgt of every item, coefficient form.
+// Target t is limb r = t (t < skip_lo) or t + w (above), of modulus index mi = r (r < cur) or L + r - cur.  One
+// thread reads the w source words of one coefficient once, splits them into 30-bit halves, and produces every
+// target from constants pre-split in shared memory (four fused wide multiply-adds per product, w <= 16 products
+// per 64-bit sum), then one Barrett fold per output.  Used by the key switch (P -> Q) and ModUp (digit ->
+// complement), whose NTTs then load plainly.
+struct ConvArgs {
+  const u64* y;     // source limb a of item i at y + i * y_item + a * N
+  long long y_item;
+  u64* out;         // target limb r of item i at out + i * out_item + r * N
+  long long out_item;
+  const u64* H;     // H[a * h_row + mi]
+  int h_row;
+  int w, ntgt, skip_lo, cur, L, items;
+};
+template <int WMAX>
+__global__ void __launch_bounds__(256) k_conv(ConvArgs a, int log_n, const Mod* __restrict__ mods) {
+  extern __shared__ uint2 hs[];  // [ntgt][w]: the split constant of source a for target t
+  const int N = 1 << log_n;
+  for (int e = threadIdx.x; e < a.ntgt * a.w; e += blockDim.x) {
+    const int t = e / a.w, k = e % a.w;
+    const int r = t < a.skip_lo ? t : t + a.w;
+    const int mi = r < a.cur ? r : a.L + r - a.cur;
+    const u64 h = a.H[(size_t)k * a.h_row + mi];
+    hs[e] = make_uint2((uint32_t)(h & ((1ull << 30) - 1)), (uint32_t)(h >> 30));
+  }
+  __syncthreads();
+  const size_t total = (size_t)a.items << log_n;
+  for (size_t g = blockIdx.x * (size_t)blockDim.x + threadIdx.x; g < total; g += (size_t)gridDim.x * blockDim.x) {
+    const int item = (int)(g >> log_n);
+    const int n = (int)(g & (N - 1));
+    const u64* yp = a.y + item * a.y_item + n;
+    uint2 ys[WMAX];
+#pragma unroll
+    for (int k = 0; k < WMAX; ++k) {
+      const u64 v = k < a.w ? yp[(size_t)k << log_n] : 0;
+      ys[k] = make_uint2((uint32_t)(v & ((1ull << 30) - 1)), (uint32_t)(v >> 30));
+    }
+    u64* op = a.out + item * a.out_item + n;
+    for (int t = 0; t < a.ntgt; ++t) {
+      const uint2* h = hs + t * a.w;
+      Split4 s{0, 0, 0, 0};
+#pragma unroll
+      for (int k = 0; k < WMAX; ++k) {
+        if (k < a.w) {
+          const uint2 c = h[k];
+          s.s00 += (u64)ys[k].x * c.x;
+          s.sa += (u64)ys[k].x * c.y;
+          s.sb += (u64)ys[k].y * c.x;
+          s.s11 += (u64)ys[k].y * c.y;
+        }
+      }
+      const int r = t < a.skip_lo ? t : t + a.w;
+      const int mi = r < a.cur ? r : a.L + r - a.cur;
+      op[(size_t)r << log_n] = fold_split(s, mods[mi]);
+    }
+  }
+}
+static int conv_launch(const HolmesCtx& c, const ConvArgs& a, cudaStream_t st) {
+  if (a.w < 1 || a.w > MAXA || a.ntgt < 1) return -3;
+  const size_t smem = (size_t)a.ntgt * a.w * sizeof(uint2);
+  const size_t work = (size_t)a.items << c.log_n;
+  size_t blocks = (work + 255) / 256;
+  if (blocks > 148 * 8) blocks = 148 * 8;
+  count_launch();
+  if (a.w <= 8) k_conv<8><<<(unsigned)blocks, 256, smem, st>>>(a, c.log_n, c.d_mod);
+  else k_conv<16><<<(unsigned)blocks, 256, smem, st>>>(a, c.log_n, c.d_mod);
+  return (int)cudaGetLastError();
+}
+// Plain load / in-place store of the target limbs of one ModUp digit (poly p = item * ntgt + t).
+struct DigitRows {
+  u64* base;
+  long long item;
+  int lo, w, ntgt, log_n;
+  struct S { u64* p; };
+  __device__ int row(int p) const {
+    const int t = p % ntgt;
+    return t < lo ? t : t + w;
+  }
+  __device__ S prep(int p) const { return S{base + (p / ntgt) * item + ((size_t)row(p) << log_n)}; }
+  __device__ u64 load(const S& s, int n) const { return s.p[n]; }
+  __device__ void store(const S& s, int n, u64 v) const { s.p[n] = v; }
+};
+template <int LOGN>
+__global__ void HOLMES_NTT_BOUNDS(LOGN) k_digit_ntt(NttTables T, DigitRows d, int cur, int L) {
+  const int p = blockIdx.x / NttGeom<LOGN>::CL;
+  const int r = d.row(p);
+  ntt_forward_body<LOGN>(p, r < cur ? r : L + r - cur, T, d, d);
+}
+// Plain load of the converted Q limbs of the key switch (poly p = (item * 2 + c) * cur + i).
+struct LdRows {
+  const u64* base;
+  int log_n;
+  struct S { const u64* p; };
+  __device__ S prep(int p) const { return S{base + ((size_t)p << log_n)}; }
+  __device__ u64 load(const S& s, int n) const { return s.p[n]; }
+};
+
 template <int LOGN>
 __global__ void HOLMES_NTT_BOUNDS(LOGN) k_fwd_plain(NttTables T, PolyMap pm, LdPlain ld, StPlain st) {
   const int p = blockIdx.x / NttGeom<LOGN>::CL;
@@ -80,58 +182,6 @@ int ntt_plain(const HolmesCtx& c, const u64* src, u64* dst, PolyMap pm, int poly
 // --------------------------------------------------------------------------------------------- ModUp
 // Base conversion of one digit's scaled coefficients y_a (a < w) to modulus m: sum_a y_a hat_a mod m.
 // Polynomial p of a digit launch: item p / ntgt, target limb t (the digit's own limbs skipped).
-struct LdConv {
-  const u64* y;      // scratch + lo * N: [items][cur][N], digit limbs from lo
-  long long y_item;
-  const u64* hat;    // mu_hat(cur) + (j * A) * T: [A][T]
-  const Mod* mods;
-  int w, lo, cur, ntgt, L, T, log_n;
-  struct S {
-    const u64* y;
-    const u64* h;  // hat constants of the target modulus, stride T (read through the cache at use)
-    Mod m;
-  };
-  __device__ int target(int p) const {
-    const int r = p % ntgt;
-    return r < lo ? r : r + w;
-  }
-  __device__ S prep(int p) const {
-    const int t = target(p);
-    const int mi = t < cur ? t : L + t - cur;
-    S s;
-    s.y = y + (p / ntgt) * y_item;
-    s.h = hat + mi;
-    s.m = mods[mi];
-    return s;
-  }
-  __device__ u64 load(const S& s, int n) const {
-    U128 acc{0, 0};
-#pragma unroll 4
-    for (int a = 0; a < w; ++a) mac128(acc, s.y[((size_t)a << log_n) + n], __ldg(s.h + a * T));
-    return reduce128(acc, s.m);
-  }
-};
-struct StDigit {
-  u64* out;  // digits[item][j]: [cur + K][N]
-  long long out_item;
-  int lo, w, ntgt, log_n;
-  struct S { u64* p; };
-  __device__ S prep(int p) const {
-    const int r = p % ntgt;
-    const int t = r < lo ? r : r + w;
-    return S{out + (p / ntgt) * out_item + ((size_t)t << log_n)};
-  }
-  __device__ void store(const S& s, int n, u64 v) const { s.p[n] = v; }
-};
-
-template <int LOGN>
-__global__ void HOLMES_NTT_BOUNDS(LOGN) k_modup_ntt(NttTables T, LdConv ld, StDigit st) {
-  const int p = blockIdx.x / NttGeom<LOGN>::CL;
-  const int t = ld.target(p);
-  const int mi = t < ld.cur ? t : ld.L + t - ld.cur;
-  ntt_forward_body<LOGN>(p, mi, T, ld, st);
-}
-
 int modup(const HolmesCtx& c, const u64* c1, long long c1_item, int cur, int items, u64* digits, long long dig_item,
           u64* scratch, cudaStream_t st) {
   if (cur < 1 || cur > c.L || items < 1) return -2;
@@ -167,14 +217,18 @@ int modup(const HolmesCtx& c, const u64* c1, long long c1_item, int cur, int ite
                                       st));
     NttTables T{c.d_tw, c.d_mod};
     const int ntgt = cur + K - w;
-    LdConv ld{scratch + (size_t)lo * N, y_item, c.mu_hat(cur) + (size_t)j * A * c.T, c.d_mod, w, lo, cur, ntgt, c.L,
-              c.T, c.log_n};
-    StDigit sd{dj, dig_item, lo, w, ntgt, c.log_n};
+    ConvArgs ca{scratch + (size_t)lo * N, y_item, dj, dig_item, c.mu_hat(cur) + (size_t)j * A * c.T, c.T,
+                w, ntgt, lo, cur, c.L, items};
+    {
+      const int e = conv_launch(c, ca, st);
+      if (e) return e;
+    }
+    DigitRows dr{dj, dig_item, lo, w, ntgt, c.log_n};
     const int polys = items * ntgt;
 #define L_(LG)                                                                                                   \
   {                                                                                                              \
     using G = NttGeom<LG>;                                                                                       \
-    cudaError_t e = launch_ntt(k_modup_ntt<LG>, G::LOGCL, G::THREADS, G::SMEM, polys, st, T, ld, sd);           \
+    cudaError_t e = launch_ntt(k_digit_ntt<LG>, G::LOGCL, G::THREADS, G::SMEM, polys, st, T, dr, cur, c.L);     \
     if (e != cudaSuccess) return (int)e;                                                                         \
     break;                                                                                                       \
   }
@@ -230,32 +284,8 @@ __global__ void HOLMES_NTT_BOUNDS(LOGN) k_ks_p(NttTables T, const Tw* md_scale, 
   ntt_inverse_body<LOGN>(p, ld.L + k, md_scale[k], T, ld, st);
 }
 
-// Q limbs: conv_c[i] = NTT(sum_k y_c[k] (P/p_k) mod q_i); out = (inner - conv) P^-1 + perm(add)
-struct LdKsQ {
-  const u64* scratch;  // [items][2][K][N]
-  const u64* md_hat;   // [K][L]
-  const Mod* mods;
-  int cur, K, L, log_n;
-  struct S {
-    const u64* y;
-    const u64* h;  // (P/p_k) mod q_i for k < K, stride L (read through the cache at use)
-    Mod m;
-  };
-  __device__ S prep(int p) const {
-    const int item = p / (2 * cur), r = p % (2 * cur), c = r / cur, i = r % cur;
-    S s;
-    s.y = scratch + (((size_t)item * 2 + c) * K << log_n);
-    s.h = md_hat + i;
-    s.m = mods[i];
-    return s;
-  }
-  __device__ u64 load(const S& s, int n) const {
-    U128 acc{0, 0};
-#pragma unroll 4
-    for (int k = 0; k < K; ++k) mac128(acc, s.y[((size_t)k << log_n) + n], __ldg(s.h + k * L));
-    return reduce128(acc, s.m);
-  }
-};
+// Q limbs: conv_c[i] = NTT(sum_k y_c[k] (P/p_k) mod q_i) (k_conv, then a plain-load NTT); out = (inner - conv) P^-1
+// + perm(add)
 struct StKsQ {
   const u64* digits;
   long long dig_item;
@@ -310,9 +340,9 @@ struct StKsQ {
   }
 };
 template <int LOGN>
-__global__ void HOLMES_NTT_BOUNDS(LOGN) k_ks_q(NttTables T, LdKsQ ld, StKsQ st) {
+__global__ void HOLMES_NTT_BOUNDS(LOGN) k_ks_q(NttTables T, LdRows ld, StKsQ st) {
   const int p = blockIdx.x / NttGeom<LOGN>::CL;
-  ntt_forward_body<LOGN>(p, (p % (2 * ld.cur)) % ld.cur, T, ld, st);
+  ntt_forward_body<LOGN>(p, (p % (2 * st.cur)) % st.cur, T, ld, st);
 }
 
 int ks_apply(const HolmesCtx& c, const KsArgs& a, cudaStream_t st) {
@@ -336,9 +366,16 @@ int ks_apply(const HolmesCtx& c, const KsArgs& a, cudaStream_t st) {
     HOLMES_LOGN_SWITCH(c.log_n, L_)
 #undef L_
   }
+  u64* conv = a.scratch + (size_t)a.items * 2 * K * c.n;  // [items][2][cur][N], coefficient form
+  {
+    ConvArgs ca{a.scratch, (long long)K * c.n, conv, (long long)a.cur * c.n, c.d_md_hat, c.L,
+                K, a.cur, a.cur, a.cur, c.L, a.items * 2};
+    const int e = conv_launch(c, ca, st);
+    if (e) return e;
+  }
   {
     NttTables T{c.d_tw, c.d_mod};
-    LdKsQ ld{a.scratch, c.d_md_hat, c.d_mod, a.cur, K, c.L, c.log_n};
+    LdRows ld{conv, c.log_n};
     StKsQ sq{a.digits, a.dig_item, a.key, a.add0, a.add1, a.add_item, a.post0, a.post1, a.post_item, a.out0, a.out1,
              a.out_item, c.d_mod,
              c.d_md_pinv, g, a.cur, a.key_cap, K, beta, key_beta, c.log_n};

@@ -534,7 +534,7 @@ def _modup(ctx: Context, c1: torch.Tensor, cur: int, items: int) -> tuple[torch.
 def _keyswitch(ctx: Context, digits: torch.Tensor, dig_item: int, cur: int, galois: int, key, add0, add1, add_item,
                out0: torch.Tensor, out1: torch.Tensor, items: int, post0=None, post1=None, post_item: int = 0) -> None:
     key_t, cap = key
-    scratch = ctx.workspace("ks", items * 2 * ctx.K * ctx.N)
+    scratch = ctx.workspace("ks", items * 2 * (ctx.K + cur) * ctx.N)
     beta = ctx.beta(cur)
     words = items * (beta * (cur + ctx.K) + 2 * cur) + 2 * beta * (cur + ctx.K)
     words += items * cur * ((add0 is not None) + (add1 is not None) + (post0 is not None) + (post1 is not None))

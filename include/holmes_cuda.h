@@ -125,7 +125,7 @@ int holmes_modup(void* ctx, const uint64_t* c1, long long c1_item, int cur, int 
  *   out0 = perm(add0) + ModDown(sum_j perm(digit_j) key_b[j]) + post0
  *   out1 = perm(add1) + ModDown(sum_j perm(digit_j) key_a[j]) + post1
  * perm = automorphism X -> X^galois (galois <= 1: identity); every addend may be NULL;
- * scratch >= items * 2 * K * N words */
+ * scratch >= items * 2 * (K + cur) * N words */
 int holmes_keyswitch(void* ctx, const uint64_t* digits, long long digit_item, int cur, const uint64_t* key, int key_cap,
                      uint64_t galois, const uint64_t* add0, const uint64_t* add1, long long add_item,
                      const uint64_t* post0, const uint64_t* post1, long long post_item, uint64_t* out0,
