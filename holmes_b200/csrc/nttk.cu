@@ -68,13 +68,13 @@ struct ConvArgs {
   int h_row;
   int w, ntgt, skip_lo, cur, L, items;
 };
-template <int WMAX>
+template <int W>
 __global__ void __launch_bounds__(256) k_conv(ConvArgs a, int log_n, const Mod* __restrict__ mods) {
-  extern __shared__ uint2 hs[];  // [ntgt][w]: the split constant of source a for target t
+  extern __shared__ uint2 hs[];  // [ntgt][W]: the split constant of source a for target t
   const int N = 1 << log_n;
-  for (int e = threadIdx.x; e < a.ntgt * a.w; e += blockDim.x) {
-    const int t = e / a.w, k = e % a.w;
-    const int r = t < a.skip_lo ? t : t + a.w;
+  for (int e = threadIdx.x; e < a.ntgt * W; e += blockDim.x) {
+    const int t = e / W, k = e % W;
+    const int r = t < a.skip_lo ? t : t + W;
     const int mi = r < a.cur ? r : a.L + r - a.cur;
     const u64 h = a.H[(size_t)k * a.h_row + mi];
     hs[e] = make_uint2((uint32_t)(h & ((1ull << 30) - 1)), (uint32_t)(h >> 30));
@@ -85,42 +85,61 @@ __global__ void __launch_bounds__(256) k_conv(ConvArgs a, int log_n, const Mod* 
     const int item = (int)(g >> log_n);
     const int n = (int)(g & (N - 1));
     const u64* yp = a.y + item * a.y_item + n;
-    uint2 ys[WMAX];
+    uint2 ys[W];
 #pragma unroll
-    for (int k = 0; k < WMAX; ++k) {
-      const u64 v = k < a.w ? yp[(size_t)k << log_n] : 0;
+    for (int k = 0; k < W; ++k) {
+      const u64 v = yp[(size_t)k << log_n];
       ys[k] = make_uint2((uint32_t)(v & ((1ull << 30) - 1)), (uint32_t)(v >> 30));
     }
     u64* op = a.out + item * a.out_item + n;
     for (int t = 0; t < a.ntgt; ++t) {
-      const uint2* h = hs + t * a.w;
+      const uint2* h = hs + t * W;
       Split4 s{0, 0, 0, 0};
 #pragma unroll
-      for (int k = 0; k < WMAX; ++k) {
-        if (k < a.w) {
-          const uint2 c = h[k];
-          s.s00 += (u64)ys[k].x * c.x;
-          s.sa += (u64)ys[k].x * c.y;
-          s.sb += (u64)ys[k].y * c.x;
-          s.s11 += (u64)ys[k].y * c.y;
-        }
+      for (int k = 0; k < W; ++k) {
+        const uint2 c = h[k];
+        s.s00 += (u64)ys[k].x * c.x;
+        s.sa += (u64)ys[k].x * c.y;
+        s.sb += (u64)ys[k].y * c.x;
+        s.s11 += (u64)ys[k].y * c.y;
       }
-      const int r = t < a.skip_lo ? t : t + a.w;
+      const int r = t < a.skip_lo ? t : t + W;
       const int mi = r < a.cur ? r : a.L + r - a.cur;
       op[(size_t)r << log_n] = fold_split(s, mods[mi]);
     }
   }
 }
-static int conv_launch(const HolmesCtx& c, const ConvArgs& a, cudaStream_t st) {
-  if (a.w < 1 || a.w > MAXA || a.ntgt < 1) return -3;
-  const size_t smem = (size_t)a.ntgt * a.w * sizeof(uint2);
+template <int W>
+static int conv_launch_w(const HolmesCtx& c, const ConvArgs& a, cudaStream_t st) {
+  const size_t smem = (size_t)a.ntgt * W * sizeof(uint2);
   const size_t work = (size_t)a.items << c.log_n;
   size_t blocks = (work + 255) / 256;
   if (blocks > 148 * 8) blocks = 148 * 8;
   count_launch();
-  if (a.w <= 8) k_conv<8><<<(unsigned)blocks, 256, smem, st>>>(a, c.log_n, c.d_mod);
-  else k_conv<16><<<(unsigned)blocks, 256, smem, st>>>(a, c.log_n, c.d_mod);
+  k_conv<W><<<(unsigned)blocks, 256, smem, st>>>(a, c.log_n, c.d_mod);
   return (int)cudaGetLastError();
+}
+static int conv_launch(const HolmesCtx& c, const ConvArgs& a, cudaStream_t st) {
+  if (a.ntgt < 1) return -3;
+  switch (a.w) {
+    case 1: return conv_launch_w<1>(c, a, st);
+    case 2: return conv_launch_w<2>(c, a, st);
+    case 3: return conv_launch_w<3>(c, a, st);
+    case 4: return conv_launch_w<4>(c, a, st);
+    case 5: return conv_launch_w<5>(c, a, st);
+    case 6: return conv_launch_w<6>(c, a, st);
+    case 7: return conv_launch_w<7>(c, a, st);
+    case 8: return conv_launch_w<8>(c, a, st);
+    case 9: return conv_launch_w<9>(c, a, st);
+    case 10: return conv_launch_w<10>(c, a, st);
+    case 11: return conv_launch_w<11>(c, a, st);
+    case 12: return conv_launch_w<12>(c, a, st);
+    case 13: return conv_launch_w<13>(c, a, st);
+    case 14: return conv_launch_w<14>(c, a, st);
+    case 15: return conv_launch_w<15>(c, a, st);
+    case 16: return conv_launch_w<16>(c, a, st);
+    default: return -3;
+  }
 }
 // Plain load / in-place store of the target limbs of one ModUp digit (poly p = item * ntgt + t).
 struct DigitRows {
@@ -339,8 +358,12 @@ struct StKsQ {
     s.o[n] = r;
   }
 };
+// resident CTAs per SM for the key-switch NTTs (their fused loads / stores hold more state than a plain NTT)
+#ifndef HOLMES_KS_MINB
+#define HOLMES_KS_MINB HOLMES_NTT_MINB
+#endif
 template <int LOGN>
-__global__ void HOLMES_NTT_BOUNDS(LOGN) k_ks_q(NttTables T, LdRows ld, StKsQ st) {
+__global__ void __launch_bounds__(NttGeom<LOGN>::THREADS, HOLMES_KS_MINB) k_ks_q(NttTables T, LdRows ld, StKsQ st) {
   const int p = blockIdx.x / NttGeom<LOGN>::CL;
   ntt_forward_body<LOGN>(p, (p % (2 * st.cur)) % st.cur, T, ld, st);
 }
