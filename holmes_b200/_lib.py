@@ -52,6 +52,7 @@ SIGNATURES = {
     "holmes_bsgs_mac": [p, p, p, p, i64, i32, i32, p, i64, i32, i32, p],
     "holmes_modsum": [p, p, i32, p, i32, i32, i64, p],
     "holmes_launch_count": [ctypes.POINTER(ctypes.c_ulonglong)],
+    "holmes_device_error": [i32, ctypes.POINTER(ctypes.c_int)],
     "holmes_mac_multi":[p, p, p, i64, i32, i32, p, i64, i32, i32, i32, p, p, p, p],
 }
 

@@ -219,6 +219,11 @@ int holmes_launch_count(unsigned long long* out) {
   return 0;
 }
 
+int holmes_device_error(int reset, int* flag_out) {
+  if (!flag_out) return -1;
+  return tc_error_flag(reset, flag_out);
+}
+
 int holmes_mac_multi(uint64_t* res, const uint64_t* const* c0s, const uint64_t* const* c1s, long long bstride, int nb,
                      int inputs, const uint64_t* pts, long long pstride, int groups, int ti, int limbs,
                      const uint64_t* primes, const uint64_t* ratios, const uint64_t* ks, void* stream_ptr) {

@@ -141,11 +141,6 @@ int add_const(const HolmesCtx& c, const u64* a, const u64* consts, u64* out, int
 // sums (reduced every 16 baby steps: 16 products of canonical residues stay below 14 2^k).  Warps of
 // one block read the same plaintext words, so the plaintext row is fetched from HBM once per block
 // and served from L1 to the other inputs.
-constexpr int kMaxInputs = 32;
-struct InPtrs {
-  const u64* c0[kMaxInputs];
-  const u64* c1[kMaxInputs];
-};
 template <int TG>
 __global__ void __launch_bounds__(256) k_bsgs_mac(u64* __restrict__ res, InPtrs in, long long bstride, int nb,
                                                   int inputs, int G, const u64* __restrict__ pts, long long pstride,
@@ -545,6 +540,16 @@ int bsgs_mac(ModSrc ms, u64* res, const u64* const* c0s, const u64* const* c1s,
   for (int i = 0; i < kMaxInputs; ++i) {
     in.c0[i] = c0s[i < inputs ? i : 0];
     in.c1[i] = c1s[i < inputs ? i : 0];
+  }
+  // HOLMES_MAC_TC=1 selects the tensor-core kernel (mac_tc.cu) for the shapes it takes.  It is bit-exact but
+  // measured slower than k_bsgs_mac3 at the bench shape (19.7 vs 11.7 ms per 512-row chunk of 16 ciphertexts):
+  // its byte-recombination epilogue and per-item overheads cost ~720 instructions per output.
+  const char* tc = getenv("HOLMES_MAC_TC");
+  if (tc && tc[0] == '1') {
+    int lg = 0;
+    while ((1 << lg) < n) ++lg;
+    const int r = bsgs_mac_tc(ms, res, in, bstride, nb, inputs, pts, pstride, groups, limbs, lg, st);
+    if (r != -7) return r;
   }
   if (getenv("HOLMES_MAC_V1")) {  // the first-generation kernel, kept for A/B timing
     constexpr int TG = 8;

@@ -106,6 +106,17 @@ int mul_const(const HolmesCtx& c, const u64* a, const u64* consts, u64* out, int
               long long o_item, cudaStream_t st);
 
 // BSGS baby-step multiply-accumulate (see mac.cu)
+// per-input baby pointers of the BSGS MAC (both components)
+constexpr int kMaxInputs = 32;
+struct InPtrs {
+  const u64* c0[kMaxInputs];
+  const u64* c1[kMaxInputs];
+};
+// tensor-core MAC (mac_tc.cu): nb <= 128; returns -7 for shapes it does not take
+int bsgs_mac_tc(ModSrc ms, u64* res, const InPtrs& in, long long bstride, int nb, int inputs, const u64* pts,
+                long long pstride, int groups, int limbs, int log_n, cudaStream_t st);
+// the tensor-core MAC's device error flag (a bounded wait ran out); reset clears it
+int tc_error_flag(int reset, int* out);
 int bsgs_mac(ModSrc ms, u64* res, const u64* const* c0s, const u64* const* c1s,
              long long bstride, int nb, int inputs, const u64* pts, long long pstride, int groups, int limbs, int n,
              cudaStream_t st);

@@ -146,6 +146,11 @@ int holmes_modsum(void* ctx, const uint64_t* const* srcs, int nsrc, uint64_t* ou
 /* kernels launched by this library since it was loaded (all streams, all contexts) */
 int holmes_launch_count(unsigned long long* count_out);
 
+/* 1 when a tensor-core kernel's bounded wait ran out since the last reset (the kernel then stopped early and
+ * its output is incomplete); reset != 0 clears the flag.  Synchronises with the device.  No reference
+ * counterpart: EasyFHE kernels do not wait on hardware barriers. */
+int holmes_device_error(int reset, int* flag_out);
+
 /* ---- drop-in for the reference's own ctypes binding (bench/cmp/kernels/holmes_mac.cu:359-402, bound in
  *      bench/cmp/holmes_multi_mac.py:33-54): same signature, arguments and return codes; N = 2^16;
  *      `ti` is accepted from the reference's tile set and used only as a hint. */
