@@ -716,6 +716,88 @@ def homo_mul_relin_rescale_postop(a: Cipher, b: Cipher, ctx) -> Cipher:
     return rescale(homo_mul_relin(a, b, ctx), ctx)
 
 
+# ----------------------------------------------------------------------------------------------------- scalars
+# A real scalar v at scale S is the constant polynomial round(v S): the same residue in every NTT word, so scalar
+# products and sums are per-limb constant kernels (holmes_mul_const / holmes_add_const).  Names and argument
+# meaning follow the EasyFHE calls llama3fhe makes (operators/nonlinear/bootstrap.py:604-623,
+# operators/norm/refresh.py:21-31).
+
+
+@dataclass
+class EncodedScalar:
+    value: float
+    integer: int  # round(value * scaling_factor)
+    state: CipherState
+
+    def residues(self, ctx, limbs: int) -> torch.Tensor:
+        return torch.tensor([self.integer % ctx.q(i) for i in range(int(limbs))], dtype=torch.uint64,
+                            device=ctx.device)
+
+
+def encode_scalar(value, cur_limbs: int, scale_degree: int = 1, scaling_factor: float | None = None,
+                  context=None) -> EncodedScalar:
+    ctx = _ctx(context)
+    if isinstance(value, complex) or np.iscomplexobj(value):
+        raise ValueError("encode_scalar encodes real values; multiply by i with homo_mul_i")
+    sf = float(scaling_factor) if scaling_factor is not None else ctx.scale_at(int(cur_limbs))
+    return EncodedScalar(float(value), int(round(float(value) * sf)), CipherState(int(cur_limbs), int(scale_degree), sf))
+
+
+def _const_kernel(name: str, a: Cipher, k: torch.Tensor, out: Cipher, comps: range, ctx: Context) -> None:
+    cur = int(a.state.cur_limbs)
+    for c in comps:
+        _lib.call(name, ctx.handle, a.cv[c].data_ptr(), k.data_ptr(), out.cv[c].data_ptr(), a.batch_size, cur,
+                  _item_stride(a.cv[c]), _item_stride(out.cv[c]), _stream())
+
+
+def homo_mul_scalar(a: Cipher, scalar: EncodedScalar, ctx) -> Cipher:
+    """a * scalar without rescale: the scale degrees and factors multiply."""
+    ctx = _ctx(ctx)
+    cur = int(a.state.cur_limbs)
+    sf = None
+    if a.state.scaling_factor is not None and scalar.state.scaling_factor is not None:
+        sf = float(a.state.scaling_factor) * float(scalar.state.scaling_factor)
+    out = _new_cipher(ctx, a.batch_size, cur,
+                      CipherState(cur, int(a.state.scale_degree) + int(scalar.state.scale_degree), sf), a.slots)
+    _const_kernel("holmes_mul_const", a, scalar.residues(ctx, cur), out, range(len(a.cv)), ctx)
+    return out
+
+
+def homo_mul_scalar_rescale(a: Cipher, scalar: EncodedScalar, ctx) -> Cipher:
+    return rescale(homo_mul_scalar(a, scalar, ctx), ctx)
+
+
+def homo_add_scalar(a: Cipher, scalar, ctx) -> Cipher:
+    """a + scalar; a float is encoded at the ciphertext's own scale, an EncodedScalar must carry that scale."""
+    ctx = _ctx(ctx)
+    cur = int(a.state.cur_limbs)
+    sf = float(a.state.scaling_factor if a.state.scaling_factor is not None else ctx.scale_at(cur))
+    if not isinstance(scalar, EncodedScalar):
+        scalar = encode_scalar(float(scalar), cur, int(a.state.scale_degree), sf, ctx)
+    elif scalar.state.scaling_factor is not None and abs(float(scalar.state.scaling_factor) - sf) > 1e-9 * sf:
+        raise ValueError("homo_add_scalar: the scalar's scale differs from the ciphertext's")
+    out = a.cipher_like([torch.empty_like(a.cv[0][:, :cur])] + [c[:, :cur].clone() for c in a.cv[1:]],
+                        state=a.state)
+    _const_kernel("holmes_add_const", a, scalar.residues(ctx, cur), out, range(1), ctx)
+    return out
+
+
+def homo_add_pt(a: Cipher, pt: Plaintext, ctx) -> Cipher:
+    """a + pt (pt at the ciphertext's scale and degree, at least as many limbs)."""
+    ctx = _ctx(ctx)
+    cur = int(a.state.cur_limbs)
+    if int(pt.state.cur_limbs) < cur:
+        raise ValueError("homo_add_pt: plaintext has fewer limbs than the ciphertext")
+    if int(pt.state.scale_degree) != int(a.state.scale_degree):
+        raise ValueError("homo_add_pt: scale degree mismatch")
+    out = a.cipher_like([torch.empty_like(a.cv[0][:, :cur])] + [c[:, :cur].clone() for c in a.cv[1:]],
+                        state=a.state)
+    p = pt.cv[0][:1].expand(a.batch_size, -1, -1) if pt.cv[0].shape[0] == 1 else pt.cv[0]
+    _lib.call("holmes_elementwise", ctx.handle, 0, a.cv[0].data_ptr(), p.data_ptr(), out.cv[0].data_ptr(),
+              a.batch_size, cur, _item_stride(a.cv[0]), int(p.stride(0)), _item_stride(out.cv[0]), _stream())
+    return out
+
+
 # ----------------------------------------------------------------------------------------------------- constants
 
 

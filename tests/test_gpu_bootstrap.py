@@ -62,6 +62,26 @@ def test_refresh_many_matches_single(boot):
     assert op.batch_calls >= 1
 
 
+def test_pair_bootstrap_and_halve(boot):
+    """Two real ciphertexts through one refresh as a + i b (stations.pair_bootstrap), unpacked with the
+    conjugation to (2a, 2b), then halved."""
+    from holmes_b200 import refresh as R
+
+    _, client, ctx, op = boot
+    rng = np.random.default_rng(3)
+    a, b = rng.normal(size=ctx.max_slots) * 0.3, rng.normal(size=ctx.max_slots) * 0.3
+    cts = [client.encrypt(a, cur_limbs=3, counter=40), client.encrypt(b, cur_limbs=3, counter=41)]
+    out, factor = R.pair_bootstrap(cts, context=ctx, bootstrap_operator=op)
+    assert factor == 2.0 and len(out) == 2
+    assert np.abs(client.decrypt(out[0]) - 2 * a).max() < 1e-5
+    assert np.abs(client.decrypt(out[1]) - 2 * b).max() < 1e-5
+    half = R.halve(out, context=ctx)
+    assert np.abs(client.decrypt(half[0]) - a).max() < 1e-5
+    assert np.abs(client.decrypt(half[1]) - b).max() < 1e-5
+    with pytest.raises(ValueError):
+        R.pair_bootstrap(cts[:1], context=ctx, bootstrap_operator=op)
+
+
 def test_bootstrap_rejects_bad_input(boot):
     _, client, ctx, op = boot
     ct = client.encrypt(np.zeros(ctx.max_slots), cur_limbs=1, counter=30)
