@@ -7,13 +7,14 @@ import torch
 from oracle.oracle import Oracle, OracleParams
 
 
-def make_pair(log_n=10, limbs=4, dnum=2, dcrt=40, first=50, special=50, K=None, hamming=32, seed=0):
+def make_pair(log_n=10, limbs=4, dnum=2, dcrt=40, first=50, special=50, K=None, hamming=32, seed=0, scale_bits=None):
     from holmes_b200 import fhe as F
 
     op = OracleParams(log_n=log_n, limbs=limbs, dnum=dnum, dcrt_bits=dcrt, first_mod_bits=first, special_bits=special,
-                      special_limbs=K, hamming=hamming, seed=seed)
+                      special_limbs=K, hamming=hamming, seed=seed, scale_bits=scale_bits)
     spec = F.CKKSContextSpec(depth=limbs - 1, log_n=log_n, dnum=dnum, dcrt_bits=dcrt, first_mod=first,
                              special_bits=special, special_limbs=K, hamming_weight=hamming, seed=seed,
+                             scale_bits=scale_bits,
                              secret_key_dist="SPARSE_TERNARY" if hamming else "UNIFORM_TERNARY",
                              auto_load_keys=False)
     client, ctx = F.generate_client_context(spec)
