@@ -470,6 +470,79 @@ def run_kernel(args) -> None:
     ctx.close()
 
 
+def run_primitives(args) -> None:
+    """BASELINE config 2, the RNS-CKKS primitive sweep: N = 2^16, ~50-bit primes, dnum 3 (alpha = K = 12),
+    L = 1..36 active limbs, residues uniform in [0, q_i) (seed 0).  Per L: batched forward / inverse NTT,
+    a rotation (hoisted-free key switch) of a batch of 16 ciphertexts sharing one key, the plaintext x
+    ciphertext product and a rescale, each timed with CUDA events after a warm-up (inputs above L2 at the
+    larger sizes).  Algorithmic bytes per op: NTT 16 b L N; key switch per ciphertext
+    (L + 2 beta (L + K) / batch + L + 2 L) N 8 with the key read once per batch; plaintext product 5 L N 8;
+    rescale (2 L + 2 (L - 1)) N 8.  One JSON line with a row per (op, L)."""
+    import torch
+
+    from holmes_b200 import _lib as L_
+    from holmes_b200 import fhe as F
+
+    peak, peak_kind = peaks()
+    lmax = 36
+    spec = F.CKKSContextSpec(depth=lmax - 1, log_n=16, dnum=3, dcrt_bits=50, first_mod=50, special_bits=50, seed=0,
+                             hamming_weight=192, auto_load_keys=False)
+    client, ctx = F.generate_client_context(spec)
+    N, K = ctx.N, ctx.K
+    gen = torch.Generator(device=ctx.device).manual_seed(0)
+    qcol = torch.tensor(list(ctx.moduli[:lmax]), dtype=torch.int64, device=ctx.device).view(1, lmax, 1)
+
+    def rand(items, limbs):
+        r = torch.randint(0, 2 ** 62, (items, limbs, N), device=ctx.device, dtype=torch.int64, generator=gen)
+        return (r % qcol[:, :limbs]).to(torch.uint64)
+
+    def timed(fn, reps):
+        fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(reps):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / reps / 1e3
+
+    rows = []
+
+    def row(op, limbs, batch, seconds, nbytes, units):
+        rows.append({"op": op, "limbs": limbs, "batch": batch, "ms": round(seconds * 1e3, 4),
+                     "ops_per_s": round(units / seconds, 1), "gbs": round(nbytes / seconds / 1e9, 1),
+                     "hbm_frac": round(nbytes / seconds / 1e9 / peak, 4)})
+
+    for limbs in (1, 4, 8, 16, 24, 36):
+        for b in (1, 16, 256 if limbs <= 8 else 64):
+            x = rand(b, limbs)
+            for inv in (0, 1):
+                t = timed(lambda: L_.call("holmes_ntt", ctx.handle, x.data_ptr(), b, limbs, limbs * N, 0, inv, 0), 5)
+                row("intt" if inv else "ntt", limbs, b, t, 16 * b * limbs * N, b * limbs)
+            del x
+        I = 16
+        c0, c1 = rand(I, limbs), rand(I, limbs)
+        o0, o1 = torch.empty_like(c0), torch.empty_like(c1)
+        g = ctx.galois(1)
+        key = ctx.switch_key(g, limbs)
+        beta = ctx.beta(limbs)
+        t = timed(lambda: F.rotate_batch(ctx, c0, c1, limbs, 1, o0, o1), 3)
+        row("rotate", limbs, I, t, (I * 4 * limbs + 2 * beta * (limbs + K)) * N * 8, I)
+        ct = F.Cipher([c0, c1], F.CipherState(limbs, 1, ctx.scale), ctx.max_slots, False, I, ctx)
+        pt = F.Plaintext([rand(1, limbs)], F.CipherState(limbs, 1, ctx.scale), ctx.max_slots, False, 1, ctx)
+        t = timed(lambda: F.homo_mul_pt(ct, pt, ctx), 5)
+        row("mul_pt", limbs, I, t, (limbs + 4 * limbs * I) * N * 8, I)
+        if limbs >= 2:
+            ct2 = F.Cipher([c0, c1], F.CipherState(limbs, 2, ctx.scale ** 2), ctx.max_slots, False, I, ctx)
+            t = timed(lambda: F.rescale(ct2, ctx), 5)
+            row("rescale", limbs, I, t, I * (4 * limbs - 2) * N * 8, I)
+        del c0, c1, o0, o1, key
+    print(json.dumps({"workload": "primitives (config 2)", "n": N, "dnum": 3, "alpha": ctx.alpha, "K": K,
+                      "peak_gbs": peak, "peak_kind": peak_kind, "rows": rows}), flush=True)
+    ctx.close()
+
+
 def run_bootstrap(args) -> None:
     """Production-size bootstrap: N = 2^16, 38 limbs (59/60-bit, dnum 5), level budget (5, 5) -> 18 limbs left
     (llama3fhe/parallel/presets.py:25-60), a batch of ``--boot-batch`` ciphertexts refreshed together
@@ -513,7 +586,7 @@ def run_bootstrap(args) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--workload", choices=("linear", "bootstrap"), default="linear")
+    ap.add_argument("--workload", choices=("linear", "bootstrap", "primitives"), default="linear")
     ap.add_argument("--boot-batch", type=int, default=8)
     ap.add_argument("--kernel", default=None, help="profile one kernel family (see run_kernel)")
     ap.add_argument("--gpus", type=int, default=1)
@@ -531,6 +604,8 @@ def main() -> None:
         run_kernel(args)
     elif args.workload == "bootstrap":
         run_bootstrap(args)
+    elif args.workload == "primitives":
+        run_primitives(args)
     elif args.impl == "reference":
         run_reference(args)
     else:
