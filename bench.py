@@ -12,8 +12,13 @@ basis, re-encodes all 4096 diagonal rows online (pack -> special FFT -> round ->
 reference does per projection.  Weights ~ N(0, 0.02^2) (complex), pre-multiplied by a seeded +-1 Walsh-
 Hadamard rotation (QuaRot); inputs ~ N(0, 1); all synthetic and seeded.
 
-Multi-GPU (torchrun): the 16 inputs are token-sharded over the ranks (16 / W each), as the reference's
-feature-major token ownership does (parallel/prefill/ownership.py:1-44); no data-path collective.
+Multi-GPU (torchrun), default ``--parallelism chunk``: rank r key-switches 1 / W of the 64 baby rotations of all 16
+inputs and an NCCL all-gather completes the basis on every rank, then the rank encodes, MACs and runs the giant
+Horner chain of its 8 / W BSGS chunks (the reference's decode-style chunk ownership,
+parallel/decode/decode_ownership.py), and a modular reduce-scatter (all-to-all of raw limbs + the engine's mod-q
+sum) delivers each rank its token shard (16 / W outputs, parallel/prefill/ownership.py:1-44) to rescale.
+``--parallelism token`` instead gives each rank 16 / W inputs end to end with no data-path collective, which
+repeats the page's encode on every rank.
 
 ``--impl reference`` times the CPU restatement of the same path (``oracle/``) on the host cores, on a bounded
 sample scaled to one page.  EasyFHE, the reference's engine, is not distributed with the reference and
@@ -185,7 +190,9 @@ def run_engine(args) -> None:
     # chunk sharding: every rank holds all inputs and MACs its BSGS chunks; token sharding: its own inputs
     held = list(range(n_inputs)) if chunked else mine
     cts = [session.encrypt(carriers[i], level=level, counter=i) for i in held]
-    op = LN.LinearOperator(crypto_context=session, token_lanes=LANES, config=cfg)
+    # chunk sharding also splits the baby key switches over the ranks and all-gathers the basis
+    op = LN.LinearOperator(crypto_context=session, token_lanes=LANES, config=cfg,
+                           baby_shard=(rank, world, None) if chunked else None)
     lw = LN.LinearWeight(weight, dtype=np.complex128, crypto_context=session)
     lw.prepare(cfg)
     my_chunks = C.chunk_shard(len(op.plan(DIM).chunks), world, rank)
@@ -254,7 +261,8 @@ def run_engine(args) -> None:
             dev_in.append(F.Cipher([d[0:1], d[1:2]], cts[0].state, cts[0].slots, False, 1, ctx))
         w_dev = host_w.to(ctx.device, non_blocking=True)
         with LN.LinearWeight(w_dev, dtype=np.complex128, crypto_context=session) as lw2:
-            with LN.LinearOperator(crypto_context=session, token_lanes=LANES, config=cfg) as op2:
+            with LN.LinearOperator(crypto_context=session, token_lanes=LANES, config=cfg,
+                                   baby_shard=(rank, world, None) if chunked else None) as op2:
                 res = page(op2, dev_in, lw2)
         back = [torch.stack([r.cv[0][0], r.cv[1][0]]).to("cpu", non_blocking=True) for r in res]
         out_bytes = sum(b.numel() * 8 for b in back)
@@ -309,7 +317,7 @@ def run_engine(args) -> None:
             "config": {"workload": f"QKV-shaped linear page: {n_inputs} ciphertexts x one 4096x4096 complex page, "
                                    f"N=2^16, {cur}/{DEPTH + 1} limbs, dnum {DNUM} (alpha {ctx.alpha}, K {ctx.K}), "
                                    f"baby 64, 8 chunks x 8 giants, lanes 8, rescale",
-                       "parallelism": (f"chunk-sharded x{world} + modular reduce-scatter" if chunked
+                       "parallelism": (f"chunk-sharded x{world} + baby all-gather + modular reduce-scatter" if chunked
                                        else f"token-sharded x{world}"), "inputs_per_rank": len(mine),
                        "l2": "working set (plaintext chunks 3.4 GB, baby basis 13.6 GB) >> 126 MB L2",
                        "keys": f"{len(rots)} rotation keys capped at {cur} limbs"},
@@ -595,7 +603,7 @@ def main() -> None:
     ap.add_argument("--impl", choices=("holmes", "reference"), default="holmes")
     ap.add_argument("--inputs", type=int, default=INPUTS)
     ap.add_argument("--limbs", type=int, default=CUR_LIMBS)
-    ap.add_argument("--parallelism", choices=("token", "chunk"), default="token")
+    ap.add_argument("--parallelism", choices=("token", "chunk"), default="chunk")
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--cpu-sample", default="small")
     ap.add_argument("--no-check", dest="check", action="store_false")

@@ -60,6 +60,19 @@ def exchange_partials(partials: torch.Tensor, world: int, group=None) -> torch.T
     return recv
 
 
+def all_gather_rows(storage: torch.Tensor, lo: int, hi: int, world: int, group=None) -> None:
+    """In-place all-gather along dim 0: this rank filled rows [lo, hi) of ``storage`` (equal contiguous ranges
+    per rank, in rank order); afterwards every rank holds every row.  Residues travel as their bit pattern."""
+    rows = int(storage.shape[0])
+    if rows % world or hi - lo != rows // world:
+        raise ValueError(f"rows [{lo}, {hi}) are not this rank's equal share of {rows} over {world}")
+    flat = storage.view(torch.int64).reshape(-1)
+    per = flat.numel() // world
+    r = lo // (hi - lo)
+    if world > 1:
+        dist.all_gather_into_tensor(flat, flat[r * per:(r + 1) * per], group=group)
+
+
 def modsum(ctx, buffers: torch.Tensor, limbs: int) -> torch.Tensor:
     """Sum [k][items][limbs][N] buffers modulo q limb-wise on the GPU -> [items][limbs][N]."""
     k, items = int(buffers.shape[0]), int(buffers.shape[1])

@@ -420,7 +420,8 @@ _EMPTY_PROFILE = {"weight_prepare_cpu": 0.0, "weight_upload": 0.0, "baby_precomp
 
 
 class _Babies:
-    """Baby basis of a batch of inputs: storage [2][B][I][cur][N] (input i's block is strided by I)."""
+    """Baby basis of a batch of inputs: storage [B][2][I][cur][N] (baby-major, so a contiguous range of babies is
+    one contiguous block for the sharded build's all-gather; input i's babies are strided by 2 I cur N)."""
 
     def __init__(self, sources, level: int, storage: torch.Tensor, state: F.CipherState, slots: int) -> None:
         self.sources = tuple(sources)
@@ -430,11 +431,11 @@ class _Babies:
         self.slots = slots
 
     def blocks(self, ctx: F.Context) -> list[F.Cipher]:
-        B, inputs = int(self.storage.shape[1]), int(self.storage.shape[2])
+        B, inputs = int(self.storage.shape[0]), int(self.storage.shape[2])
         out = []
         for i in range(inputs):
-            c0 = self.storage[0, :, i]
-            c1 = self.storage[1, :, i]
+            c0 = self.storage[:, 0, i]
+            c1 = self.storage[:, 1, i]
             out.append(F.Cipher([c0, c1], self.state, self.slots, False, B, ctx))
         return out
 
@@ -442,8 +443,12 @@ class _Babies:
 class LinearOperator:
     """A reusable BSGS schedule with an operator-local baby cache (reference: operator.py:58-639)."""
 
-    def __init__(self, *, crypto_context, token_lanes: int, config: LinearOperatorConfig | None = None) -> None:
+    def __init__(self, *, crypto_context, token_lanes: int, config: LinearOperatorConfig | None = None,
+                 baby_shard=None) -> None:
+        """``baby_shard = (rank, world, group)`` splits the baby key switches over the ranks of ``group`` (each
+        rank holding the same inputs) and all-gathers the basis; None builds it locally."""
         self.crypto_context = crypto_context
+        self.baby_shard = None if baby_shard is None else (int(baby_shard[0]), int(baby_shard[1]), baby_shard[2])
         self.token_lanes = int(token_lanes)
         if self.token_lanes <= 0:
             raise ValueError("token_lanes must be positive.")
@@ -476,21 +481,32 @@ class LinearOperator:
         return None
 
     def _build_babies(self, inputs, plan: LinearPlan, level: int) -> _Babies:
+        """All B baby rotations of every input.  With a baby shard (rank, world, group) set, this rank key-switches
+        only its contiguous range of babies and an all-gather over the group fills in the rest: every rank then
+        holds the whole basis at 1 / world of the key switches."""
         ctx = self.crypto_context.context
         cur = int(inputs[0].state.cur_limbs)
         n_in = len(inputs)
         B = int(plan.baby_steps)
-        storage = torch.empty((2, B, n_in, cur, ctx.N), dtype=torch.uint64, device=ctx.device)
+        storage = torch.empty((B, 2, n_in, cur, ctx.N), dtype=torch.uint64, device=ctx.device)
         c0 = torch.stack([c.cv[0][0, :cur] for c in inputs])
         c1 = torch.stack([c.cv[1][0, :cur] for c in inputs])
-        storage[0, 0].copy_(c0)
-        storage[1, 0].copy_(c1)
-        if B > 1:
+        lo, hi = 0, B
+        shard = self.baby_shard
+        if shard is not None and B % shard[1] == 0 and shard[1] > 1:
+            lo, hi = shard[0] * B // shard[1], (shard[0] + 1) * B // shard[1]
+        if lo == 0:
+            storage[0, 0].copy_(c0)
+            storage[0, 1].copy_(c1)
+        if max(lo, 1) < hi:
             digits, dig_item = F._modup(ctx, c1, cur, n_in)
-            for b in range(1, B):
+            for b in range(max(lo, 1), hi):
                 g = ctx.galois(plan.baby_offsets[b])
                 F._keyswitch(ctx, digits, dig_item, cur, g, ctx.switch_key(g, cur), c0, None, F._item_stride(c0),
-                             storage[0, b], storage[1, b], n_in)
+                             storage[b, 0], storage[b, 1], n_in)
+        if (lo, hi) != (0, B):
+            from .collectives import all_gather_rows
+            all_gather_rows(storage, lo, hi, shard[1], shard[2])
         entry = _Babies(inputs, level, storage, inputs[0].state, int(inputs[0].slots))
         if bool(self.config.reuse_baby_rotations):
             self._baby_cache[self._baby_key(inputs, plan)] = entry

@@ -64,3 +64,76 @@ def test_modular_reduce_scatter_two_gpus(tmp_path):
         want = sum(p[owned].astype(object) for p in parts)
         for li, ql in enumerate(q):
             assert np.array_equal(got[:, li].astype(object), want[:, li] % ql)
+
+
+def _linear_worker(rank, world, port, out_dir):
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from holmes_b200 import collectives as C
+    from holmes_b200 import fhe as F
+    from holmes_b200 import linear as LN
+    from tests.gpu_helpers import make_pair
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        _, client, ctx = make_pair(log_n=11, limbs=4, dnum=2, dcrt=45, first=55, special=55)
+        session = LN.Session(client, ctx)
+        dim, lanes = 64, 16
+        cfg = LN.LinearOperatorConfig(baby_steps=8, baby_anchor_step=8, max_plaintext_rows=16)
+        rng = np.random.default_rng(26081431)
+        w = rng.normal(scale=0.02, size=(dim, dim))
+        xs = rng.normal(size=(4, lanes, dim))
+        cts = [client.encrypt(x.T.reshape(-1), cur_limbs=ctx.L, counter=100 + i) for i, x in enumerate(xs)]
+        op = LN.LinearOperator(crypto_context=session, token_lanes=lanes, config=cfg, baby_shard=(rank, world, None))
+        lw = LN.LinearWeight(w, dtype=w.dtype, crypto_context=session)
+        chunks = C.chunk_shard(len(op.plan(dim).chunks), world, rank)
+        parts, _ = op.apply(cts, lw, chunk_indices=chunks, rescale=False)
+        s0 = C.modular_reduce_scatter(ctx, torch.cat([p.cv[0] for p in parts]), world)
+        s1 = C.modular_reduce_scatter(ctx, torch.cat([p.cv[1] for p in parts]), world)
+        mine = list(C.token_shard(4, world, rank))
+        res = F.rescale(F.Cipher([s0, s1], parts[0].state, parts[0].slots, False, len(mine), ctx), ctx)
+        torch.cuda.synchronize()
+        np.save(os.path.join(out_dir, f"lin{rank}.npy"), torch.stack([res.cv[0], res.cv[1]]).cpu().numpy())
+        dist.barrier()
+        ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_chunk_sharded_linear_with_baby_all_gather_two_gpus(tmp_path):
+    """Chunk sharding with the baby key switches split over the ranks and all-gathered: every owner's rescaled
+    output equals the oracle's single-process linear residue for residue."""
+    import torch.multiprocessing as mp
+
+    from holmes_b200 import collectives as C
+    from holmes_b200 import linear as LN
+    from tests.gpu_helpers import make_pair
+    from tests.test_gpu_parity import _oracle_linear
+
+    world = 2
+    mp.spawn(_linear_worker, args=(world, _port(), str(tmp_path)), nprocs=world, join=True)
+    o, _, ctx = make_pair(log_n=11, limbs=4, dnum=2, dcrt=45, first=55, special=55)
+    try:
+        dim, lanes = 64, 16
+        plan = LN.LinearOperatorConfig(baby_steps=8, baby_anchor_step=8, max_plaintext_rows=16).plan(
+            dimension=dim, token_lanes=lanes)
+        rng = np.random.default_rng(26081431)
+        w = rng.normal(scale=0.02, size=(dim, dim))
+        xs = rng.normal(size=(4, lanes, dim))
+        refs = [o.encrypt(x.T.reshape(-1), ctx.L, counter=100 + i) for i, x in enumerate(xs)]
+        expect = _oracle_linear(o, refs, w, plan, ctx.L, ctx.scale)
+        for r in range(world):
+            got = np.load(tmp_path / f"lin{r}.npy")
+            for k, i in enumerate(C.token_shard(4, world, r)):
+                np.testing.assert_array_equal(got[0, k], expect[i][0])
+                np.testing.assert_array_equal(got[1, k], expect[i][1])
+    finally:
+        ctx.close()

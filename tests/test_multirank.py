@@ -73,3 +73,29 @@ def test_exchange_partials_gloo_world2(tmp_path):
         want = sum(p[owned].astype(object) for p in parts)
         for li in range(3):
             assert np.array_equal(total[:, li].astype(object), want[:, li] % q[li])
+
+
+def _gather_worker(rank, world, port, out_dir):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        rows, per_row = 8, 5
+        storage = torch.zeros((rows, per_row), dtype=torch.uint64)
+        lo, hi = rank * rows // world, (rank + 1) * rows // world
+        for r in range(lo, hi):  # this rank's babies: row r holds 1000 r + k, with the top bit set in some words
+            storage[r] = torch.tensor([(1000 * r + k) | ((k % 2) << 63) for k in range(per_row)], dtype=torch.uint64)
+        C.all_gather_rows(storage, lo, hi, world)
+        np.save(os.path.join(out_dir, f"g{rank}.npy"), storage.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_all_gather_rows_gloo_world2(tmp_path):
+    """The sharded baby-basis build: each rank fills its contiguous rows, the in-place all-gather fills the rest
+    bit for bit (uint64 through int64 views)."""
+    world = 2
+    mp.spawn(_gather_worker, args=(world, _port(), str(tmp_path)), nprocs=world, join=True)
+    want = np.array([[(1000 * r + k) | ((k % 2) << 63) for k in range(5)] for r in range(8)], dtype=np.uint64)
+    for r in range(world):
+        np.testing.assert_array_equal(np.load(tmp_path / f"g{r}.npy"), want)
