@@ -60,9 +60,10 @@ def exchange_partials(partials: torch.Tensor, world: int, group=None) -> torch.T
     return recv
 
 
-def all_gather_rows(storage: torch.Tensor, lo: int, hi: int, world: int, group=None) -> None:
+def all_gather_rows(storage: torch.Tensor, lo: int, hi: int, world: int, group=None, async_op: bool = False):
     """In-place all-gather along dim 0: this rank filled rows [lo, hi) of ``storage`` (equal contiguous ranges
-    per rank, in rank order); afterwards every rank holds every row.  Residues travel as their bit pattern."""
+    per rank, in rank order); afterwards every rank holds every row.  Residues travel as their bit pattern.
+    With ``async_op`` the work handle is returned: ``storage`` may not be read before ``handle.wait()``."""
     rows = int(storage.shape[0])
     if rows % world or hi - lo != rows // world:
         raise ValueError(f"rows [{lo}, {hi}) are not this rank's equal share of {rows} over {world}")
@@ -70,7 +71,8 @@ def all_gather_rows(storage: torch.Tensor, lo: int, hi: int, world: int, group=N
     per = flat.numel() // world
     r = lo // (hi - lo)
     if world > 1:
-        dist.all_gather_into_tensor(flat, flat[r * per:(r + 1) * per], group=group)
+        return dist.all_gather_into_tensor(flat, flat[r * per:(r + 1) * per], group=group, async_op=async_op)
+    return None
 
 
 def modsum(ctx, buffers: torch.Tensor, limbs: int) -> torch.Tensor:

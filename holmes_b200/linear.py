@@ -429,6 +429,13 @@ class _Babies:
         self.storage = storage
         self.state = state
         self.slots = slots
+        self.pending = None  # all-gather still filling other ranks' babies (sharded build)
+
+    def ready(self) -> None:
+        """Make the current stream wait for the sharded build's all-gather."""
+        if self.pending is not None:
+            self.pending.wait()
+            self.pending = None
 
     def blocks(self, ctx: F.Context) -> list[F.Cipher]:
         B, inputs = int(self.storage.shape[0]), int(self.storage.shape[2])
@@ -504,10 +511,11 @@ class LinearOperator:
                 g = ctx.galois(plan.baby_offsets[b])
                 F._keyswitch(ctx, digits, dig_item, cur, g, ctx.switch_key(g, cur), c0, None, F._item_stride(c0),
                              storage[b, 0], storage[b, 1], n_in)
+        entry = _Babies(inputs, level, storage, inputs[0].state, int(inputs[0].slots))
         if (lo, hi) != (0, B):
             from .collectives import all_gather_rows
-            all_gather_rows(storage, lo, hi, shard[1], shard[2])
-        entry = _Babies(inputs, level, storage, inputs[0].state, int(inputs[0].slots))
+            # asynchronous: the first chunk's encode (which needs no babies) overlaps the transfer
+            entry.pending = all_gather_rows(storage, lo, hi, shard[1], shard[2], async_op=True)
         if bool(self.config.reuse_baby_rotations):
             self._baby_cache[self._baby_key(inputs, plan)] = entry
         return entry
@@ -597,6 +605,7 @@ class LinearOperator:
             pts = weight.plaintext(plan, chunk, level=level, operator_config=self.config)
             e1.record()
             pt_state = pts.state
+            babies.ready()
             res = F.bsgs_partial_sums(ctx, blocks, pts, int(chunk.giant_count))
             del pts
             g0, g1 = F.giant_horner(ctx, res, int(plan.giant_offset))
