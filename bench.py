@@ -96,6 +96,14 @@ class ClockSampler:
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
+    def ready(self, timeout: float = 5.0) -> None:
+        """Wait for nvidia-smi's first sample, then keep only samples from here on (the timed region starts
+        right after this call)."""
+        t0 = time.time()
+        while self.proc is not None and not self.lines and time.time() - t0 < timeout:
+            time.sleep(0.02)
+        self.first = len(self.lines)
+
     def stop(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
@@ -108,7 +116,10 @@ class ClockSampler:
             self.thread.join(timeout=2)
         sm, mx, reasons = [], None, set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for line in self.lines:
+        # samples from the timed region; when it is shorter than one sampling period, the sample at its start
+        first = getattr(self, "first", 0)
+        window = self.lines[first:] or self.lines[max(0, first - 1):first]
+        for line in window:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
@@ -218,10 +229,11 @@ def run_engine(args) -> None:
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
     sampler = ClockSampler(local)
     sampler.start()
+    sampler.ready()
+    if world > 1:
+        dist.barrier()
     count0 = _lib.ctypes.c_ulonglong()
     _lib.call("holmes_launch_count", _lib.ctypes.byref(count0))
     F.OPTIMER.reset()
