@@ -584,13 +584,14 @@ def run_bootstrap(args) -> None:
     rng = np.random.default_rng(0)
     zs = [(rng.normal(size=ctx.max_slots) + 1j * rng.normal(size=ctx.max_slots)) * 0.5 for _ in range(args.boot_batch)]
     cts = [client.encrypt(z, cur_limbs=3, counter=i) for i, z in enumerate(zs)]
+    it = int(args.boot_iterations)
     for _ in range(max(1, args.warmup)):
-        op.refresh_many(cts)
+        op.refresh_many(cts, iterations=it)
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
     for _ in range(args.steps):
-        outs = op.refresh_many(cts)
+        outs = op.refresh_many(cts, iterations=it)
     b.record()
     torch.cuda.synchronize()
     ms = a.elapsed_time(b) / args.steps
@@ -600,7 +601,7 @@ def run_bootstrap(args) -> None:
                       "ms_per_batch": round(ms, 2), "steps": args.steps, "higher_is_better": False,
                       "max_abs_err": err, "setup_s": round(setup, 1), "rotation_keys": len(op.program.rotations),
                       "key_gb": round(ctx.key_bytes / 1e9, 1), "depth": op.program.spec.depth,
-                      "output_limbs": op.program.output_limbs}), flush=True)
+                      "iterations": it, "output_limbs": int(outs[0].state.cur_limbs)}), flush=True)
     ctx.close()
 
 
@@ -608,6 +609,7 @@ def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--workload", choices=("linear", "bootstrap", "primitives"), default="linear")
     ap.add_argument("--boot-batch", type=int, default=8)
+    ap.add_argument("--boot-iterations", type=int, default=1, help="2 = Meta-BTS correction")
     ap.add_argument("--kernel", default=None, help="profile one kernel family (see run_kernel)")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=3)

@@ -183,15 +183,15 @@ class BootstrapProgram:
     def output_state(self) -> F.CipherState:
         return F.CipherState(self.output_limbs, 1, self.context.scale)
 
-    def diagonal_plaintexts(self, which: str, level: int, cur: int):
-        """Encoded diagonals of one transform level at ``cur`` limbs, scale q_{cur-1} (cached)."""
-        key = (which, level, cur)
+    def diagonal_plaintexts(self, which: str, level: int, cur: int, adjust: float = 1.0):
+        """Encoded diagonals of one transform level at ``cur`` limbs, scale q_{cur-1}, times ``adjust`` (cached)."""
+        key = (which, level, cur, float(adjust))
         hit = self._plain.get(key)
         if hit is not None:
             return hit
         ctx = self.context
         mats = self.c2s if which == "c2s" else self.s2c
-        factor = self.c2s_scale if which == "c2s" else self.s2c_scale
+        factor = (self.c2s_scale if which == "c2s" else self.s2c_scale) * float(adjust)
         mat = mats[level]
         offsets = sorted(mat)
         rows = np.stack([mat[r] * factor for r in offsets])
@@ -436,17 +436,52 @@ def bootstrap(ct: F.Cipher, ctx, program: BootstrapProgram) -> F.Cipher:
     re = eval_mod(re, program)
     im = eval_mod(im, program)
     z = F.homo_add(re, F.homo_mul_i(im, ctx), ctx)
+    # S2C's constant assumes the message at the nominal scale: z carries the input's message at scale
+    # S_z Delta / m_scale.  The first S2C level also multiplies by rho = s_in / that, so the output lands on the
+    # input's own scale s_in (rho is within a few 2^-20 of 1; the diagonals absorb it, no level is spent).
+    m_scale = s_in * k_pre * 2.0 ** program.cf / float(ctx.q(1))
+    rho = s_in / (float(z.state.scaling_factor) * float(ctx.scale) / m_scale)
     for lvl in range(len(program.s2c)):
-        offsets, pt = program.diagonal_plaintexts("s2c", lvl, int(z.state.cur_limbs))
+        offsets, pt = program.diagonal_plaintexts("s2c", lvl, int(z.state.cur_limbs), rho if lvl == 0 else 1.0)
         z = linear_level(z, offsets, pt)
     z = drop_to(z, program.output_limbs)
-    # S2C's constant assumed the message at the nominal scale: declare the scale at which z holds the input values
-    m_scale = s_in * k_pre * 2.0 ** program.cf / float(ctx.q(1))
-    z.state = F.CipherState(int(z.state.cur_limbs), 1, float(z.state.scaling_factor) * float(ctx.scale) / m_scale)
+    z.state = F.CipherState(int(z.state.cur_limbs), 1, s_in)
     return z
 
 
 # --------------------------------------------------------------------------------------------------------- operator
+
+
+def with_correction(cipher: F.Cipher, ctx, once, iterations: int, precision_bits: int) -> F.Cipher:
+    """One bootstrap, or Meta-BTS: refresh, subtract the input from the refreshed value (both times 2^p, at the
+    input's level), refresh that difference, subtract it, multiply by 2^-p with one rescale.  The output then has one
+    limb fewer than a single refresh; as in the reference, a refresh that gained no limbs is returned unchanged.
+    Names and steps follow the reference's _bootstrap_with_optional_correction (bootstrap.py:626-711)."""
+    if int(iterations) not in (1, 2):
+        raise ValueError("bootstrap iterations must be one or two.")
+    first = once(cipher)
+    if int(iterations) == 1:
+        return first
+    if int(first.state.cur_limbs) <= int(cipher.state.cur_limbs):
+        return first
+    if int(precision_bits) <= 0:
+        first_down = F.align_to(first, cipher.state, ctx)
+        error = once(F.homo_sub(first_down, F.align_to(cipher, first_down.state, ctx), ctx))
+        return F.homo_sub(F.align_to(first, error.state, ctx), error, ctx)
+    factor = F.encode_scalar(1 << int(precision_bits), cur_limbs=int(first.state.cur_limbs), scale_degree=0,
+                             mode="integer", context=ctx)
+    first_scaled = F.homo_mul_scalar(first, factor, ctx)
+    first_down = F.align_to(first_scaled, cipher.state, ctx)
+    original_scaled = F.homo_mul_scalar(cipher, factor, ctx)
+    original_scaled = F.align_to(original_scaled, first_down.state, ctx)
+    error = once(F.homo_sub(first_down, original_scaled, ctx))
+    corrected = F.homo_sub(F.align_to(first_scaled, error.state, ctx), F.align_to(error, first_scaled.state, ctx), ctx)
+    cur = int(corrected.state.cur_limbs)
+    inv = F.encode_scalar(1.0 / float(1 << int(precision_bits)), cur_limbs=cur, scale_degree=1,
+                          scaling_factor=float(ctx.q(cur - 1)), context=ctx)
+    out = F.homo_mul_scalar_rescale(corrected, inv, ctx)
+    out.state = out.state.replace(scaling_factor=cipher.state.scaling_factor)
+    return out
 
 
 @dataclass(frozen=True)
@@ -494,25 +529,30 @@ class BootstrapOperator:
     def required_rotations(*, log_n: int, log_slots: int = 15, level_budget: tuple = (4, 4), **_) -> tuple:
         return requirements([BootstrapSpec(log_slots=log_slots, level_budget=tuple(level_budget))], log_n).rotations
 
-    def refresh(self, cipher, **_) -> F.Cipher:
-        if int(self.config.iterations) != 1:
-            raise NotImplementedError("the two-pass (Meta-BTS) correction is not implemented")
+    def refresh(self, cipher, *, iterations: int | None = None, precision_bits: int | None = None, **_) -> F.Cipher:
+        """One bootstrap, or the two-pass Meta-BTS correction (``iterations = 2``, reference bootstrap.py:626-711)."""
+        it = int(self.config.iterations if iterations is None else iterations)
+        bits = int(self.config.precision_bits if precision_bits is None else precision_bits)
         self.calls += 1
-        return bootstrap(cipher, self.crypto_context.context, self.program)
+        ctx = self.crypto_context.context
+        return with_correction(cipher, ctx, lambda c: bootstrap(c, ctx, self.program), it, bits)
 
-    def refresh_many(self, ciphers, **kw) -> list:
+    def refresh_many(self, ciphers, *, iterations: int | None = None, precision_bits: int | None = None,
+                     **kw) -> list:
         """All ciphertexts of one state in one batched pass (every step runs on the batch)."""
         ciphers = list(ciphers)
         if not ciphers:
             return []
         if len(ciphers) == 1 or any(c.state != ciphers[0].state for c in ciphers):
-            return [self.refresh(c, **kw) for c in ciphers]
+            return [self.refresh(c, iterations=iterations, precision_bits=precision_bits, **kw) for c in ciphers]
+        it = int(self.config.iterations if iterations is None else iterations)
+        bits = int(self.config.precision_bits if precision_bits is None else precision_bits)
         ctx = self.crypto_context.context
         cur = int(ciphers[0].state.cur_limbs)
         c0 = torch.stack([c.cv[0][0, :cur] for c in ciphers])
         c1 = torch.stack([c.cv[1][0, :cur] for c in ciphers])
         batch = F.Cipher([c0, c1], ciphers[0].state, ciphers[0].slots, False, len(ciphers), ctx)
-        out = bootstrap(batch, ctx, self.program)
+        out = with_correction(batch, ctx, lambda c: bootstrap(c, ctx, self.program), it, bits)
         self.calls += len(ciphers)
         self.batch_calls += 1
         return [out.cipher_like([out.cv[0][i:i + 1], out.cv[1][i:i + 1]], batch_size=1) for i in range(len(ciphers))]

@@ -735,10 +735,17 @@ class EncodedScalar:
 
 
 def encode_scalar(value, cur_limbs: int, scale_degree: int = 1, scaling_factor: float | None = None,
-                  context=None) -> EncodedScalar:
+                  context=None, mode: str = "real") -> EncodedScalar:
+    """``mode="integer"`` encodes the integer itself (scale 1, degree 0): multiplying by it keeps the scale."""
     ctx = _ctx(context)
     if isinstance(value, complex) or np.iscomplexobj(value):
         raise ValueError("encode_scalar encodes real values; multiply by i with homo_mul_i")
+    if mode == "integer":
+        if int(value) != value:
+            raise ValueError("integer-mode scalars must be integers")
+        return EncodedScalar(float(value), int(value), CipherState(int(cur_limbs), 0, 1.0))
+    if mode != "real":
+        raise ValueError(f"unknown scalar mode {mode!r}")
     sf = float(scaling_factor) if scaling_factor is not None else ctx.scale_at(int(cur_limbs))
     return EncodedScalar(float(value), int(round(float(value) * sf)), CipherState(int(cur_limbs), int(scale_degree), sf))
 

@@ -162,11 +162,46 @@ class OracleBootstrap:
         re, im = self.eval_mod(re), self.eval_mod((i0, i1, d[2]))
         j0, j1 = o.mul_i(im[:2])
         z = self._add(re, (j0, j1, im[2]))
-        for lvl in prog.s2c:
-            z = self.linear(z, lvl, prog.s2c_scale)
-        z = self.drop(z, prog.output_limbs)
         m_scale = s_in * k_pre * 2.0 ** prog.cf / float(self.pr.q[1])
-        return z[0], z[1], float(z[2]) * self.delta / m_scale
+        rho = s_in / (float(z[2]) * self.delta / m_scale)
+        for k, lvl in enumerate(prog.s2c):
+            z = self.linear(z, lvl, prog.s2c_scale * (rho if k == 0 else 1.0))
+        z = self.drop(z, prog.output_limbs)
+        return z[0], z[1], s_in
+
+    def refresh(self, ct, s_in, iterations=1, precision_bits=8):
+        """One bootstrap or the Meta-BTS correction (same steps as holmes_b200.bootstrap.with_correction)."""
+        o = self.o
+        first = self.bootstrap(ct, s_in)
+        cur_in = ct[0].shape[0]
+        if iterations == 1 or first[0].shape[0] <= cur_in:
+            return first
+
+        def sub(a, b):
+            ids = self._ids(a[0].shape[0])
+            return o.sub(a[0], b[0], ids), o.sub(a[1], b[1], ids)
+
+        def mul_int(c, k):
+            ids = self._ids(c[0].shape[0])
+            r = [int(k) % self.pr.q[i] for i in ids]
+            return o.mul_scalar(c[0], r, ids), o.mul_scalar(c[1], r, ids)
+
+        if precision_bits <= 0:
+            first_down = (first[0][:cur_in], first[1][:cur_in])
+            err = self.bootstrap(sub(first_down, (ct[0][:cur_in], ct[1][:cur_in])), s_in)
+            lim = err[0].shape[0]
+            d0, d1 = sub((first[0][:lim], first[1][:lim]), err)
+            return d0, d1, s_in
+        f = 1 << int(precision_bits)
+        fs = mul_int(first, f)
+        first_down = (fs[0][:cur_in], fs[1][:cur_in])
+        orig = mul_int((ct[0][:cur_in], ct[1][:cur_in]), f)
+        err = self.bootstrap(sub(first_down, orig), s_in)
+        lim = min(err[0].shape[0], fs[0].shape[0])
+        c0, c1 = sub((fs[0][:lim], fs[1][:lim]), (err[0][:lim], err[1][:lim]))
+        k = int(round(1.0 / float(f) * float(self.pr.q[lim - 1])))
+        d0, d1 = o.rescale(mul_int((c0, c1), k))
+        return d0, d1, s_in
 
 
 __all__ = ["OracleBootstrap"]

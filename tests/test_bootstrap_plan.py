@@ -61,3 +61,13 @@ def test_requirements_and_depth():
     assert all(0 < r < (1 << 11) or r == (2 << 12) - 1 for r in req.rotations)
     with pytest.raises(ValueError):
         BS.BootstrapSpec(mode="slots_first")
+
+
+def test_refresh_iterations_validated_on_host():
+    """Meta-BTS accepts one or two iterations; the check runs before any device work."""
+    from holmes_b200 import bootstrap as BS
+
+    calls = []
+    with pytest.raises(ValueError):
+        BS.with_correction(object(), None, lambda c: calls.append(c), 3, 8)
+    assert not calls

@@ -62,6 +62,32 @@ def test_refresh_many_matches_single(boot):
     assert op.batch_calls >= 1
 
 
+def test_meta_bts_correction(boot):
+    """The two-pass Meta-BTS correction (iterations = 2): residue for residue against the oracle, output at the
+    input's scale with one limb fewer than a single refresh, and a smaller error than one refresh."""
+    from oracle.bootstrap_oracle import OracleBootstrap
+
+    o, client, ctx, op = boot
+    rng = np.random.default_rng(5)
+    z = rng.normal(size=ctx.max_slots) * 0.4
+    ct = client.encrypt(z, cur_limbs=3, counter=60)
+    ref = o.encrypt(z, 3, counter=60)
+    one = op.refresh(ct)
+    two = op.refresh(ct, iterations=2, precision_bits=8)
+    assert int(two.state.cur_limbs) == int(one.state.cur_limbs) - 1
+    assert float(two.state.scaling_factor) == float(ct.state.scaling_factor)
+    e0, e1, esf = OracleBootstrap(o, op.program).refresh(ref, float(ct.state.scaling_factor), 2, 8)
+    np.testing.assert_array_equal(host(two.cv[0][0]), e0)
+    np.testing.assert_array_equal(host(two.cv[1][0]), e1)
+    err1 = np.abs(client.decrypt(one) - z).max()
+    err2 = np.abs(client.decrypt(two) - z).max()
+    assert err2 < err1 / 8, (err1, err2)
+    many = op.refresh_many([ct, ct], iterations=2, precision_bits=8)
+    np.testing.assert_array_equal(host(many[1].cv[0][0]), host(two.cv[0][0]))
+    with pytest.raises(ValueError):
+        op.refresh(ct, iterations=3)
+
+
 def test_pair_bootstrap_and_halve(boot):
     """Two real ciphertexts through one refresh as a + i b (stations.pair_bootstrap), unpacked with the
     conjugation to (2a, 2b), then halved."""
