@@ -16,12 +16,19 @@
 // [8 rows][16 bytes], offsets 512 / 128.  The accumulator of one (coefficient, M-tile) is 128 TMEM lanes x 64
 // columns (row m = lane m).
 //
-// Work: a persistent CTA (two per SM) takes items of 4 coefficients x 8 inputs x 8 giants of one limb and runs
-// them as one stream of 32-baby stages through a 4-deep cp.async ring; one thread issues the MMAs of a stage and
-// commits them to that ring slot's mbarrier.  The epilogue of an item (256 threads) reads its TMEM rows,
-// folds the 8 column bytes of each giant (W_g = sum_a D 256^a), combines the 8 lanes of each (input, component)
-// in three butterfly rounds (shifts 2^32, 2^16, 2^8; lane bb ends with giant bb), reduces mod q_l and stores.
-// Every wait is bounded; a wait that runs out sets g_tc_error, stops the CTA's work and still frees its TMEM.
+// Work: one persistent CTA per SM takes items of 4 coefficients x 8 inputs x 8 giants of one limb and runs them as
+// one stream of 32-baby stages, with warps specialised by role:
+//   * producers (4 warps) copy the stage's words into a 6-slot ring with 8-byte cp.async (thread p takes coefficient
+//     p % 4 of baby p / 4 for every row group and giant, so 4 lanes read each 32-byte sector together) and arrive on
+//     the slot's "full" mbarrier once their copies have landed (two stages in flight per thread);
+//   * one thread issues the stage's MMAs into one of two TMEM accumulator buffers and commits them to the slot's
+//     "empty" mbarrier (the producers may refill it) and, after an item's last stage, to the buffer's "full";
+//   * the epilogue (8 warps, two per TMEM lane quadrant) reads the finished buffer, folds the 8 column bytes of each
+//     giant, shifts by its own row byte, combines the 8 byte rows of each (input, component) in three butterfly
+//     rounds over lanes ^4, ^2, ^1 (lane bb ends with giant bb), reduces mod q_l, stores, and arrives on the
+//     buffer's "empty" so the MMAs of the item after next may overwrite it.
+// Every wait is bounded and polls a shared abort flag; a wait that runs out sets g_tc_error and the flag, every
+// role leaves its loop, and the CTA still waits (bounded) for its MMAs and copies and frees its TMEM.
 #include "ops.h"
 
 namespace holmes {
@@ -32,8 +39,6 @@ namespace {
 
 constexpr int kT = 4;    // coefficient positions per item (one 32-byte sector of every row)
 constexpr int kKS = 32;  // babies per stage (the K of one MMA)
-constexpr int kNB = 4;   // ring slots
-constexpr int kPF = kNB - 1;
 constexpr u32 kIdesc = (2u << 4)               // D: s32
                        | (0u << 7) | (0u << 10)  // A, B: u8
                        | (1u << 15) | (1u << 16) // A, B: MN-major
@@ -43,14 +48,20 @@ constexpr long long kWaitLimit = 1ll << 20;  // try_wait polls; a healthy wait e
 
 // One item: kT coefficients x 8 inputs (one M-tile: 8 inputs x 2 components x 8 bytes) x 8 giants of one limb.
 struct TcGeom {
-  static constexpr int THREADS = 256;        // warp w: TMEM lane quadrant w % 4, coefficients 2 (w / 4) .. +1
+  static constexpr int PRODUCERS = 128;  // warps 0-3
+  static constexpr int MMA_WARP = 4;
+  static constexpr int EPI_WARP0 = 5;    // warps 5-12: TMEM lane quadrant w % 4, coefficients 2 ((w - 5) / 4) .. +1
+  static constexpr int EPILOGUE = 256;
+  static constexpr int THREADS = PRODUCERS + 32 + EPILOGUE;
   static constexpr int A_BYTES = 128 * kKS;  // A tile of one coefficient per stage: 4 KB
   static constexpr int B_BYTES = 64 * kKS;   // B tile: 2 KB
   static constexpr int STAGE = kT * (A_BYTES + B_BYTES);
-  static constexpr int SMEM = kNB * STAGE + 1024;
-  static constexpr int TCOLS = kT * 64;      // 256: two CTAs per SM share the 512 columns
-  static constexpr int A_PER = kT * 16 * kKS / THREADS;  // A words a thread copies per stage (8)
-  static constexpr int B_PER = kT * 8 * kKS / THREADS;   // B words (4)
+  static constexpr int NS = 6;               // ring slots
+  static constexpr int LAG = 2;              // stages a producer keeps in flight before signalling one
+  static constexpr int BAR = NS * STAGE;     // barrier area
+  static constexpr int SMEM = NS * STAGE + 256;
+  static constexpr int ACC = kT * 64;        // TMEM columns of one accumulator buffer
+  static constexpr int TCOLS = 2 * ACC;      // 512: the whole TMEM, one CTA per SM
 };
 
 __device__ __forceinline__ u32 smem_u32(const void* p) { return (u32)__cvta_generic_to_shared(p); }
@@ -61,8 +72,13 @@ __device__ __forceinline__ u64 umma_desc(u32 addr, u32 lbo, u32 sbo) {
 __device__ __forceinline__ void cp_async8(u32 dst, const void* src, bool valid) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(dst), "l"(src), "r"(valid ? 8 : 0));
 }
-__device__ __forceinline__ bool mbar_wait(u32 bar, u32 parity) {
+__device__ __forceinline__ void mbar_arrive(u32 bar) {
+  asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(bar) : "memory");
+}
+// bounded wait for the phase of parity `parity`; gives up early when another role raised the abort flag
+__device__ __forceinline__ bool mbar_wait(u32 bar, u32 parity, const volatile int* abort_flag) {
   for (long long it = 0; it < kWaitLimit; ++it) {
+    if ((it & 255) == 255 && *abort_flag) return false;
     u32 ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
@@ -130,14 +146,19 @@ __device__ __forceinline__ W4 exchange(const W4& lowv, const W4& highv, bool hi,
 }  // namespace
 
 template <int SPI>
-__global__ void __launch_bounds__(TcGeom::THREADS, 2)
+__global__ void __launch_bounds__(TcGeom::THREADS, 1)
     k_bsgs_mac_tc(u64* __restrict__ res, InPtrs in, long long bstride, int nb, int inputs, int G,
                   const u64* __restrict__ pts, long long pstride, int limbs, ModSrc ms, int log_n) {
   using Geo = TcGeom;
   extern __shared__ __align__(1024) unsigned char tc_smem[];
   unsigned char* ring = tc_smem;
-  u64* mbar = reinterpret_cast<u64*>(tc_smem + kNB * Geo::STAGE);  // kNB barriers
-  u32* tmem_slot = reinterpret_cast<u32*>(mbar + kNB);
+  u64* full = reinterpret_cast<u64*>(tc_smem + Geo::BAR);  // [NS]: producers -> MMA
+  u64* empty = full + Geo::NS;                               // [NS]: MMA -> producers
+  u64* afull = empty + Geo::NS;                              // [2]: MMA -> epilogue
+  u64* aempty = afull + 2;                                   // [2]: epilogue -> MMA
+  u32* tmem_slot = reinterpret_cast<u32*>(aempty + 2);
+  int* abort_flag = reinterpret_cast<int*>(tmem_slot + 1);
+  const volatile int* abort_v = abort_flag;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int N = 1 << log_n;
   const int nblocks = N / kT;
@@ -154,7 +175,15 @@ __global__ void __launch_bounds__(TcGeom::THREADS, 2)
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::);
   }
   if (tid == 0) {
-    for (int b = 0; b < kNB; ++b) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(mbar + b)));
+    for (int b = 0; b < Geo::NS; ++b) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(full + b)), "r"((u32)Geo::PRODUCERS));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(empty + b)));
+    }
+    for (int b = 0; b < 2; ++b) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(afull + b)));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(aempty + b)), "r"((u32)Geo::EPILOGUE));
+    }
+    *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
@@ -178,155 +207,167 @@ __global__ void __launch_bounds__(TcGeom::THREADS, 2)
     x.g0 = (r / limbs) * 8;
     return x;
   };
-  // This thread's words of every stage: A word e = tid + 256 j is coefficient t = e % 4, baby bl = (e / 4) % 32,
-  // group gm = e / 128 (input gm / 2, component gm % 2); B word e = tid + 256 j is t = e % 4, bl = (e / 4) % 32,
-  // giant g = e / 128.  Shared-memory offsets are fixed; sources move with the item and the stage.
-  u32 a_dst[Geo::A_PER], b_dst[Geo::B_PER];
-  int a_row[Geo::A_PER], b_row[Geo::B_PER];  // gm or g
-  int a_off[Geo::A_PER], b_off[Geo::B_PER];  // bl * (1 << 16) + t
-#pragma unroll
-  for (int j = 0; j < Geo::A_PER; ++j) {
-    const int e = tid + Geo::THREADS * j, t = e % kT, bl = (e / kT) % kKS, gm = e / (kT * kKS);
-    a_dst[j] = (u32)(t * Geo::A_BYTES + (bl / 8) * 1024 + (gm / 2) * 128 + (bl % 8) * 16 + 8 * (gm % 2));
-    a_row[j] = gm;
-    a_off[j] = (bl << 16) | t;
-  }
-#pragma unroll
-  for (int j = 0; j < Geo::B_PER; ++j) {
-    const int e = tid + Geo::THREADS * j, t = e % kT, bl = (e / kT) % kKS, g = e / (kT * kKS);
-    b_dst[j] = (u32)(kT * Geo::A_BYTES + t * Geo::B_BYTES + (bl / 8) * 512 + (g / 2) * 128 + (bl % 8) * 16 + 8 * (g % 2));
-    b_row[j] = g;
-    b_off[j] = (bl << 16) | t;
-  }
-  // source of word j of the item being loaded, at its first stage; stage k adds k * 32 rows
-  const u64* a_src[Geo::A_PER];
-  const u64* b_src[Geo::B_PER];
-  int ld_item = -1;
-  Item ld{0, 0, 0, 0};
-  auto issue_stage = [&](int k) {
-    if (k < stages) {
-      const int it = k / spi, st = k - it * spi, b0 = st * kKS;
-      if (it != ld_item) {
-        ld_item = it;
-        ld = decode(it);
-        const size_t lpos = ((size_t)ld.limb << log_n) + ld.n0;
-#pragma unroll
-        for (int j = 0; j < Geo::A_PER; ++j) {
-          const int i = ld.i0 + a_row[j] / 2;
-          a_src[j] = i < inputs ? (a_row[j] & 1 ? in.c1[i] : in.c0[i]) + (size_t)(a_off[j] >> 16) * bstride + lpos +
-                                      (a_off[j] & 0xffff)
-                                : nullptr;
-        }
-#pragma unroll
-        for (int j = 0; j < Geo::B_PER; ++j) {
-          const int g = ld.g0 + b_row[j];
-          b_src[j] = g < G ? pts + ((size_t)g * nb + (b_off[j] >> 16)) * pstride + lpos + (b_off[j] & 0xffff)
-                           : nullptr;
-        }
-      }
-      const u32 base = smem_u32(ring + (k % kNB) * Geo::STAGE);
-      const size_t ao = (size_t)b0 * bstride, bo = (size_t)b0 * pstride;
-#pragma unroll
-      for (int j = 0; j < Geo::A_PER; ++j) {
-        const bool ok = a_src[j] != nullptr && b0 + (a_off[j] >> 16) < nb;
-        cp_async8(base + a_dst[j], ok ? a_src[j] + ao : pts, ok);
-      }
-#pragma unroll
-      for (int j = 0; j < Geo::B_PER; ++j) {
-        const bool ok = b_src[j] != nullptr && b0 + (b_off[j] >> 16) < nb;
-        cp_async8(base + b_dst[j], ok ? b_src[j] + bo : pts, ok);
-      }
-    }
-    asm volatile("cp.async.commit_group;\n" ::);
+  auto fail = [&]() {
+    *abort_flag = 1;
+    atomicExch(&g_tc_error, 1);
   };
 
-  bool failed = false;
-  int committed = -1;  // last stage whose MMAs were committed
-  for (int k = 0; k < kPF; ++k) issue_stage(k);
-  for (int k = 0; k < stages && !failed; ++k) {
-    const int slot = (int)(k % kNB);
-    asm volatile("cp.async.wait_group %0;\n" ::"n"(kPF - 1));
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-    __syncthreads();  // stage k is in shared memory for the tensor core
-    // slot (k + kPF) % kNB was read by the MMAs of stage k - 1: wait for them before refilling it
-    if (k >= 1) {
-      const int kp = k - 1;
-      if (!mbar_wait(smem_u32(mbar + kp % kNB), (u32)((kp / kNB) & 1))) failed = true;
-    }
-    failed = __syncthreads_or(failed);
-    if (failed) break;
-    issue_stage(k + kPF);
-    if (tid == 0) {
-      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-      const u32 base = smem_u32(ring + slot * Geo::STAGE);
-      const u32 accum = (k % spi) ? 1u : 0u;
-#pragma unroll
-      for (int t = 0; t < kT; ++t) {
-        const u64 da = umma_desc(base + t * Geo::A_BYTES, 1024, 128);
-        const u64 db = umma_desc(base + kT * Geo::A_BYTES + t * Geo::B_BYTES, 512, 128);
-        asm volatile(
-            "{\n\t.reg .pred p;\n\t"
-            "setp.ne.b32 p, %4, 0;\n\t"
-            "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t"
-            "}" ::"r"(tmem + (u32)(t * 64)),
-            "l"(da), "l"(db), "r"(kIdesc), "r"(accum), "r"(0u)
-            : "memory");
+  int committed = -1;  // MMA thread: last stage whose MMAs were committed
+  if (warp < Geo::PRODUCERS / 32) {
+    // ------------------------------------------------------------------ producers
+    // Thread p copies coefficient t = p % 4 of baby bl = p / 4 of the stage for all 16 row groups (A) and all 8
+    // giants (B): the 4 lanes of a (row, baby) read one 32-byte sector together, 8 sectors per warp instruction.
+    const int t = tid % kT, bl = tid / kT;
+    const u32 a_off = (u32)(t * Geo::A_BYTES + (bl / 8) * 1024 + (bl % 8) * 16);
+    const u32 b_off = (u32)(kT * Geo::A_BYTES + t * Geo::B_BYTES + (bl / 8) * 512 + (bl % 8) * 16);
+    int ld_item = -1;
+    Item x{0, 0, 0, 0};
+    int k = 0;
+    for (; k < stages; ++k) {
+      const int slot = k % Geo::NS, use = k / Geo::NS;
+      const bool ok = __all_sync(0xffffffffu, use == 0 || mbar_wait(smem_u32(empty + slot), (u32)((use - 1) & 1),
+                                                                  abort_v));
+      if (!ok) {
+        if (lane == 0) fail();
+        break;
       }
-      asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                       smem_u32(mbar + slot))
-                   : "memory");
+      const int it = k / spi, b = (k % spi) * kKS + bl;
+      if (it != ld_item) {
+        ld_item = it;
+        x = decode(it);
+      }
+      const size_t lpos = ((size_t)x.limb << log_n) + x.n0 + t;
+      const u32 base = smem_u32(ring + slot * Geo::STAGE);
+      const bool bok = b < nb;
+      const size_t boff = (size_t)b * bstride + lpos;
+#pragma unroll
+      for (int gm = 0; gm < 16; ++gm) {
+        const int i = x.i0 + gm / 2;
+        const bool ok2 = bok && i < inputs;
+        const u64* src = ok2 ? (gm & 1 ? in.c1[i] : in.c0[i]) + boff : pts;
+        cp_async8(base + a_off + (u32)((gm / 2) * 128 + 8 * (gm % 2)), src, ok2);
+      }
+#pragma unroll
+      for (int g = 0; g < 8; ++g) {
+        const bool ok2 = bok && x.g0 + g < G;
+        const u64* src = ok2 ? pts + ((size_t)(x.g0 + g) * nb + b) * pstride + lpos : pts;
+        cp_async8(base + b_off + (u32)((g / 2) * 128 + 8 * (g % 2)), src, ok2);
+      }
+      asm volatile("cp.async.commit_group;\n" ::);
+      if (k >= Geo::LAG) {
+        asm volatile("cp.async.wait_group %0;\n" ::"n"(Geo::LAG));
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        mbar_arrive(smem_u32(full + (k - Geo::LAG) % Geo::NS));
+      }
     }
-    committed = k;
-    if (k % spi != spi - 1) continue;
-    // ---- epilogue of item k / spi
-    if (!mbar_wait(smem_u32(mbar + slot), (u32)((k / kNB) & 1))) failed = true;
-    failed = __syncthreads_or(failed);
-    if (failed) break;
-    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-    const Item x = decode(k / spi);
-    const Mod m = ms.get(x.limb);
-    const int quad = warp % 4, th = warp / 4;
+    asm volatile("cp.async.wait_all;\n" ::);
+    if (k == stages) {  // the last LAG stages
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      for (int r = stages - Geo::LAG < 0 ? 0 : stages - Geo::LAG; r < stages; ++r) mbar_arrive(smem_u32(full + r % Geo::NS));
+    }
+  } else if (warp == Geo::MMA_WARP) {
+    // ------------------------------------------------------------------ MMA issue (lane 0 issues; the warp waits
+    // together so that every exit is warp-uniform)
+    for (int it = 0; it < my_items; ++it) {
+      const int buf = it & 1;
+      bool ok = it < 2 || mbar_wait(smem_u32(aempty + buf), (u32)(((it >> 1) - 1) & 1), abort_v);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) {
+        if (lane == 0) fail();
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      for (int s2 = 0; s2 < spi && ok; ++s2) {
+        const int k = it * spi + s2, slot = k % Geo::NS;
+        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(full + slot), (u32)((k / Geo::NS) & 1), abort_v));
+        if (!ok) break;
+        asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+        if (lane == 0) {
+          const u32 base = smem_u32(ring + slot * Geo::STAGE);
+#pragma unroll
+          for (int t = 0; t < kT; ++t) {
+            const u64 da = umma_desc(base + t * Geo::A_BYTES, 1024, 128);
+            const u64 db = umma_desc(base + kT * Geo::A_BYTES + t * Geo::B_BYTES, 512, 128);
+            asm volatile(
+                "{\n\t.reg .pred p;\n\t"
+                "setp.ne.b32 p, %4, 0;\n\t"
+                "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n\t"
+                "}" ::"r"(tmem + (u32)(buf * Geo::ACC + t * 64)),
+                "l"(da), "l"(db), "r"(kIdesc), "r"((u32)(s2 > 0)), "r"(0u)
+                : "memory");
+          }
+          asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                           smem_u32(empty + slot))
+                       : "memory");
+        }
+        __syncwarp();
+        committed = k;
+      }
+      if (!ok) {
+        if (lane == 0) fail();
+        break;
+      }
+      if (lane == 0)
+        asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                         smem_u32(afull + buf))
+                     : "memory");
+      __syncwarp();
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue
+    const int quad = warp % 4, th = (warp - Geo::EPI_WARP0) / 4;
     const int row = quad * 32 + lane;  // TMEM lane = accumulator row (group, byte)
     const int gm = row / 8, bb = row % 8;
     const bool hi2 = bb & 4, hi1 = bb & 2, hi0 = bb & 1;
     const u32 sh = 8u * (u32)(bb & 3);
-    u64 outv[2];
+    for (int it = 0; it < my_items; ++it) {
+      const int buf = it & 1;
+      bool ok = mbar_wait(smem_u32(afull + buf), (u32)((it >> 1) & 1), abort_v);
+      ok = __all_sync(0xffffffffu, ok);  // the TMEM loads below are warp-collective
+      if (!ok) {
+        if (lane == 0) fail();
+        break;
+      }
+      asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+      const Item x = decode(it);
+      const Mod m = ms.get(x.limb);
+      u64 outv[2];
 #pragma unroll
-    for (int tt = 0; tt < 2; ++tt) {
-      const int t = 2 * th + tt;
-      const u32 col0 = tmem + ((u32)(quad * 32) << 16) + (u32)(t * 64);
-      u32 c[64];
-      tmem_ld16(col0, *reinterpret_cast<u32(*)[16]>(c));
-      tmem_ld16(col0 + 16u, *reinterpret_cast<u32(*)[16]>(c + 16));
-      tmem_ld16(col0 + 32u, *reinterpret_cast<u32(*)[16]>(c + 32));
-      tmem_ld16(col0 + 48u, *reinterpret_cast<u32(*)[16]>(c + 48));
-      asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-      W4 v[8];
+      for (int tt = 0; tt < 2; ++tt) {
+        const int t = 2 * th + tt;
+        const u32 col0 = tmem + ((u32)(quad * 32) << 16) + (u32)(buf * Geo::ACC + t * 64);
+        u32 c[64];
+        tmem_ld16(col0, *reinterpret_cast<u32(*)[16]>(c));
+        tmem_ld16(col0 + 16u, *reinterpret_cast<u32(*)[16]>(c + 16));
+        tmem_ld16(col0 + 32u, *reinterpret_cast<u32(*)[16]>(c + 32));
+        tmem_ld16(col0 + 48u, *reinterpret_cast<u32(*)[16]>(c + 48));
+        asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+        W4 v[8];
 #pragma unroll
-      for (int g = 0; g < 8; ++g) v[g] = fold_shift(c + 8 * g, sh, hi2);
-      // reduce-scatter over bb: after the rounds across lanes ^4, ^2, ^1 lane bb holds giant bb
-      W4 x[4], y[2];
+        for (int g = 0; g < 8; ++g) v[g] = fold_shift(c + 8 * g, sh, hi2);
+        W4 xr[4], y[2];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) x[j] = exchange(v[j], v[j + 4], hi2, 4);
+        for (int j = 0; j < 4; ++j) xr[j] = exchange(v[j], v[j + 4], hi2, 4);
 #pragma unroll
-      for (int j = 0; j < 2; ++j) y[j] = exchange(x[j], x[j + 2], hi1, 2);
-      const W4 z = exchange(y[0], y[1], hi0, 1);
-      outv[tt] = reduce128(((u64)z.w[3] << 32) | z.w[2], ((u64)z.w[1] << 32) | z.w[0], m);
+        for (int j = 0; j < 2; ++j) y[j] = exchange(xr[j], xr[j + 2], hi1, 2);
+        const W4 z = exchange(y[0], y[1], hi0, 1);
+        outv[tt] = reduce128(((u64)z.w[3] << 32) | z.w[2], ((u64)z.w[1] << 32) | z.w[0], m);
+      }
+      // the accumulator buffer may be overwritten once every epilogue thread has read it
+      asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+      mbar_arrive(smem_u32(aempty + buf));
+      // lane bb holds giant g0 + bb of (input i0 + gm / 2, component gm % 2) at coefficients n0 + 2 th, +1
+      const int i = x.i0 + gm / 2, cc = gm % 2, g = x.g0 + bb;
+      if (i < inputs && g < G) {
+        const size_t is = (size_t)limbs << log_n, gs = (size_t)inputs * is;
+        u64* dst = res + ((size_t)cc * G + g) * gs + (size_t)i * is + ((size_t)x.limb << log_n) + x.n0 + 2 * th;
+        *reinterpret_cast<ulonglong2*>(dst) = make_ulonglong2(outv[0], outv[1]);
+      }
     }
-    // lane bb holds giant g0 + bb of (input i0 + gm / 2, component gm % 2) at coefficients n0 + 2 th, +1
-    const int i = x.i0 + gm / 2, c = gm % 2, g = x.g0 + bb;
-    if (i < inputs && g < G) {
-      const size_t is = (size_t)limbs << log_n, gs = (size_t)inputs * is;
-      u64* dst = res + ((size_t)c * G + g) * gs + (size_t)i * is + ((size_t)x.limb << log_n) + x.n0 + 2 * th;
-      *reinterpret_cast<ulonglong2*>(dst) = make_ulonglong2(outv[0], outv[1]);
-    }
-    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-    __syncthreads();  // the next item's first MMA overwrites these accumulators
   }
-  if (failed && tid == 0) atomicExch(&g_tc_error, 1);
-  asm volatile("cp.async.wait_all;\n" ::);
-  // let the last committed MMAs finish before the accumulators are released (bounded as well)
-  if (committed >= 0) mbar_wait(smem_u32(mbar + committed % kNB), (u32)((committed / kNB) & 1));
+  // let in-flight MMAs finish before the accumulators are released (bounded; immediate when all went well)
+  if (warp == Geo::MMA_WARP && committed >= 0)
+    mbar_wait(smem_u32(empty + committed % Geo::NS), (u32)((committed / Geo::NS) & 1), abort_v);
   asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
   __syncthreads();
   if (warp == 0)
@@ -347,8 +388,8 @@ int bsgs_mac_tc(ModSrc ms, u64* res, const InPtrs& in, long long bstride, int nb
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TcGeom::SMEM);
     if (e != cudaSuccess) return (int)e;
     count_launch();
-    kernel<<<2 * sms, TcGeom::THREADS, TcGeom::SMEM, st>>>(res, in, bstride, nb, inputs, groups, pts, pstride, limbs,
-                                                            ms, log_n);
+    kernel<<<sms, TcGeom::THREADS, TcGeom::SMEM, st>>>(res, in, bstride, nb, inputs, groups, pts, pstride, limbs,
+                                                        ms, log_n);
     return (int)cudaGetLastError();
   };
   switch (spi) {
