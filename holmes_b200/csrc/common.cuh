@@ -11,6 +11,7 @@
 //     residues with q < 2^60, or 12 products of a 60-bit source residue with a 50-bit target
 //     constant -- the remainder x - est q stays below 16 q < 2^64 and four conditional
 //     subtractions (8q, 4q, 2q, q) make it canonical;
+//   * radix-2^30 split sums (Split4) reduce through a cheaper Barrett on the top 66 bits (reduce_wide);
 //   * the NTT butterflies use a three-product Shoup estimate (shoup_lazy4) and keep lazy values below
 //     8q (forward) / 4q (inverse), Harvey-style.
 #pragma once
@@ -139,18 +140,52 @@ __device__ __forceinline__ void split_fold128(const Split4& acc, u64& hi, u64& l
   asm("add.cc.u64 %0, %0, %2;\n\taddc.u64 %1, %1, %3;" : "+l"(lo), "+l"(hi) : "l"(b_lo), "l"(b_hi));
   asm("add.cc.u64 %0, %0, %2;\n\taddc.u64 %1, %1, %3;" : "+l"(lo), "+l"(hi) : "l"(c_lo), "l"(c_hi));
 }
-// V mod q, canonical (V < 14 2^k, e.g. 16 products of residues below 2^60 and q)
+// acc += a b in split form, for a, b < 2^60
+__device__ __forceinline__ void split_mac(Split4& acc, u64 a, u64 b) {
+  const uint32_t a0 = (uint32_t)a & ((1u << 30) - 1), a1 = (uint32_t)(a >> 30);
+  const uint32_t b0 = (uint32_t)b & ((1u << 30) - 1), b1 = (uint32_t)(b >> 30);
+  acc.s00 += (u64)a0 * b0;
+  acc.sa += (u64)a0 * b1;
+  acc.sb += (u64)a1 * b0;
+  acc.s11 += (u64)a1 * b1;
+}
+// x = hi:lo mod q as a representative in [0, 8 q), for x < 2^(66 + shift) (shift = floor(log2 q) - 1): e.g. 16
+// products of residues below 2^60 with residues of q, plus a representative below 8 q.  Classic Barrett on the
+// top bits: t = floor(x / 2^shift) < 2^66 and est = floor(t mu / 2^64), mu = floor(2^(shift + 64) / q) <= 2^63,
+// taken as t's top two bits times mu plus three of the four 32 x 32 partial products of t's low word and mu.
+// Truncating x and mu costs est at most 4 + 1/2 (x / 2^(shift + 64) < 4, 2^shift / q <= 1/2), the dropped
+// product and carries at most 2 more, so est >= floor(x / q) - 7 and x - est q < 8 q.  Five quarter-rate
+// multiplies against twelve for reduce128.
+__device__ __forceinline__ u64 reduce_wide_lazy(u64 hi, u64 lo, const Mod& m) {
+  const uint32_t sh = m.shift;
+  const u64 t = (lo >> sh) | (hi << (64 - sh));
+  const uint32_t th = (uint32_t)(hi >> sh);  // < 4
+  const uint32_t t0 = (uint32_t)t, t1 = (uint32_t)(t >> 32);
+  const uint32_t m0 = (uint32_t)m.mu, m1 = (uint32_t)(m.mu >> 32);
+  u64 est = (u64)t1 * m1 + __umulhi(t0, m1) + __umulhi(t1, m0);
+  est += (u64)th * m.mu;
+  return lo - est * m.q;
+}
+__device__ __forceinline__ u64 reduce_wide(u64 hi, u64 lo, const Mod& m) {
+  u64 r = reduce_wide_lazy(hi, lo, m);
+  const u64 q = m.q;
+  if (r >= (q << 2)) r -= (q << 2);
+  if (r >= (q << 1)) r -= (q << 1);
+  if (r >= q) r -= q;
+  return r;
+}
+// V mod q, canonical, for V < 2^(66 + shift) (e.g. 16 products of residues below 2^60 and q)
 __device__ __forceinline__ u64 fold_split(const Split4& acc, const Mod& m) {
   u64 hi, lo;
   split_fold128(acc, hi, lo);
-  return reduce128(hi, lo, m);
+  return reduce_wide(hi, lo, m);
 }
-// V mod q as a representative in [0, 16 q): restarting the sums from its split (S00 < 2^30, SA < 2^34) leaves
+// V mod q as a representative in [0, 8 q): restarting the sums from its split (S00 < 2^30, SA < 2^33) leaves
 // room for 16 more products below 2^60 in every sum
 __device__ __forceinline__ u64 fold_split_lazy(const Split4& acc, const Mod& m) {
   u64 hi, lo;
   split_fold128(acc, hi, lo);
-  return reduce128_lazy(hi, lo, m);
+  return reduce_wide_lazy(hi, lo, m);
 }
 
 // bit reversal of the low `bits` bits

@@ -154,7 +154,18 @@ int build_context(HolmesCtx& c, int log_n, int limbs, int dnum, int dcrt_bits, i
     unit_neg[i] = host_shoup(qi - u, qi);
   }
 
-  // ModUp tables per level `cur` (1..L) and digit j: limbs [jA, min(jA + A, cur)).
+  // P mod q_i and P^-1 mod q_i (the ModDown factor, folded into the digits' Q rows)
+  std::vector<u64> p_mod_q(L), p_inv(L);
+  std::vector<Tw> md_pinv(L);
+  for (int i = 0; i < L; ++i) {
+    u64 P = 1;
+    for (int k = 0; k < K; ++k) P = host_mul_mod(P, q[L + k] % q[i], q[i]);
+    p_mod_q[i] = P;
+    p_inv[i] = host_inv_mod(P, q[i]);
+    md_pinv[i] = host_shoup(p_inv[i], q[i]);
+  }
+  // ModUp tables per level `cur` (1..L) and digit j: limbs [jA, min(jA + A, cur)).  The conversion constant of
+  // a Q target carries P^-1 mod q_t.
   std::vector<Tw> mu_scale((size_t)(L + 1) * B * A, Tw{0, 0});
   std::vector<u64> mu_hat((size_t)(L + 1) * B * A * T, 0);
   for (int cur = 1; cur <= L; ++cur) {
@@ -171,32 +182,21 @@ int build_context(HolmesCtx& c, int log_n, int limbs, int dnum, int dcrt_bits, i
           u64 h = 1;
           for (int mm = lo; mm < hi; ++mm)
             if (mm != k) h = host_mul_mod(h, q[mm] % q[t], q[t]);
-          mu_hat[(((size_t)cur * B + j) * A + (k - lo)) * T + t] = h;
+          mu_hat[(((size_t)cur * B + j) * A + (k - lo)) * T + t] = t < L ? host_mul_mod(h, p_inv[t], q[t]) : h;
         }
       }
     }
   }
-  // ModDown tables
-  std::vector<Tw> md_scale(K), md_pinv(L);
-  std::vector<u64> md_hat((size_t)K * L), p_mod_q(L);
+  // ModDown tables: md_hat = (P / p_k) P^-1 = p_k^-1 mod q_i
+  std::vector<Tw> md_scale(K);
+  std::vector<u64> md_hat((size_t)K * L);
   for (int k = 0; k < K; ++k) {
     const u64 pk = q[L + k];
     u64 hk = 1;
     for (int m = 0; m < K; ++m)
       if (m != k) hk = host_mul_mod(hk, q[L + m] % pk, pk);
     md_scale[k] = host_shoup(host_mul_mod(host_inv_mod(hk, pk), ninv[L + k].w, pk), pk);
-    for (int i = 0; i < L; ++i) {
-      u64 h = 1;
-      for (int m = 0; m < K; ++m)
-        if (m != k) h = host_mul_mod(h, q[L + m] % q[i], q[i]);
-      md_hat[(size_t)k * L + i] = h;
-    }
-  }
-  for (int i = 0; i < L; ++i) {
-    u64 P = 1;
-    for (int k = 0; k < K; ++k) P = host_mul_mod(P, q[L + k] % q[i], q[i]);
-    p_mod_q[i] = P;
-    md_pinv[i] = host_shoup(host_inv_mod(P, q[i]), q[i]);
+    for (int i = 0; i < L; ++i) md_hat[(size_t)k * L + i] = host_inv_mod(pk % q[i], q[i]);
   }
   // rescale: from `cur` limbs drop q_{cur-1}
   std::vector<Tw> rs((size_t)(L + 1) * L, Tw{0, 0});

@@ -26,10 +26,10 @@ struct HolmesCtx {
   Tw* d_itw = nullptr;           // [T][N] inverse twiddles psi^-bitrev(k)
   Tw* d_ninv = nullptr;          // [T] N^-1
   Tw* d_mu_scale = nullptr;      // [L+1][beta_max][alpha] N^-1 (Q_j/q_k)^-1 mod q_k (ModUp iNTT epilogue)
-  u64* d_mu_hat = nullptr;       // [L+1][beta_max][alpha][T] (Q_j/q_k) mod m_t
+  u64* d_mu_hat = nullptr;       // [L+1][beta_max][alpha][T] (Q_j/q_k) mod m_t, times P^-1 for Q targets t < L
   Tw* d_md_scale = nullptr;      // [K] N^-1 (P/p_k)^-1 mod p_k (ModDown iNTT epilogue)
-  u64* d_md_hat = nullptr;       // [K][L] (P/p_k) mod q_i
-  Tw* d_md_pinv = nullptr;       // [L] P^-1 mod q_i
+  u64* d_md_hat = nullptr;       // [K][L] (P/p_k) P^-1 = p_k^-1 mod q_i
+  Tw* d_md_pinv = nullptr;       // [L] P^-1 mod q_i (scales the digits' own limbs in ModUp)
   Tw* d_rs_qinv = nullptr;       // [L+1][L] q_{l-1}^-1 mod q_i (rescale from l limbs)
   u64* d_p_mod_q = nullptr;      // [L] P mod q_i
   Tw* d_unit = nullptr;          // [T] psi^(N/2): X^(N/2) evaluated at the first half of the NTT words

@@ -3,11 +3,15 @@
 //
 //   plain NTT / iNTT              batched [items][limbs][N]
 //   ModUp                         iNTT(c1) * N^-1 (Q_j/q_k)^-1  ->  per digit: base conversion of
-//                                 every target limb (k_conv), then their forward NTTs in place
+//                                 every target limb (k_conv, which also writes the digit's own limbs),
+//                                 then their forward NTTs in place.  A digit's Q rows carry the factor
+//                                 P^-1 mod q_i of the later ModDown (own limbs: c1 * P^-1; converted
+//                                 limbs: constants (Q_j/q_k) P^-1 mod q_i), so it is paid once per ModUp
+//                                 rather than once per key switch of a hoisted set
 //   key switch (hybrid, ModDown)  P limbs: inner product (digits through the automorphism) fused into
-//                                 the iNTT with N^-1 (P/p_k)^-1; Q limbs: base conversion P->q_i (k_conv),
-//                                 then the NTT with inner product + subtract + P^-1 + automorphed addend
-//                                 fused into its store
+//                                 the iNTT with N^-1 (P/p_k)^-1; Q limbs: base conversion P->q_i with
+//                                 constants p_k^-1 mod q_i (k_conv), then the NTT with inner product -
+//                                 conversion + automorphed addend fused into its store
 //   The base conversions run as their own elementwise pass: one thread keeps a coefficient's source
 //   words in registers for every target limb, where the NTT's load phase (fused before) recomputed its
 //   splits per target and stalled on 8 scattered loads per word with few registers to spare.
@@ -57,8 +61,9 @@ struct StPlain {
 // Target t is limb r = t (t < skip_lo) or t + w (above), of modulus index mi = r (r < cur) or L + r - cur.  One
 // thread reads the w source words of one coefficient once, splits them into 30-bit halves, and produces every
 // target from constants pre-split in shared memory (four fused wide multiply-adds per product, w <= 16 products
-// per 64-bit sum), then one Barrett fold per output.  Used by the key switch (P -> Q) and ModUp (digit ->
-// complement), whose NTTs then load plainly.
+// per 64-bit sum), then one Barrett fold per output, left lazy in [0, 8 q) for the forward NTT that follows.
+// Used by the key switch (P -> Q) and ModUp (digit -> complement), whose NTTs then load plainly.  With `own`
+// set (ModUp) the same thread also writes the skipped rows skip_lo + a: own_a * own_scale[a] mod q_(skip_lo + a).
 struct ConvArgs {
   const u64* y;     // source limb a of item i at y + i * y_item + a * N
   long long y_item;
@@ -67,6 +72,9 @@ struct ConvArgs {
   const u64* H;     // H[a * h_row + mi]
   int h_row;
   int w, ntgt, skip_lo, cur, L, items;
+  const u64* own;   // optional: row a of item i at own + i * own_item + a * N
+  long long own_item;
+  const Tw* own_scale;
 };
 template <int W>
 __global__ void __launch_bounds__(256) k_conv(ConvArgs a, int log_n, const Mod* __restrict__ mods) {
@@ -92,6 +100,14 @@ __global__ void __launch_bounds__(256) k_conv(ConvArgs a, int log_n, const Mod* 
       ys[k] = make_uint2((uint32_t)(v & ((1ull << 30) - 1)), (uint32_t)(v >> 30));
     }
     u64* op = a.out + item * a.out_item + n;
+    if (a.own) {
+      const u64* src = a.own + item * a.own_item + n;
+#pragma unroll
+      for (int k = 0; k < W; ++k) {
+        const Mod& m = mods[a.skip_lo + k];
+        op[(size_t)(a.skip_lo + k) << log_n] = shoup(src[(size_t)k << log_n], a.own_scale[k], m.q);
+      }
+    }
     for (int t = 0; t < a.ntgt; ++t) {
       const uint2* h = hs + t * W;
       Split4 s{0, 0, 0, 0};
@@ -105,7 +121,7 @@ __global__ void __launch_bounds__(256) k_conv(ConvArgs a, int log_n, const Mod* 
       }
       const int r = t < a.skip_lo ? t : t + W;
       const int mi = r < a.cur ? r : a.L + r - a.cur;
-      op[(size_t)r << log_n] = fold_split(s, mods[mi]);
+      op[(size_t)r << log_n] = fold_split_lazy(s, mods[mi]);
     }
   }
 }
@@ -230,14 +246,11 @@ int modup(const HolmesCtx& c, const u64* c1, long long c1_item, int cur, int ite
   for (int j = 0; j < beta; ++j) {
     const int lo = j * A, w = std::min(A, cur - lo);
     u64* dj = digits + (size_t)j * dstride;
-    // the digit's own limbs are the input limbs themselves
-    HOLMES_CUDA_TRY(cudaMemcpy2DAsync(dj + (size_t)lo * N, (size_t)dig_item * 8, c1 + (size_t)lo * N,
-                                      (size_t)c1_item * 8, (size_t)w * N * 8, (size_t)items, cudaMemcpyDeviceToDevice,
-                                      st));
     NttTables T{c.d_tw, c.d_mod};
     const int ntgt = cur + K - w;
+    // the digit's own limbs are the input limbs times P^-1, written by the conversion kernel
     ConvArgs ca{scratch + (size_t)lo * N, y_item, dj, dig_item, c.mu_hat(cur) + (size_t)j * A * c.T, c.T,
-                w, ntgt, lo, cur, c.L, items};
+                w, ntgt, lo, cur, c.L, items, c1 + (size_t)lo * N, c1_item, c.d_md_pinv + lo};
     {
       const int e = conv_launch(c, ca, st);
       if (e) return e;
@@ -279,13 +292,15 @@ struct LdKsP {
     s.m = mods[L + k];
     return s;
   }
+  // a representative below 4 q (the inverse NTT's input range)
   __device__ u64 load(const S& s, int n) const {
     const u32 src = galois > 1 ? automorph_src((u32)n, galois, log_n) : (u32)n;
     const size_t dstep = ((size_t)(cur + K)) << log_n, kstep = ((size_t)(cap + K)) << log_n;
-    U128 acc{0, 0};
+    Split4 acc{0, 0, 0, 0};
 #pragma unroll 4
-    for (int j = 0; j < beta; ++j) mac128(acc, s.d[j * dstep + src], s.k[j * kstep + n]);
-    return reduce128(acc, s.m);
+    for (int j = 0; j < beta; ++j) split_mac(acc, s.d[j * dstep + src], s.k[j * kstep + n]);
+    const u64 r = fold_split_lazy(acc, s.m), q4 = s.m.q << 2;
+    return r >= q4 ? r - q4 : r;
   }
 };
 struct StScratch {
@@ -303,8 +318,9 @@ __global__ void HOLMES_NTT_BOUNDS(LOGN) k_ks_p(NttTables T, const Tw* md_scale, 
   ntt_inverse_body<LOGN>(p, ld.L + k, md_scale[k], T, ld, st);
 }
 
-// Q limbs: conv_c[i] = NTT(sum_k y_c[k] (P/p_k) mod q_i) (k_conv, then a plain-load NTT); out = (inner - conv) P^-1
-// + perm(add)
+// Q limbs: conv_c[i] = NTT(sum_k y_c[k] p_k^-1 mod q_i) (k_conv, then a plain-load NTT); out = inner - conv
+// + perm(add) + post, where inner (over the digits' Q rows, which carry P^-1) is already P^-1 times the
+// hybrid inner product: together (inner - sum_k y_k (P/p_k)) P^-1, the ModDown.
 struct StKsQ {
   const u64* digits;
   long long dig_item;
@@ -319,7 +335,6 @@ struct StKsQ {
   u64* out1;
   long long out_item;
   const Mod* mods;
-  const Tw* pinv;
   u64 galois;
   int cur, cap, K, beta, key_beta, log_n;
   struct S {
@@ -329,7 +344,6 @@ struct StKsQ {
     const u64* pa;
     u64* o;
     Mod m;
-    Tw pi;
   };
   __device__ S prep(int p) const {
     const int item = p / (2 * cur), r = p % (2 * cur), c = r / cur, i = r % cur;
@@ -342,17 +356,15 @@ struct StKsQ {
     s.pa = post ? post + item * post_item + ((size_t)i << log_n) : nullptr;
     s.o = (c ? out1 : out0) + item * out_item + ((size_t)i << log_n);
     s.m = mods[i];
-    s.pi = pinv[i];
     return s;
   }
   __device__ void store(const S& s, int n, u64 v) const {
     const u32 src = galois > 1 ? automorph_src((u32)n, galois, log_n) : (u32)n;
     const size_t dstep = ((size_t)(cur + K)) << log_n, kstep = ((size_t)(cap + K)) << log_n;
-    U128 acc{0, 0};
+    Split4 acc{0, 0, 0, 0};
 #pragma unroll 4
-    for (int j = 0; j < beta; ++j) mac128(acc, s.d[j * dstep + src], s.k[j * kstep + n]);
-    const u64 inner = reduce128(acc, s.m);
-    u64 r = shoup(sub_mod(inner, v, s.m.q), s.pi, s.m.q);
+    for (int j = 0; j < beta; ++j) split_mac(acc, s.d[j * dstep + src], s.k[j * kstep + n]);
+    u64 r = sub_mod(fold_split(acc, s.m), v, s.m.q);
     if (s.a) r = add_mod(r, s.a[src], s.m.q);
     if (s.pa) r = add_mod(r, s.pa[n], s.m.q);
     s.o[n] = r;
@@ -392,7 +404,7 @@ int ks_apply(const HolmesCtx& c, const KsArgs& a, cudaStream_t st) {
   u64* conv = a.scratch + (size_t)a.items * 2 * K * c.n;  // [items][2][cur][N], coefficient form
   {
     ConvArgs ca{a.scratch, (long long)K * c.n, conv, (long long)a.cur * c.n, c.d_md_hat, c.L,
-                K, a.cur, a.cur, a.cur, c.L, a.items * 2};
+                K, a.cur, a.cur, a.cur, c.L, a.items * 2, nullptr, 0, nullptr};
     const int e = conv_launch(c, ca, st);
     if (e) return e;
   }
@@ -400,8 +412,7 @@ int ks_apply(const HolmesCtx& c, const KsArgs& a, cudaStream_t st) {
     NttTables T{c.d_tw, c.d_mod};
     LdRows ld{conv, c.log_n};
     StKsQ sq{a.digits, a.dig_item, a.key, a.add0, a.add1, a.add_item, a.post0, a.post1, a.post_item, a.out0, a.out1,
-             a.out_item, c.d_mod,
-             c.d_md_pinv, g, a.cur, a.key_cap, K, beta, key_beta, c.log_n};
+             a.out_item, c.d_mod, g, a.cur, a.key_cap, K, beta, key_beta, c.log_n};
     const int polys = a.items * 2 * a.cur;
 #define L_(LG)                                                                                        \
   {                                                                                                   \

@@ -117,7 +117,9 @@ int holmes_rescale_noalloc(void* ctx, const uint64_t* in, long long in_stride, u
 
 /* ---- hybrid key switch (EasyFHE cv_modup / cv_innerproduct / cv_moddown, bench/cmp/report.py:23-46;
  *      fhe.homo_rotate, prepare_hoisted_baby_rotations, homo_relinearize) */
-/* digits[items][beta(cur)][cur + K][N] = ModUp(c1[items][cur][N]) (item strides c1_item / digit_item words);
+/* digits[items][beta(cur)][cur + K][N] = ModUp(c1[items][cur][N]) (item strides c1_item / digit_item words),
+ * with every Q row (limb i < cur) multiplied by P^-1 mod q_i: the ModDown factor, paid here once for all the key
+ * switches of a hoisted set.  The digits are an opaque intermediate for holmes_keyswitch;
  * scratch >= items * cur * N words */
 int holmes_modup(void* ctx, const uint64_t* c1, long long c1_item, int cur, int items, uint64_t* digits,
                  long long digit_item, uint64_t* scratch, void* stream);
