@@ -588,58 +588,107 @@ int modraise(const HolmesCtx& c, const u64* in, long long in_stride, u64* out, l
 // --------------------------------------------------------------------------------------------- encode
 // Coefficient n of a row: Re(u[n / gap]) for n < N/2, Im(u[(n - N/2) / gap]) above, 0 off the gap grid;
 // rounded with llround(v * scale) (bench/cmp/kernels/holmes_encode.cu:136-159) and reduced mod q_i.
-struct LdEncode {
-  const double* u;
-  long long row_stride;  // doubles
+// Two steps: k_round_rows rounds every coefficient once per row (the 2^61 range check included) into the
+// storage of the row's last output limb; the forward NTTs of the other limbs then load those integers, and the
+// last limb's NTT runs afterwards in place (a cluster loads all its words before any CTA of it stores).  The
+// rounding is thus paid once per coefficient rather than once per limb.
+__global__ void k_round_rows(const double* __restrict__ u, long long row_stride, int rows, int gap_log, int log_n,
+                             double scale, u64* out, long long out_row_stride, int* flag) {
+  const int half = 1 << (log_n - 1);
+  const size_t total = (size_t)rows << log_n;
+  for (size_t g = blockIdx.x * (size_t)blockDim.x + threadIdx.x; g < total; g += (size_t)gridDim.x * blockDim.x) {
+    const int r = (int)(g >> log_n), n = (int)(g & ((1u << log_n) - 1));
+    const int im = n >= half;
+    const int k = n - im * half;
+    i64 m = 0;
+    if (!(k & ((1 << gap_log) - 1))) {
+      const double v = __dmul_rn(u[r * row_stride + 2 * (k >> gap_log) + im], scale);
+      if (fabs(v) < 2305843009213693952.0) {
+        m = (i64)llround(v);
+      } else {
+        *flag = 1;
+      }
+    }
+    out[r * out_row_stride + n] = (u64)m;
+  }
+}
+// Load of a rounded coefficient m (|m| < 2^61) as a representative below 8 q (the forward NTT's input range):
+// m itself or m + 8 q when every modulus of the launch has 8 q > 2^61 (WIDE), a signed Barrett reduction
+// otherwise.
+template <bool WIDE>
+struct LdRounded {
+  const u64* base;       // row r's integers at base + r * row_stride
+  long long row_stride;
   const Mod* mods;
-  double scale;
-  int cur, gap_log, log_n;
-  int* flag;
+  int cur, first;        // poly p = (r, first + p % (cur - first))
   struct S {
-    const double* r;
+    const i64* r;
     Mod m;
   };
   __device__ S prep(int p) const {
+    const int w = cur - first;
     S s;
-    s.r = u + (p / cur) * row_stride;
-    s.m = mods[p % cur];
+    s.r = reinterpret_cast<const i64*>(base + (p / w) * row_stride);
+    s.m = mods[first + p % w];
     return s;
   }
   __device__ u64 load(const S& s, int n) const {
-    const int half = 1 << (log_n - 1);
-    const int im = n >= half;
-    const int k = n - im * half;
-    if (k & ((1 << gap_log) - 1)) return 0;
-    const double v = __dmul_rn(s.r[2 * (k >> gap_log) + im], scale);
-    if (!(fabs(v) < 2305843009213693952.0)) {
-      *flag = 1;
-      return 0;
+    const i64 m = s.r[n];
+    if constexpr (WIDE) {
+      return m >= 0 ? (u64)m : (u64)m + (s.m.q << 3);
+    } else {
+      const u64 a = reduce_wide(0, m >= 0 ? (u64)m : (u64)(-m), s.m);
+      return m >= 0 ? a : (a ? s.m.q - a : 0);
     }
-    return signed_residue((i64)llround(v), s.m);
   }
 };
-template <int LOGN>
-__global__ void HOLMES_NTT_BOUNDS(LOGN) k_encode(NttTables T, LdEncode ld, StPlain st) {
+template <int LOGN, bool WIDE>
+__global__ void HOLMES_NTT_BOUNDS(LOGN) k_encode(NttTables T, LdRounded<WIDE> ld, StPlain st) {
   const int p = blockIdx.x / NttGeom<LOGN>::CL;
-  ntt_forward_body<LOGN>(p, p % ld.cur, T, ld, st);
+  ntt_forward_body<LOGN>(p, ld.first + p % (ld.cur - ld.first), T, ld, st);
 }
 
 int encode_rows(const HolmesCtx& c, const double* u, long long row_stride, int rows, int slots, double scale, int cur,
                 u64* out, long long out_row_stride, int* flag, cudaStream_t st) {
   if (cur < 1 || cur > c.T) return -2;
   if (slots < 1 || slots > c.n / 2 || (slots & (slots - 1))) return -3;
+  if (out_row_stride < (long long)cur * c.n) return -4;
   int gap_log = 0;
   while ((slots << (gap_log + 1)) < c.n) ++gap_log;
-  NttTables T{c.d_tw, c.d_mod};
-  LdEncode ld{u, row_stride, c.d_mod, scale, cur, gap_log, c.log_n, flag};
-  StPlain sp{out, poly_map(cur, out_row_stride, c.n, 0)};
-#define L_(LG)                                                                                          \
-  {                                                                                                     \
-    using G = NttGeom<LG>;                                                                              \
-    return (int)launch_ntt(k_encode<LG>, G::LOGCL, G::THREADS, G::SMEM, rows * cur, st, T, ld, sp);    \
+  u64* ints = out + (size_t)(cur - 1) * c.n;  // row r's integers at ints + r * out_row_stride
+  {
+    const size_t work = (size_t)rows << c.log_n;
+    size_t blocks = (work + 255) / 256;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    count_launch();
+    k_round_rows<<<(unsigned)blocks, 256, 0, st>>>(u, row_stride, rows, gap_log, c.log_n, scale, ints, out_row_stride,
+                                                    flag);
+    HOLMES_CUDA_TRY(cudaGetLastError());
   }
-  HOLMES_LOGN_SWITCH(c.log_n, L_)
+  NttTables T{c.d_tw, c.d_mod};
+  // limbs 0 .. cur-2 from the integers, then limb cur-1 in place
+  for (int pass = 0; pass < 2; ++pass) {
+    const int first = pass ? cur - 1 : 0, last = pass ? cur : cur - 1;
+    if (last <= first) continue;
+    bool wide = true;
+    for (int l = first; l < last; ++l) wide = wide && (c.q[l] << 3) > (1ull << 61);
+    LdRounded<true> lw{ints, out_row_stride, c.d_mod, last, first};
+    LdRounded<false> ln{ints, out_row_stride, c.d_mod, last, first};
+    PolyMap pm = poly_map(last - first, out_row_stride, c.n, 0);
+    StPlain sp{out + (size_t)first * c.n, pm};
+    const int polys = rows * (last - first);
+#define L_(LG)                                                                                                   \
+  {                                                                                                              \
+    using G = NttGeom<LG>;                                                                                       \
+    cudaError_t e = wide ? launch_ntt(k_encode<LG, true>, G::LOGCL, G::THREADS, G::SMEM, polys, st, T, lw, sp)  \
+                         : launch_ntt(k_encode<LG, false>, G::LOGCL, G::THREADS, G::SMEM, polys, st, T, ln, sp); \
+    if (e != cudaSuccess) return (int)e;                                                                         \
+    break;                                                                                                       \
+  }
+    HOLMES_LOGN_SWITCH(c.log_n, L_)
 #undef L_
+  }
+  return 0;
 }
 
 // --------------------------------------------------------------------------------------------- decrypt

@@ -115,6 +115,26 @@ def test_encode_bitexact(pair, slots):
         np.testing.assert_array_equal(got[r], o.encode(rows[r], 4, ctx.scale, slots))
 
 
+@pytest.mark.parametrize("log_n,slots", [(12, 2048), (14, 1024)])
+def test_encode_bitexact_production_width_primes(log_n, slots):
+    """59/60-bit moduli take the encoder's direct signed load (8 q > 2^61); 2^14 runs the cluster NTT.  Values
+    near the 2^61 limit (coefficients up to 2^60.8 of either sign) exercise the widest inputs."""
+    o, _, ctx = make_pair(log_n=log_n, limbs=3, dnum=1, dcrt=59, first=60, special=60)
+    try:
+        from holmes_b200 import fhe as F
+
+        rng = np.random.default_rng(log_n)
+        rows = (rng.uniform(-1, 1, size=(2, slots)) + 1j * rng.uniform(-1, 1, size=(2, slots))) * 56.0
+        rows[1] *= 2.0 ** -30
+        pt = F.encode_rows(ctx, torch.from_numpy(rows).to(ctx.device), 3, ctx.scale, slots)
+        ctx.check_encode_range()
+        got = host(pt)
+        for r in range(2):
+            np.testing.assert_array_equal(got[r], o.encode(rows[r], 3, ctx.scale, slots))
+    finally:
+        ctx.close()
+
+
 def test_encode_range_error_is_raised(pair):
     _, _, ctx = pair
     from holmes_b200 import fhe as F
