@@ -555,6 +555,12 @@ class LinearOperator:
     def apply(self, input_ciphers, weight: LinearWeight, *, chunk_indices=None, rescale: bool = True):
         if self._closed:
             raise RuntimeError("linear operator is closed.")
+        strategy = str(self.config.hoist_strategy).lower()
+        if strategy != "normal":
+            # The extended-basis schedules keep the babies and the MAC in Q*P and ModDown later; their rounding is
+            # EasyFHE's and cannot be pinned here, so they are refused rather than silently run as "normal".
+            raise NotImplementedError(f"hoist_strategy {strategy!r} is not built; the production linear schedule "
+                                      "(operators/linear/config.py:123-135) is 'normal'")
         inputs = tuple(input_ciphers)
         if not inputs:
             return (), dict(_EMPTY_PROFILE)
