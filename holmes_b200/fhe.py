@@ -572,18 +572,42 @@ def homo_rotate(a: Cipher, rotation: int, ctx) -> Cipher:
     return out
 
 
-def fast_rotate(a: Cipher, rotation: int, ctx) -> Cipher:
-    return homo_rotate(a, rotation, ctx)
+def fast_rotate(a: Cipher, rotations, ctx) -> Cipher:
+    """One rotation (an int: ``homo_rotate``) or, for a sequence of offsets, the batch ``[len(offsets)]`` of
+    rotations from one hoisted ModUp (the reference's use: ``operators/linear/shifted_lane.py:75-76``, unpacked
+    with ``unpack_cipher_batch``).  Residue-identical to rotating one at a time."""
+    if isinstance(rotations, (int, np.integer)):
+        return homo_rotate(a, int(rotations), ctx)
+    return prepare_hoisted_baby_rotations(a, tuple(int(r) for r in rotations), ctx)
+
+
+def pack_cipher_batch(ciphers) -> Cipher:
+    """One batch cipher from single (or batch) ciphers of one level, scale and slot count, items in order."""
+    ciphers = tuple(ciphers)
+    if not ciphers:
+        raise ValueError("pack_cipher_batch needs at least one cipher")
+    first = ciphers[0]
+    cur = int(first.state.cur_limbs)
+    for c in ciphers[1:]:
+        if int(c.state.cur_limbs) != cur or int(c.state.scale_degree) != int(first.state.scale_degree) \
+                or c.slots != first.slots or c.is_ext != first.is_ext or len(c.cv) != len(first.cv):
+            raise ValueError("pack_cipher_batch: ciphers differ in level, scale degree, slots or form")
+    cv = [torch.cat([c.cv[k][:, :cur] for c in ciphers], dim=0) for k in range(len(first.cv))]
+    return first.cipher_like(cv, batch_size=int(cv[0].shape[0]))
+
+
+def unpack_cipher_batch(batch: Cipher) -> tuple:
+    """The items of a batch cipher as single ciphers (views of the batch storage)."""
+    return tuple(batch.cipher_like([c[i:i + 1] for c in batch.cv], batch_size=1) for i in range(batch.batch_size))
 
 
 def prepare_hoisted_baby_rotations(a: Cipher, baby_offsets, ctx, strategy: str = "normal",
                                    baby_anchor_step: int = -1):
-    """Baby basis rot(a, offset) for every offset from one hoisted ModUp; one block ``[nb]`` batch.
-
-    Every hoist strategy name of the reference is accepted; all return the ModDown'ed (non-extended)
-    basis, which is the ``normal`` strategy's result.
-    """
-    del strategy, baby_anchor_step
+    """Baby basis rot(a, offset) for every offset from one hoisted ModUp; one block ``[nb]`` batch (the
+    ``normal`` strategy; the extended-basis strategies are not built and raise)."""
+    del baby_anchor_step
+    if str(strategy).lower() != "normal":
+        raise NotImplementedError(f"hoist strategy {strategy!r} is not built (only 'normal')")
     ctx = _ctx(ctx)
     if a.batch_size != 1:
         raise ValueError("prepare_hoisted_baby_rotations expects one ciphertext")

@@ -22,6 +22,8 @@ alignment, accumulation, rescale), so the result is residue-for-residue what a p
 """
 from __future__ import annotations
 
+import hashlib
+
 import os
 import time
 from dataclasses import dataclass, field
@@ -281,6 +283,27 @@ class Session:
 
     def decrypt(self, cipher, item: int = 0) -> np.ndarray:
         return np.asarray(self.client.decrypt(cipher, item)).reshape(-1)
+
+    def plaintext(self, values, *, name: str, level: int, slots: int | None = None, dtype=np.float64,
+                  is_ext: bool = False) -> F.Plaintext:
+        """A public vector encoded at ``level``'s limbs and scale (reference: backend.py:303-330), cached per
+        name, level, slot count and contents."""
+        if is_ext:
+            raise NotImplementedError("extended-basis plaintexts are not built")
+        array = np.ascontiguousarray(np.asarray(values, dtype=dtype).reshape(-1))
+        slots = self.max_slots if slots is None else int(slots)
+        key = (str(name), int(level), slots, hashlib.sha1(array.tobytes()).hexdigest())
+        cache = self.__dict__.setdefault("_plaintexts", {})
+        hit = cache.get(key)
+        if hit is not None:
+            return hit
+        ctx = self.context
+        cur = int(ctx.L) - int(level)
+        bundle = F.ConstantBundle({"value": F.PackedRaw(torch.from_numpy(array.astype(np.complex128)))})
+        pt = bundle.plaintext("value", state=F.CipherState(cur, 1, ctx.scale_at(cur)), slots=slots, context=ctx)
+        ctx.check_encode_range()
+        cache[key] = pt
+        return pt
 
 
 def create_session(spec: F.CKKSContextSpec, device: str = "cuda") -> Session:

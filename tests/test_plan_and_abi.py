@@ -119,3 +119,46 @@ def test_c_abi_exports_every_declared_symbol():
     raw = ctypes.CDLL(_lib.LIB_PATH)
     for name in names:
         getattr(raw, name)
+
+
+def test_shifted_lane_layout_matches_golden_semantics():
+    """Carrier layout (layouts/shifted_lane.py:41-175): pack, lane-0 pack, unpack per lane, expansion offsets."""
+    import numpy as np
+    from holmes_b200.shifted_lane import ShiftedLaneLayout, lane0_mask_vector
+
+    lay = ShiftedLaneLayout(hidden_dim=64, slots=512)
+    assert (lay.lanes, lay.shift) == (8, 8)
+    x = np.arange(64, dtype=np.float64)
+    sl = lay.pack(x)
+    assert lay.is_shifted_lane(sl)
+    for lane in range(8):
+        np.testing.assert_array_equal(lay.unpack(sl, lane=lane), x)
+    assert sl[lay.slot(3, 2)] == x[(3 + 8 * 2) % 64]
+    lr = lay.pack_lane0(x)
+    # rotating the lane-0 carrier by each expansion offset and adding builds the SL carrier
+    built = lr.copy()
+    for off in lay.lane0_to_shifted_offsets():
+        built = built + np.roll(lr, -off)
+    np.testing.assert_array_equal(built, sl)
+    assert lay.fold_offsets() == (1, 2, 4)
+    plan = LN.LinearOperatorConfig(baby_steps=16, lane_shift=128).plan(dimension=1024, token_lanes=8)
+    mask = lane0_mask_vector(plan, slots=8192)
+    assert mask.sum() == 1024 and mask[::8].all()
+    assert plan.lane_expand_offsets == tuple(1023 * l for l in range(1, 8))
+    with pytest.raises(ValueError):
+        ShiftedLaneLayout(hidden_dim=48, slots=512)
+
+
+def test_cipher_batch_pack_unpack_on_host_tensors():
+    import torch
+    from holmes_b200 import fhe as F
+
+    st = F.CipherState(2, 1, 2.0 ** 40)
+    a = F.Cipher([torch.zeros((1, 3, 8), dtype=torch.int64), torch.ones((1, 3, 8), dtype=torch.int64)], st, 4)
+    b = F.Cipher([torch.full((1, 2, 8), 2, dtype=torch.int64), torch.full((1, 2, 8), 3, dtype=torch.int64)], st, 4)
+    batch = F.pack_cipher_batch([a, b])
+    assert batch.batch_size == 2 and tuple(batch.cv[0].shape) == (2, 2, 8)
+    items = F.unpack_cipher_batch(batch)
+    assert [int(i.cv[1][0, 0, 0]) for i in items] == [1, 3]
+    with pytest.raises(ValueError):
+        F.pack_cipher_batch([a, a.cipher_like(a.cv, state=F.CipherState(3, 1, 2.0 ** 40))])
