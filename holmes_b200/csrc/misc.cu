@@ -340,9 +340,10 @@ __global__ void __launch_bounds__(256, 2) k_bsgs_mac2(u64* __restrict__ res, InP
 //   * each thread splits the words it copied into (low 30 bits, high 30 bits) pairs in place once they land;
 //     a product of two such pairs is then four fused wide multiply-adds, whereas splitting a 64-bit word in
 //     registers right before the multiply costs the compiler about eight extra instructions per product;
-//   * the sums are folded lazily (any representative below 16 q, restarted from its split) except at the last.
+//   * the sums are folded lazily (a representative below 8 q, restarted from its split; one accumulator per step
+//     of every other stage) except at the last fold.
 // Tiles: IW inputs x 8 giants per block, GPT giants per thread (HOLMES_MAC_TILE="IWxGPT" selects one for A/B
-// timing; 4x4 is the default, 11.7 ms per 512-row chunk of 16 ciphertexts at 13 limbs).
+// timing; 4x4 is the default, 10.5 ms per 512-row chunk of 16 ciphertexts at 13 limbs).
 constexpr int kM3SB = 8;   // baby steps per stage
 constexpr int kM3NS = 3;   // stages in the ring
 
@@ -370,12 +371,24 @@ __device__ __forceinline__ void m3_step(MacAcc<GPT>& A, const uint2* bb, const u
     A.s11[GPT + g] += (u64)y.y * p.y;
   }
 }
+// lazy fold of accumulator K alone (a representative below 8 q, restarted from its split): issued between the
+// products of a step, one accumulator at a time, so its temporaries never pile up
+template <int K, int GPT>
+__device__ __forceinline__ void m3_fold_one(MacAcc<GPT>& A, const Mod& m) {
+  const Split4 s{A.s00[K], A.sa[K], A.sb[K], A.s11[K]};
+  const u64 r = fold_split_lazy(s, m);
+  A.s00[K] = r & ((1ull << 30) - 1);
+  A.sa[K] = r >> 30;
+  A.sb[K] = 0;
+  A.s11[K] = 0;
+}
 template <bool CANON, int GPT>
 __device__ __forceinline__ void m3_fold(MacAcc<GPT>& A, const Mod& m) {
 #pragma unroll
   for (int k = 0; k < 2 * GPT; ++k) {
     const Split4 s{A.s00[k], A.sa[k], A.sb[k], A.s11[k]};
-    // the full-width Barrett here: with reduce_wide the 4x4 tile spills and runs 1% slower (measured)
+    // the full-width Barrett here (the last, canonical fold of all sums at once): with reduce_wide the 4x4 tile
+    // spills
     u64 hi, lo;
     split_fold128(s, hi, lo);
     const u64 r = CANON ? reduce128(hi, lo, m) : reduce128_lazy(hi, lo, m);
@@ -383,6 +396,25 @@ __device__ __forceinline__ void m3_fold(MacAcc<GPT>& A, const Mod& m) {
     A.sa[k] = r >> 30;
     A.sb[k] = 0;
     A.s11[k] = 0;
+  }
+}
+template <int GPT, int K>
+__device__ __forceinline__ void m3_fold_at(MacAcc<GPT>& A, int st, const Mod& m) {
+  if constexpr (K < 2 * GPT) {
+    if (st == K) m3_fold_one<K, GPT>(A, m);
+    else m3_fold_at<GPT, K + 1>(A, st, m);
+  }
+}
+// one stage of `steps` (<= 8) baby steps; FOLD: accumulator st folded after step st
+template <int GPT, bool FOLD>
+__device__ __forceinline__ void m3_stage(MacAcc<GPT>& A, const uint2* bb, const uint2* pt, int steps, const Mod& m) {
+  static_assert(2 * GPT <= kM3SB, "one fold slot per step");
+#pragma unroll
+  for (int st = 0; st < kM3SB; ++st) {
+    if (st < steps) {
+      m3_step<GPT>(A, bb, pt, st);
+      if constexpr (FOLD) m3_fold_at<GPT, 0>(A, st, m);
+    }
   }
 }
 // the words w at p, p + 1 become the pairs (w mod 2^30, w >> 30) in place
@@ -489,16 +521,23 @@ __global__ void __launch_bounds__(M3Geom<IW, GPT>::THREADS, M3Geom<IW, GPT>::MIN
       const u64* base = mac_smem + (size_t)(s % kM3NS) * Geo::STAGE_WORDS;
       const uint2* pt = reinterpret_cast<const uint2*>(base) + (gq * GPT) * kM3SB * 32 + lane;
       const uint2* bb = reinterpret_cast<const uint2*>(base + Geo::PT_WORDS) + (iw * 2) * kM3SB * 32 + lane;
+      // In odd stages accumulator k is folded (lazily) right after step k's products, so every sum takes at most
+      // 16 products between folds: 8 - k - 1 + 8 + k + 1 across full stages, and in a short last stage of
+      // `steps` babies either k < steps (folded in it) or 8 - k - 1 + 8 + steps <= 15.  The last fold of the
+      // kernel is canonical.
+      const bool odd = s & 1;
       if (steps == kM3SB) {
+        if (odd) {
+          m3_stage<GPT, true>(A, bb, pt, kM3SB, m);
+        } else {
 #pragma unroll
-        for (int st = 0; st < kM3SB; ++st) m3_step<GPT>(A, bb, pt, st);
+          for (int st = 0; st < kM3SB; ++st) m3_step<GPT>(A, bb, pt, st);
+        }
       } else {
-        for (int st = 0; st < steps; ++st) m3_step<GPT>(A, bb, pt, st);
+        if (odd) m3_stage<GPT, true>(A, bb, pt, steps, m);
+        else m3_stage<GPT, false>(A, bb, pt, steps, m);
       }
-      // at most 16 products per sum between folds (two 8-step stages); the sums restart from any
-      // representative below 16 q, and only the last fold is made canonical
       if (s == nstages - 1) m3_fold<true, GPT>(A, m);
-      else if (s & 1) m3_fold<false, GPT>(A, m);
     }
   }
   asm volatile("cp.async.wait_all;\n" ::);

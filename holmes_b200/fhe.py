@@ -578,7 +578,7 @@ def fast_rotate(a: Cipher, rotations, ctx) -> Cipher:
     with ``unpack_cipher_batch``).  Residue-identical to rotating one at a time."""
     if isinstance(rotations, (int, np.integer)):
         return homo_rotate(a, int(rotations), ctx)
-    return prepare_hoisted_baby_rotations(a, tuple(int(r) for r in rotations), ctx)
+    return prepare_hoisted_baby_rotations(a, tuple(int(r) for r in rotations), ctx)[0]
 
 
 def pack_cipher_batch(ciphers) -> Cipher:
