@@ -21,6 +21,7 @@
 //   decrypt, keygen, encrypt      c0 + c1 s / CBD error sampling fused into the NTT load; the key /
 //                                 ciphertext assembly fused into the store
 #include "ntt.cuh"
+#include "ntt16.cuh"
 #include "ops.h"
 #include "sampler.cuh"
 
@@ -55,6 +56,62 @@ struct StPlain {
   __device__ S prep(int p) const { return S{dst + pm.off(p)}; }
   __device__ void store(const S& s, int n, u64 v) const { s.p[n] = v; }
 };
+
+// --------------------------------------------------------------------------------------------- N = 2^16, two passes
+// The kernels below run the NTTs of N = 2^16 as two launches (ntt16.cuh); MOD maps a polynomial to its modulus
+// index, SC to its final inverse scale, IM to the intermediate the first pass writes and the second reads.
+struct IMRows {
+  u64* base;
+  __device__ u64* at(int p) const { return base + ((size_t)p << 16); }
+};
+struct IMPlain {
+  u64* base;
+  PolyMap pm;
+  __device__ u64* at(int p) const { return base + pm.off(p); }
+};
+struct ModPlain {
+  PolyMap pm;
+  __device__ int operator()(int p) const { return pm.mod(p); }
+};
+struct ScLimb {  // scale[limb of p] or scale[modulus of p]
+  const Tw* scale;
+  int by_limb;
+  PolyMap pm;
+  __device__ Tw operator()(int p) const { return scale[by_limb ? p % pm.limbs : pm.mod(p)]; }
+};
+template <class MOD, class LD, class IM>
+__global__ void HOLMES_NTT16_BOUNDS k16_fwd_a(NttTables T, MOD mo, LD ld, IM im) {
+  const int p = blockIdx.x >> 4;
+  fwd16_cols(p, blockIdx.x & 15, mo(p), T, ld, im.at(p));
+}
+template <class MOD, class IM, class ST>
+__global__ void HOLMES_NTT16_BOUNDS k16_fwd_b(NttTables T, MOD mo, IM im, ST st) {
+  const int p = blockIdx.x >> 4;
+  fwd16_rows(p, blockIdx.x & 15, mo(p), T, im.at(p), st);
+}
+template <class MOD, class LD, class IM>
+__global__ void HOLMES_NTT16_BOUNDS k16_inv_b(NttTables T, MOD mo, LD ld, IM im) {
+  const int p = blockIdx.x >> 4;
+  inv16_rows(p, blockIdx.x & 15, mo(p), T, ld, im.at(p));
+}
+template <class MOD, class SC, class IM, class ST>
+__global__ void HOLMES_NTT16_BOUNDS k16_inv_a(NttTables T, MOD mo, SC sc, IM im, ST st) {
+  const int p = blockIdx.x >> 4;
+  inv16_cols(p, blockIdx.x & 15, mo(p), sc(p), T, im.at(p), st);
+}
+// forward: ld -> im (pass A), im -> st (pass B); inverse: ld -> im (pass B'), im -> scale -> st (pass A')
+template <class MOD, class LD, class IM, class ST>
+static int ntt16_forward(NttTables T, MOD mo, LD ld, IM im, ST st, int polys, cudaStream_t s) {
+  cudaError_t e = launch_ntt16(k16_fwd_a<MOD, LD, IM>, polys, s, T, mo, ld, im);
+  if (e == cudaSuccess) e = launch_ntt16(k16_fwd_b<MOD, IM, ST>, polys, s, T, mo, im, st);
+  return (int)e;
+}
+template <class MOD, class SC, class LD, class IM, class ST>
+static int ntt16_inverse(NttTables T, MOD mo, SC sc, LD ld, IM im, ST st, int polys, cudaStream_t s) {
+  cudaError_t e = launch_ntt16(k16_inv_b<MOD, LD, IM>, polys, s, T, mo, ld, im);
+  if (e == cudaSuccess) e = launch_ntt16(k16_inv_a<MOD, SC, IM, ST>, polys, s, T, mo, sc, im, st);
+  return (int)e;
+}
 
 // --------------------------------------------------------------------------------------------- base conversion
 // out_t[n] = sum_{a < w} y_a[n] H[a][mi(t)] mod q_mi(t) for every target t < ntgt of every item, coefficient form.
@@ -171,6 +228,18 @@ struct DigitRows {
   __device__ u64 load(const S& s, int n) const { return s.p[n]; }
   __device__ void store(const S& s, int n, u64 v) const { s.p[n] = v; }
 };
+struct ModDigit {
+  DigitRows d;
+  int cur, L;
+  __device__ int operator()(int p) const {
+    const int r = d.row(p);
+    return r < cur ? r : L + r - cur;
+  }
+};
+struct IMDigit {
+  DigitRows d;
+  __device__ u64* at(int p) const { return d.prep(p).p; }
+};
 template <int LOGN>
 __global__ void HOLMES_NTT_BOUNDS(LOGN) k_digit_ntt(NttTables T, DigitRows d, int cur, int L) {
   const int p = blockIdx.x / NttGeom<LOGN>::CL;
@@ -203,6 +272,10 @@ int ntt_plain(const HolmesCtx& c, const u64* src, u64* dst, PolyMap pm, int poly
   NttTables T{inverse ? c.d_itw : c.d_tw, c.d_mod};
   LdPlain ld{src, pm};
   StPlain sp{dst, pm};
+  if (c.log_n == 16) {
+    return inverse ? ntt16_inverse(T, ModPlain{pm}, ScLimb{c.d_ninv, 0, pm}, ld, IMPlain{dst, pm}, sp, polys, st)
+                   : ntt16_forward(T, ModPlain{pm}, ld, IMPlain{dst, pm}, sp, polys, st);
+  }
 #define L_(LG)                                                                                                   \
   {                                                                                                              \
     using G = NttGeom<LG>;                                                                                       \
@@ -230,6 +303,11 @@ int modup(const HolmesCtx& c, const u64* c1, long long c1_item, int cur, int ite
     PolyMap ps = poly_map(cur, y_item, N, 0);
     LdPlain ld{c1, pm};
     StPlain sp{scratch, ps};
+    if (c.log_n == 16) {
+      const int e = ntt16_inverse(T, ModPlain{pm}, ScLimb{c.mu_scale(cur), 1, pm}, ld, IMPlain{scratch, ps}, sp,
+                                  items * cur, st);
+      if (e) return e;
+    } else {
 #define L_(LG)                                                                                                     \
   {                                                                                                                \
     using G = NttGeom<LG>;                                                                                         \
@@ -238,8 +316,9 @@ int modup(const HolmesCtx& c, const u64* c1, long long c1_item, int cur, int ite
     if (e != cudaSuccess) return (int)e;                                                                           \
     break;                                                                                                         \
   }
-    HOLMES_LOGN_SWITCH(c.log_n, L_)
+      HOLMES_LOGN_SWITCH(c.log_n, L_)
 #undef L_
+    }
   }
   const int beta = c.beta(cur);
   const size_t dstride = (size_t)(cur + K) * N;
@@ -257,6 +336,11 @@ int modup(const HolmesCtx& c, const u64* c1, long long c1_item, int cur, int ite
     }
     DigitRows dr{dj, dig_item, lo, w, ntgt, c.log_n};
     const int polys = items * ntgt;
+    if (c.log_n == 16) {
+      const int e = ntt16_forward(T, ModDigit{dr, cur, c.L}, dr, IMDigit{dr}, dr, polys, st);
+      if (e) return e;
+      continue;
+    }
 #define L_(LG)                                                                                                   \
   {                                                                                                              \
     using G = NttGeom<LG>;                                                                                       \
@@ -309,6 +393,19 @@ struct StScratch {
   struct S { u64* p; };
   __device__ S prep(int p) const { return S{dst + ((size_t)p << log_n)}; }
   __device__ void store(const S& s, int n, u64 v) const { s.p[n] = v; }
+};
+struct ModKsP {
+  int L, K;
+  __device__ int operator()(int p) const { return L + (p % (2 * K)) % K; }
+};
+struct ScKsP {
+  const Tw* md_scale;
+  int K;
+  __device__ Tw operator()(int p) const { return md_scale[(p % (2 * K)) % K]; }
+};
+struct ModKsQ {
+  int cur;
+  __device__ int operator()(int p) const { return (p % (2 * cur)) % cur; }
 };
 template <int LOGN>
 __global__ void HOLMES_NTT_BOUNDS(LOGN) k_ks_p(NttTables T, const Tw* md_scale, LdKsP ld,
@@ -391,6 +488,10 @@ int ks_apply(const HolmesCtx& c, const KsArgs& a, cudaStream_t st) {
     LdKsP ld{a.digits, a.dig_item, a.key, c.d_mod, g, a.cur, a.key_cap, K, c.L, beta, key_beta, c.log_n};
     StScratch ss{a.scratch, c.log_n};
     const int polys = a.items * 2 * K;
+    if (c.log_n == 16) {
+      const int e = ntt16_inverse(T, ModKsP{c.L, K}, ScKsP{c.d_md_scale, K}, ld, IMRows{a.scratch}, ss, polys, st);
+      if (e) return e;
+    } else {
 #define L_(LG)                                                                                              \
   {                                                                                                         \
     using G = NttGeom<LG>;                                                                                  \
@@ -398,8 +499,9 @@ int ks_apply(const HolmesCtx& c, const KsArgs& a, cudaStream_t st) {
     if (e != cudaSuccess) return (int)e;                                                                    \
     break;                                                                                                  \
   }
-    HOLMES_LOGN_SWITCH(c.log_n, L_)
+      HOLMES_LOGN_SWITCH(c.log_n, L_)
 #undef L_
+    }
   }
   u64* conv = a.scratch + (size_t)a.items * 2 * K * c.n;  // [items][2][cur][N], coefficient form
   {
@@ -414,6 +516,7 @@ int ks_apply(const HolmesCtx& c, const KsArgs& a, cudaStream_t st) {
     StKsQ sq{a.digits, a.dig_item, a.key, a.add0, a.add1, a.add_item, a.post0, a.post1, a.post_item, a.out0, a.out1,
              a.out_item, c.d_mod, g, a.cur, a.key_cap, K, beta, key_beta, c.log_n};
     const int polys = a.items * 2 * a.cur;
+    if (c.log_n == 16) return ntt16_forward(T, ModKsQ{a.cur}, ld, IMRows{conv}, sq, polys, st);
 #define L_(LG)                                                                                        \
   {                                                                                                   \
     using G = NttGeom<LG>;                                                                            \
@@ -642,6 +745,10 @@ struct LdRounded {
     }
   }
 };
+struct ModEnc {
+  int first, w;
+  __device__ int operator()(int p) const { return first + p % w; }
+};
 template <int LOGN, bool WIDE>
 __global__ void HOLMES_NTT_BOUNDS(LOGN) k_encode(NttTables T, LdRounded<WIDE> ld, StPlain st) {
   const int p = blockIdx.x / NttGeom<LOGN>::CL;
@@ -677,6 +784,14 @@ int encode_rows(const HolmesCtx& c, const double* u, long long row_stride, int r
     PolyMap pm = poly_map(last - first, out_row_stride, c.n, 0);
     StPlain sp{out + (size_t)first * c.n, pm};
     const int polys = rows * (last - first);
+    if (c.log_n == 16) {
+      const int e = wide ? ntt16_forward(T, ModEnc{first, last - first}, lw, IMPlain{out + (size_t)first * c.n, pm}, sp,
+                                         polys, st)
+                         : ntt16_forward(T, ModEnc{first, last - first}, ln, IMPlain{out + (size_t)first * c.n, pm}, sp,
+                                         polys, st);
+      if (e) return e;
+      continue;
+    }
 #define L_(LG)                                                                                                   \
   {                                                                                                              \
     using G = NttGeom<LG>;                                                                                       \
