@@ -8,7 +8,7 @@
 //
 // These are exactly the rounds, pairs and roots of ntt_forward_body / ntt_inverse_body (ntt.cuh), so the results
 // are word for word the same; only the schedule differs.  Each pass is its own launch of 16 CTAs per polynomial
-// (256 threads, 16 columns or 16 rows of 256 words, 32 KB of shared memory, four CTAs per SM), with no
+// (256 threads, 16 columns or 16 rows of 256 words, 32 KB of shared memory, three CTAs per SM), with no
 // cluster: an 8-CTA cluster of the one-launch NTT cannot tile a GPC's SMs and leaves about a tenth of the B200's
 // CTA slots idle, and it needs two cluster-wide barriers plus four shared-memory passes where this needs two or
 // three block barriers per pass.  The price is one extra round trip of the polynomial between the passes, written
@@ -28,9 +28,11 @@ struct Ntt16 {
   static constexpr int THREADS = 256;
   static constexpr int CTAS = 16;          // per polynomial and pass
   static constexpr int SMEM = 4096 * 8;    // 16 x 256 words
-  static constexpr int MINB = 3;
+#ifndef HOLMES_NTT16_MINB
+#define HOLMES_NTT16_MINB 3
+#endif
+  static constexpr int MINB = HOLMES_NTT16_MINB;  // resident CTAs per SM asked of the register allocator (3: 80 registers)
 };
-#define HOLMES_NTT16_BOUNDS __launch_bounds__(Ntt16::THREADS, Ntt16::MINB)
 
 // tile index of (row-in-tile r, word w < 256) for the row passes: the low 4 bits of w are XORed with its bits 4..7
 __device__ __forceinline__ int rsw(int r, int w) { return (r << 8) | (w ^ ((w >> 4) & 15)); }

@@ -79,39 +79,44 @@ struct ScLimb {  // scale[limb of p] or scale[modulus of p]
   PolyMap pm;
   __device__ Tw operator()(int p) const { return scale[by_limb ? p % pm.limbs : pm.mod(p)]; }
 };
-template <class MOD, class LD, class IM>
-__global__ void HOLMES_NTT16_BOUNDS k16_fwd_a(NttTables T, MOD mo, LD ld, IM im) {
+template <int MINB, class MOD, class LD, class IM>
+__global__ void __launch_bounds__(Ntt16::THREADS, MINB) k16_fwd_a(NttTables T, MOD mo, LD ld, IM im) {
   const int p = blockIdx.x >> 4;
   fwd16_cols(p, blockIdx.x & 15, mo(p), T, ld, im.at(p));
 }
-template <class MOD, class IM, class ST>
-__global__ void HOLMES_NTT16_BOUNDS k16_fwd_b(NttTables T, MOD mo, IM im, ST st) {
+template <int MINB, class MOD, class IM, class ST>
+__global__ void __launch_bounds__(Ntt16::THREADS, MINB) k16_fwd_b(NttTables T, MOD mo, IM im, ST st) {
   const int p = blockIdx.x >> 4;
   fwd16_rows(p, blockIdx.x & 15, mo(p), T, im.at(p), st);
 }
-template <class MOD, class LD, class IM>
-__global__ void HOLMES_NTT16_BOUNDS k16_inv_b(NttTables T, MOD mo, LD ld, IM im) {
+template <int MINB, class MOD, class LD, class IM>
+__global__ void __launch_bounds__(Ntt16::THREADS, MINB) k16_inv_b(NttTables T, MOD mo, LD ld, IM im) {
   const int p = blockIdx.x >> 4;
   inv16_rows(p, blockIdx.x & 15, mo(p), T, ld, im.at(p));
 }
-template <class MOD, class SC, class IM, class ST>
-__global__ void HOLMES_NTT16_BOUNDS k16_inv_a(NttTables T, MOD mo, SC sc, IM im, ST st) {
+template <int MINB, class MOD, class SC, class IM, class ST>
+__global__ void __launch_bounds__(Ntt16::THREADS, MINB) k16_inv_a(NttTables T, MOD mo, SC sc, IM im, ST st) {
   const int p = blockIdx.x >> 4;
   inv16_cols(p, blockIdx.x & 15, mo(p), sc(p), T, im.at(p), st);
 }
-// forward: ld -> im (pass A), im -> st (pass B); inverse: ld -> im (pass B'), im -> scale -> st (pass A')
-template <class MOD, class LD, class IM, class ST>
+// forward: ld -> im (pass A), im -> st (pass B); inverse: ld -> im (pass B'), im -> scale -> st (pass A').
+// MINB: resident CTAs per SM asked of the register allocator (3: 80 registers; 4: 64).
+template <int MINB = Ntt16::MINB, class MOD, class LD, class IM, class ST>
 static int ntt16_forward(NttTables T, MOD mo, LD ld, IM im, ST st, int polys, cudaStream_t s) {
-  cudaError_t e = launch_ntt16(k16_fwd_a<MOD, LD, IM>, polys, s, T, mo, ld, im);
-  if (e == cudaSuccess) e = launch_ntt16(k16_fwd_b<MOD, IM, ST>, polys, s, T, mo, im, st);
+  cudaError_t e = launch_ntt16(k16_fwd_a<MINB, MOD, LD, IM>, polys, s, T, mo, ld, im);
+  if (e == cudaSuccess) e = launch_ntt16(k16_fwd_b<MINB, MOD, IM, ST>, polys, s, T, mo, im, st);
   return (int)e;
 }
-template <class MOD, class SC, class LD, class IM, class ST>
+template <int MINB = Ntt16::MINB, class MOD, class SC, class LD, class IM, class ST>
 static int ntt16_inverse(NttTables T, MOD mo, SC sc, LD ld, IM im, ST st, int polys, cudaStream_t s) {
-  cudaError_t e = launch_ntt16(k16_inv_b<MOD, LD, IM>, polys, s, T, mo, ld, im);
-  if (e == cudaSuccess) e = launch_ntt16(k16_inv_a<MOD, SC, IM, ST>, polys, s, T, mo, sc, im, st);
+  cudaError_t e = launch_ntt16(k16_inv_b<MINB, MOD, LD, IM>, polys, s, T, mo, ld, im);
+  if (e == cudaSuccess) e = launch_ntt16(k16_inv_a<MINB, MOD, SC, IM, ST>, polys, s, T, mo, sc, im, st);
   return (int)e;
 }
+// resident CTAs per SM of the key switch's two-pass NTTs
+#ifndef HOLMES_KS16_MINB
+#define HOLMES_KS16_MINB 4
+#endif
 
 // --------------------------------------------------------------------------------------------- base conversion
 // out_t[n] = sum_{a < w} y_a[n] H[a][mi(t)] mod q_mi(t) for every target t < ntgt of every item, coefficient form.
@@ -489,7 +494,8 @@ int ks_apply(const HolmesCtx& c, const KsArgs& a, cudaStream_t st) {
     StScratch ss{a.scratch, c.log_n};
     const int polys = a.items * 2 * K;
     if (c.log_n == 16) {
-      const int e = ntt16_inverse(T, ModKsP{c.L, K}, ScKsP{c.d_md_scale, K}, ld, IMRows{a.scratch}, ss, polys, st);
+      const int e = ntt16_inverse<HOLMES_KS16_MINB>(T, ModKsP{c.L, K}, ScKsP{c.d_md_scale, K}, ld, IMRows{a.scratch},
+                                                    ss, polys, st);
       if (e) return e;
     } else {
 #define L_(LG)                                                                                              \
@@ -516,7 +522,7 @@ int ks_apply(const HolmesCtx& c, const KsArgs& a, cudaStream_t st) {
     StKsQ sq{a.digits, a.dig_item, a.key, a.add0, a.add1, a.add_item, a.post0, a.post1, a.post_item, a.out0, a.out1,
              a.out_item, c.d_mod, g, a.cur, a.key_cap, K, beta, key_beta, c.log_n};
     const int polys = a.items * 2 * a.cur;
-    if (c.log_n == 16) return ntt16_forward(T, ModKsQ{a.cur}, ld, IMRows{conv}, sq, polys, st);
+    if (c.log_n == 16) return ntt16_forward<HOLMES_KS16_MINB>(T, ModKsQ{a.cur}, ld, IMRows{conv}, sq, polys, st);
 #define L_(LG)                                                                                        \
   {                                                                                                   \
     using G = NttGeom<LG>;                                                                            \
