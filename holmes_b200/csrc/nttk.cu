@@ -8,10 +8,10 @@
 //                                 P^-1 mod q_i of the later ModDown (own limbs: c1 * P^-1; converted
 //                                 limbs: constants (Q_j/q_k) P^-1 mod q_i), so it is paid once per ModUp
 //                                 rather than once per key switch of a hoisted set
-//   key switch (hybrid, ModDown)  P limbs: inner product (digits through the automorphism) fused into
-//                                 the iNTT with N^-1 (P/p_k)^-1; Q limbs: base conversion P->q_i with
-//                                 constants p_k^-1 mod q_i (k_conv), then the NTT with inner product -
-//                                 conversion + automorphed addend fused into its store
+//   key switch (hybrid, ModDown)  inner products of every Q and P limb, both components, digits through the
+//                                 automorphism, addends folded in (k_ks_inner, elementwise); P limbs: iNTT
+//                                 with N^-1 (P/p_k)^-1; base conversion P->q_i with constants p_k^-1 mod q_i
+//                                 (k_conv); Q limbs: NTT with "out -= conversion" fused into its store
 //   The base conversions run as their own elementwise pass: one thread keeps a coefficient's source
 //   words in registers for every target limb, where the NTT's load phase (fused before) recomputed its
 //   splits per target and stalled on 8 scattered loads per word with few registers to spare.
@@ -115,7 +115,7 @@ static int ntt16_inverse(NttTables T, MOD mo, SC sc, LD ld, IM im, ST st, int po
 }
 // resident CTAs per SM of the key switch's two-pass NTTs
 #ifndef HOLMES_KS16_MINB
-#define HOLMES_KS16_MINB 4
+#define HOLMES_KS16_MINB 3
 #endif
 
 // --------------------------------------------------------------------------------------------- base conversion
@@ -360,38 +360,71 @@ int modup(const HolmesCtx& c, const u64* c1, long long c1_item, int cur, int ite
 }
 
 // --------------------------------------------------------------------------------------------- key switch
-// P limbs: acc_c[k][n] = sum_j D_j[cur + k][perm(n)] key_c[j][cap + k][n]
-struct LdKsP {
+// Inner products, one thread per (item, limb r of Q u P, word n) and both components at once (each digit word is
+// read once): acc_c = sum_j D_j[r][perm(n)] key_c[j][r'][n], r' = r (Q limb) or cap + k (special limb k = r - cur).
+//   Q limbs:  out_c[r][n] = acc_c + perm(add_c)[r][n] + post_c[r][n] (mod q_r); the digits' Q rows carry P^-1,
+//             so after the ModDown NTT below subtracts its conversion this is the key-switched ciphertext.
+//   P limbs:  scratch[item][c][k][n] = acc_c mod p_k, the input of the ModDown inverse NTT.
+// The memory-latency-bound loads run here, at full occupancy, instead of inside the NTTs' loads and stores.
+struct KsInnerArgs {
   const u64* digits;
   long long dig_item;
   const u64* key;
-  const Mod* mods;
+  const u64* add0;
+  const u64* add1;
+  long long add_item;
+  const u64* post0;
+  const u64* post1;
+  long long post_item;
+  u64* out0;
+  u64* out1;
+  long long out_item;
+  u64* pscratch;  // [items][2][K][N]
   u64 galois;
-  int cur, cap, K, L, beta, key_beta, log_n;
-  struct S {
-    const u64* d;
-    const u64* k;
-    Mod m;
-  };
-  __device__ S prep(int p) const {
-    const int item = p / (2 * K), r = p % (2 * K), c = r / K, k = r % K;
-    S s;
-    s.d = digits + item * dig_item + ((size_t)(cur + k) << log_n);
-    s.k = key + ((((size_t)c * key_beta) * (cap + K) + cap + k) << log_n);
-    s.m = mods[L + k];
-    return s;
-  }
-  // a representative below 4 q (the inverse NTT's input range)
-  __device__ u64 load(const S& s, int n) const {
-    const u32 src = galois > 1 ? automorph_src((u32)n, galois, log_n) : (u32)n;
-    const size_t dstep = ((size_t)(cur + K)) << log_n, kstep = ((size_t)(cap + K)) << log_n;
-    Split4 acc{0, 0, 0, 0};
-#pragma unroll 4
-    for (int j = 0; j < beta; ++j) split_mac(acc, s.d[j * dstep + src], s.k[j * kstep + n]);
-    const u64 r = fold_split_lazy(acc, s.m), q4 = s.m.q << 2;
-    return r >= q4 ? r - q4 : r;
-  }
+  int cur, cap, K, L, beta, key_beta, items;
 };
+__global__ void __launch_bounds__(256) k_ks_inner(KsInnerArgs a, int log_n, const Mod* __restrict__ mods) {
+  const int N = 1 << log_n, rows = a.cur + a.K;
+  const size_t total = ((size_t)a.items * rows) << log_n;
+  const size_t dstep = (size_t)rows << log_n, kstep = (size_t)(a.cap + a.K) << log_n;
+  const size_t kcomp = (size_t)a.key_beta * kstep;
+  for (size_t g = blockIdx.x * (size_t)blockDim.x + threadIdx.x; g < total; g += (size_t)gridDim.x * blockDim.x) {
+    const int n = (int)(g & (N - 1));
+    const size_t ir = g >> log_n;
+    const int r = (int)(ir % rows), item = (int)(ir / rows);
+    const u32 src = a.galois > 1 ? automorph_src((u32)n, a.galois, log_n) : (u32)n;
+    const bool qlimb = r < a.cur;
+    const int kr = qlimb ? r : a.cap + (r - a.cur);
+    const u64* d = a.digits + item * a.dig_item + ((size_t)r << log_n) + src;
+    const u64* k0 = a.key + ((size_t)kr << log_n) + n;
+    Split4 s0{0, 0, 0, 0}, s1{0, 0, 0, 0};
+#pragma unroll 4
+    for (int j = 0; j < a.beta; ++j) {
+      const u64 dv = d[j * dstep];
+      split_mac(s0, dv, k0[j * kstep]);
+      split_mac(s1, dv, k0[kcomp + j * kstep]);
+    }
+    if (qlimb) {
+      const Mod m = mods[r];
+      u64 u0 = fold_split(s0, m), u1 = fold_split(s1, m);
+      const size_t ao = item * a.add_item + ((size_t)r << log_n);
+      if (a.add0) u0 = add_mod(u0, a.add0[ao + src], m.q);
+      if (a.add1) u1 = add_mod(u1, a.add1[ao + src], m.q);
+      const size_t po = item * a.post_item + ((size_t)r << log_n) + n;
+      if (a.post0) u0 = add_mod(u0, a.post0[po], m.q);
+      if (a.post1) u1 = add_mod(u1, a.post1[po], m.q);
+      const size_t oo = item * a.out_item + ((size_t)r << log_n) + n;
+      a.out0[oo] = u0;
+      a.out1[oo] = u1;
+    } else {
+      const int k = r - a.cur;
+      const Mod m = mods[a.L + k];
+      u64* ps = a.pscratch + (((size_t)item * 2 * a.K + k) << log_n) + n;
+      ps[0] = fold_split(s0, m);
+      ps[(size_t)a.K << log_n] = fold_split(s1, m);
+    }
+  }
+}
 struct StScratch {
   u64* dst;
   int log_n;
@@ -399,6 +432,45 @@ struct StScratch {
   __device__ S prep(int p) const { return S{dst + ((size_t)p << log_n)}; }
   __device__ void store(const S& s, int n, u64 v) const { s.p[n] = v; }
 };
+// ModDown, P limbs: scratch [items][2][K][N] in place, iNTT * N^-1 (P/p_k)^-1
+template <int LOGN>
+__global__ void HOLMES_NTT_BOUNDS(LOGN) k_ks_p(NttTables T, const Tw* md_scale, int L, int K, LdRows ld,
+                                              StScratch st) {
+  const int p = blockIdx.x / NttGeom<LOGN>::CL;
+  const int k = (p % (2 * K)) % K;
+  ntt_inverse_body<LOGN>(p, L + k, md_scale[k], T, ld, st);
+}
+
+// ModDown, Q limbs: conv_c[i] = NTT(sum_k y_c[k] p_k^-1 mod q_i) (k_conv, then a plain-load NTT); the store
+// subtracts it from what k_ks_inner left in out_c: out = inner + perm(add) + post - conv.  With the inner product
+// over the digits' P^-1-scaled Q rows, that is (inner - sum_k y_k (P/p_k)) P^-1 + perm(add) + post, the ModDown.
+struct StKsSub {
+  u64* out0;
+  u64* out1;
+  long long out_item;
+  const Mod* mods;
+  int cur, log_n;
+  struct S {
+    u64* o;
+    u64 q;
+  };
+  __device__ S prep(int p) const {
+    const int item = p / (2 * cur), r = p % (2 * cur), c = r / cur, i = r % cur;
+    return S{(c ? out1 : out0) + item * out_item + ((size_t)i << log_n), mods[i].q};
+  }
+  __device__ void store(const S& s, int n, u64 v) const { s.o[n] = sub_mod(s.o[n], v, s.q); }
+};
+// resident CTAs per SM for the key-switch NTTs (their stores read as well as write)
+#ifndef HOLMES_KS_MINB
+#define HOLMES_KS_MINB HOLMES_NTT_MINB
+#endif
+template <int LOGN>
+__global__ void __launch_bounds__(NttGeom<LOGN>::THREADS, HOLMES_KS_MINB) k_ks_q(NttTables T, LdRows ld,
+                                                                                   StKsSub st) {
+  const int p = blockIdx.x / NttGeom<LOGN>::CL;
+  ntt_forward_body<LOGN>(p, (p % (2 * st.cur)) % st.cur, T, ld, st);
+}
+
 struct ModKsP {
   int L, K;
   __device__ int operator()(int p) const { return L + (p % (2 * K)) % K; }
@@ -412,75 +484,6 @@ struct ModKsQ {
   int cur;
   __device__ int operator()(int p) const { return (p % (2 * cur)) % cur; }
 };
-template <int LOGN>
-__global__ void HOLMES_NTT_BOUNDS(LOGN) k_ks_p(NttTables T, const Tw* md_scale, LdKsP ld,
-                                                                  StScratch st) {
-  const int p = blockIdx.x / NttGeom<LOGN>::CL;
-  const int k = (p % (2 * ld.K)) % ld.K;
-  ntt_inverse_body<LOGN>(p, ld.L + k, md_scale[k], T, ld, st);
-}
-
-// Q limbs: conv_c[i] = NTT(sum_k y_c[k] p_k^-1 mod q_i) (k_conv, then a plain-load NTT); out = inner - conv
-// + perm(add) + post, where inner (over the digits' Q rows, which carry P^-1) is already P^-1 times the
-// hybrid inner product: together (inner - sum_k y_k (P/p_k)) P^-1, the ModDown.
-struct StKsQ {
-  const u64* digits;
-  long long dig_item;
-  const u64* key;
-  const u64* add0;
-  const u64* add1;
-  long long add_item;
-  const u64* post0;
-  const u64* post1;
-  long long post_item;
-  u64* out0;
-  u64* out1;
-  long long out_item;
-  const Mod* mods;
-  u64 galois;
-  int cur, cap, K, beta, key_beta, log_n;
-  struct S {
-    const u64* d;
-    const u64* k;
-    const u64* a;
-    const u64* pa;
-    u64* o;
-    Mod m;
-  };
-  __device__ S prep(int p) const {
-    const int item = p / (2 * cur), r = p % (2 * cur), c = r / cur, i = r % cur;
-    S s;
-    s.d = digits + item * dig_item + ((size_t)i << log_n);
-    s.k = key + ((((size_t)c * key_beta) * (cap + K) + i) << log_n);
-    const u64* add = c ? add1 : add0;
-    s.a = add ? add + item * add_item + ((size_t)i << log_n) : nullptr;
-    const u64* post = c ? post1 : post0;
-    s.pa = post ? post + item * post_item + ((size_t)i << log_n) : nullptr;
-    s.o = (c ? out1 : out0) + item * out_item + ((size_t)i << log_n);
-    s.m = mods[i];
-    return s;
-  }
-  __device__ void store(const S& s, int n, u64 v) const {
-    const u32 src = galois > 1 ? automorph_src((u32)n, galois, log_n) : (u32)n;
-    const size_t dstep = ((size_t)(cur + K)) << log_n, kstep = ((size_t)(cap + K)) << log_n;
-    Split4 acc{0, 0, 0, 0};
-#pragma unroll 4
-    for (int j = 0; j < beta; ++j) split_mac(acc, s.d[j * dstep + src], s.k[j * kstep + n]);
-    u64 r = sub_mod(fold_split(acc, s.m), v, s.m.q);
-    if (s.a) r = add_mod(r, s.a[src], s.m.q);
-    if (s.pa) r = add_mod(r, s.pa[n], s.m.q);
-    s.o[n] = r;
-  }
-};
-// resident CTAs per SM for the key-switch NTTs (their fused loads / stores hold more state than a plain NTT)
-#ifndef HOLMES_KS_MINB
-#define HOLMES_KS_MINB HOLMES_NTT_MINB
-#endif
-template <int LOGN>
-__global__ void __launch_bounds__(NttGeom<LOGN>::THREADS, HOLMES_KS_MINB) k_ks_q(NttTables T, LdRows ld, StKsQ st) {
-  const int p = blockIdx.x / NttGeom<LOGN>::CL;
-  ntt_forward_body<LOGN>(p, (p % (2 * st.cur)) % st.cur, T, ld, st);
-}
 
 int ks_apply(const HolmesCtx& c, const KsArgs& a, cudaStream_t st) {
   if (a.cur < 1 || a.cur > a.key_cap || a.key_cap > c.L) return -2;
@@ -489,8 +492,18 @@ int ks_apply(const HolmesCtx& c, const KsArgs& a, cudaStream_t st) {
   const int beta = c.beta(a.cur), key_beta = c.beta(a.key_cap), K = c.K;
   const u64 g = a.galois <= 1 ? 1 : a.galois;
   {
+    KsInnerArgs ia{a.digits, a.dig_item, a.key, a.add0, a.add1, a.add_item, a.post0, a.post1, a.post_item, a.out0,
+                   a.out1, a.out_item, a.scratch, g, a.cur, a.key_cap, K, c.L, beta, key_beta, a.items};
+    const size_t work = ((size_t)a.items * (a.cur + K)) << c.log_n;
+    size_t blocks = (work + 255) / 256;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    count_launch();
+    k_ks_inner<<<(unsigned)blocks, 256, 0, st>>>(ia, c.log_n, c.d_mod);
+    HOLMES_CUDA_TRY(cudaGetLastError());
+  }
+  {
     NttTables T{c.d_itw, c.d_mod};
-    LdKsP ld{a.digits, a.dig_item, a.key, c.d_mod, g, a.cur, a.key_cap, K, c.L, beta, key_beta, c.log_n};
+    LdRows ld{a.scratch, c.log_n};
     StScratch ss{a.scratch, c.log_n};
     const int polys = a.items * 2 * K;
     if (c.log_n == 16) {
@@ -498,12 +511,13 @@ int ks_apply(const HolmesCtx& c, const KsArgs& a, cudaStream_t st) {
                                                     ss, polys, st);
       if (e) return e;
     } else {
-#define L_(LG)                                                                                              \
-  {                                                                                                         \
-    using G = NttGeom<LG>;                                                                                  \
-    cudaError_t e = launch_ntt(k_ks_p<LG>, G::LOGCL, G::THREADS, G::SMEM, polys, st, T, c.d_md_scale, ld, ss); \
-    if (e != cudaSuccess) return (int)e;                                                                    \
-    break;                                                                                                  \
+#define L_(LG)                                                                                                   \
+  {                                                                                                              \
+    using G = NttGeom<LG>;                                                                                       \
+    cudaError_t e = launch_ntt(k_ks_p<LG>, G::LOGCL, G::THREADS, G::SMEM, polys, st, T, c.d_md_scale, c.L, K, ld, \
+                               ss);                                                                              \
+    if (e != cudaSuccess) return (int)e;                                                                         \
+    break;                                                                                                       \
   }
       HOLMES_LOGN_SWITCH(c.log_n, L_)
 #undef L_
@@ -519,8 +533,7 @@ int ks_apply(const HolmesCtx& c, const KsArgs& a, cudaStream_t st) {
   {
     NttTables T{c.d_tw, c.d_mod};
     LdRows ld{conv, c.log_n};
-    StKsQ sq{a.digits, a.dig_item, a.key, a.add0, a.add1, a.add_item, a.post0, a.post1, a.post_item, a.out0, a.out1,
-             a.out_item, c.d_mod, g, a.cur, a.key_cap, K, beta, key_beta, c.log_n};
+    StKsSub sq{a.out0, a.out1, a.out_item, c.d_mod, a.cur, c.log_n};
     const int polys = a.items * 2 * a.cur;
     if (c.log_n == 16) return ntt16_forward<HOLMES_KS16_MINB>(T, ModKsQ{a.cur}, ld, IMRows{conv}, sq, polys, st);
 #define L_(LG)                                                                                        \
