@@ -231,6 +231,21 @@ int build_context(HolmesCtx& c, int log_n, int limbs, int dnum, int dcrt_bits, i
   if ((rc = upload(c, &c.d_unit_neg, unit_neg))) return rc;
   if ((rc = upload(c, &c.d_rot_group, rot))) return rc;
   if ((rc = upload(c, &c.d_ksi, ksi))) return rc;
+  {
+    // root of butterfly j of special-FFT stage len: ksi[(4 len - rot[j] mod 4 len) M / (4 len)], gathered once
+    // here so the FFT reads it in j order instead of through two dependent random lookups
+    const u64 M = 2ULL * N;
+    std::vector<double> ftw((size_t)N);  // (N/2 - 1) complex roots, padded to N doubles
+    for (int len = 2; len <= N / 2; len <<= 1) {
+      const u64 lenq = (u64)len << 2;
+      for (int j = 0; j < len / 2; ++j) {
+        const u64 k = (lenq - (rot[j] & (lenq - 1))) * (M / lenq);
+        ftw[2 * ((size_t)len / 2 - 1 + j)] = ksi[2 * k];
+        ftw[2 * ((size_t)len / 2 - 1 + j) + 1] = ksi[2 * k + 1];
+      }
+    }
+    if ((rc = upload(c, &c.d_fft_tw, ftw))) return rc;
+  }
   std::vector<u64> zeros((size_t)T * N, 0);
   if ((rc = upload(c, &c.d_secret, zeros))) return rc;
   return 0;

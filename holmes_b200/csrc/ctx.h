@@ -36,6 +36,7 @@ struct HolmesCtx {
   Tw* d_unit_neg = nullptr;      // [T] q - psi^(N/2)
   u64* d_rot_group = nullptr;    // [N/2] 5^j mod 2N
   double* d_ksi = nullptr;       // [2N][2] cos/sin(2 pi k / 2N)
+  double* d_fft_tw = nullptr;    // [N/2 - 1][2] special-FFT roots by stage: stage len at len/2 - 1 + j
   u64* d_secret = nullptr;       // [T][N] secret key, NTT form (client side of the simulation context)
   std::vector<void*> owned;
 

@@ -629,24 +629,61 @@ int bsgs_mac(ModSrc ms, u64* res, const u64* const* c0s, const u64* const* c1s,
 // butterfly sweeps len = slots .. 2 with twiddle ksi[(4 len - rot[j] mod 4 len) * M / (4 len)], then
 // bit reversal and a 1 / slots scale.  Every double operation is written out with _rn intrinsics in
 // the same order as the CPU restatement, so both produce identical bits.
-__global__ void k_fft_special_inv(double* __restrict__ z, long long row_stride, int slots, int log_slots,
-                                  const u64* __restrict__ rot, const double* __restrict__ ksi, u64 M) {
+// One butterfly of stage `len` on the pair (x, x + len / 2), x the lower index: j = x mod len / 2, root
+// ksi[(4 len - rot[j] mod 4 len) M / (4 len)], read from the per-stage table (context.cu).
+__device__ __forceinline__ void fft_bfly(double2& a, double2& b, int j, int len, const double2* __restrict__ ftw) {
+  const double2 w = ftw[(len >> 1) - 1 + j];
+  const double wr = w.x, wi = w.y;
+  const double ur = __dadd_rn(a.x, b.x), ui = __dadd_rn(a.y, b.y);
+  const double vr = __dsub_rn(a.x, b.x), vi = __dsub_rn(a.y, b.y);
+  const double p1 = __dmul_rn(vr, wr), p2 = __dmul_rn(vi, wi), p3 = __dmul_rn(vr, wi), p4 = __dmul_rn(vi, wr);
+  a = make_double2(ur, ui);
+  b = make_double2(__dsub_rn(p1, p2), __dadd_rn(p3, p4));
+}
+// One CTA per row.  Stages whose pairs lie more than kFftBlock apart run first as one pass over global memory
+// (each thread takes the 2^G elements x0 + m kFftBlock, G <= 3, through all G of them); then each block of
+// kFftBlock consecutive elements is staged in shared memory for the remaining stages (they stay inside it), and
+// the bit reversal with the 1 / slots scale ends the row.  Same butterflies in the same stage order as the
+// one-sweep-per-stage form, so the same bits.
+constexpr int kFftBlock = 4096;  // complex elements: 64 KB of shared memory
+__global__ void __launch_bounds__(512) k_fft_special_inv(double* __restrict__ z, long long row_stride, int slots,
+                                                         int log_slots, const double2* __restrict__ ftw) {
+  extern __shared__ double2 fb[];
   double2* r = reinterpret_cast<double2*>(z + blockIdx.x * row_stride);
-  for (int len = slots; len >= 2; len >>= 1) {
-    const int half = len >> 1;
-    const u64 lenq = (u64)len << 2, stride = M / lenq;
-    for (int t = threadIdx.x; t < slots / 2; t += blockDim.x) {
-      const int j = t & (half - 1);
-      const int i = (t / half) * len;
-      const u64 k = (lenq - (rot[j] & (lenq - 1))) * stride;
-      const double2 a = r[i + j], b = r[i + j + half];
-      const double wr = ksi[2 * k], wi = ksi[2 * k + 1];
-      const double ur = __dadd_rn(a.x, b.x), ui = __dadd_rn(a.y, b.y);
-      const double vr = __dsub_rn(a.x, b.x), vi = __dsub_rn(a.y, b.y);
-      const double p1 = __dmul_rn(vr, wr), p2 = __dmul_rn(vi, wi), p3 = __dmul_rn(vr, wi), p4 = __dmul_rn(vi, wr);
-      r[i + j] = make_double2(ur, ui);
-      r[i + j + half] = make_double2(__dsub_rn(p1, p2), __dadd_rn(p3, p4));
+  const int bs = slots < kFftBlock ? slots : kFftBlock;
+  // global stages: len = slots .. 2 bs
+  if (slots > bs) {
+    const int G = log_slots - 12;  // 1..3 (slots <= 2^15)
+    const int groups = slots >> G;  // = bs
+    for (int x0 = threadIdx.x; x0 < groups; x0 += blockDim.x) {
+      double2 v[8];
+      for (int m = 0; m < (1 << G); ++m) v[m] = r[x0 + m * bs];
+      for (int g = G - 1; g >= 0; --g) {  // len = bs 2^(g+1), pairs m, m + 2^g
+        const int len = bs << (g + 1), half = len >> 1;
+        for (int m = 0; m < (1 << G); ++m) {
+          if (m & (1 << g)) continue;
+          const int x = x0 + m * bs;
+          fft_bfly(v[m], v[m + (1 << g)], x & (half - 1), len, ftw);
+        }
+      }
+      for (int m = 0; m < (1 << G); ++m) r[x0 + m * bs] = v[m];
     }
+    __syncthreads();
+  }
+  // block stages: len = bs .. 2 inside each block of bs elements
+  for (int base = 0; base < slots; base += bs) {
+    for (int i = threadIdx.x; i < bs; i += blockDim.x) fb[i] = r[base + i];
+    __syncthreads();
+    for (int len = bs; len >= 2; len >>= 1) {
+      const int half = len >> 1;
+      for (int t = threadIdx.x; t < bs / 2; t += blockDim.x) {
+        const int j = t & (half - 1);
+        const int i = (t / half) * len;
+        fft_bfly(fb[i + j], fb[i + j + half], j, len, ftw);
+      }
+      __syncthreads();
+    }
+    for (int i = threadIdx.x; i < bs; i += blockDim.x) r[base + i] = fb[i];
     __syncthreads();
   }
   const double inv = 1.0 / (double)slots;
@@ -665,13 +702,17 @@ __global__ void k_fft_special_inv(double* __restrict__ z, long long row_stride, 
 
 int fft_special_inv(const HolmesCtx& c, double* z, long long row_stride, int rows, int slots, cudaStream_t st) {
   if (slots < 2 || slots > c.n / 2 || (slots & (slots - 1))) return -3;
+  if (slots > 8 * kFftBlock) return -3;
   if (rows < 1) return 0;
   int log_slots = 0;
   while ((1 << log_slots) < slots) ++log_slots;
-  const int threads = slots / 2 < 1024 ? (slots / 2 < 32 ? 32 : slots / 2) : 1024;
+  const int bs = slots < kFftBlock ? slots : kFftBlock;
+  const int threads = bs / 2 < 512 ? (bs / 2 < 32 ? 32 : bs / 2) : 512;
+  const size_t smem = (size_t)bs * sizeof(double2);
+  HOLMES_CUDA_TRY(cudaFuncSetAttribute(k_fft_special_inv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   count_launch();
-  k_fft_special_inv<<<rows, threads, 0, st>>>(z, row_stride, slots, log_slots, c.d_rot_group, c.d_ksi,
-                                              2ull * (u64)c.n);
+  k_fft_special_inv<<<rows, threads, smem, st>>>(z, row_stride, slots, log_slots,
+                                                 reinterpret_cast<const double2*>(c.d_fft_tw));
   return (int)cudaGetLastError();
 }
 
