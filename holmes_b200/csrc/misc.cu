@@ -22,9 +22,9 @@ __global__ void k_elementwise(int op, const u64* __restrict__ a, const u64* __re
   const size_t total = (size_t)items * per_item / 2;
   for (size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x; t < total; t += (size_t)gridDim.x * blockDim.x) {
     const size_t w = 2 * t;
-    const int item = (int)(w / per_item);
-    const size_t r = w - (size_t)item * per_item;
-    const int limb = (int)(r >> log_n);
+    const unsigned wl = (unsigned)(w >> log_n);  // item * limbs + limb (32-bit division)
+    const int item = (int)(wl / (unsigned)limbs), limb = (int)(wl - (unsigned)item * limbs);
+    const size_t r = ((size_t)limb << log_n) | (w & (((size_t)1 << log_n) - 1));
     const Mod m = mods[limb];
     const ulonglong2 x = *reinterpret_cast<const ulonglong2*>(a + item * ai + r);
     ulonglong2 y = make_ulonglong2(0, 0);
@@ -58,8 +58,9 @@ __global__ void k_mul_i(const u64* __restrict__ a, u64* __restrict__ o, int item
   const size_t total = (size_t)items * per_item;
   const size_t half = (size_t)1 << (log_n - 1);
   for (size_t w = blockIdx.x * (size_t)blockDim.x + threadIdx.x; w < total; w += (size_t)gridDim.x * blockDim.x) {
-    const int item = (int)(w / per_item);
-    const size_t r = w - (size_t)item * per_item;
+    const unsigned wl = (unsigned)(w >> log_n);  // item * limbs + limb (32-bit division)
+    const int item = (int)(wl / (unsigned)limbs);
+    const size_t r = ((size_t)(wl - (unsigned)item * limbs) << log_n) | (w & (((size_t)1 << log_n) - 1));
     const int limb = (int)(r >> log_n);
     const size_t n = r & (((size_t)1 << log_n) - 1);
     const u64 q = mods[limb].q;
@@ -80,8 +81,9 @@ __global__ void k_automorph(const u64* __restrict__ a, u64* __restrict__ o, u64 
   const size_t per_item = (size_t)limbs << log_n;
   const size_t total = (size_t)items * per_item;
   for (size_t w = blockIdx.x * (size_t)blockDim.x + threadIdx.x; w < total; w += (size_t)gridDim.x * blockDim.x) {
-    const int item = (int)(w / per_item);
-    const size_t r = w - (size_t)item * per_item;
+    const unsigned wl = (unsigned)(w >> log_n);  // item * limbs + limb (32-bit division)
+    const int item = (int)(wl / (unsigned)limbs);
+    const size_t r = ((size_t)(wl - (unsigned)item * limbs) << log_n) | (w & (((size_t)1 << log_n) - 1));
     const size_t row = r >> log_n << log_n;
     const u32 n = (u32)(r - row);
     o[item * oi + r] = a[item * ai + row + automorph_src(n, g, log_n)];
@@ -101,8 +103,9 @@ __global__ void k_mul_const(const u64* __restrict__ a, const u64* __restrict__ k
   const size_t per_item = (size_t)limbs << log_n;
   const size_t total = (size_t)items * per_item;
   for (size_t w = blockIdx.x * (size_t)blockDim.x + threadIdx.x; w < total; w += (size_t)gridDim.x * blockDim.x) {
-    const int item = (int)(w / per_item);
-    const size_t r = w - (size_t)item * per_item;
+    const unsigned wl = (unsigned)(w >> log_n);  // item * limbs + limb (32-bit division)
+    const int item = (int)(wl / (unsigned)limbs);
+    const size_t r = ((size_t)(wl - (unsigned)item * limbs) << log_n) | (w & (((size_t)1 << log_n) - 1));
     const int limb = (int)(r >> log_n);
     o[item * oi + r] = mul_mod(a[item * ai + r], k[limb], mods[limb]);
   }
@@ -120,8 +123,9 @@ __global__ void k_add_const(const u64* __restrict__ a, const u64* __restrict__ k
   const size_t per_item = (size_t)limbs << log_n;
   const size_t total = (size_t)items * per_item;
   for (size_t w = blockIdx.x * (size_t)blockDim.x + threadIdx.x; w < total; w += (size_t)gridDim.x * blockDim.x) {
-    const int item = (int)(w / per_item);
-    const size_t r = w - (size_t)item * per_item;
+    const unsigned wl = (unsigned)(w >> log_n);  // item * limbs + limb (32-bit division)
+    const int item = (int)(wl / (unsigned)limbs);
+    const size_t r = ((size_t)(wl - (unsigned)item * limbs) << log_n) | (w & (((size_t)1 << log_n) - 1));
     const int limb = (int)(r >> log_n);
     o[item * oi + r] = add_mod(a[item * ai + r], k[limb], mods[limb].q);
   }
@@ -756,9 +760,10 @@ __global__ void k_modsum(SrcPtrs s, int nsrc, u64* __restrict__ out, int items, 
   const size_t total = (size_t)items * per_item / 2;
   for (size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x; t < total; t += (size_t)gridDim.x * blockDim.x) {
     const size_t w = 2 * t;
-    const int item = (int)(w / per_item);
-    const size_t r = w - (size_t)item * per_item;
-    const u64 q = mods[r >> log_n].q;
+    const unsigned wl = (unsigned)(w >> log_n);  // item * limbs + limb (32-bit division)
+    const int item = (int)(wl / (unsigned)limbs), limb = (int)(wl - (unsigned)item * limbs);
+    const size_t r = ((size_t)limb << log_n) | (w & (((size_t)1 << log_n) - 1));
+    const u64 q = mods[limb].q;
     const size_t off = item * item_stride + r;
     u64 a = 0, b = 0;
     for (int k = 0; k < nsrc; ++k) {

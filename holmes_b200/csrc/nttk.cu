@@ -383,15 +383,14 @@ struct KsInnerArgs {
   u64 galois;
   int cur, cap, K, L, beta, key_beta, items;
 };
+// grid (N / 256, rows, items): no index division
 __global__ void __launch_bounds__(256) k_ks_inner(KsInnerArgs a, int log_n, const Mod* __restrict__ mods) {
-  const int N = 1 << log_n, rows = a.cur + a.K;
-  const size_t total = ((size_t)a.items * rows) << log_n;
+  const int rows = a.cur + a.K;
   const size_t dstep = (size_t)rows << log_n, kstep = (size_t)(a.cap + a.K) << log_n;
   const size_t kcomp = (size_t)a.key_beta * kstep;
-  for (size_t g = blockIdx.x * (size_t)blockDim.x + threadIdx.x; g < total; g += (size_t)gridDim.x * blockDim.x) {
-    const int n = (int)(g & (N - 1));
-    const size_t ir = g >> log_n;
-    const int r = (int)(ir % rows), item = (int)(ir / rows);
+  {
+    const int n = blockIdx.x * blockDim.x + threadIdx.x;
+    const int r = blockIdx.y, item = blockIdx.z;
     const u32 src = a.galois > 1 ? automorph_src((u32)n, a.galois, log_n) : (u32)n;
     const bool qlimb = r < a.cur;
     const int kr = qlimb ? r : a.cap + (r - a.cur);
@@ -488,17 +487,16 @@ struct ModKsQ {
 int ks_apply(const HolmesCtx& c, const KsArgs& a, cudaStream_t st) {
   if (a.cur < 1 || a.cur > a.key_cap || a.key_cap > c.L) return -2;
   if (c.alpha > MAXA || c.K > MAXA) return -3;
-  if (a.items < 1) return -4;
+  if (a.items < 1 || a.items > 65535) return -4;
   const int beta = c.beta(a.cur), key_beta = c.beta(a.key_cap), K = c.K;
   const u64 g = a.galois <= 1 ? 1 : a.galois;
   {
     KsInnerArgs ia{a.digits, a.dig_item, a.key, a.add0, a.add1, a.add_item, a.post0, a.post1, a.post_item, a.out0,
                    a.out1, a.out_item, a.scratch, g, a.cur, a.key_cap, K, c.L, beta, key_beta, a.items};
-    const size_t work = ((size_t)a.items * (a.cur + K)) << c.log_n;
-    size_t blocks = (work + 255) / 256;
-    if (blocks > 148 * 16) blocks = 148 * 16;
+    if (c.n < 256) return -5;
     count_launch();
-    k_ks_inner<<<(unsigned)blocks, 256, 0, st>>>(ia, c.log_n, c.d_mod);
+    k_ks_inner<<<dim3((unsigned)(c.n / 256), (unsigned)(a.cur + K), (unsigned)a.items), 256, 0, st>>>(ia, c.log_n,
+                                                                                                    c.d_mod);
     HOLMES_CUDA_TRY(cudaGetLastError());
   }
   {
