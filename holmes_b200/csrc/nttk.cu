@@ -383,41 +383,72 @@ struct KsInnerArgs {
   u64 galois;
   int cur, cap, K, L, beta, key_beta, items;
 };
-// grid (N / 256, rows, items): no index division
+// grid (N / 256, rows): a thread takes word n of limb r for every item, so each key word is read (and split)
+// once when beta <= MAXB (MAXB = 0: keys re-read per item, any beta); digits, addends and outputs stream per item
+template <int MAXB>
 __global__ void __launch_bounds__(256) k_ks_inner(KsInnerArgs a, int log_n, const Mod* __restrict__ mods) {
+  constexpr int KB = MAXB > 0 ? MAXB : 1;
   const int rows = a.cur + a.K;
   const size_t dstep = (size_t)rows << log_n, kstep = (size_t)(a.cap + a.K) << log_n;
   const size_t kcomp = (size_t)a.key_beta * kstep;
-  {
-    const int n = blockIdx.x * blockDim.x + threadIdx.x;
-    const int r = blockIdx.y, item = blockIdx.z;
-    const u32 src = a.galois > 1 ? automorph_src((u32)n, a.galois, log_n) : (u32)n;
-    const bool qlimb = r < a.cur;
-    const int kr = qlimb ? r : a.cap + (r - a.cur);
-    const u64* d = a.digits + item * a.dig_item + ((size_t)r << log_n) + src;
-    const u64* k0 = a.key + ((size_t)kr << log_n) + n;
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  const int r = blockIdx.y;
+  const u32 src = a.galois > 1 ? automorph_src((u32)n, a.galois, log_n) : (u32)n;
+  const bool qlimb = r < a.cur;
+  const int kr = qlimb ? r : a.cap + (r - a.cur);
+  const Mod m = mods[qlimb ? r : a.L + (r - a.cur)];
+  const u64* kp = a.key + ((size_t)kr << log_n) + n;
+  uint2 kb[KB], ka[KB];  // the beta key words of (r, n) per component, split into 30-bit halves
+  if constexpr (MAXB > 0) {
+#pragma unroll
+    for (int j = 0; j < MAXB; ++j) {
+      if (j < a.beta) {
+        const u64 x = kp[j * kstep], y = kp[kcomp + j * kstep];
+        kb[j] = make_uint2((uint32_t)x & ((1u << 30) - 1), (uint32_t)(x >> 30));
+        ka[j] = make_uint2((uint32_t)y & ((1u << 30) - 1), (uint32_t)(y >> 30));
+      }
+    }
+  }
+  const size_t roff = (size_t)r << log_n;
+  for (int item = 0; item < a.items; ++item) {
+    const u64* d = a.digits + item * a.dig_item + roff + src;
     Split4 s0{0, 0, 0, 0}, s1{0, 0, 0, 0};
-#pragma unroll 4
-    for (int j = 0; j < a.beta; ++j) {
-      const u64 dv = d[j * dstep];
-      split_mac(s0, dv, k0[j * kstep]);
-      split_mac(s1, dv, k0[kcomp + j * kstep]);
+    if constexpr (MAXB > 0) {
+#pragma unroll
+      for (int j = 0; j < MAXB; ++j) {
+        if (j < a.beta) {
+          const u64 dv = d[j * dstep];
+          const uint32_t d0 = (uint32_t)dv & ((1u << 30) - 1), d1 = (uint32_t)(dv >> 30);
+          s0.s00 += (u64)d0 * kb[j].x;
+          s0.sa += (u64)d0 * kb[j].y;
+          s0.sb += (u64)d1 * kb[j].x;
+          s0.s11 += (u64)d1 * kb[j].y;
+          s1.s00 += (u64)d0 * ka[j].x;
+          s1.sa += (u64)d0 * ka[j].y;
+          s1.sb += (u64)d1 * ka[j].x;
+          s1.s11 += (u64)d1 * ka[j].y;
+        }
+      }
+    } else {
+      for (int j = 0; j < a.beta; ++j) {
+        const u64 dv = d[j * dstep];
+        split_mac(s0, dv, kp[j * kstep]);
+        split_mac(s1, dv, kp[kcomp + j * kstep]);
+      }
     }
     if (qlimb) {
-      const Mod m = mods[r];
       u64 u0 = fold_split(s0, m), u1 = fold_split(s1, m);
-      const size_t ao = item * a.add_item + ((size_t)r << log_n);
+      const size_t ao = item * a.add_item + roff;
       if (a.add0) u0 = add_mod(u0, a.add0[ao + src], m.q);
       if (a.add1) u1 = add_mod(u1, a.add1[ao + src], m.q);
-      const size_t po = item * a.post_item + ((size_t)r << log_n) + n;
+      const size_t po = item * a.post_item + roff + n;
       if (a.post0) u0 = add_mod(u0, a.post0[po], m.q);
       if (a.post1) u1 = add_mod(u1, a.post1[po], m.q);
-      const size_t oo = item * a.out_item + ((size_t)r << log_n) + n;
+      const size_t oo = item * a.out_item + roff + n;
       a.out0[oo] = u0;
       a.out1[oo] = u1;
     } else {
       const int k = r - a.cur;
-      const Mod m = mods[a.L + k];
       u64* ps = a.pscratch + (((size_t)item * 2 * a.K + k) << log_n) + n;
       ps[0] = fold_split(s0, m);
       ps[(size_t)a.K << log_n] = fold_split(s1, m);
@@ -487,7 +518,7 @@ struct ModKsQ {
 int ks_apply(const HolmesCtx& c, const KsArgs& a, cudaStream_t st) {
   if (a.cur < 1 || a.cur > a.key_cap || a.key_cap > c.L) return -2;
   if (c.alpha > MAXA || c.K > MAXA) return -3;
-  if (a.items < 1 || a.items > 65535) return -4;
+  if (a.items < 1) return -4;
   const int beta = c.beta(a.cur), key_beta = c.beta(a.key_cap), K = c.K;
   const u64 g = a.galois <= 1 ? 1 : a.galois;
   {
@@ -495,8 +526,10 @@ int ks_apply(const HolmesCtx& c, const KsArgs& a, cudaStream_t st) {
                    a.out1, a.out_item, a.scratch, g, a.cur, a.key_cap, K, c.L, beta, key_beta, a.items};
     if (c.n < 256) return -5;
     count_launch();
-    k_ks_inner<<<dim3((unsigned)(c.n / 256), (unsigned)(a.cur + K), (unsigned)a.items), 256, 0, st>>>(ia, c.log_n,
-                                                                                                    c.d_mod);
+    const dim3 grid((unsigned)(c.n / 256), (unsigned)(a.cur + K));
+    if (beta <= 2) k_ks_inner<2><<<grid, 256, 0, st>>>(ia, c.log_n, c.d_mod);
+    else if (beta <= 5) k_ks_inner<5><<<grid, 256, 0, st>>>(ia, c.log_n, c.d_mod);
+    else k_ks_inner<0><<<grid, 256, 0, st>>>(ia, c.log_n, c.d_mod);
     HOLMES_CUDA_TRY(cudaGetLastError());
   }
   {

@@ -167,6 +167,25 @@ def test_rotation_and_conjugation_bitexact(pair, cur):
     assert np.abs(client.decrypt(F.homo_rotate(ct, 7, ctx)) - want).max() < 1e-5
 
 
+@pytest.mark.parametrize("dnum", [7, 3])
+def test_rotation_bitexact_many_digits(dnum):
+    """beta = ceil(cur / alpha) above the key-switch inner product's register-cached key counts (2 and 5): seven
+    one-limb digits, and three digits of three limbs."""
+    o, client, ctx = make_pair(log_n=11, limbs=7, dnum=dnum, dcrt=45, first=50, special=50, K=1 if dnum == 7 else 3)
+    try:
+        from holmes_b200 import fhe as F
+
+        z = np.random.default_rng(dnum).normal(size=ctx.max_slots) * 0.5
+        ct, ref = _cipher(o, client, z, 7, 9)
+        for r in (3, 2 * ctx.N - 1):
+            out = F.homo_rotate(ct, r, ctx)
+            e0, e1 = o.rotate(ref, r)
+            np.testing.assert_array_equal(host(out.cv[0][0]), e0)
+            np.testing.assert_array_equal(host(out.cv[1][0]), e1)
+    finally:
+        ctx.close()
+
+
 def test_hoisted_babies_bitexact(pair):
     o, client, ctx = pair
     from holmes_b200 import fhe as F
