@@ -423,8 +423,8 @@ def run_reference(args) -> None:
 
 def run_kernel(args) -> None:
     """One bench-shaped launch of one kernel family (N = 2^16, 13 limbs, 16 ciphertexts), after one warm-up
-    launch, for profiler captures: ``mac`` (one chunk: 8 giants x 64 babies), ``keyswitch`` (k_ks_p + k_ks_q of
-    one baby rotation), ``modup``, ``ntt`` (forward NTT of 16 x 13 polynomials), ``encode`` (one chunk's 512 rows).
+    launch, for profiler captures: ``mac`` (one chunk: 8 giants x 64 babies), ``keyswitch`` (the key switch of
+    one baby rotation: inner products, P-limb iNTT, P -> Q conversion, Q-limb NTT), ``modup``, ``ntt`` (forward NTT of 16 x 13 polynomials), ``encode`` (one chunk's 512 rows).
     ``--inputs`` / ``--limbs`` shrink the case (multi-pass captures want a few GB on the device); at the bench
     shape memory on the device stays below 20 GB."""
     import torch

@@ -588,7 +588,7 @@ int bsgs_mac(ModSrc ms, u64* res, const u64* const* c0s, const u64* const* c1s,
     in.c1[i] = c1s[i < inputs ? i : 0];
   }
   // HOLMES_MAC_TC=1 selects the tensor-core kernel (mac_tc.cu) for the shapes it takes.  It is bit-exact but
-  // measured slower than k_bsgs_mac3 at the bench shape (20 vs 11.7 ms per 512-row chunk of 16 ciphertexts): with
+  // measured slower than k_bsgs_mac3 at the bench shape (20 vs 10.5 ms per 512-row chunk of 16 ciphertexts): with
   // 4 coefficients per item (TMEM holds two items' accumulators) its operand gathers are 32-byte sectors from
   // 2560 rows per item and it stays latency-bound on them (tensor pipe ~2% busy).
   const char* tc = getenv("HOLMES_MAC_TC");
