@@ -176,6 +176,7 @@ class BootstrapProgram:
     s2c_scale: float
     cheb: np.ndarray
     rotations: tuple
+    gap: int = 1             # N / (2 n): sparse slots when > 1
     _plain: dict = field(default_factory=dict)
     setup_seconds: float = 0.0
 
@@ -213,6 +214,7 @@ def requirements(specs, log_n: int) -> Requirements:
             for mat in fft_levels(n, M, int(budget), inverse):
                 rots.update(int(r) for r in mat if int(r))
         rots.add(M - 1)
+        rots.update(n << i for i in range(int(log_n) - 1 - int(spec.log_slots)))  # sparse-slot subsum
         depth = max(depth, spec.depth)
     return Requirements(tuple(sorted(rots)), depth)
 
@@ -222,8 +224,9 @@ def generate(context, spec: BootstrapSpec) -> BootstrapProgram:
     start = time.perf_counter()
     ctx = context
     n = 1 << int(spec.log_slots)
-    if n != ctx.N // 2:
-        raise ValueError(f"only full-slot bootstrapping is implemented (slots {ctx.N // 2}, got {n})")
+    if not 2 <= n <= ctx.N // 2:
+        raise ValueError(f"bootstrap slots must be a power of two in [2, {ctx.N // 2}], got {n}")
+    gap = ctx.N // (2 * n)
     raise_to = ctx.L
     out_limbs = raise_to - spec.depth
     if out_limbs < 2:
@@ -236,13 +239,13 @@ def generate(context, spec: BootstrapSpec) -> BootstrapProgram:
     B = float(spec.k_bound + 1)
     c2s = fft_levels(n, ctx.M, int(spec.level_budget[0]), True)
     s2c = fft_levels(n, ctx.M, int(spec.level_budget[1]), False)
-    c2s_total = delta / (2.0 * n * q0 * B)
+    c2s_total = delta / (2.0 * n * gap * q0 * B)  # the sparse subsum multiplies the message by gap
     s2c_total = q0 * (2.0 ** cf) / (2.0 * math.pi * delta)
     cheb = chebyshev_cos(B, int(spec.double_angles), int(spec.cheb_degree))
     req = requirements([spec], ctx.logN)
     prog = BootstrapProgram(spec=spec, context=ctx, n=n, raise_to_limbs=raise_to, output_limbs=out_limbs, cf=cf, B=B,
                             c2s=c2s, s2c=s2c, c2s_scale=c2s_total ** (1.0 / len(c2s)),
-                            s2c_scale=s2c_total ** (1.0 / len(s2c)), cheb=cheb, rotations=req.rotations)
+                            s2c_scale=s2c_total ** (1.0 / len(s2c)), cheb=cheb, rotations=req.rotations, gap=gap)
     prog.setup_seconds = time.perf_counter() - start
     return prog
 
@@ -427,6 +430,13 @@ def bootstrap(ct: F.Cipher, ctx, program: BootstrapProgram) -> F.Cipher:
         _lib.call("holmes_modraise", ctx.handle, x.cv[c].data_ptr(), F._item_stride(x.cv[c]), raised.cv[c].data_ptr(),
                   F._item_stride(raised.cv[c]), raise_to, items, scratch.data_ptr(), _stream())
     y = raised
+    # Sparse slots (n < N/2): after ModRaise the overflow q0 I fills every coefficient, not only the multiples of
+    # gap = N/(2n) that carry the n-slot message.  Summing the rotations by n j (j < gap), the automorphisms that
+    # fix X^gap, keeps gap times the multiples-of-gap part: log2(gap) rotate-and-add steps, no level.
+    g = 1
+    while g < program.gap:
+        y = F.homo_add(y, F.homo_rotate(y, program.n * g, ctx), ctx)
+        g *= 2
     for lvl in range(len(program.c2s)):
         offsets, pt = program.diagonal_plaintexts("c2s", lvl, int(y.state.cur_limbs))
         y = linear_level(y, offsets, pt)

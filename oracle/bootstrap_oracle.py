@@ -1,4 +1,4 @@
-"""CPU restatement of full-slot CKKS bootstrapping -- TEST INFRASTRUCTURE ONLY.
+"""CPU restatement of CKKS bootstrapping (full and sparse slots) -- TEST INFRASTRUCTURE ONLY.
 
 Same pass order as the reference's batched bootstrap (``bench/cmp/holmes_batch_bs.py:65-118``: ModRaise ->
 CoeffsToSlots -> conjugate / real / imaginary -> EvalMod x 2 -> recombine -> SlotsToCoeffs) and as
@@ -85,7 +85,7 @@ class OracleBootstrap:
         rots = o.hoisted_rotations((c0, c1), offs)
         acc = None
         for r, (r0, r1) in zip(offs, rots):
-            pt = o.encode(mat[r] * factor, cur, float(self.pr.q[cur - 1]))
+            pt = o.encode(mat[r] * factor, cur, float(self.pr.q[cur - 1]), slots=len(mat[r]))
             t = (o.mul(r0, pt, self._ids(cur)), o.mul(r1, pt, self._ids(cur)))
             acc = t if acc is None else (o.add(acc[0], t[0], self._ids(cur)), o.add(acc[1], t[1], self._ids(cur)))
         d0, d1 = o.rescale(acc)
@@ -151,6 +151,12 @@ class OracleBootstrap:
         k_pre = int(round(2.0 ** (-prog.cf) * float(self.pr.q[1])))
         x = self.int_mul_rescale(x, k_pre, s_in)
         y = self.modraise(x, prog.raise_to_limbs)
+        g = 1
+        while g < getattr(prog, "gap", 1):   # sparse slots: sum of the rotations by n j, j < gap
+            r0, r1 = o.rotate(y[:2], prog.n * g)
+            ids = self._ids(y[0].shape[0])
+            y = (o.add(y[0], r0, ids), o.add(y[1], r1, ids), y[2])
+            g *= 2
         for lvl in prog.c2s:
             y = self.linear(y, lvl, prog.c2s_scale)
         cur = y[0].shape[0]

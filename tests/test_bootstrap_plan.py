@@ -14,10 +14,11 @@ def _bitrev(v):
     return v[idx]
 
 
-@pytest.mark.parametrize(("log_n", "budget"), [(10, 3), (12, 3), (12, 4), (13, 5)])
-def test_transform_levels_match_special_fft(log_n, budget):
+@pytest.mark.parametrize(("log_n", "budget", "sparse"), [(10, 3, 1), (12, 3, 1), (12, 4, 1), (13, 5, 1), (12, 3, 4),
+                                                     (13, 2, 64)])
+def test_transform_levels_match_special_fft(log_n, budget, sparse):
     o = Oracle(OracleParams(log_n=log_n, limbs=2, dnum=1, dcrt_bits=40, first_mod_bits=50, special_bits=50))
-    n, M = o.pr.n // 2, 2 * o.pr.n
+    n, M = o.pr.n // 2 // sparse, 2 * o.pr.n
     rng = np.random.default_rng(log_n)
     v = rng.normal(size=n) + 1j * rng.normal(size=n)
     # oracle special inverse FFT (with bit reversal and 1/n)
@@ -61,6 +62,39 @@ def test_requirements_and_depth():
     assert all(0 < r < (1 << 11) or r == (2 << 12) - 1 for r in req.rotations)
     with pytest.raises(ValueError):
         BS.BootstrapSpec(mode="slots_first")
+
+
+def _automorph(t: np.ndarray, k: int) -> np.ndarray:
+    """sigma_k(t)(X) = t(X^k) in Z[X]/(X^N + 1)."""
+    N = t.size
+    out = np.zeros_like(t)
+    for i, c in enumerate(t):
+        e = (i * k) % (2 * N)
+        if e < N:
+            out[e] += c
+        else:
+            out[e - N] -= c
+    return out
+
+
+@pytest.mark.parametrize("log_slots", [6, 8])
+def test_sparse_subsum_is_gap_times_the_subring_part(log_slots):
+    """Rotations by n j (j < gap) are the automorphisms X -> X^(5^(n j)) fixing X^gap: the log2(gap) rotate-and-add
+    steps of the sparse-slot bootstrap leave gap times the coefficients at multiples of gap, the rest cancels."""
+    N, n = 1 << 10, 1 << log_slots
+    gap = N // (2 * n)
+    t = np.random.default_rng(log_slots).integers(-1000, 1000, size=N)
+    acc = t.copy()
+    g = 1
+    while g < gap:
+        acc = acc + _automorph(acc, pow(5, n * g, 2 * N))
+        g *= 2
+    want = np.zeros_like(t)
+    want[::gap] = gap * t[::gap]
+    np.testing.assert_array_equal(acc, want)
+    spec = BS.BootstrapSpec(log_slots=log_slots, level_budget=(2, 2))
+    req = BS.requirements([spec], log_n=10)
+    assert {n << i for i in range(int(np.log2(gap)))} <= set(req.rotations)
 
 
 def test_refresh_iterations_validated_on_host():

@@ -113,3 +113,38 @@ def test_bootstrap_rejects_bad_input(boot):
     ct = client.encrypt(np.zeros(ctx.max_slots), cur_limbs=1, counter=30)
     with pytest.raises(ValueError):
         op.refresh(ct)
+
+
+@pytest.fixture(scope="module")
+def sparse_boot():
+    from holmes_b200 import bootstrap as BS
+    from holmes_b200 import linear as LN
+
+    o, client, ctx = make_pair(log_n=12, limbs=20, dnum=4, dcrt=59, first=60, special=60, hamming=64, seed=2)
+    session = LN.Session(client, ctx)
+    cfg = BS.BootstrapConfig(log_slots=8, level_budget=(3, 3), k_bound=12)   # 256 slots of 2048: gap 8
+    op = BS.BootstrapOperator.prepare(session, cfg)
+    yield o, client, ctx, op
+    ctx.close()
+
+
+def test_sparse_slot_bootstrap_decodes_and_matches_oracle(sparse_boot):
+    """Sparse slots (the reference's 2^3 .. 2^12-slot programs): subsum over the rotations by n j, then the
+    n-point CoeffsToSlots / EvalMod / SlotsToCoeffs; decoded against the message, residues against the oracle."""
+    from oracle.bootstrap_oracle import OracleBootstrap
+
+    o, client, ctx, op = sparse_boot
+    n = op.program.n
+    assert op.program.gap == ctx.N // (2 * n) == 8
+    rng = np.random.default_rng(3)
+    z = (rng.normal(size=n) + 1j * rng.normal(size=n)) * 0.5
+    ct = client.encrypt(z, slots=n, cur_limbs=3, counter=31)
+    out = op.refresh(ct)
+    assert int(out.slots) == n
+    err = np.abs(client.decrypt(out) - z).max()
+    assert err < 1e-6, err
+    ref = o.encrypt(z, 3, counter=31, slots=n)
+    e0, e1, esf = OracleBootstrap(o, op.program).bootstrap(ref, s_in=float(ct.state.scaling_factor))
+    np.testing.assert_array_equal(host(out.cv[0][0]), e0)
+    np.testing.assert_array_equal(host(out.cv[1][0]), e1)
+    assert float(out.state.scaling_factor) == esf
