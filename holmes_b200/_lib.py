@@ -38,6 +38,7 @@ SIGNATURES = {
     "holmes_encode": [p, p, i64, i32, i32, d, i32, p, i64, p, p],
     "holmes_fft_special_inv": [p, p, i64, i32, i32, p],
     "holmes_encode_fft": [p, p, i64, i32, i32, d, i32, p, i64, p, p],
+    "holmes_encode_fft_ext": [p, p, i64, i32, i32, d, i32, p, i64, p, p],
     "holmes_pack_diagonals":[p, i32, i32, i32, i32, i32, i32, i32, i32, p, i64, p],
     "holmes_elementwise": [p, i32, p, p, p, i32, i32, i64, i64, i64, p],
     "holmes_mul_i": [p, p, p, i32, i32, i64, i64, p],
@@ -50,6 +51,9 @@ SIGNATURES = {
     "holmes_modup": [p, p, i64, i32, i32, p, i64, p, p],
     "holmes_keyswitch": [p, p, i64, i32, p, i32, u64, p, p, i64, p, p, i64, p, p, i64, i32, p, p],
     "holmes_bsgs_mac": [p, p, p, p, i64, i32, i32, p, i64, i32, i32, p],
+    "holmes_keyswitch_ext": [p, p, i64, i32, p, i32, u64, p, i64, p, p, i64, i32, p],
+    "holmes_moddown": [p, p, p, i64, i32, p, p, i64, i32, p, p],
+    "holmes_bsgs_mac_ext": [p, p, p, p, i64, i32, i32, p, i64, i32, i32, p],
     "holmes_modsum": [p, p, i32, p, i32, i32, i64, p],
     "holmes_launch_count": [ctypes.POINTER(ctypes.c_ulonglong)],
     "holmes_device_error": [i32, ctypes.POINTER(ctypes.c_int)],

@@ -132,6 +132,19 @@ int holmes_encode_fft(void* ctx, const double* u, long long row_stride, int rows
   return encode_rows(*C(ctx), u, row_stride, rows, slots, scale, cur, out, out_row_stride, flag, S(stream));
 }
 
+int holmes_encode_fft_ext(void* ctx, const double* u, long long row_stride, int rows, int slots, double scale, int cur,
+                          uint64_t* out, long long out_row_stride, int* flag, void* stream) {
+  if (!ctx || !u || !out || !flag) return -1;
+  if (rows < 1) return 0;
+  const HolmesCtx& c = *C(ctx);
+  if (cur < 1 || cur > c.L) return -2;
+  if (out_row_stride < (long long)(cur + c.K) * c.n) return -4;
+  const int e = encode_rows(c, u, row_stride, rows, slots, scale, cur, out, out_row_stride, flag, S(stream));
+  if (e) return e;
+  return encode_rows(c, u, row_stride, rows, slots, scale, c.K, out + (size_t)cur * c.n, out_row_stride, flag,
+                     S(stream), c.L);
+}
+
 int holmes_pack_diagonals(const double* weight, int weight_complex, int dim, int lanes, int baby, int giant_base,
                           int giant_count, int lane_shift, int slots, double* out, long long row_stride, void* stream) {
   if (!weight || !out) return -1;
@@ -205,6 +218,32 @@ int holmes_bsgs_mac(void* ctx, uint64_t* res, const uint64_t* const* c0s, const 
   if (limbs < 1 || limbs > c.L) return -2;
   ModSrc ms{c.d_mod, 0, nullptr, nullptr, nullptr};
   return bsgs_mac(ms, res, c0s, c1s, bstride, nb, inputs, pts, pstride, groups, limbs, c.n, S(stream));
+}
+
+int holmes_keyswitch_ext(void* ctx, const uint64_t* digits, long long digit_item, int cur, const uint64_t* key,
+                         int key_cap, uint64_t galois, const uint64_t* add0, long long add_item, uint64_t* out0,
+                         uint64_t* out1, long long out_item, int items, void* stream) {
+  if (!ctx || !digits || !key || !out0 || !out1) return -1;
+  if (galois > 1 && !(galois & 1)) return -3;
+  KsArgs a{digits, digit_item, cur, key, key_cap, galois, add0, nullptr, add_item,
+           nullptr, nullptr, 0, out0, out1, out_item, items, nullptr};
+  return ks_apply_ext(*C(ctx), a, S(stream));
+}
+
+int holmes_moddown(void* ctx, const uint64_t* in0, const uint64_t* in1, long long in_item, int cur, uint64_t* out0,
+                   uint64_t* out1, long long out_item, int items, uint64_t* scratch, void* stream) {
+  if (!ctx || !in0 || !in1 || !out0 || !out1 || !scratch) return -1;
+  return moddown_ext(*C(ctx), in0, in1, in_item, cur, out0, out1, out_item, items, scratch, S(stream));
+}
+
+int holmes_bsgs_mac_ext(void* ctx, uint64_t* res, const uint64_t* const* c0s, const uint64_t* const* c1s,
+                        long long bstride, int nb, int inputs, const uint64_t* pts, long long pstride, int groups,
+                        int cur, void* stream) {
+  if (!ctx || !res || !c0s || !c1s || !pts) return -1;
+  const HolmesCtx& c = *C(ctx);
+  if (cur < 1 || cur > c.L) return -2;
+  ModSrc ms{c.d_mod, 0, nullptr, nullptr, nullptr, cur, c.L};
+  return bsgs_mac(ms, res, c0s, c1s, bstride, nb, inputs, pts, pstride, groups, cur + c.K, c.n, S(stream));
 }
 
 int holmes_modsum(void* ctx, const uint64_t* const* srcs, int nsrc, uint64_t* out, int items, int limbs,

@@ -58,8 +58,10 @@ struct ModSrc {
   const u64* primes;
   const u64* ratios;
   const u64* ks;
+  int ext_cur = 0;  // > 0: limb l >= ext_cur is special limb ext_L + l - ext_cur (extended basis Q u P)
+  int ext_L = 0;
   __device__ __forceinline__ Mod get(int limb) const {
-    if (mods) return mods[first + limb];
+    if (mods) return mods[ext_cur > 0 && limb >= ext_cur ? ext_L + limb - ext_cur : first + limb];
     Mod m;
     m.q = primes[limb];
     m.mu = ratios[limb];

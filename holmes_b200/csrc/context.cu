@@ -227,6 +227,11 @@ int build_context(HolmesCtx& c, int log_n, int limbs, int dnum, int dcrt_bits, i
   if ((rc = upload(c, &c.d_md_pinv, md_pinv))) return rc;
   if ((rc = upload(c, &c.d_rs_qinv, rs))) return rc;
   if ((rc = upload(c, &c.d_p_mod_q, p_mod_q))) return rc;
+  {
+    std::vector<Tw> pq(L);
+    for (int i = 0; i < L; ++i) pq[i] = host_shoup(p_mod_q[i], q[i]);
+    if ((rc = upload(c, &c.d_pmodq_tw, pq))) return rc;
+  }
   if ((rc = upload(c, &c.d_unit, unit))) return rc;
   if ((rc = upload(c, &c.d_unit_neg, unit_neg))) return rc;
   if ((rc = upload(c, &c.d_rot_group, rot))) return rc;

@@ -32,6 +32,7 @@ struct HolmesCtx {
   Tw* d_md_pinv = nullptr;       // [L] P^-1 mod q_i (scales the digits' own limbs in ModUp)
   Tw* d_rs_qinv = nullptr;       // [L+1][L] q_{l-1}^-1 mod q_i (rescale from l limbs)
   u64* d_p_mod_q = nullptr;      // [L] P mod q_i
+  Tw* d_pmodq_tw = nullptr;      // [L] P mod q_i with its Shoup companion
   Tw* d_unit = nullptr;          // [T] psi^(N/2): X^(N/2) evaluated at the first half of the NTT words
   Tw* d_unit_neg = nullptr;      // [T] q - psi^(N/2)
   u64* d_rot_group = nullptr;    // [N/2] 5^j mod 2N

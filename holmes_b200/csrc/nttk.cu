@@ -379,7 +379,10 @@ struct KsInnerArgs {
   u64* out0;
   u64* out1;
   long long out_item;
-  u64* pscratch;  // [items][2][K][N]
+  u64* p0;        // P limb k of component c of item i at p_c + i * p_item + k * N
+  u64* p1;
+  long long p_item;
+  const Tw* qscale;  // optional: Q outputs times qscale[r] (P mod q_r for the extended basis)
   u64 galois;
   int cur, cap, K, L, beta, key_beta, items;
 };
@@ -444,14 +447,17 @@ __global__ void __launch_bounds__(256) k_ks_inner(KsInnerArgs a, int log_n, cons
       const size_t po = item * a.post_item + roff + n;
       if (a.post0) u0 = add_mod(u0, a.post0[po], m.q);
       if (a.post1) u1 = add_mod(u1, a.post1[po], m.q);
+      if (a.qscale) {
+        u0 = shoup(u0, a.qscale[r], m.q);
+        u1 = shoup(u1, a.qscale[r], m.q);
+      }
       const size_t oo = item * a.out_item + roff + n;
       a.out0[oo] = u0;
       a.out1[oo] = u1;
     } else {
-      const int k = r - a.cur;
-      u64* ps = a.pscratch + (((size_t)item * 2 * a.K + k) << log_n) + n;
-      ps[0] = fold_split(s0, m);
-      ps[(size_t)a.K << log_n] = fold_split(s1, m);
+      const size_t po = item * a.p_item + ((size_t)(r - a.cur) << log_n) + n;
+      a.p0[po] = fold_split(s0, m);
+      a.p1[po] = fold_split(s1, m);
     }
   }
 }
@@ -515,30 +521,29 @@ struct ModKsQ {
   __device__ int operator()(int p) const { return (p % (2 * cur)) % cur; }
 };
 
-int ks_apply(const HolmesCtx& c, const KsArgs& a, cudaStream_t st) {
-  if (a.cur < 1 || a.cur > a.key_cap || a.key_cap > c.L) return -2;
-  if (c.alpha > MAXA || c.K > MAXA) return -3;
-  if (a.items < 1) return -4;
-  const int beta = c.beta(a.cur), key_beta = c.beta(a.key_cap), K = c.K;
-  const u64 g = a.galois <= 1 ? 1 : a.galois;
-  {
-    KsInnerArgs ia{a.digits, a.dig_item, a.key, a.add0, a.add1, a.add_item, a.post0, a.post1, a.post_item, a.out0,
-                   a.out1, a.out_item, a.scratch, g, a.cur, a.key_cap, K, c.L, beta, key_beta, a.items};
-    if (c.n < 256) return -5;
-    count_launch();
-    const dim3 grid((unsigned)(c.n / 256), (unsigned)(a.cur + K));
-    if (beta <= 2) k_ks_inner<2><<<grid, 256, 0, st>>>(ia, c.log_n, c.d_mod);
-    else if (beta <= 5) k_ks_inner<5><<<grid, 256, 0, st>>>(ia, c.log_n, c.d_mod);
-    else k_ks_inner<0><<<grid, 256, 0, st>>>(ia, c.log_n, c.d_mod);
-    HOLMES_CUDA_TRY(cudaGetLastError());
-  }
+static int ks_inner_launch(const HolmesCtx& c, const KsInnerArgs& ia, cudaStream_t st) {
+  if (c.n < 256) return -5;
+  count_launch();
+  const dim3 grid((unsigned)(c.n / 256), (unsigned)(ia.cur + ia.K));
+  if (ia.beta <= 2) k_ks_inner<2><<<grid, 256, 0, st>>>(ia, c.log_n, c.d_mod);
+  else if (ia.beta <= 5) k_ks_inner<5><<<grid, 256, 0, st>>>(ia, c.log_n, c.d_mod);
+  else k_ks_inner<0><<<grid, 256, 0, st>>>(ia, c.log_n, c.d_mod);
+  return (int)cudaGetLastError();
+}
+
+// ModDown tail: P-limb inner products in scratch [items][2][K][N] (coefficients' NTT form, canonical), Q outputs
+// out_c already holding what the conversion is subtracted from.  P iNTT in place, P -> Q conversion into
+// scratch + items 2 K N, Q NTT with "out -= conversion".
+static int moddown_tail(const HolmesCtx& c, u64* scratch, u64* out0, u64* out1, long long out_item, int cur, int items,
+                        cudaStream_t st) {
+  const int K = c.K;
   {
     NttTables T{c.d_itw, c.d_mod};
-    LdRows ld{a.scratch, c.log_n};
-    StScratch ss{a.scratch, c.log_n};
-    const int polys = a.items * 2 * K;
+    LdRows ld{scratch, c.log_n};
+    StScratch ss{scratch, c.log_n};
+    const int polys = items * 2 * K;
     if (c.log_n == 16) {
-      const int e = ntt16_inverse<HOLMES_KS16_MINB>(T, ModKsP{c.L, K}, ScKsP{c.d_md_scale, K}, ld, IMRows{a.scratch},
+      const int e = ntt16_inverse<HOLMES_KS16_MINB>(T, ModKsP{c.L, K}, ScKsP{c.d_md_scale, K}, ld, IMRows{scratch},
                                                     ss, polys, st);
       if (e) return e;
     } else {
@@ -554,19 +559,19 @@ int ks_apply(const HolmesCtx& c, const KsArgs& a, cudaStream_t st) {
 #undef L_
     }
   }
-  u64* conv = a.scratch + (size_t)a.items * 2 * K * c.n;  // [items][2][cur][N], coefficient form
+  u64* conv = scratch + (size_t)items * 2 * K * c.n;  // [items][2][cur][N], coefficient form
   {
-    ConvArgs ca{a.scratch, (long long)K * c.n, conv, (long long)a.cur * c.n, c.d_md_hat, c.L,
-                K, a.cur, a.cur, a.cur, c.L, a.items * 2, nullptr, 0, nullptr};
+    ConvArgs ca{scratch, (long long)K * c.n, conv, (long long)cur * c.n, c.d_md_hat, c.L,
+                K, cur, cur, cur, c.L, items * 2, nullptr, 0, nullptr};
     const int e = conv_launch(c, ca, st);
     if (e) return e;
   }
   {
     NttTables T{c.d_tw, c.d_mod};
     LdRows ld{conv, c.log_n};
-    StKsSub sq{a.out0, a.out1, a.out_item, c.d_mod, a.cur, c.log_n};
-    const int polys = a.items * 2 * a.cur;
-    if (c.log_n == 16) return ntt16_forward<HOLMES_KS16_MINB>(T, ModKsQ{a.cur}, ld, IMRows{conv}, sq, polys, st);
+    StKsSub sq{out0, out1, out_item, c.d_mod, cur, c.log_n};
+    const int polys = items * 2 * cur;
+    if (c.log_n == 16) return ntt16_forward<HOLMES_KS16_MINB>(T, ModKsQ{cur}, ld, IMRows{conv}, sq, polys, st);
 #define L_(LG)                                                                                        \
   {                                                                                                   \
     using G = NttGeom<LG>;                                                                            \
@@ -578,6 +583,66 @@ int ks_apply(const HolmesCtx& c, const KsArgs& a, cudaStream_t st) {
 #undef L_
   }
   return 0;
+}
+
+int ks_apply(const HolmesCtx& c, const KsArgs& a, cudaStream_t st) {
+  if (a.cur < 1 || a.cur > a.key_cap || a.key_cap > c.L) return -2;
+  if (c.alpha > MAXA || c.K > MAXA) return -3;
+  if (a.items < 1) return -4;
+  const int beta = c.beta(a.cur), key_beta = c.beta(a.key_cap), K = c.K;
+  const u64 g = a.galois <= 1 ? 1 : a.galois;
+  KsInnerArgs ia{a.digits, a.dig_item, a.key, a.add0, a.add1, a.add_item, a.post0, a.post1, a.post_item, a.out0,
+                 a.out1, a.out_item, a.scratch, a.scratch + (size_t)K * c.n, (long long)2 * K * c.n, nullptr, g,
+                 a.cur, a.key_cap, K, c.L, beta, key_beta, a.items};
+  const int e = ks_inner_launch(c, ia, st);
+  if (e) return e;
+  return moddown_tail(c, a.scratch, a.out0, a.out1, a.out_item, a.cur, a.items, st);
+}
+
+// Key switch without the ModDown: out_c [items][cur + K][N] over Q u P (Q limbs first) =
+//   Q limbs: P perm(add_c) + inner_c (the digits' Q rows carry P^-1, so this is P (u) with u the Q output above),
+//   P limbs: inner_c.
+int ks_apply_ext(const HolmesCtx& c, const KsArgs& a, cudaStream_t st) {
+  if (a.cur < 1 || a.cur > a.key_cap || a.key_cap > c.L) return -2;
+  if (c.alpha > MAXA || c.K > MAXA) return -3;
+  if (a.items < 1) return -4;
+  const int beta = c.beta(a.cur), key_beta = c.beta(a.key_cap);
+  const u64 g = a.galois <= 1 ? 1 : a.galois;
+  KsInnerArgs ia{a.digits, a.dig_item, a.key, a.add0, a.add1, a.add_item, a.post0, a.post1, a.post_item, a.out0,
+                 a.out1, a.out_item, a.out0 + (size_t)a.cur * c.n, a.out1 + (size_t)a.cur * c.n, a.out_item,
+                 c.d_pmodq_tw, g, a.cur, a.key_cap, c.K, c.L, beta, key_beta, a.items};
+  return ks_inner_launch(c, ia, st);
+}
+
+// ModDown of extended-basis ciphertexts in_c [items][cur + K][N] (Q limbs first) to out_c [items][cur][N]:
+// (in_Q - conv(iNTT(in_P))) P^-1.  The Q part is scaled by P^-1 into out first (the conversion's constants
+// p_k^-1 mod q_i already carry P^-1), the P part copied into scratch.
+__global__ void k_ext_split(const u64* __restrict__ in0, const u64* __restrict__ in1, long long in_item,
+                            u64* __restrict__ out0, u64* __restrict__ out1, long long out_item, u64* __restrict__ scr,
+                            int cur, int K, int log_n, const Tw* __restrict__ pinv, const Mod* __restrict__ mods) {
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  const int r = blockIdx.y, item = blockIdx.z;
+  const size_t src = item * in_item + ((size_t)r << log_n) + n;
+  if (r < cur) {
+    const u64 q = mods[r].q;
+    const size_t dst = item * out_item + ((size_t)r << log_n) + n;
+    out0[dst] = shoup(in0[src], pinv[r], q);
+    out1[dst] = shoup(in1[src], pinv[r], q);
+  } else {
+    const size_t dst = (((size_t)item * 2 * K + (r - cur)) << log_n) + n;
+    scr[dst] = in0[src];
+    scr[dst + ((size_t)K << log_n)] = in1[src];
+  }
+}
+int moddown_ext(const HolmesCtx& c, const u64* in0, const u64* in1, long long in_item, int cur, u64* out0, u64* out1,
+                long long out_item, int items, u64* scratch, cudaStream_t st) {
+  if (cur < 1 || cur > c.L) return -2;
+  if (items < 1 || items > 65535 || c.n < 256) return -4;
+  count_launch();
+  k_ext_split<<<dim3((unsigned)(c.n / 256), (unsigned)(cur + c.K), (unsigned)items), 256, 0, st>>>(
+      in0, in1, in_item, out0, out1, out_item, scratch, cur, c.K, c.log_n, c.d_md_pinv, c.d_mod);
+  HOLMES_CUDA_TRY(cudaGetLastError());
+  return moddown_tail(c, scratch, out0, out1, out_item, cur, items, st);
 }
 
 // --------------------------------------------------------------------------------------------- rescale
@@ -806,8 +871,8 @@ __global__ void HOLMES_NTT_BOUNDS(LOGN) k_encode(NttTables T, LdRounded<WIDE> ld
 }
 
 int encode_rows(const HolmesCtx& c, const double* u, long long row_stride, int rows, int slots, double scale, int cur,
-                u64* out, long long out_row_stride, int* flag, cudaStream_t st) {
-  if (cur < 1 || cur > c.T) return -2;
+                u64* out, long long out_row_stride, int* flag, cudaStream_t st, int mod_first) {
+  if (cur < 1 || mod_first < 0 || mod_first + cur > c.T) return -2;
   if (slots < 1 || slots > c.n / 2 || (slots & (slots - 1))) return -3;
   if (out_row_stride < (long long)cur * c.n) return -4;
   int gap_log = 0;
@@ -822,15 +887,17 @@ int encode_rows(const HolmesCtx& c, const double* u, long long row_stride, int r
                                                     flag);
     HOLMES_CUDA_TRY(cudaGetLastError());
   }
-  NttTables T{c.d_tw, c.d_mod};
+  // output limb l has modulus mod_first + l: the tables are taken from there on
+  NttTables T{c.d_tw + (size_t)mod_first * c.n, c.d_mod + mod_first};
+  const Mod* mods = c.d_mod + mod_first;
   // limbs 0 .. cur-2 from the integers, then limb cur-1 in place
   for (int pass = 0; pass < 2; ++pass) {
     const int first = pass ? cur - 1 : 0, last = pass ? cur : cur - 1;
     if (last <= first) continue;
     bool wide = true;
-    for (int l = first; l < last; ++l) wide = wide && (c.q[l] << 3) > (1ull << 61);
-    LdRounded<true> lw{ints, out_row_stride, c.d_mod, last, first};
-    LdRounded<false> ln{ints, out_row_stride, c.d_mod, last, first};
+    for (int l = first; l < last; ++l) wide = wide && (c.q[mod_first + l] << 3) > (1ull << 61);
+    LdRounded<true> lw{ints, out_row_stride, mods, last, first};
+    LdRounded<false> ln{ints, out_row_stride, mods, last, first};
     PolyMap pm = poly_map(last - first, out_row_stride, c.n, 0);
     StPlain sp{out + (size_t)first * c.n, pm};
     const int polys = rows * (last - first);

@@ -66,6 +66,9 @@ struct KsArgs {
   u64* scratch;
 };
 int ks_apply(const HolmesCtx& c, const KsArgs& a, cudaStream_t st);
+int ks_apply_ext(const HolmesCtx& c, const KsArgs& a, cudaStream_t st);
+int moddown_ext(const HolmesCtx& c, const u64* in0, const u64* in1, long long in_item, int cur, u64* out0, u64* out1,
+                long long out_item, int items, u64* scratch, cudaStream_t st);
 
 // Rescale by the last limb: `comps` polynomials-of-limbs in [comps][cur] layout (stride in_stride / out_stride
 // between components) -> [comps][cur - 1]; scratch >= comps * N words.
@@ -83,7 +86,7 @@ int add_const(const HolmesCtx& c, const u64* a, const u64* consts, u64* out, int
 // Rows of slot vectors after the special inverse FFT ([rows][slots] complex, interleaved doubles) ->
 // [rows][cur][N] NTT plaintexts at `scale`.  Out-of-range values set *flag = 1.
 int encode_rows(const HolmesCtx& c, const double* u, long long row_stride, int rows, int slots, double scale, int cur,
-                u64* out, long long out_row_stride, int* flag, cudaStream_t st);
+                u64* out, long long out_row_stride, int* flag, cudaStream_t st, int mod_first = 0);
 
 int fft_special_inv(const HolmesCtx& c, double* z, long long row_stride, int rows, int slots, cudaStream_t st);
 

@@ -205,6 +205,11 @@ class Context:
     def q(self, i: int) -> int:
         return self.moduli[i]
 
+    def p_mod_q(self, cur: int) -> list:
+        """P = product of the special primes, modulo q_0 .. q_{cur-1}."""
+        P = math.prod(self.moduli[self.L:self.L + self.K])
+        return [P % self.moduli[i] for i in range(int(cur))]
+
     def beta(self, cur: int) -> int:
         return -(-int(cur) // self.alpha)
 
@@ -298,8 +303,9 @@ def _as_slots(values, slots: int) -> np.ndarray:
 
 
 def encode_rows(ctx: Context, rows: torch.Tensor, cur_limbs: int, scale: float, slots: int,
-                already_transformed: bool = False) -> torch.Tensor:
-    """[rows][slots] complex128 (device) -> NTT plaintexts [rows][cur][N]."""
+                already_transformed: bool = False, ext: bool = False) -> torch.Tensor:
+    """[rows][slots] complex128 (device) -> NTT plaintexts [rows][cur][N] (``ext``: [rows][cur + K][N] over the
+    extended basis, the Q limbs first)."""
     if rows.dim() == 1:
         rows = rows.reshape(1, -1)
     nrows = int(rows.shape[0])
@@ -309,15 +315,16 @@ def encode_rows(ctx: Context, rows: torch.Tensor, cur_limbs: int, scale: float, 
     if z.data_ptr() == rows.data_ptr() and not already_transformed:
         z = z.clone()
     zr = torch.view_as_real(z)
-    out = torch.empty((nrows, int(cur_limbs), ctx.N), dtype=torch.uint64, device=ctx.device)
+    limbs = int(cur_limbs) + (ctx.K if ext else 0)
+    out = torch.empty((nrows, limbs, ctx.N), dtype=torch.uint64, device=ctx.device)
     if not already_transformed:
         tok = OPTIMER.start("fft_special")
         _lib.call("holmes_fft_special_inv", ctx.handle, zr.data_ptr(), 2 * slots, nrows, slots, _stream())
         OPTIMER.stop(tok, 2 * nrows * slots * 16)
     tok = OPTIMER.start("encode_ntt")
-    _lib.call("holmes_encode_fft", ctx.handle, zr.data_ptr(), 2 * slots, nrows, slots, float(scale), int(cur_limbs),
-              out.data_ptr(), int(cur_limbs) * ctx.N, ctx._flag.data_ptr(), _stream())
-    OPTIMER.stop(tok, nrows * slots * 16 + nrows * int(cur_limbs) * ctx.N * 8)
+    _lib.call("holmes_encode_fft_ext" if ext else "holmes_encode_fft", ctx.handle, zr.data_ptr(), 2 * slots, nrows,
+              slots, float(scale), int(cur_limbs), out.data_ptr(), limbs * ctx.N, ctx._flag.data_ptr(), _stream())
+    OPTIMER.stop(tok, nrows * slots * 16 + nrows * limbs * ctx.N * 8)
     return out
 
 
@@ -572,13 +579,97 @@ def homo_rotate(a: Cipher, rotation: int, ctx) -> Cipher:
     return out
 
 
-def fast_rotate(a: Cipher, rotations, ctx) -> Cipher:
+def fast_rotate(a: Cipher, rotations, ctx, output_ext: bool = False) -> Cipher:
     """One rotation (an int: ``homo_rotate``) or, for a sequence of offsets, the batch ``[len(offsets)]`` of
     rotations from one hoisted ModUp (the reference's use: ``operators/linear/shifted_lane.py:75-76``, unpacked
-    with ``unpack_cipher_batch``).  Residue-identical to rotating one at a time."""
+    with ``unpack_cipher_batch``).  Residue-identical to rotating one at a time.
+
+    ``output_ext`` (``operators/attention/prefill/input.py:1200-1205``): the rotations stay in the extended basis
+    Q u P, before their ModDown -- ``(P perm(c0) + <perm(d), key_b>, <perm(d), key_a>)`` over ``cur + K`` limbs,
+    ``is_ext`` set -- so that a multiply-accumulate over them (``grouped_pairwise_mac``) pays one ModDown
+    (``moddown_from_ext``) instead of one per rotation.  ``moddown_from_ext`` of one is ``homo_rotate``, word for word."""
     if isinstance(rotations, (int, np.integer)):
-        return homo_rotate(a, int(rotations), ctx)
-    return prepare_hoisted_baby_rotations(a, tuple(int(r) for r in rotations), ctx)[0]
+        rotations = (int(rotations),)
+        single = True
+    else:
+        single = False
+    if not output_ext:
+        if single:
+            return homo_rotate(a, rotations[0], ctx)
+        return prepare_hoisted_baby_rotations(a, tuple(int(r) for r in rotations), ctx)[0]
+    ctx = _ctx(ctx)
+    if a.batch_size != 1 or a.is_ext:
+        raise ValueError("fast_rotate(output_ext=True) expects one non-extended ciphertext")
+    cur = int(a.state.cur_limbs)
+    offsets = [int(r) for r in rotations]
+    block = _new_cipher(ctx, len(offsets), cur + ctx.K, a.state, a.slots)
+    block.is_ext = True
+    digits = dig_item = None
+    for b, off in enumerate(offsets):
+        g = ctx.galois(off)
+        if g == 1:   # (P c0, P c1): P is 0 modulo the special primes
+            pm = torch.tensor(ctx.p_mod_q(cur), dtype=torch.uint64, device=ctx.device)
+            for c in range(2):
+                block.cv[c][b, cur:].zero_()
+                _lib.call("holmes_mul_const", ctx.handle, a.cv[c][:1, :cur].data_ptr(), pm.data_ptr(),
+                          block.cv[c][b:b + 1].data_ptr(), 1, cur, _item_stride(a.cv[c]), _item_stride(block.cv[c]),
+                          _stream())
+            continue
+        if digits is None:
+            digits, dig_item = _modup(ctx, a.cv[1], cur, 1)
+        key_t, cap = ctx.switch_key(g, cur)
+        _lib.call("holmes_keyswitch_ext", ctx.handle, digits.data_ptr(), dig_item, cur, key_t.data_ptr(), cap, int(g),
+                  a.cv[0].data_ptr(), _item_stride(a.cv[0]), block.cv[0][b:b + 1].data_ptr(),
+                  block.cv[1][b:b + 1].data_ptr(), _item_stride(block.cv[0]), 1, _stream())
+    return block
+
+
+def moddown_from_ext(a: Cipher, ctx) -> Cipher:
+    """ModDown of an extended-basis ciphertext (``is_ext``, ``cur + K`` limbs) back to its ``cur`` Q limbs."""
+    ctx = _ctx(ctx)
+    if not a.is_ext:
+        raise ValueError("moddown_from_ext expects an extended-basis ciphertext")
+    cur = int(a.state.cur_limbs)
+    out = _new_cipher(ctx, a.batch_size, cur, a.state, a.slots)
+    scratch = ctx.workspace("ks", a.batch_size * 2 * (ctx.K + cur) * ctx.N)
+    _lib.call("holmes_moddown", ctx.handle, a.cv[0].data_ptr(), a.cv[1].data_ptr(), _item_stride(a.cv[0]), cur,
+              out.cv[0].data_ptr(), out.cv[1].data_ptr(), _item_stride(out.cv[0]), a.batch_size, scratch.data_ptr(),
+              _stream())
+    return out
+
+
+def grouped_pairwise_mac(batch: Cipher, plaintexts: Plaintext, groups: int, ctx) -> Cipher:
+    """``out[g] = sum_b plaintexts[g B + b] * batch[b]`` for a batch of B ciphertexts and ``groups * B`` plaintext
+    rows, a ``groups``-item batch (the reference's attention transforms call it with one group,
+    ``operators/attention/prefill/input.py:1019-1021``).  Extended-basis inputs (``is_ext``, e.g. from
+    ``fast_rotate(output_ext=True)``) need extended plaintexts (``Session.plaintext(..., is_ext=True)``) and give an
+    extended result."""
+    ctx = _ctx(ctx)
+    groups = int(groups)
+    nb = int(batch.batch_size)
+    cur = int(batch.state.cur_limbs)
+    pv = plaintexts.cv[0]
+    if int(pv.shape[0]) != groups * nb:
+        raise ValueError(f"grouped_pairwise_mac: {pv.shape[0]} plaintext rows for {groups} groups of {nb}")
+    if bool(batch.is_ext) != bool(plaintexts.is_ext):
+        raise ValueError("grouped_pairwise_mac: ciphertexts and plaintexts must both be extended or both not")
+    limbs = cur + (ctx.K if batch.is_ext else 0)
+    if int(pv.shape[1]) < limbs or int(plaintexts.state.cur_limbs) < cur:
+        raise ValueError("grouped_pairwise_mac: plaintexts have fewer limbs than the ciphertexts")
+    sf = None
+    if batch.state.scaling_factor is not None and plaintexts.state.scaling_factor is not None:
+        sf = float(batch.state.scaling_factor) * float(plaintexts.state.scaling_factor)
+    state = CipherState(cur, int(batch.state.scale_degree) + int(plaintexts.state.scale_degree), sf)
+    res = torch.empty((2, groups, 1, limbs, ctx.N), dtype=torch.uint64, device=ctx.device)
+    c0s = _lib.ptr_array([batch.cv[0].data_ptr()])
+    c1s = _lib.ptr_array([batch.cv[1].data_ptr()])
+    if batch.is_ext:
+        _lib.call("holmes_bsgs_mac_ext", ctx.handle, res.data_ptr(), c0s, c1s, _item_stride(batch.cv[0]), nb, 1,
+                  pv.data_ptr(), _item_stride(pv), groups, cur, _stream())
+    else:
+        _lib.call("holmes_bsgs_mac", ctx.handle, res.data_ptr(), c0s, c1s, _item_stride(batch.cv[0]), nb, 1,
+                  pv.data_ptr(), _item_stride(pv), groups, cur, _stream())
+    return Cipher([res[0, :, 0], res[1, :, 0]], state, batch.slots, bool(batch.is_ext), groups, ctx)
 
 
 def pack_cipher_batch(ciphers) -> Cipher:

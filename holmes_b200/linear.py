@@ -288,19 +288,22 @@ class Session:
                   is_ext: bool = False) -> F.Plaintext:
         """A public vector encoded at ``level``'s limbs and scale (reference: backend.py:303-330), cached per
         name, level, slot count and contents."""
-        if is_ext:
-            raise NotImplementedError("extended-basis plaintexts are not built")
         array = np.ascontiguousarray(np.asarray(values, dtype=dtype).reshape(-1))
         slots = self.max_slots if slots is None else int(slots)
-        key = (str(name), int(level), slots, hashlib.sha1(array.tobytes()).hexdigest())
+        key = (str(name), int(level), slots, bool(is_ext), hashlib.sha1(array.tobytes()).hexdigest())
         cache = self.__dict__.setdefault("_plaintexts", {})
         hit = cache.get(key)
         if hit is not None:
             return hit
         ctx = self.context
         cur = int(ctx.L) - int(level)
-        bundle = F.ConstantBundle({"value": F.PackedRaw(torch.from_numpy(array.astype(np.complex128)))})
-        pt = bundle.plaintext("value", state=F.CipherState(cur, 1, ctx.scale_at(cur)), slots=slots, context=ctx)
+        if is_ext:   # the extended basis Q u P (operators/attention/prefill/input.py:1013-1018)
+            z = torch.from_numpy(array.astype(np.complex128)).reshape(1, slots)
+            pv = F.encode_rows(ctx, z, cur, ctx.scale_at(cur), slots, ext=True)
+            pt = F.Plaintext([pv], F.CipherState(cur, 1, ctx.scale_at(cur)), slots, True, 1, ctx)
+        else:
+            bundle = F.ConstantBundle({"value": F.PackedRaw(torch.from_numpy(array.astype(np.complex128)))})
+            pt = bundle.plaintext("value", state=F.CipherState(cur, 1, ctx.scale_at(cur)), slots=slots, context=ctx)
         ctx.check_encode_range()
         cache[key] = pt
         return pt

@@ -71,6 +71,10 @@ int holmes_encode(void* ctx, double* z, long long row_stride, int rows, int slot
 int holmes_fft_special_inv(void* ctx, double* z, long long row_stride, int rows, int slots, void* stream);
 int holmes_encode_fft(void* ctx, const double* u, long long row_stride, int rows, int slots, double scale, int cur,
                       uint64_t* out, long long out_row_stride, int* flag, void* stream);
+/* holmes_encode_fft onto the extended basis: out[rows][cur + K][N], the Q limbs first, then the K special limbs
+ * (plaintexts for holmes_bsgs_mac_ext; EasyFHE's is_ext constants) */
+int holmes_encode_fft_ext(void* ctx, const double* u, long long row_stride, int rows, int slots, double scale, int cur,
+                          uint64_t* out, long long out_row_stride, int* flag, void* stream);
 /* diagonal rows of one BSGS chunk (weight.py:122-154 _cpu_packer / gpu_packer.py:48-200):
  * out[giant_count * baby][slots][2] complex; weight [dim][dim] float64 or complex128 (weight_complex = 1) */
 int holmes_pack_diagonals(const double* weight, int weight_complex, int dim, int lanes, int baby, int giant_base,
@@ -132,6 +136,23 @@ int holmes_keyswitch(void* ctx, const uint64_t* digits, long long digit_item, in
                      uint64_t galois, const uint64_t* add0, const uint64_t* add1, long long add_item,
                      const uint64_t* post0, const uint64_t* post1, long long post_item, uint64_t* out0,
                      uint64_t* out1, long long out_item, int items, uint64_t* scratch, void* stream);
+
+/* ---- extended basis Q u P (EasyFHE fast_rotate(output_ext=True) / grouped_pairwise_mac / moddown_from_ext,
+ *      llama3fhe/operators/attention/prefill/input.py:1007-1031, 1198-1236).  Extended ciphertexts are
+ *      [items][cur + K][N] with the Q limbs first. */
+/* the key switch of holmes_keyswitch without its ModDown: out0 = P perm(add0) + sum_j perm(digit_j) key_b[j],
+ * out1 = sum_j perm(digit_j) key_a[j], over all cur + K limbs (add0 may be NULL) */
+int holmes_keyswitch_ext(void* ctx, const uint64_t* digits, long long digit_item, int cur, const uint64_t* key,
+                         int key_cap, uint64_t galois, const uint64_t* add0, long long add_item, uint64_t* out0,
+                         uint64_t* out1, long long out_item, int items, void* stream);
+/* out_c [items][cur][N] = (in_c,Q - conv_{P->Q}(in_c,P)) P^-1, the ModDown; holmes_moddown(holmes_keyswitch_ext(x))
+ * equals holmes_keyswitch(x) word for word; scratch >= items * 2 * (K + cur) * N words */
+int holmes_moddown(void* ctx, const uint64_t* in0, const uint64_t* in1, long long in_item, int cur, uint64_t* out0,
+                   uint64_t* out1, long long out_item, int items, uint64_t* scratch, void* stream);
+/* holmes_bsgs_mac over the cur + K limbs of extended babies and plaintexts (limb l >= cur: special prime l - cur) */
+int holmes_bsgs_mac_ext(void* ctx, uint64_t* res, const uint64_t* const* c0s, const uint64_t* const* c1s,
+                        long long bstride, int nb, int inputs, const uint64_t* pts, long long pstride, int groups,
+                        int cur, void* stream);
 
 /* ---- BSGS plaintext multiply-accumulate (fhe.hoisted_mac_sum baby step, holmes_multi_mac.py:148-194):
  * res[2][groups][inputs][limbs][N] = sum_b pts[g * nb + b][limb] * baby_i[b][c][limb] (mod q_limb);
