@@ -694,11 +694,15 @@ def unpack_cipher_batch(batch: Cipher) -> tuple:
 
 def prepare_hoisted_baby_rotations(a: Cipher, baby_offsets, ctx, strategy: str = "normal",
                                    baby_anchor_step: int = -1):
-    """Baby basis rot(a, offset) for every offset from one hoisted ModUp; one block ``[nb]`` batch (the
-    ``normal`` strategy; the extended-basis strategies are not built and raise)."""
+    """Baby basis rot(a, offset) for every offset from one hoisted ModUp; one block ``[nb]`` batch.  ``ext_normal``
+    keeps the block over the extended basis Q u P (``fast_rotate(output_ext=True)``); ``ext_double_hoist`` is not
+    built and raises."""
     del baby_anchor_step
-    if str(strategy).lower() != "normal":
-        raise NotImplementedError(f"hoist strategy {strategy!r} is not built (only 'normal')")
+    strategy = str(strategy).lower()
+    if strategy == "ext_normal":
+        return (fast_rotate(a, tuple(int(o) for o in baby_offsets), ctx, output_ext=True),)
+    if strategy != "normal":
+        raise NotImplementedError(f"hoist strategy {strategy!r} is not built ('normal' and 'ext_normal' are)")
     ctx = _ctx(ctx)
     if a.batch_size != 1:
         raise ValueError("prepare_hoisted_baby_rotations expects one ciphertext")
@@ -720,22 +724,27 @@ def prepare_hoisted_baby_rotations(a: Cipher, baby_offsets, ctx, strategy: str =
 
 
 def bsgs_partial_sums(ctx: Context, baby_blocks, plaintexts: Plaintext, giants: int) -> torch.Tensor:
-    """res [2][giants][inputs][cur][N] = sum_b pt[g B + b] * baby_i[b] for every input's baby block."""
+    """res [2][giants][inputs][cur][N] = sum_b pt[g B + b] * baby_i[b] for every input's baby block (extended
+    blocks and plaintexts: [cur + K] limbs, over Q u P)."""
     blocks = list(baby_blocks)
     cur = int(blocks[0].state.cur_limbs)
     nb = int(blocks[0].batch_size)
+    ext = bool(blocks[0].is_ext)
+    if ext != bool(plaintexts.is_ext):
+        raise ValueError("bsgs_partial_sums: babies and plaintexts must both be extended or both not")
+    limbs = cur + (ctx.K if ext else 0)
     pv = plaintexts.cv[0]
     if int(pv.shape[0]) != giants * nb:
         raise ValueError(f"plaintext chunk has {pv.shape[0]} rows, expected {giants} x {nb}")
-    if int(plaintexts.state.cur_limbs) < cur or int(pv.shape[1]) < cur:
+    if int(plaintexts.state.cur_limbs) < cur or int(pv.shape[1]) < limbs:
         raise ValueError("plaintext chunk has fewer limbs than the baby basis")
-    res = torch.empty((2, giants, len(blocks), cur, ctx.N), dtype=torch.uint64, device=ctx.device)
+    res = torch.empty((2, giants, len(blocks), limbs, ctx.N), dtype=torch.uint64, device=ctx.device)
     bstride = _item_stride(blocks[0].cv[0])
     c0s = _lib.ptr_array([b.cv[0].data_ptr() for b in blocks])
     c1s = _lib.ptr_array([b.cv[1].data_ptr() for b in blocks])
     tok = OPTIMER.start("bsgs_mac")
-    _lib.call("holmes_bsgs_mac", ctx.handle, res.data_ptr(), c0s, c1s, bstride, nb, len(blocks), pv.data_ptr(),
-              _item_stride(pv), giants, cur, _stream())
+    _lib.call("holmes_bsgs_mac_ext" if ext else "holmes_bsgs_mac", ctx.handle, res.data_ptr(), c0s, c1s, bstride, nb,
+              len(blocks), pv.data_ptr(), _item_stride(pv), giants, cur, _stream())
     OPTIMER.stop(tok, (giants * nb + len(blocks) * nb * 2 + 2 * giants * len(blocks)) * cur * ctx.N * 8)
     return res
 
@@ -761,6 +770,10 @@ def hoisted_mac_sum(cipher: Cipher, baby_offsets, plaintexts: Plaintext, giant_o
         baby_rotations = prepare_hoisted_baby_rotations(cipher, baby_offsets, ctx, strategy, baby_anchor_step)
     block = baby_rotations[0]
     res = bsgs_partial_sums(ctx, [block], plaintexts, int(giant_count))
+    if block.is_ext:   # one ModDown per giant partial, then the plain Horner chain
+        down = moddown_from_ext(Cipher([res[0, :, 0], res[1, :, 0]], block.state, block.slots, True,
+                                       int(giant_count), ctx), ctx)
+        res = torch.stack([down.cv[0], down.cv[1]]).unsqueeze(2)
     acc0, acc1 = giant_horner(ctx, res, int(giant_offset))
     sf = None
     if block.state.scaling_factor is not None and plaintexts.state.scaling_factor is not None:
@@ -977,9 +990,9 @@ class ConstantBundle:
 
     def plaintext(self, name: str, *, state: CipherState, slots: int, context, is_ext: bool = False,
                   cache: bool = False) -> Plaintext:
-        del is_ext
+        """``is_ext``: encoded over the extended basis Q u P (``cur + K`` limbs, Q first)."""
         ctx = _ctx(context)
-        key = (name, int(slots), int(state.cur_limbs), float(state.scaling_factor or ctx.scale))
+        key = (name, int(slots), int(state.cur_limbs), float(state.scaling_factor or ctx.scale), bool(is_ext))
         hit = self._plain.get(key)
         if hit is not None:
             self._stats["plain_hits"] += 1
@@ -987,9 +1000,9 @@ class ConstantBundle:
         self._stats["plain_misses"] += 1
         mid = self._encoded_middle(name, slots=slots, context=ctx)
         scale = float(state.scaling_factor) if state.scaling_factor is not None else ctx.scale_at(state.cur_limbs)
-        pv = encode_rows(ctx, mid, int(state.cur_limbs), scale, int(slots), already_transformed=True)
-        pt = Plaintext([pv], CipherState(int(state.cur_limbs), int(state.scale_degree), scale), int(slots), False,
-                       int(pv.shape[0]), ctx)
+        pv = encode_rows(ctx, mid, int(state.cur_limbs), scale, int(slots), already_transformed=True, ext=bool(is_ext))
+        pt = Plaintext([pv], CipherState(int(state.cur_limbs), int(state.scale_degree), scale), int(slots),
+                       bool(is_ext), int(pv.shape[0]), ctx)
         if self.cache_mode in ("plain", "both") or (cache and self.cache_mode != "none"):
             self._plain[key] = pt
         return pt

@@ -447,14 +447,17 @@ _EMPTY_PROFILE = {"weight_prepare_cpu": 0.0, "weight_upload": 0.0, "baby_precomp
 
 class _Babies:
     """Baby basis of a batch of inputs: storage [B][2][I][cur][N] (baby-major, so a contiguous range of babies is
-    one contiguous block for the sharded build's all-gather; input i's babies are strided by 2 I cur N)."""
+    one contiguous block for the sharded build's all-gather; input i's babies are strided by 2 I cur N); with
+    ``ext`` the babies are over the extended basis Q u P, [cur + K] limbs."""
 
-    def __init__(self, sources, level: int, storage: torch.Tensor, state: F.CipherState, slots: int) -> None:
+    def __init__(self, sources, level: int, storage: torch.Tensor, state: F.CipherState, slots: int,
+                 ext: bool = False) -> None:
         self.sources = tuple(sources)
         self.level = level
         self.storage = storage
         self.state = state
         self.slots = slots
+        self.ext = bool(ext)
         self.pending = None  # all-gather still filling other ranks' babies (sharded build)
 
     def ready(self) -> None:
@@ -469,7 +472,7 @@ class _Babies:
         for i in range(inputs):
             c0 = self.storage[:, 0, i]
             c1 = self.storage[:, 1, i]
-            out.append(F.Cipher([c0, c1], self.state, self.slots, False, B, ctx))
+            out.append(F.Cipher([c0, c1], self.state, self.slots, self.ext, B, ctx))
         return out
 
 
@@ -521,7 +524,9 @@ class LinearOperator:
         cur = int(inputs[0].state.cur_limbs)
         n_in = len(inputs)
         B = int(plan.baby_steps)
-        storage = torch.empty((B, 2, n_in, cur, ctx.N), dtype=torch.uint64, device=ctx.device)
+        ext = str(self.config.hoist_strategy).lower() == "ext_normal"
+        limbs = cur + (ctx.K if ext else 0)
+        storage = torch.empty((B, 2, n_in, limbs, ctx.N), dtype=torch.uint64, device=ctx.device)
         c0 = torch.stack([c.cv[0][0, :cur] for c in inputs])
         c1 = torch.stack([c.cv[1][0, :cur] for c in inputs])
         lo, hi = 0, B
@@ -529,15 +534,28 @@ class LinearOperator:
         if shard is not None and B % shard[1] == 0 and shard[1] > 1:
             lo, hi = shard[0] * B // shard[1], (shard[0] + 1) * B // shard[1]
         if lo == 0:
-            storage[0, 0].copy_(c0)
-            storage[0, 1].copy_(c1)
+            if ext:   # baby 0 over Q u P: (P c0, P c1), zero on the special limbs
+                pm = torch.tensor(ctx.p_mod_q(cur), dtype=torch.uint64, device=ctx.device)
+                for c, src in ((0, c0), (1, c1)):
+                    storage[0, c, :, cur:].zero_()
+                    _lib.call("holmes_mul_const", ctx.handle, src.data_ptr(), pm.data_ptr(), storage[0, c].data_ptr(),
+                              n_in, cur, F._item_stride(src), F._item_stride(storage[0, c]), F._stream())
+            else:
+                storage[0, 0].copy_(c0)
+                storage[0, 1].copy_(c1)
         if max(lo, 1) < hi:
             digits, dig_item = F._modup(ctx, c1, cur, n_in)
             for b in range(max(lo, 1), hi):
                 g = ctx.galois(plan.baby_offsets[b])
-                F._keyswitch(ctx, digits, dig_item, cur, g, ctx.switch_key(g, cur), c0, None, F._item_stride(c0),
-                             storage[b, 0], storage[b, 1], n_in)
-        entry = _Babies(inputs, level, storage, inputs[0].state, int(inputs[0].slots))
+                if ext:
+                    key_t, cap = ctx.switch_key(g, cur)
+                    _lib.call("holmes_keyswitch_ext", ctx.handle, digits.data_ptr(), dig_item, cur, key_t.data_ptr(),
+                              cap, int(g), c0.data_ptr(), F._item_stride(c0), storage[b, 0].data_ptr(),
+                              storage[b, 1].data_ptr(), F._item_stride(storage[b, 0]), n_in, F._stream())
+                else:
+                    F._keyswitch(ctx, digits, dig_item, cur, g, ctx.switch_key(g, cur), c0, None, F._item_stride(c0),
+                                 storage[b, 0], storage[b, 1], n_in)
+        entry = _Babies(inputs, level, storage, inputs[0].state, int(inputs[0].slots), ext)
         if (lo, hi) != (0, B):
             from .collectives import all_gather_rows
             # asynchronous: the first chunk's encode (which needs no babies) overlaps the transfer
@@ -582,11 +600,12 @@ class LinearOperator:
         if self._closed:
             raise RuntimeError("linear operator is closed.")
         strategy = str(self.config.hoist_strategy).lower()
-        if strategy != "normal":
-            # The extended-basis schedules keep the babies and the MAC in Q*P and ModDown later; their rounding is
-            # EasyFHE's and cannot be pinned here, so they are refused rather than silently run as "normal".
-            raise NotImplementedError(f"hoist_strategy {strategy!r} is not built; the production linear schedule "
-                                      "(operators/linear/config.py:123-135) is 'normal'")
+        if strategy not in ("normal", "ext_normal"):
+            # ext_double_hoist also keeps the giant rotations in Q*P; its schedule is EasyFHE's and cannot be pinned
+            # here, so it is refused rather than silently run as another strategy.
+            raise NotImplementedError(f"hoist_strategy {strategy!r} is not built ('normal' and 'ext_normal' are; the "
+                                      "production linear schedule, operators/linear/config.py:123-135, is 'normal')")
+        ext = strategy == "ext_normal"
         inputs = tuple(input_ciphers)
         if not inputs:
             return (), dict(_EMPTY_PROFILE)
@@ -640,6 +659,14 @@ class LinearOperator:
             babies.ready()
             res = F.bsgs_partial_sums(ctx, blocks, pts, int(chunk.giant_count))
             del pts
+            if ext:   # ext_normal: babies and MAC over Q u P, one ModDown per giant partial, then the plain Horner
+                G = int(res.shape[1])
+                down = torch.empty((2, G, n_in, cur, ctx.N), dtype=torch.uint64, device=ctx.device)
+                scratch = ctx.workspace("ks", G * n_in * 2 * (ctx.K + cur) * ctx.N)
+                _lib.call("holmes_moddown", ctx.handle, res[0].data_ptr(), res[1].data_ptr(), (cur + ctx.K) * ctx.N,
+                          cur, down[0].data_ptr(), down[1].data_ptr(), cur * ctx.N, G * n_in, scratch.data_ptr(),
+                          F._stream())
+                res = down
             g0, g1 = F.giant_horner(ctx, res, int(plan.giant_offset))
             shift = int(chunk.giant_base) * int(plan.giant_offset)
             if acc0 is None:

@@ -273,6 +273,60 @@ def _oracle_linear(o, ref_inputs, weight, plan, cur, scale):
     return outs
 
 
+def _oracle_linear_ext(o, ref_inputs, weight, plan, cur, scale):
+    """ext_normal restatement: babies and MAC over Q u P, one ModDown per giant partial, then the plain Horner."""
+    ids = o.ext_ids(cur)
+    moduli = [o.pr.q[i] for i in ids]
+    outs = []
+    for ref in ref_inputs:
+        babies = [o.rotate_ext(ref, r) for r in plan.baby_offsets]
+        acc = None
+        for chunk in plan.chunks:
+            rows = packing.diagonal_rows(weight, dimension=plan.dimension, token_lanes=plan.token_lanes,
+                                         baby_steps=plan.baby_steps, giant_base=chunk.giant_base,
+                                         giant_count=chunk.giant_count, lane_shift=plan.lane_shift)
+            pts = np.stack([o.encode_ext(r, cur, scale) for r in rows])
+            part = o.bsgs_mac(pts, babies, chunk.giant_count, moduli=moduli)
+            down = [np.stack([o.moddown(part[c][g], cur) for g in range(chunk.giant_count)]) for c in range(2)]
+            res = o.giant_horner(down, plan.giant_offset)
+            if chunk.giant_base:
+                res = o.rotate(res, chunk.giant_base * plan.giant_offset)
+            acc = res if acc is None else (o.add(acc[0], res[0], range(cur)), o.add(acc[1], res[1], range(cur)))
+        outs.append(o.rescale(acc))
+    return outs
+
+
+def test_linear_operator_ext_normal_bitexact_and_decodes():
+    """hoist_strategy "ext_normal": the same page residue for residue against its restatement, decoded like
+    "normal" (the ModDowns move, the rounding differs by noise only)."""
+    from holmes_b200 import linear as LN
+
+    o, client, ctx = make_pair(log_n=11, limbs=4, dnum=2, dcrt=45, first=55, special=55)
+    session = LN.Session(client, ctx)
+    dim, lanes = 64, 16
+    cfg = LN.LinearOperatorConfig(baby_steps=8, baby_anchor_step=8, max_plaintext_rows=16, hoist_strategy="ext_normal")
+    plan = cfg.plan(dimension=dim, token_lanes=lanes)
+    rng = np.random.default_rng(7)
+    w = rng.normal(scale=0.02, size=(dim, dim))
+    xs = rng.normal(size=(2, lanes, dim))
+    cur = ctx.L
+    cts, refs = [], []
+    for i, x in enumerate(xs):
+        ct, ref = _cipher(o, client, x.T.reshape(-1), cur, 200 + i)
+        cts.append(ct)
+        refs.append(ref)
+    with LN.LinearOperator(crypto_context=session, token_lanes=lanes, config=cfg) as op, \
+            LN.LinearWeight(w, dtype=w.dtype, crypto_context=session) as lw:
+        outs, _ = op.apply(cts, lw)
+    expect = _oracle_linear_ext(o, refs, w, plan, cur, ctx.scale)
+    for got, e, x in zip(outs, expect, xs):
+        np.testing.assert_array_equal(host(got.cv[0][0]), e[0])
+        np.testing.assert_array_equal(host(got.cv[1][0]), e[1])
+        dec = client.decrypt(got).reshape(dim, lanes).T
+        np.testing.assert_allclose(dec, x @ w.T, atol=2e-8 * 50, rtol=2e-6)
+    ctx.close()
+
+
 @pytest.mark.parametrize("complex_weight", [False, True])
 def test_linear_operator_bitexact_and_decodes(complex_weight):
     from holmes_b200 import linear as LN
