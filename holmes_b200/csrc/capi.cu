@@ -176,6 +176,12 @@ int holmes_mul_const(void* ctx, const uint64_t* a, const uint64_t* consts, uint6
   return mul_const(*C(ctx), a, consts, out, items, limbs, a_item, out_item, S(stream));
 }
 
+int holmes_weighted_acc(void* ctx, const uint64_t* a, long long a_item, int nk, const uint64_t* weights, uint64_t* out,
+                        long long out_item, int groups, int limbs, void* stream) {
+  if (!ctx || !a || !weights || !out) return -1;
+  return weighted_acc(*C(ctx), a, a_item, nk, weights, out, out_item, groups, limbs, S(stream));
+}
+
 int holmes_rescale(void* ctx, const uint64_t* in, long long in_stride, uint64_t* out, long long out_stride, int cur,
                    int comps, uint64_t* scratch, void* stream) {
   if (!ctx || !in || !out || !scratch || comps < 1) return -1;

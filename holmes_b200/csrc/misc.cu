@@ -118,6 +118,34 @@ int mul_const(const HolmesCtx& c, const u64* a, const u64* consts, u64* out, int
   return (int)cudaGetLastError();
 }
 
+// out[g][l][n] = sum_k w[g][k][l] * a[k][l][n] mod q_l (the Chebyshev / Paterson-Stockmeyer linear combination,
+// grouped_scalar_weighted_acc): grid (N / 256, limbs, groups), radix-2^30 split products folded every 16 terms.
+__global__ void k_weighted_acc(const u64* __restrict__ a, long long ai, int nk, const u64* __restrict__ w,
+                               u64* __restrict__ o, long long oi, int limbs, int log_n, const Mod* __restrict__ mods) {
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  const int l = blockIdx.y, g = blockIdx.z;
+  const Mod m = mods[l];
+  const u64* ap = a + ((size_t)l << log_n) + n;
+  const u64* wp = w + ((size_t)g * nk) * limbs + l;
+  Split4 s{0, 0, 0, 0};
+  for (int k = 0; k < nk; ++k) {
+    split_mac(s, ap[k * ai], wp[(size_t)k * limbs]);
+    if ((k & 15) == 15 && k + 1 < nk) {  // restart from a representative below 8 q: 16 more products fit
+      const u64 r = fold_split_lazy(s, m);
+      s = Split4{r & ((1ull << 30) - 1), r >> 30, 0, 0};
+    }
+  }
+  o[g * oi + ((size_t)l << log_n) + n] = fold_split(s, m);
+}
+int weighted_acc(const HolmesCtx& c, const u64* a, long long a_item, int nk, const u64* w, u64* out, long long o_item,
+                 int groups, int limbs, cudaStream_t st) {
+  if (limbs < 1 || limbs > c.T || nk < 1 || groups < 1 || groups > 65535 || c.n < 256) return -2;
+  count_launch();
+  k_weighted_acc<<<dim3((unsigned)(c.n / 256), (unsigned)limbs, (unsigned)groups), 256, 0, st>>>(
+      a, a_item, nk, w, out, o_item, limbs, c.log_n, c.d_mod);
+  return (int)cudaGetLastError();
+}
+
 __global__ void k_add_const(const u64* __restrict__ a, const u64* __restrict__ k, u64* __restrict__ o, int items,
                             int limbs, long long ai, long long oi, int log_n, const Mod* __restrict__ mods) {
   const size_t per_item = (size_t)limbs << log_n;

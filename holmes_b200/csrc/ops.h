@@ -105,6 +105,8 @@ int mul_i(const HolmesCtx& c, const u64* a, u64* out, int items, int limbs, long
           cudaStream_t st);
 int automorph(const HolmesCtx& c, const u64* a, u64* out, u64 galois, int items, int limbs, long long a_item,
               long long o_item, cudaStream_t st);
+int weighted_acc(const HolmesCtx& c, const u64* a, long long a_item, int nk, const u64* w, u64* out, long long o_item,
+                 int groups, int limbs, cudaStream_t st);
 int mul_const(const HolmesCtx& c, const u64* a, const u64* consts, u64* out, int items, int limbs, long long a_item,
               long long o_item, cudaStream_t st);
 

@@ -20,6 +20,7 @@ from __future__ import annotations
 
 import dataclasses
 import math
+import types
 from dataclasses import dataclass, field
 
 import numpy as np
@@ -851,15 +852,57 @@ def homo_mul_relin_rescale_postop(a: Cipher, b: Cipher, ctx) -> Cipher:
 # operators/norm/refresh.py:21-31).
 
 
-@dataclass
 class EncodedScalar:
-    value: float
-    integer: int  # round(value * scaling_factor)
-    state: CipherState
+    """One encoded scalar ``EncodedScalar(value, integer, state)`` (``integer = round(value * scaling_factor)``), or
+    the reference's weight table ``EncodedScalar(residues, cur_limbs, scale_degree, scaling_factor)`` with
+    ``residues`` a ``[groups][n][cur]`` uint64 tensor (``operators/nonlinear/polynomial.py:286-291``) for
+    ``grouped_scalar_weighted_acc``."""
+
+    def __init__(self, *args) -> None:
+        if args and torch.is_tensor(args[0]):
+            residues, cur_limbs, scale_degree, scaling_factor = args
+            self.table = residues
+            self.value = None
+            self.integer = None
+            self.state = CipherState(int(cur_limbs), int(scale_degree),
+                                     None if scaling_factor is None else float(scaling_factor))
+        else:
+            value, integer, state = args
+            self.table = None
+            self.value = float(value)
+            self.integer = int(integer)
+            self.state = state
 
     def residues(self, ctx, limbs: int) -> torch.Tensor:
+        if self.table is not None:
+            raise ValueError("a weight table has no single residue vector")
         return torch.tensor([self.integer % ctx.q(i) for i in range(int(limbs))], dtype=torch.uint64,
                             device=ctx.device)
+
+
+def grouped_scalar_weighted_acc(batch: Cipher, table: EncodedScalar, ctx) -> Cipher:
+    """``out[g] = sum_k table[g][k] * batch[k]`` in one launch per component, residue-identical to the loop of
+    scalar multiplies and adds (each product reduced mod q_l, the sum exact mod q_l); ``groups`` items out."""
+    ctx = _ctx(ctx)
+    if table.table is None:
+        raise ValueError("grouped_scalar_weighted_acc needs a weight table EncodedScalar")
+    res = table.table.to(device=ctx.device, dtype=torch.uint64).contiguous()
+    cur = int(batch.state.cur_limbs)
+    n = int(batch.batch_size)
+    if res.dim() != 3 or int(res.shape[1]) != n or int(res.shape[2]) < cur:
+        raise ValueError(f"weight table of shape {tuple(res.shape)} for {n} ciphertexts at {cur} limbs")
+    if int(res.shape[2]) != cur:
+        res = res[:, :, :cur].contiguous()
+    groups = int(res.shape[0])
+    sf = None
+    if batch.state.scaling_factor is not None and table.state.scaling_factor is not None:
+        sf = float(batch.state.scaling_factor) * float(table.state.scaling_factor)
+    state = CipherState(cur, int(batch.state.scale_degree) + int(table.state.scale_degree), sf)
+    out = _new_cipher(ctx, groups, cur, state, batch.slots)
+    for c in range(len(batch.cv)):
+        _lib.call("holmes_weighted_acc", ctx.handle, batch.cv[c].data_ptr(), _item_stride(batch.cv[c]), n,
+                  res.data_ptr(), out.cv[c].data_ptr(), _item_stride(out.cv[c]), groups, cur, _stream())
+    return out
 
 
 def encode_scalar(value, cur_limbs: int, scale_degree: int = 1, scaling_factor: float | None = None,
@@ -962,10 +1005,11 @@ class ConstantBundle:
     """Named plaintext constants with an optional cache of the FFT'd values ("middle") and/or the final
     NTT plaintexts ("plain"), per ``cache_mode`` in {"none", "middle", "plain", "both"}."""
 
-    def __init__(self, vectors: dict, cache_mode: str = "none") -> None:
+    def __init__(self, vectors: dict | None = None, cache_mode: str = "none", scalars: dict | None = None) -> None:
         if cache_mode not in ("none", "middle", "plain", "both"):
             raise ValueError(f"unknown cache_mode {cache_mode!r}")
-        self.vectors = dict(vectors)
+        self.vectors = dict(vectors or {})
+        self.scalars = {str(k): float(v) for k, v in (scalars or {}).items()}
         self.cache_mode = cache_mode
         self._middle: dict = {}
         self._plain: dict = {}
@@ -1006,6 +1050,20 @@ class ConstantBundle:
         if self.cache_mode in ("plain", "both") or (cache and self.cache_mode != "none"):
             self._plain[key] = pt
         return pt
+
+    def encoded_scalars(self, names, *, cur_limbs: int, scale_degree: int = 1, context=None,
+                        scaling_factor: float | None = None, cache: bool = False):
+        """The named scalars as residues ``[len(names)][cur]`` of ``round(value * scaling_factor)`` (the reference's
+        weight-table source, ``operators/nonlinear/polynomial.py:278-285``)."""
+        del cache
+        ctx = _ctx(context)
+        cur = int(cur_limbs)
+        sf = float(scaling_factor) if scaling_factor is not None else ctx.scale_at(cur)
+        ints = [int(round(self.scalars[str(nm)] * sf)) for nm in names]
+        residues = torch.tensor([[v % ctx.q(i) for i in range(cur)] for v in ints], dtype=torch.uint64,
+                                device=ctx.device)
+        return types.SimpleNamespace(residues=residues, cur_limbs=cur, scale_degree=int(scale_degree),
+                                     scaling_factor=sf)
 
     def cache_info(self) -> dict:
         mb = sum(int(t.numel()) * t.element_size() for t in self._middle.values())

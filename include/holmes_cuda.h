@@ -91,6 +91,10 @@ int holmes_mul_i(void* ctx, const uint64_t* a, uint64_t* out, int items, int lim
 /* NTT-domain automorphism X -> X^galois */
 int holmes_automorph(void* ctx, const uint64_t* a, uint64_t* out, uint64_t galois, int items, int limbs,
                      long long a_item, long long out_item, void* stream);
+/* out[g][l][n] = sum_k weights[g][k][l] * a[k][l][n] (mod q_l) for k < nk, canonical residues (one component;
+ * EasyFHE grouped_scalar_weighted_acc, llama3fhe/operators/nonlinear/polynomial.py:255-300) */
+int holmes_weighted_acc(void* ctx, const uint64_t* a, long long a_item, int nk, const uint64_t* weights, uint64_t* out,
+                        long long out_item, int groups, int limbs, void* stream);
 /* multiply limb l by consts[l] (device array of canonical residues) */
 int holmes_mul_const(void* ctx, const uint64_t* a, const uint64_t* consts, uint64_t* out, int items, int limbs,
                      long long a_item, long long out_item, void* stream);

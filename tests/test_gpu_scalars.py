@@ -51,3 +51,33 @@ def test_add_scalar_and_pt(env):
     assert np.abs(client.decrypt(out) - (z + w)).max() < 1e-6
     with pytest.raises(ValueError):
         F.encode_scalar(1j, cur_limbs=4, context=ctx)
+
+
+def test_grouped_scalar_weighted_acc_matches_the_loop():
+    """polynomial.py:255-300: the weight table through one launch equals the scalar-multiply-and-add loop residue for
+    residue (20 terms: the kernel's sums restart after 16)."""
+    from holmes_b200 import fhe as F
+
+    o, client, ctx = make_pair(log_n=10, limbs=4, dnum=2, dcrt=40, first=50, special=50)
+    try:
+        rng = np.random.default_rng(11)
+        n, cur = 20, 3
+        cts = [client.encrypt(rng.normal(size=ctx.max_slots) * 0.3, cur_limbs=cur, counter=60 + i) for i in range(n)]
+        batch = F.pack_cipher_batch(cts)
+        weights = rng.normal(size=(2, n))
+        sf = float(cts[0].state.scaling_factor)
+        bundle = F.ConstantBundle(scalars={f"w{g}_{k}": weights[g, k] for g in range(2) for k in range(n)})
+        tables = [bundle.encoded_scalars([f"w{g}_{k}" for k in range(n)], cur_limbs=cur, scale_degree=1, context=ctx,
+                                         scaling_factor=sf) for g in range(2)]
+        table = F.EncodedScalar(F.torch.stack([t.residues for t in tables]), cur, 1, sf)
+        acc = F.grouped_scalar_weighted_acc(batch, table, ctx)
+        assert acc.batch_size == 2
+        for g in range(2):
+            loop = None
+            for k in range(n):
+                term = F.homo_mul_scalar(cts[k], F.encode_scalar(weights[g, k], cur, 1, sf, ctx), ctx)
+                loop = term if loop is None else F.homo_add(loop, term, ctx)
+            for c in range(2):
+                np.testing.assert_array_equal(host(acc.cv[c][g]), host(loop.cv[c][0, :cur]))
+    finally:
+        ctx.close()
