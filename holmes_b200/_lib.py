@@ -39,6 +39,7 @@ SIGNATURES = {
     "holmes_fft_special_inv": [p, p, i64, i32, i32, p],
     "holmes_encode_fft": [p, p, i64, i32, i32, d, i32, p, i64, p, p],
     "holmes_encode_fft_ext": [p, p, i64, i32, i32, d, i32, p, i64, p, p],
+    "holmes_encode_stage2": [p, p, i64, i32, d, i32, p, p, p, p, p, p, p, i32, i32, i32],
     "holmes_pack_diagonals":[p, i32, i32, i32, i32, i32, i32, i32, i32, p, i64, p],
     "holmes_elementwise": [p, i32, p, p, p, i32, i32, i64, i64, i64, p],
     "holmes_mul_i": [p, p, p, i32, i32, i64, i64, p],

@@ -120,6 +120,19 @@ int holmes_encode(void* ctx, double* z, long long row_stride, int rows, int slot
   return encode_rows(*C(ctx), z, row_stride, rows, slots, scale, cur, out, out_row_stride, flag, S(stream));
 }
 
+int holmes_encode_stage2(void* out, const void* in, long long in_stride, int rows, double sf, int limbs,
+                         const void* primes, const void* diffs, const void* ratios, const void* ks, const void* roots,
+                         const void* roots_shoup, void* stream, int rows_per_launch, int parts, int limbs_per_block) {
+  (void)diffs;             // negative values are reduced as signed integers directly
+  (void)rows_per_launch;   // scheduling hints of the reference's kernels
+  (void)limbs_per_block;
+  if (!out || !in || !primes || !ratios || !ks || !roots || !roots_shoup) return -1;
+  if ((parts & 3) == 0) return 0;
+  return encode_stage2((u64*)out, (const double*)in, in_stride, rows, sf, limbs, (const u64*)primes,
+                       (const u64*)ratios, (const u64*)ks, (const u64*)roots, (const u64*)roots_shoup, nullptr,
+                       S(stream));
+}
+
 int holmes_fft_special_inv(void* ctx, double* z, long long row_stride, int rows, int slots, void* stream) {
   if (!ctx || !z) return -1;
   return fft_special_inv(*C(ctx), z, row_stride, rows, slots, S(stream));

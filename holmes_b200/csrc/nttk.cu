@@ -20,6 +20,10 @@
 //   encode                        llround(v * scale) and the signed reduction fused into the NTT load
 //   decrypt, keygen, encrypt      c0 + c1 s / CBD error sampling fused into the NTT load; the key /
 //                                 ciphertext assembly fused into the store
+#include <map>
+#include <mutex>
+#include <tuple>
+
 #include "ntt.cuh"
 #include "ntt16.cuh"
 #include "ops.h"
@@ -870,41 +874,42 @@ __global__ void HOLMES_NTT_BOUNDS(LOGN) k_encode(NttTables T, LdRounded<WIDE> ld
   ntt_forward_body<LOGN>(p, ld.first + p % (ld.cur - ld.first), T, ld, st);
 }
 
-int encode_rows(const HolmesCtx& c, const double* u, long long row_stride, int rows, int slots, double scale, int cur,
-                u64* out, long long out_row_stride, int* flag, cudaStream_t st, int mod_first) {
-  if (cur < 1 || mod_first < 0 || mod_first + cur > c.T) return -2;
-  if (slots < 1 || slots > c.n / 2 || (slots & (slots - 1))) return -3;
-  if (out_row_stride < (long long)cur * c.n) return -4;
+// The encode on explicit tables: output limb l has twiddles tw + l N and modulus mods[l]; qs (host, may be null)
+// lets a limb take the direct signed load when 8 q > 2^61.
+static int encode_rows_tables(const Tw* tw, const Mod* mods, const u64* qs, int log_n, const double* u,
+                              long long row_stride, int rows, int slots, double scale, int cur, u64* out,
+                              long long out_row_stride, int* flag, cudaStream_t st) {
+  const int n = 1 << log_n;
+  if (slots < 1 || slots > n / 2 || (slots & (slots - 1))) return -3;
+  if (out_row_stride < (long long)cur * n) return -4;
   int gap_log = 0;
-  while ((slots << (gap_log + 1)) < c.n) ++gap_log;
-  u64* ints = out + (size_t)(cur - 1) * c.n;  // row r's integers at ints + r * out_row_stride
+  while ((slots << (gap_log + 1)) < n) ++gap_log;
+  u64* ints = out + (size_t)(cur - 1) * n;  // row r's integers at ints + r * out_row_stride
   {
-    const size_t work = (size_t)rows << c.log_n;
+    const size_t work = (size_t)rows << log_n;
     size_t blocks = (work + 255) / 256;
     if (blocks > 148 * 16) blocks = 148 * 16;
     count_launch();
-    k_round_rows<<<(unsigned)blocks, 256, 0, st>>>(u, row_stride, rows, gap_log, c.log_n, scale, ints, out_row_stride,
+    k_round_rows<<<(unsigned)blocks, 256, 0, st>>>(u, row_stride, rows, gap_log, log_n, scale, ints, out_row_stride,
                                                     flag);
     HOLMES_CUDA_TRY(cudaGetLastError());
   }
-  // output limb l has modulus mod_first + l: the tables are taken from there on
-  NttTables T{c.d_tw + (size_t)mod_first * c.n, c.d_mod + mod_first};
-  const Mod* mods = c.d_mod + mod_first;
+  NttTables T{tw, mods};
   // limbs 0 .. cur-2 from the integers, then limb cur-1 in place
   for (int pass = 0; pass < 2; ++pass) {
     const int first = pass ? cur - 1 : 0, last = pass ? cur : cur - 1;
     if (last <= first) continue;
-    bool wide = true;
-    for (int l = first; l < last; ++l) wide = wide && (c.q[mod_first + l] << 3) > (1ull << 61);
+    bool wide = qs != nullptr;
+    for (int l = first; l < last && wide; ++l) wide = (qs[l] << 3) > (1ull << 61);
     LdRounded<true> lw{ints, out_row_stride, mods, last, first};
     LdRounded<false> ln{ints, out_row_stride, mods, last, first};
-    PolyMap pm = poly_map(last - first, out_row_stride, c.n, 0);
-    StPlain sp{out + (size_t)first * c.n, pm};
+    PolyMap pm = poly_map(last - first, out_row_stride, n, 0);
+    StPlain sp{out + (size_t)first * n, pm};
     const int polys = rows * (last - first);
-    if (c.log_n == 16) {
-      const int e = wide ? ntt16_forward(T, ModEnc{first, last - first}, lw, IMPlain{out + (size_t)first * c.n, pm}, sp,
+    if (log_n == 16) {
+      const int e = wide ? ntt16_forward(T, ModEnc{first, last - first}, lw, IMPlain{out + (size_t)first * n, pm}, sp,
                                          polys, st)
-                         : ntt16_forward(T, ModEnc{first, last - first}, ln, IMPlain{out + (size_t)first * c.n, pm}, sp,
+                         : ntt16_forward(T, ModEnc{first, last - first}, ln, IMPlain{out + (size_t)first * n, pm}, sp,
                                          polys, st);
       if (e) return e;
       continue;
@@ -917,10 +922,68 @@ int encode_rows(const HolmesCtx& c, const double* u, long long row_stride, int r
     if (e != cudaSuccess) return (int)e;                                                                         \
     break;                                                                                                       \
   }
-    HOLMES_LOGN_SWITCH(c.log_n, L_)
+    HOLMES_LOGN_SWITCH(log_n, L_)
 #undef L_
   }
   return 0;
+}
+
+int encode_rows(const HolmesCtx& c, const double* u, long long row_stride, int rows, int slots, double scale, int cur,
+                u64* out, long long out_row_stride, int* flag, cudaStream_t st, int mod_first) {
+  if (cur < 1 || mod_first < 0 || mod_first + cur > c.T) return -2;
+  // output limb l has modulus mod_first + l: the tables are taken from there on
+  return encode_rows_tables(c.d_tw + (size_t)mod_first * c.n, c.d_mod + mod_first, c.q.data() + mod_first, c.log_n,
+                            u, row_stride, rows, slots, scale, cur, out, out_row_stride, flag, st);
+}
+
+// The reference's in-tree encode ABI (bench/cmp/kernels/holmes_encode.cu:240-285), context-free: the caller's
+// per-limb primes / Barrett ratios and exponents and its root tables (psi^bitrev(k) and their Shoup companions,
+// [limbs][N]) are gathered once per table address into this engine's interleaved form (cached per device).
+__global__ void k_gather_tables(const u64* __restrict__ roots, const u64* __restrict__ roots_shoup,
+                                const u64* __restrict__ primes, const u64* __restrict__ ratios,
+                                const u64* __restrict__ ks, int limbs, int log_n, Tw* __restrict__ tw,
+                                Mod* __restrict__ mods) {
+  const size_t total = (size_t)limbs << log_n;
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x)
+    tw[i] = Tw{roots[i], roots_shoup[i]};
+  const size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (t < (size_t)limbs) mods[t] = Mod{primes[t], ratios[t], (u32)(ks[t] - 64), 0};
+}
+__device__ int g_stage2_range;  // the 2^61 range flag of encode_stage2 calls (the reference checks on the host)
+int encode_stage2(u64* out, const double* in, long long in_stride, int rows, double sf, int limbs, const u64* primes,
+                  const u64* ratios, const u64* ks, const u64* roots, const u64* roots_shoup, int* flag,
+                  cudaStream_t st) {
+  constexpr int kLogN = 16;
+  if (limbs < 1 || rows < 0) return -2;
+  if (rows == 0) return 0;
+  if (!flag) HOLMES_CUDA_TRY(cudaGetSymbolAddress((void**)&flag, g_stage2_range));
+  struct Entry {
+    Tw* tw;
+    Mod* mods;
+  };
+  static std::mutex mu;
+  static std::map<std::tuple<int, const void*, const void*, int>, Entry> cache;
+  int dev = 0;
+  HOLMES_CUDA_TRY(cudaGetDevice(&dev));
+  Entry e{};
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    const auto key = std::make_tuple(dev, (const void*)roots, (const void*)primes, limbs);
+    auto it = cache.find(key);
+    if (it == cache.end()) {
+      HOLMES_CUDA_TRY(cudaMalloc(&e.tw, ((size_t)limbs << kLogN) * sizeof(Tw)));
+      HOLMES_CUDA_TRY(cudaMalloc(&e.mods, (size_t)limbs * sizeof(Mod)));
+      count_launch();
+      k_gather_tables<<<148 * 4, 256, 0, st>>>(roots, roots_shoup, primes, ratios, ks, limbs, kLogN, e.tw, e.mods);
+      HOLMES_CUDA_TRY(cudaGetLastError());
+      cache.emplace(key, e);
+    } else {
+      e = it->second;
+    }
+  }
+  // full slots (N / 2 complex values per row, interleaved), the generic signed reduction (no host moduli)
+  return encode_rows_tables(e.tw, e.mods, nullptr, kLogN, in, in_stride, rows, 1 << (kLogN - 1), sf, limbs, out,
+                            (long long)limbs << kLogN, flag, st);
 }
 
 // --------------------------------------------------------------------------------------------- decrypt

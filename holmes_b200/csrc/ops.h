@@ -85,6 +85,9 @@ int add_const(const HolmesCtx& c, const u64* a, const u64* consts, u64* out, int
 
 // Rows of slot vectors after the special inverse FFT ([rows][slots] complex, interleaved doubles) ->
 // [rows][cur][N] NTT plaintexts at `scale`.  Out-of-range values set *flag = 1.
+int encode_stage2(u64* out, const double* in, long long in_stride, int rows, double sf, int limbs, const u64* primes,
+                  const u64* ratios, const u64* ks, const u64* roots, const u64* roots_shoup, int* flag,
+                  cudaStream_t st);
 int encode_rows(const HolmesCtx& c, const double* u, long long row_stride, int rows, int slots, double scale, int cur,
                 u64* out, long long out_row_stride, int* flag, cudaStream_t st, int mod_first = 0);
 

@@ -69,6 +69,15 @@ int holmes_encode(void* ctx, double* z, long long row_stride, int rows, int slot
 /* the two halves of holmes_encode: the inverse special FFT in place (EasyFHE cv_pre_encode_stage1), and the
  * rounding / reduction / NTT of already transformed rows (cv_encode, holmes_encode.cu:115-226) */
 int holmes_fft_special_inv(void* ctx, double* z, long long row_stride, int rows, int slots, void* stream);
+/* The reference's in-tree encode ABI (bench/cmp/kernels/holmes_encode.cu:240-285, bound by
+ * bench/cmp/holmes_fast_stage2.py:21-39), N = 2^16 full slots: in[rows][in_stride] interleaved stage-1 doubles ->
+ * out[rows][limbs][N] NTT plaintexts at scale sf, from the caller's per-limb primes / Barrett ratios / exponents and
+ * root tables (psi^bitrev(k) and Shoup companions, [limbs][N]; gathered once per table address and device).  diffs,
+ * rows_per_launch and limbs_per_block are scheduling details of the reference's kernels and are not needed;
+ * parts & 3 == 0 does nothing (the reference's single-kernel timing modes), any other value encodes. */
+int holmes_encode_stage2(void* out, const void* in, long long in_stride, int rows, double sf, int limbs,
+                         const void* primes, const void* diffs, const void* ratios, const void* ks, const void* roots,
+                         const void* roots_shoup, void* stream, int rows_per_launch, int parts, int limbs_per_block);
 int holmes_encode_fft(void* ctx, const double* u, long long row_stride, int rows, int slots, double scale, int cur,
                       uint64_t* out, long long out_row_stride, int* flag, void* stream);
 /* holmes_encode_fft onto the extended basis: out[rows][cur + K][N], the Q limbs first, then the K special limbs

@@ -391,3 +391,40 @@ def test_full_ring_rotation_round_trip_and_linearity():
     np.testing.assert_array_equal(host(g.cv[0][0]), e0)
     np.testing.assert_array_equal(host(g.cv[1][0]), e1)
     ctx.close()
+
+
+def test_reference_encode_stage2_abi_matches_encode():
+    """holmes_encode_stage2 with the reference's signature (bench/cmp/kernels/holmes_encode.cu:240-285): the caller's
+    primes / Barrett tables and psi^bitrev root tables, interleaved stage-1 doubles in; the same plaintexts as
+    holmes_encode_fft (N = 2^16, full slots, values of both signs)."""
+    from holmes_b200 import fhe as F
+
+    o, _, ctx = make_pair(log_n=16, limbs=3, dnum=1, dcrt=59, first=60, special=60)
+    try:
+        n, limbs, rows = o.pr.n, 3, 2
+        rng = np.random.default_rng(12)
+        z = F.torch.from_numpy(rng.normal(size=(rows, n // 2)) + 1j * rng.normal(size=(rows, n // 2))).to(ctx.device)
+        mid = F.fft_special_inv_rows(ctx, z, n // 2)
+        want = F.encode_rows(ctx, mid, limbs, ctx.scale, n // 2, already_transformed=True)
+        bits = o.pr.log_n
+        rev = np.array([int(format(k, f"0{bits}b")[::-1], 2) for k in range(n)])
+        roots = np.empty((limbs, n), dtype=np.uint64)
+        shoup = np.empty((limbs, n), dtype=np.uint64)
+        for li in range(limbs):
+            q, psi = o.pr.q[li], o.pr.psi[li]
+            pw = [1] * n
+            for k in range(1, n):
+                pw[k] = pw[k - 1] * psi % q
+            r = [pw[int(rev[k])] for k in range(n)]
+            roots[li] = np.array(r, dtype=np.uint64)
+            shoup[li] = np.array([(v << 64) // q for v in r], dtype=np.uint64)
+        rt, st = dev(roots), dev(shoup)
+        out = F.torch.empty((rows, limbs, n), dtype=F.torch.uint64, device=ctx.device)
+        zr = F.torch.view_as_real(mid)
+        rc = _lib().load().holmes_encode_stage2(out.data_ptr(), zr.data_ptr(), n, rows, float(ctx.scale), limbs,
+                                               ctx.primes.data_ptr(), 0, ctx.barret_ratio.data_ptr(),
+                                               ctx.barret_k.data_ptr(), rt.data_ptr(), st.data_ptr(), 0, 0, 3, 0)
+        assert rc == 0
+        np.testing.assert_array_equal(host(out), host(want))
+    finally:
+        ctx.close()
