@@ -53,6 +53,7 @@ SIGNATURES = {
     "holmes_modup": [p, p, i64, i32, i32, p, i64, p, p],
     "holmes_keyswitch": [p, p, i64, i32, p, i32, u64, p, p, i64, p, p, i64, p, p, i64, i32, p, p],
     "holmes_bsgs_mac": [p, p, p, p, i64, i32, i32, p, i64, i32, i32, p],
+    "holmes_mac_gather": [p, p, p, i64, p, p, p, i32, i32, p, i64, i32, i32, p, p, p, p],
     "holmes_keyswitch_ext": [p, p, i64, i32, p, i32, u64, p, i64, p, p, i64, i32, p],
     "holmes_moddown": [p, p, p, i64, i32, p, p, i64, i32, p, p],
     "holmes_bsgs_mac_ext": [p, p, p, p, i64, i32, i32, p, i64, i32, i32, p],

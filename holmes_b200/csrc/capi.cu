@@ -282,6 +282,16 @@ int holmes_device_error(int reset, int* flag_out) {
   return tc_error_flag(reset, flag_out);
 }
 
+int holmes_mac_gather(uint64_t* res, const uint64_t* const* c0s, const uint64_t* const* c1s, long long bstride,
+                      const int* idx, const int* prow, const int* seg, int inputs, int K, const uint64_t* pts,
+                      long long pstride, int ti, int limbs, const uint64_t* primes, const uint64_t* ratios,
+                      const uint64_t* ks, void* stream_ptr) {
+  if (!res || !c0s || !c1s || !idx || !prow || !seg || !pts || !primes || !ratios || !ks) return -1;
+  ModSrc ms{nullptr, 0, primes, ratios, ks};
+  return mac_gather(ms, res, c0s, c1s, bstride, idx, prow, seg, inputs, K, pts, pstride, ti, limbs, 16,
+                    S(stream_ptr));
+}
+
 int holmes_mac_multi(uint64_t* res, const uint64_t* const* c0s, const uint64_t* const* c1s, long long bstride, int nb,
                      int inputs, const uint64_t* pts, long long pstride, int groups, int ti, int limbs,
                      const uint64_t* primes, const uint64_t* ratios, const uint64_t* ks, void* stream_ptr) {

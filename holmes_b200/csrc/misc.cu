@@ -656,6 +656,86 @@ int bsgs_mac(ModSrc ms, u64* res, const u64* const* c0s, const u64* const* c1s,
   }
 }
 
+// --------------------------------------------------------------------------------------------- gathered MAC
+// The attention sparse-BSGS MAC (the reference's holmes_mac_gather, bench/cmp/kernels/holmes_mac.cu:276-347): group k
+// sums rows seg[k] <= r < seg[k + 1], row r multiplying plaintext row prow[r] by baby idx[r] of every input:
+//   res[c][k][i][l][n] = sum_r pts[prow[r]][l][n] * baby_i[idx[r]][c][l][n]  (mod q_l).
+// Grid (N / 256 * input tiles, limbs, K); TI inputs per thread, both components; radix-2^30 split products, sums
+// restarted from a representative below 8 q every 16 rows, canonical at the end (the same residues).
+template <int TI>
+__global__ void __launch_bounds__(256) k_mac_gather(u64* __restrict__ res, InPtrs in, long long bstride,
+                                                    const int* __restrict__ idx, const int* __restrict__ prow,
+                                                    const int* __restrict__ seg, int inputs, int K,
+                                                    const u64* __restrict__ pts, long long pstride, int limbs,
+                                                    ModSrc ms, int log_n) {
+  const int ntile = (inputs + TI - 1) / TI;
+  const int n = (blockIdx.x / ntile) * 256 + threadIdx.x, i0 = (blockIdx.x % ntile) * TI;
+  const int limb = blockIdx.y, k = blockIdx.z;
+  const Mod m = ms.get(limb);
+  const size_t ln = ((size_t)limb << log_n) + n;
+  const int r0 = seg[k], r1 = seg[k + 1];
+  Split4 acc[TI][2];
+  const u64* cp[TI][2];
+#pragma unroll
+  for (int t = 0; t < TI; ++t) {
+    const int i = i0 + t < inputs ? i0 + t : i0;
+    cp[t][0] = in.c0[i] + ln;
+    cp[t][1] = in.c1[i] + ln;
+#pragma unroll
+    for (int c = 0; c < 2; ++c) acc[t][c] = Split4{0, 0, 0, 0};
+  }
+  for (int r = r0, cnt = 1; r < r1; ++r, ++cnt) {
+    const u64 w = pts[(size_t)prow[r] * pstride + ln];
+    const size_t bo = (size_t)idx[r] * bstride;
+#pragma unroll
+    for (int t = 0; t < TI; ++t)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) split_mac(acc[t][c], cp[t][c][bo], w);
+    if ((cnt & 15) == 0 && r + 1 < r1) {
+#pragma unroll
+      for (int t = 0; t < TI; ++t)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const u64 v = fold_split_lazy(acc[t][c], m);
+          acc[t][c] = Split4{v & ((1ull << 30) - 1), v >> 30, 0, 0};
+        }
+    }
+  }
+  const size_t is = (size_t)limbs << log_n, gs = (size_t)inputs * is;
+#pragma unroll
+  for (int t = 0; t < TI; ++t) {
+    const int i = i0 + t;
+    if (i >= inputs) break;
+#pragma unroll
+    for (int c = 0; c < 2; ++c) res[((size_t)c * K + k) * gs + (size_t)i * is + ln] = fold_split(acc[t][c], m);
+  }
+}
+int mac_gather(ModSrc ms, u64* res, const u64* const* c0s, const u64* const* c1s, long long bstride, const int* idx,
+               const int* prow, const int* seg, int inputs, int K, const u64* pts, long long pstride, int ti,
+               int limbs, int log_n, cudaStream_t st) {
+  if (inputs < 1 || inputs > kMaxInputs) return -1;
+  if (K < 1 || K > 65535) return -3;
+  if (limbs < 1 || log_n < 8) return -2;
+  InPtrs in;
+  for (int i = 0; i < kMaxInputs; ++i) {
+    in.c0[i] = c0s[i < inputs ? i : 0];
+    in.c1[i] = c1s[i < inputs ? i : 0];
+  }
+  const unsigned nblk = (1u << log_n) / 256;
+#define L_(TI)                                                                                                  \
+  {                                                                                                             \
+    count_launch();                                                                                             \
+    k_mac_gather<TI><<<dim3(nblk * ((inputs + TI - 1) / TI), limbs, K), 256, 0, st>>>(                          \
+        res, in, bstride, idx, prow, seg, inputs, K, pts, pstride, limbs, ms, log_n);                           \
+    return (int)cudaGetLastError();                                                                             \
+  }
+  if (ti == 1) L_(1)
+  if (ti == 2) L_(2)
+  if (ti == 4) L_(4)
+#undef L_
+  return -4;
+}
+
 // --------------------------------------------------------------------------------------------- special FFT
 // Inverse CKKS embedding of `slots` complex values per row (Cheon-Kim-Kim-Song 2017 "special FFT"):
 // butterfly sweeps len = slots .. 2 with twiddle ksi[(4 len - rot[j] mod 4 len) * M / (4 len)], then

@@ -120,6 +120,9 @@ struct InPtrs {
   const u64* c0[kMaxInputs];
   const u64* c1[kMaxInputs];
 };
+int mac_gather(ModSrc ms, u64* res, const u64* const* c0s, const u64* const* c1s, long long bstride, const int* idx,
+               const int* prow, const int* seg, int inputs, int K, const u64* pts, long long pstride, int ti,
+               int limbs, int log_n, cudaStream_t st);
 // tensor-core MAC (mac_tc.cu): nb <= 128; returns -7 for shapes it does not take
 int bsgs_mac_tc(ModSrc ms, u64* res, const InPtrs& in, long long bstride, int nb, int inputs, const u64* pts,
                 long long pstride, int groups, int limbs, int log_n, cudaStream_t st);

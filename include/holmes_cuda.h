@@ -187,6 +187,15 @@ int holmes_launch_count(unsigned long long* count_out);
  * counterpart: EasyFHE kernels do not wait on hardware barriers. */
 int holmes_device_error(int reset, int* flag_out);
 
+/* The reference's gathered MAC for the attention sparse BSGS (bench/cmp/kernels/holmes_mac.cu:276-347, 404-428),
+ * same signature and return codes (N = 2^16): res[c][k][i][l][n] = sum_{seg[k] <= r < seg[k+1]}
+ * pts[prow[r]][l][n] * baby_i[idx[r]][c][l][n] (mod q_l), res [2][K][inputs][limbs][N]; c0s / c1s host arrays of
+ * `inputs` (<= 32) device pointers to baby bases (item stride bstride); idx / prow [rows], seg [K + 1] (int32,
+ * device); ti in {1, 2, 4}; moduli from the reference's primes / barret_ratio / barret_k arrays. */
+int holmes_mac_gather(uint64_t* res, const uint64_t* const* c0s, const uint64_t* const* c1s, long long bstride,
+                      const int* idx, const int* prow, const int* seg, int inputs, int K, const uint64_t* pts,
+                      long long pstride, int ti, int limbs, const uint64_t* primes, const uint64_t* ratios,
+                      const uint64_t* ks, void* stream_ptr);
 /* ---- drop-in for the reference's own ctypes binding (bench/cmp/kernels/holmes_mac.cu:359-402, bound in
  *      bench/cmp/holmes_multi_mac.py:33-54): same signature, arguments and return codes; N = 2^16;
  *      `ti` is accepted from the reference's tile set and used only as a hint. */

@@ -428,3 +428,47 @@ def test_reference_encode_stage2_abi_matches_encode():
         np.testing.assert_array_equal(host(out), host(want))
     finally:
         ctx.close()
+
+
+@pytest.mark.parametrize("ti", [1, 2, 4])
+def test_reference_mac_gather_abi(ti):
+    """holmes_mac_gather with the reference's signature (bench/cmp/kernels/holmes_mac.cu:404-428): segmented rows of
+    gathered (plaintext row, baby) pairs; exact against Python integers at sampled coefficients (a 20-row segment
+    crosses the 16-row fold)."""
+    import ctypes
+    from holmes_b200 import fhe as F
+
+    o, _, ctx = make_pair(log_n=16, limbs=2, dnum=1, dcrt=59, first=60, special=60)
+    try:
+        n, limbs, inputs, nb, npt = o.pr.n, 2, 3, 6, 10
+        rng = np.random.default_rng(ti)
+        babies = [np.stack([np.stack([residues(o.pr.q, limbs, n, rng) for _ in range(2)]) for _ in range(nb)])
+                  for _ in range(inputs)]                                   # [nb][2][limbs][N] per input
+        pts = np.stack([residues(o.pr.q, limbs, n, rng) for _ in range(npt)])   # [npt][limbs][N]
+        seg = np.array([0, 4, 9, 29], dtype=np.int32)
+        rows = int(seg[-1])
+        idx = rng.integers(0, nb, rows).astype(np.int32)
+        prow = rng.integers(0, npt, rows).astype(np.int32)
+        K = len(seg) - 1
+        bt = [dev(b) for b in babies]
+        bstride = 2 * limbs * n
+        c0s = F._lib.ptr_array([b[:, 0].data_ptr() for b in bt])
+        c1s = F._lib.ptr_array([b[:, 1].data_ptr() for b in bt])
+        pt_d, idx_d, prow_d, seg_d = dev(pts), dev(idx), dev(prow), dev(seg)
+        res = F.torch.empty((2, K, inputs, limbs, n), dtype=F.torch.uint64, device=ctx.device)
+        rc = _lib().load().holmes_mac_gather(res.data_ptr(), c0s, c1s, bstride, idx_d.data_ptr(), prow_d.data_ptr(),
+                                             seg_d.data_ptr(), inputs, K, pt_d.data_ptr(), limbs * n, ti, limbs,
+                                             ctx.primes.data_ptr(), ctx.barret_ratio.data_ptr(),
+                                             ctx.barret_k.data_ptr(), 0)
+        assert rc == 0
+        got = host(res)
+        for j in (0, 7, 40000, n - 1):
+            for k in range(K):
+                for i in range(inputs):
+                    for c in range(2):
+                        for l in range(limbs):
+                            want = sum(int(pts[prow[r], l, j]) * int(babies[i][idx[r], c, l, j])
+                                       for r in range(seg[k], seg[k + 1])) % o.pr.q[l]
+                            assert int(got[c, k, i, l, j]) == want
+    finally:
+        ctx.close()
