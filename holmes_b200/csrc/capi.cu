@@ -201,6 +201,14 @@ int holmes_rescale(void* ctx, const uint64_t* in, long long in_stride, uint64_t*
   return rescale(*C(ctx), in, in_stride, out, out_stride, cur, comps, scratch, S(stream));
 }
 
+int holmes_rescale_postop(void* ctx, const uint64_t* in, long long in_stride, uint64_t* out, long long out_stride,
+                          int cur, int comps, uint64_t* scratch, int apply_double, const uint64_t* sub,
+                          long long sub_stride, const uint64_t* consts, void* stream) {
+  if (!ctx || !in || !out || !scratch || comps < 1) return -1;
+  return rescale(*C(ctx), in, in_stride, out, out_stride, cur, comps, scratch, S(stream), apply_double ? 1 : 0, sub,
+                 sub_stride, consts);
+}
+
 int holmes_modraise(void* ctx, const uint64_t* in, long long in_stride, uint64_t* out, long long out_stride, int raise,
                     int comps, uint64_t* scratch, void* stream) {
   if (!ctx || !in || !out || !scratch) return -1;

@@ -674,6 +674,9 @@ struct LdRescale {
     return v > (ql >> 1) ? sub_mod(r, s.qlm, s.m.q) : r;
   }
 };
+// Store of the rescale, with the post-operations of EasyFHE's homo_mul_relin_rescale_postop fused in
+// (operators/nonlinear/polynomial.py:139-193): r = (a - v) q_L^-1, then r = 2r (dbl), r -= sub (item e, limb i at
+// sub + e sub_stride + i N: a modulus drop of a deeper ciphertext is only its stride), r += cst[i].
 struct StRescale {
   const u64* in;
   long long in_stride;
@@ -682,22 +685,34 @@ struct StRescale {
   const Mod* mods;
   const Tw* qinv;
   int cur, log_n;
+  const u64* sub = nullptr;
+  long long sub_stride = 0;
+  const u64* cst = nullptr;
+  int dbl = 0;
   struct S {
     const u64* a;
+    const u64* b;
     u64* o;
-    u64 q;
+    u64 q, k;
     Tw t;
   };
   __device__ S prep(int p) const {
     const int e = p / (cur - 1), i = p % (cur - 1);
     S s;
     s.a = in + e * in_stride + ((size_t)i << log_n);
+    s.b = sub ? sub + e * sub_stride + ((size_t)i << log_n) : nullptr;
     s.o = out + e * out_stride + ((size_t)i << log_n);
     s.q = mods[i].q;
+    s.k = cst ? cst[i] : 0;
     s.t = qinv[i];
     return s;
   }
-  __device__ void store(const S& s, int n, u64 v) const { s.o[n] = shoup(sub_mod(s.a[n], v, s.q), s.t, s.q); }
+  __device__ void store(const S& s, int n, u64 v) const {
+    u64 r = shoup(sub_mod(s.a[n], v, s.q), s.t, s.q);
+    if (dbl) r = add_mod(r, r, s.q);
+    if (s.b) r = sub_mod(r, s.b[n], s.q);
+    s.o[n] = add_mod(r, s.k, s.q);
+  }
 };
 template <int LOGN>
 __global__ void HOLMES_NTT_BOUNDS(LOGN) k_rescale(NttTables T, LdRescale ld, StRescale st) {
@@ -706,7 +721,7 @@ __global__ void HOLMES_NTT_BOUNDS(LOGN) k_rescale(NttTables T, LdRescale ld, StR
 }
 
 int rescale(const HolmesCtx& c, const u64* in, long long in_stride, u64* out, long long out_stride, int cur, int comps,
-            u64* scratch, cudaStream_t st) {
+            u64* scratch, cudaStream_t st, int dbl, const u64* sub, long long sub_stride, const u64* cst) {
   if (cur < 2 || cur > c.L) return -2;
   const int N = c.n;
   {
@@ -729,7 +744,7 @@ int rescale(const HolmesCtx& c, const u64* in, long long in_stride, u64* out, lo
   {
     NttTables T{c.d_tw, c.d_mod};
     LdRescale ld{scratch, c.d_mod, c.q[cur - 1], cur, c.log_n};
-    StRescale sr{in, in_stride, out, out_stride, c.d_mod, c.rs_qinv(cur), cur, c.log_n};
+    StRescale sr{in, in_stride, out, out_stride, c.d_mod, c.rs_qinv(cur), cur, c.log_n, sub, sub_stride, cst, dbl};
     const int polys = comps * (cur - 1);
 #define L_(LG)                                                                                      \
   {                                                                                                 \

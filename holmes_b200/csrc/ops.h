@@ -71,9 +71,12 @@ int moddown_ext(const HolmesCtx& c, const u64* in0, const u64* in1, long long in
                 long long out_item, int items, u64* scratch, cudaStream_t st);
 
 // Rescale by the last limb: `comps` polynomials-of-limbs in [comps][cur] layout (stride in_stride / out_stride
-// between components) -> [comps][cur - 1]; scratch >= comps * N words.
+// between components) -> [comps][cur - 1]; scratch >= comps * N words.  Optional post-operations on the
+// rescaled words: doubled (dbl), minus sub[comp][limb] (component stride sub_stride, >= cur - 1 limbs), plus
+// cst[limb].
 int rescale(const HolmesCtx& c, const u64* in, long long in_stride, u64* out, long long out_stride, int cur, int comps,
-            u64* scratch, cudaStream_t st);
+            u64* scratch, cudaStream_t st, int dbl = 0, const u64* sub = nullptr, long long sub_stride = 0,
+            const u64* cst = nullptr);
 
 // Mod raise: [comps][1][N] modulo q0 (item stride in_stride) -> [comps][raise][N] (centred lift), scratch >= comps * N.
 int modraise(const HolmesCtx& c, const u64* in, long long in_stride, u64* out, long long out_stride, int raise,

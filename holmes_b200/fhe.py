@@ -206,6 +206,10 @@ class Context:
     def q(self, i: int) -> int:
         return self.moduli[i]
 
+    def rescale_divisor_at(self, cur_limbs: int) -> int:
+        """The prime a rescale divides by when its output has ``cur_limbs`` limbs (the limb it drops)."""
+        return self.moduli[int(cur_limbs)]
+
     def p_mod_q(self, cur: int) -> list:
         """P = product of the special primes, modulo q_0 .. q_{cur-1}."""
         P = math.prod(self.moduli[self.L:self.L + self.K])
@@ -841,8 +845,58 @@ def homo_mul_relin(a: Cipher, b: Cipher, ctx) -> Cipher:
     return homo_relinearize(homo_mul_no_relin(a, b, ctx), ctx)
 
 
-def homo_mul_relin_rescale_postop(a: Cipher, b: Cipher, ctx) -> Cipher:
-    return rescale(homo_mul_relin(a, b, ctx), ctx)
+def _drop_limbs(a: Cipher, limbs: int) -> Cipher:
+    if int(a.state.cur_limbs) == int(limbs):
+        return a
+    return a.cipher_like([c[:, :limbs] for c in a.cv], state=a.state.replace(cur_limbs=int(limbs)))
+
+
+def homo_mul_relin_rescale_postop(a: Cipher, b: Cipher, ctx, apply_double: bool = False, sub: Cipher | None = None,
+                                  scalar: EncodedScalar | None = None) -> Cipher:
+    """``rescale(a * b)``, then doubled (``apply_double``), minus ``sub``, plus ``scalar``, the post-operations
+    fused into the rescale's store (EasyFHE's fused kernel as llama3fhe calls it,
+    ``operators/nonlinear/polynomial.py:139-193``: ``T_2j = 2 T_j^2 - 1``, ``T_2j+1 = 2 T_j T_j+1 - T_1``).
+
+    The deeper operand is dropped to the other's limbs first; ``sub`` (a deeper ciphertext is read at the
+    output's limbs, its modulus drop) and ``scalar`` (encoded for the output state, ``ctx.rescale_divisor_at``)
+    land at the output, which has one limb fewer than the shallower operand."""
+    ctx = _ctx(ctx)
+    cur = min(int(a.state.cur_limbs), int(b.state.cur_limbs))
+    prod = homo_mul_relin(_drop_limbs(a, cur), _drop_limbs(b, cur), ctx)
+    if cur < 2:
+        raise ValueError("homo_mul_relin_rescale_postop needs at least two limbs")
+    ql = ctx.q(cur - 1)
+    sf = None if prod.state.scaling_factor is None else float(prod.state.scaling_factor) / ql
+    state = CipherState(cur - 1, max(1, int(prod.state.scale_degree) - 1), sf)
+    n = prod.batch_size
+    broadcast = False
+    if sub is not None:
+        if sub.is_ext or len(sub.cv) != 2:
+            raise ValueError("homo_mul_relin_rescale_postop: sub must be a two-component, non-extended ciphertext")
+        if int(sub.state.cur_limbs) < cur - 1:
+            raise ValueError(f"homo_mul_relin_rescale_postop: sub has {sub.state.cur_limbs} limbs, the output "
+                             f"{cur - 1}")
+        if int(sub.state.scale_degree) != int(state.scale_degree):
+            raise ValueError("homo_mul_relin_rescale_postop: sub's scale degree differs from the output's")
+        if sub.batch_size not in (1, n):
+            raise ValueError(f"homo_mul_relin_rescale_postop: sub batch {sub.batch_size} for {n} products")
+        broadcast = sub.batch_size == 1 and n > 1
+    k = None
+    if scalar is not None:
+        if int(scalar.state.cur_limbs) < cur - 1:
+            raise ValueError("homo_mul_relin_rescale_postop: the scalar is encoded for fewer limbs than the output")
+        k = scalar.residues(ctx, cur - 1)
+    out = _new_cipher(ctx, n, cur - 1, state, prod.slots)
+    scratch = ctx.workspace("rescale", n * ctx.N)
+    tok = OPTIMER.start("rescale")
+    for c in range(2):
+        _lib.call("holmes_rescale_postop", ctx.handle, prod.cv[c].data_ptr(), _item_stride(prod.cv[c]),
+                  out.cv[c].data_ptr(), _item_stride(out.cv[c]), cur, n, scratch.data_ptr(), int(bool(apply_double)),
+                  0 if sub is None else sub.cv[c].data_ptr(),
+                  0 if (sub is None or broadcast) else _item_stride(sub.cv[c]),
+                  0 if (k is None or c) else k.data_ptr(), _stream())
+    OPTIMER.stop(tok, 2 * n * (2 * cur - 1) * ctx.N * 8)
+    return out
 
 
 # ----------------------------------------------------------------------------------------------------- scalars

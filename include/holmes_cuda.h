@@ -112,6 +112,16 @@ int holmes_mul_const(void* ctx, const uint64_t* a, const uint64_t* consts, uint6
 int holmes_rescale(void* ctx, const uint64_t* in, long long in_stride, uint64_t* out, long long out_stride, int cur,
                    int comps, uint64_t* scratch, void* stream);
 
+/* holmes_rescale with the post-operations of EasyFHE's homo_mul_relin_rescale_postop fused into its store
+ * (llama3fhe/operators/nonlinear/polynomial.py:139-193, the Chebyshev basis T_2j = 2 T_j^2 - 1 and
+ * T_2j+1 = 2 T_j T_j+1 - T_1): every rescaled word is doubled when apply_double != 0, then sub[comp][limb][N]
+ * (component stride sub_stride, at least cur - 1 limbs: a deeper ciphertext's modulus drop) is subtracted when
+ * sub is not null, then consts[limb] (device, canonical residues) is added when consts is not null.  Pass sub
+ * and consts for the components they apply to (a scalar to component 0 only). */
+int holmes_rescale_postop(void* ctx, const uint64_t* in, long long in_stride, uint64_t* out, long long out_stride,
+                          int cur, int comps, uint64_t* scratch, int apply_double, const uint64_t* sub,
+                          long long sub_stride, const uint64_t* consts, void* stream);
+
 /* bootstrapping's ModRaise (EasyFHE bs.openfhe raise_ciphertext, bench/cmp/holmes_batch_bs.py:65-90): in[comps][1][N]
  * modulo q0 (NTT) is read as centred integers and written modulo q_0..q_{raise-1}: out[comps][raise][N];
  * scratch >= comps * N words */
