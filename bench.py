@@ -271,8 +271,8 @@ def run_engine(args) -> None:
         for h in host_in:
             d = h.to(ctx.device, non_blocking=True)
             dev_in.append(F.Cipher([d[0:1], d[1:2]], cts[0].state, cts[0].slots, False, 1, ctx))
-        w_dev = host_w.to(ctx.device, non_blocking=True)
-        with LN.LinearWeight(w_dev, dtype=np.complex128, crypto_context=session) as lw2:
+        # the pinned page goes to LinearWeight as is: it uploads it on a side stream behind the baby rotations
+        with LN.LinearWeight(host_w, dtype=np.complex128, crypto_context=session) as lw2:
             with LN.LinearOperator(crypto_context=session, token_lanes=LANES, config=cfg,
                                    baby_shard=(rank, world, None) if chunked else None) as op2:
                 res = page(op2, dev_in, lw2)

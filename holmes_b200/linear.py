@@ -347,6 +347,7 @@ class LinearWeight:
         self._weight = w
         self._dimension = int(shape[0])
         self._device_source = None
+        self._upload_event = None
         self._bundles: dict = {}
         self._closed = False
         self.setup_seconds = 0.0
@@ -371,7 +372,23 @@ class LinearWeight:
             w = self._weight
             if not torch.is_tensor(w):
                 w = torch.from_numpy(np.ascontiguousarray(np.asarray(w, dtype=self.dtype)))
-            self._device_source = w.to(device=ctx.device, dtype=tdtype).contiguous()
+            if w.device.type == "cpu" and w.is_pinned() and w.dtype == tdtype and w.is_contiguous():
+                # A pinned host page is uploaded on a side stream, so the copy overlaps what the caller's stream
+                # runs before the first encode (the baby rotations of apply); plaintext() waits for it.
+                main = torch.cuda.current_stream(ctx.device)
+                up = getattr(ctx, "_upload_stream", None)
+                if up is None:
+                    up = ctx._upload_stream = torch.cuda.Stream(device=ctx.device)
+                dev = torch.empty(w.shape, dtype=tdtype, device=ctx.device)
+                up.wait_stream(main)
+                with torch.cuda.stream(up):
+                    dev.copy_(w, non_blocking=True)
+                dev.record_stream(up)
+                self._upload_event = torch.cuda.Event()
+                self._upload_event.record(up)
+                self._device_source = dev
+            else:
+                self._device_source = w.to(device=ctx.device, dtype=tdtype).contiguous()
         elapsed = time.perf_counter() - start
         self.setup_seconds += elapsed
         return elapsed
@@ -403,6 +420,8 @@ class LinearWeight:
         ctx = self.crypto_context.context
         cur = int(ctx.L) - int(level)
         bundle = self._bundle(plan, chunk, operator_config)
+        if self._upload_event is not None:
+            torch.cuda.current_stream(ctx.device).wait_event(self._upload_event)
         return bundle.plaintext(chunk.name, state=F.CipherState(cur, 1, ctx.scale_at(cur)),
                                 slots=int(self.crypto_context.max_slots), context=ctx,
                                 is_ext=str(operator_config.hoist_strategy).lower() != "normal", cache=True)
@@ -425,6 +444,7 @@ class LinearWeight:
     def close(self) -> None:
         self.clear_cache()
         self._device_source = None
+        self._upload_event = None
         self._weight = None
         self._closed = True
 

@@ -362,6 +362,14 @@ def test_linear_operator_bitexact_and_decodes(complex_weight):
     for a, b in zip(outs, again):
         np.testing.assert_array_equal(host(a.cv[0]), host(b.cv[0]))
     assert profile["online"] > 0
+    # a pinned host page is uploaded on a side stream behind the babies: same residues
+    pinned = torch.from_numpy(np.ascontiguousarray(w)).pin_memory()
+    with LN.LinearOperator(crypto_context=session, token_lanes=lanes, config=cfg) as op, \
+            LN.LinearWeight(pinned, dtype=w.dtype, crypto_context=session) as lw:
+        via_host, _ = op.apply(cts, lw)
+    for a, b in zip(outs, via_host):
+        np.testing.assert_array_equal(host(a.cv[0]), host(b.cv[0]))
+        np.testing.assert_array_equal(host(a.cv[1]), host(b.cv[1]))
     ctx.close()
 
 
