@@ -137,3 +137,78 @@ def test_chunk_sharded_linear_with_baby_all_gather_two_gpus(tmp_path):
                 np.testing.assert_array_equal(got[1, k], expect[i][1])
     finally:
         ctx.close()
+
+
+def _transport_worker(rank, world, port, out_dir):
+    import time
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    from holmes_b200 import transport as T
+    from tests.gpu_helpers import make_pair
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        _, client, ctx = make_pair(log_n=12, limbs=4, dnum=2, dcrt=45, first=55, special=55)
+        tr = T.build_transport(kind="nccl", default_timeout=60.0)
+        assert tr.device_payloads and tr.device.type == "cuda"
+        z = np.random.default_rng(rank).normal(size=ctx.max_slots) * 0.5
+        ct = client.encrypt(z, cur_limbs=4, counter=rank)
+        mine = [c.clone() for c in ct.cv]
+        # point to point: rank 0 -> 1, received out of order
+        if rank == 0:
+            tr.send(1, "late", T.pack_cipher(ct, tag="late"))
+            tr.send(1, "early", {"n": 7})
+        else:
+            first = tr.recv(0, "early")
+            got = T.unpack_cipher(tr.recv(0, "late"), ctx)
+            assert first == {"n": 7} and got.cv[0].device.type == "cuda"
+            np.save(os.path.join(out_dir, "p2p.npy"), torch.stack([c[0] for c in got.cv]).cpu().numpy())
+        # all_to_all of packets (device to device), then a timed page-sized exchange: 16 ciphertexts at 13 limbs
+        # of N = 2^16 (218 MB) split over the ranks
+        got = tr.all_to_all("cts", [T.pack_cipher(ct) for _ in range(world)])
+        np.save(os.path.join(out_dir, f"a2a{rank}.npy"),
+                np.stack([torch.stack([c[0] for c in g.components]).cpu().numpy() for g in got]))
+        np.save(os.path.join(out_dir, f"mine{rank}.npy"), torch.stack([m[0] for m in mine]).cpu().numpy())
+        big = torch.randint(0, 2**62, (16 // world, 2, 13, 1 << 16), dtype=torch.int64, device="cuda")
+        for _ in range(2):
+            tr.all_to_all("warm", [big] * world)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        reps = 5
+        for _ in range(reps):
+            tr.all_to_all("page", [big] * world)
+        torch.cuda.synchronize()
+        dt = (time.perf_counter() - t0) / reps
+        with open(os.path.join(out_dir, f"gbs{rank}.txt"), "w") as f:
+            f.write(f"{big.numel() * 8 * (world - 1) / dt / 1e9:.1f}")
+        tr.close()
+        dist.barrier()
+        ctx.close()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_nccl_transport_two_gpus(tmp_path):
+    """The reference's Transport protocol over NCCL: ciphertext packets move GPU to GPU bit for bit (point to point
+    with out-of-order tags, all_to_all); a page-sized all_to_all reports its per-rank send bandwidth."""
+    import torch.multiprocessing as mp
+
+    world = 2
+    mp.spawn(_transport_worker, args=(world, _port(), str(tmp_path)), nprocs=world, join=True)
+    mine = [np.load(tmp_path / f"mine{r}.npy") for r in range(world)]
+    np.testing.assert_array_equal(np.load(tmp_path / "p2p.npy"), mine[0])
+    for r in range(world):
+        got = np.load(tmp_path / f"a2a{r}.npy")
+        for s in range(world):
+            np.testing.assert_array_equal(got[s], mine[s])
+    gbs = [float((tmp_path / f"gbs{r}.txt").read_text()) for r in range(world)]
+    print("transport all_to_all GB/s per rank:", gbs)
+    assert min(gbs) > 1.0
