@@ -700,14 +700,13 @@ def unpack_cipher_batch(batch: Cipher) -> tuple:
 def prepare_hoisted_baby_rotations(a: Cipher, baby_offsets, ctx, strategy: str = "normal",
                                    baby_anchor_step: int = -1):
     """Baby basis rot(a, offset) for every offset from one hoisted ModUp; one block ``[nb]`` batch.  ``ext_normal``
-    keeps the block over the extended basis Q u P (``fast_rotate(output_ext=True)``); ``ext_double_hoist`` is not
-    built and raises."""
+    and ``ext_double_hoist`` keep the block over the extended basis Q u P (``fast_rotate(output_ext=True)``)."""
     del baby_anchor_step
     strategy = str(strategy).lower()
-    if strategy == "ext_normal":
+    if strategy in ("ext_normal", "ext_double_hoist"):
         return (fast_rotate(a, tuple(int(o) for o in baby_offsets), ctx, output_ext=True),)
     if strategy != "normal":
-        raise NotImplementedError(f"hoist strategy {strategy!r} is not built ('normal' and 'ext_normal' are)")
+        raise ValueError(f"unknown hoist strategy {strategy!r}")
     ctx = _ctx(ctx)
     if a.batch_size != 1:
         raise ValueError("prepare_hoisted_baby_rotations expects one ciphertext")
@@ -767,9 +766,47 @@ def giant_horner(ctx: Context, res: torch.Tensor, giant_offset: int) -> tuple[to
     return acc0, acc1
 
 
+def giant_double_hoist(ctx: Context, res: torch.Tensor, giant_offset: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """sum_g rot(res[g], g giant_offset) for res [2][G][items][cur][N], double hoisted (the ``ext_double_hoist``
+    strategy, whose key set has every local giant offset, ``operators/linear/config.py:354-359``): each giant's
+    key switch stays over Q u P (``holmes_keyswitch_ext``; giant 0 lifted as (P c0, P c1)), the G results are summed
+    over Q u P by one multiply-accumulate launch against a plaintext of ones, and ONE ModDown brings the sum back,
+    where the Horner chain pays a ModDown per giant."""
+    G, items, cur = int(res.shape[1]), int(res.shape[2]), int(res.shape[3])
+    K, N = ctx.K, ctx.N
+    ext = torch.empty((2, G, items, cur + K, N), dtype=torch.uint64, device=ctx.device)
+    pm = torch.tensor(ctx.p_mod_q(cur), dtype=torch.uint64, device=ctx.device)
+    for c in range(2):
+        ext[c, 0, :, cur:].zero_()
+        _lib.call("holmes_mul_const", ctx.handle, res[c, 0].data_ptr(), pm.data_ptr(), ext[c, 0].data_ptr(), items,
+                  cur, cur * N, (cur + K) * N, _stream())
+    for g in range(1, G):
+        gal = ctx.galois(g * int(giant_offset))
+        c0, c1 = res[0, g], res[1, g]
+        digits, dig_item = _modup(ctx, c1, cur, items)
+        key_t, cap = ctx.switch_key(gal, cur)
+        tok = OPTIMER.start("keyswitch")
+        _lib.call("holmes_keyswitch_ext", ctx.handle, digits.data_ptr(), dig_item, cur, key_t.data_ptr(), cap, int(gal),
+                  c0.data_ptr(), _item_stride(c0), ext[0, g].data_ptr(), ext[1, g].data_ptr(), (cur + K) * N, items,
+                  _stream())
+        OPTIMER.stop(tok, items * (ctx.beta(cur) * (cur + K) + 3 * cur + 2 * K) * N * 8)
+    ones = torch.ones((G, cur + K, N), dtype=torch.uint64, device=ctx.device)
+    summed = torch.empty((2, 1, items, cur + K, N), dtype=torch.uint64, device=ctx.device)
+    c0s = _lib.ptr_array([ext[0, 0, i].data_ptr() for i in range(items)])
+    c1s = _lib.ptr_array([ext[1, 0, i].data_ptr() for i in range(items)])
+    _lib.call("holmes_bsgs_mac_ext", ctx.handle, summed.data_ptr(), c0s, c1s, items * (cur + K) * N, G, items,
+              ones.data_ptr(), (cur + K) * N, 1, cur, _stream())
+    out = torch.empty((2, items, cur, N), dtype=torch.uint64, device=ctx.device)
+    scratch = ctx.workspace("ks", items * 2 * (K + cur) * N)
+    _lib.call("holmes_moddown", ctx.handle, summed[0, 0].data_ptr(), summed[1, 0].data_ptr(), (cur + K) * N, cur,
+              out[0].data_ptr(), out[1].data_ptr(), cur * N, items, scratch.data_ptr(), _stream())
+    return out[0], out[1]
+
+
 def hoisted_mac_sum(cipher: Cipher, baby_offsets, plaintexts: Plaintext, giant_offset: int, giant_count: int, ctx,
                     strategy: str = "normal", baby_anchor_step: int = -1, baby_rotations=None) -> Cipher:
-    """sum_g rot(sum_b pt[g B + b] baby[b], g giant_offset) via Horner; scale degree adds the plaintext's."""
+    """sum_g rot(sum_b pt[g B + b] baby[b], g giant_offset) via Horner (``ext_double_hoist``: every giant rotated
+    directly over Q u P and one ModDown of the sum); scale degree adds the plaintext's."""
     ctx = _ctx(ctx)
     if baby_rotations is None:
         baby_rotations = prepare_hoisted_baby_rotations(cipher, baby_offsets, ctx, strategy, baby_anchor_step)
@@ -779,7 +816,10 @@ def hoisted_mac_sum(cipher: Cipher, baby_offsets, plaintexts: Plaintext, giant_o
         down = moddown_from_ext(Cipher([res[0, :, 0], res[1, :, 0]], block.state, block.slots, True,
                                        int(giant_count), ctx), ctx)
         res = torch.stack([down.cv[0], down.cv[1]]).unsqueeze(2)
-    acc0, acc1 = giant_horner(ctx, res, int(giant_offset))
+    if str(strategy).lower() == "ext_double_hoist":
+        acc0, acc1 = giant_double_hoist(ctx, res, int(giant_offset))
+    else:
+        acc0, acc1 = giant_horner(ctx, res, int(giant_offset))
     sf = None
     if block.state.scaling_factor is not None and plaintexts.state.scaling_factor is not None:
         sf = float(block.state.scaling_factor) * float(plaintexts.state.scaling_factor)

@@ -544,7 +544,7 @@ class LinearOperator:
         cur = int(inputs[0].state.cur_limbs)
         n_in = len(inputs)
         B = int(plan.baby_steps)
-        ext = str(self.config.hoist_strategy).lower() == "ext_normal"
+        ext = str(self.config.hoist_strategy).lower() != "normal"
         limbs = cur + (ctx.K if ext else 0)
         storage = torch.empty((B, 2, n_in, limbs, ctx.N), dtype=torch.uint64, device=ctx.device)
         c0 = torch.stack([c.cv[0][0, :cur] for c in inputs])
@@ -620,12 +620,10 @@ class LinearOperator:
         if self._closed:
             raise RuntimeError("linear operator is closed.")
         strategy = str(self.config.hoist_strategy).lower()
-        if strategy not in ("normal", "ext_normal"):
-            # ext_double_hoist also keeps the giant rotations in Q*P; its schedule is EasyFHE's and cannot be pinned
-            # here, so it is refused rather than silently run as another strategy.
-            raise NotImplementedError(f"hoist_strategy {strategy!r} is not built ('normal' and 'ext_normal' are; the "
-                                      "production linear schedule, operators/linear/config.py:123-135, is 'normal')")
-        ext = strategy == "ext_normal"
+        if strategy not in _HOIST_STRATEGIES:
+            raise ValueError(f"unknown hoist_strategy {strategy!r}")
+        ext = strategy != "normal"
+        double = strategy == "ext_double_hoist"
         inputs = tuple(input_ciphers)
         if not inputs:
             return (), dict(_EMPTY_PROFILE)
@@ -679,7 +677,7 @@ class LinearOperator:
             babies.ready()
             res = F.bsgs_partial_sums(ctx, blocks, pts, int(chunk.giant_count))
             del pts
-            if ext:   # ext_normal: babies and MAC over Q u P, one ModDown per giant partial, then the plain Horner
+            if ext:   # babies and MAC over Q u P, one ModDown per giant partial
                 G = int(res.shape[1])
                 down = torch.empty((2, G, n_in, cur, ctx.N), dtype=torch.uint64, device=ctx.device)
                 scratch = ctx.workspace("ks", G * n_in * 2 * (ctx.K + cur) * ctx.N)
@@ -687,7 +685,10 @@ class LinearOperator:
                           cur, down[0].data_ptr(), down[1].data_ptr(), cur * ctx.N, G * n_in, scratch.data_ptr(),
                           F._stream())
                 res = down
-            g0, g1 = F.giant_horner(ctx, res, int(plan.giant_offset))
+            if double:   # ext_double_hoist: every giant rotated directly over Q u P, summed, one ModDown
+                g0, g1 = F.giant_double_hoist(ctx, res, int(plan.giant_offset))
+            else:        # normal / ext_normal: the Horner chain
+                g0, g1 = F.giant_horner(ctx, res, int(plan.giant_offset))
             shift = int(chunk.giant_base) * int(plan.giant_offset)
             if acc0 is None:
                 if shift:

@@ -273,8 +273,10 @@ def _oracle_linear(o, ref_inputs, weight, plan, cur, scale):
     return outs
 
 
-def _oracle_linear_ext(o, ref_inputs, weight, plan, cur, scale):
-    """ext_normal restatement: babies and MAC over Q u P, one ModDown per giant partial, then the plain Horner."""
+def _oracle_linear_ext(o, ref_inputs, weight, plan, cur, scale, double=False):
+    """ext_normal restatement: babies and MAC over Q u P, one ModDown per giant partial, then the plain Horner.
+    ``double`` (ext_double_hoist): every giant partial rotated by g giant_offset before its ModDown (giant 0 lifted
+    as P times itself), the rotations summed over Q u P, one ModDown."""
     ids = o.ext_ids(cur)
     moduli = [o.pr.q[i] for i in ids]
     outs = []
@@ -288,12 +290,60 @@ def _oracle_linear_ext(o, ref_inputs, weight, plan, cur, scale):
             pts = np.stack([o.encode_ext(r, cur, scale) for r in rows])
             part = o.bsgs_mac(pts, babies, chunk.giant_count, moduli=moduli)
             down = [np.stack([o.moddown(part[c][g], cur) for g in range(chunk.giant_count)]) for c in range(2)]
-            res = o.giant_horner(down, plan.giant_offset)
+            if double:
+                terms = [o.rotate_ext((down[0][g], down[1][g]), g * plan.giant_offset)
+                         for g in range(chunk.giant_count)]
+                tot = terms[0]
+                for t in terms[1:]:
+                    tot = (o.add(tot[0], t[0], ids), o.add(tot[1], t[1], ids))
+                res = (o.moddown(tot[0], cur), o.moddown(tot[1], cur))
+            else:
+                res = o.giant_horner(down, plan.giant_offset)
             if chunk.giant_base:
                 res = o.rotate(res, chunk.giant_base * plan.giant_offset)
             acc = res if acc is None else (o.add(acc[0], res[0], range(cur)), o.add(acc[1], res[1], range(cur)))
         outs.append(o.rescale(acc))
     return outs
+
+
+def test_linear_operator_ext_double_hoist_bitexact_and_decodes():
+    """hoist_strategy "ext_double_hoist" (4 giants per chunk, each rotated with its own key over Q u P, one ModDown of
+    their sum): residue for residue against its restatement, decoded like "normal"."""
+    from holmes_b200 import linear as LN
+
+    o, client, ctx = make_pair(log_n=11, limbs=4, dnum=2, dcrt=45, first=55, special=55)
+    session = LN.Session(client, ctx)
+    dim, lanes = 64, 16
+    cfg = LN.LinearOperatorConfig(baby_steps=8, baby_anchor_step=8, max_plaintext_rows=32,
+                                  hoist_strategy="ext_double_hoist")
+    plan = cfg.plan(dimension=dim, token_lanes=lanes)
+    assert plan.chunk_giants == 4
+    rng = np.random.default_rng(17)
+    w = rng.normal(scale=0.02, size=(dim, dim))
+    xs = rng.normal(size=(2, lanes, dim))
+    cur = ctx.L
+    cts, refs = [], []
+    for i, x in enumerate(xs):
+        ct, ref = _cipher(o, client, x.T.reshape(-1), cur, 300 + i)
+        cts.append(ct)
+        refs.append(ref)
+    from holmes_b200 import fhe as F
+
+    with LN.LinearOperator(crypto_context=session, token_lanes=lanes, config=cfg) as op, \
+            LN.LinearWeight(w, dtype=w.dtype, crypto_context=session) as lw:
+        outs, _ = op.apply(cts, lw)
+        # the single-input EasyFHE call takes the same path
+        pts = lw.plaintext(plan, plan.chunks[1], level=0, operator_config=cfg)
+        one = F.hoisted_mac_sum(cts[0], plan.baby_offsets, pts, plan.giant_offset, plan.chunks[1].giant_count, ctx,
+                                strategy="ext_double_hoist")
+        assert int(one.state.cur_limbs) == cur and not one.is_ext
+    expect = _oracle_linear_ext(o, refs, w, plan, cur, ctx.scale, double=True)
+    for got, e, x in zip(outs, expect, xs):
+        np.testing.assert_array_equal(host(got.cv[0][0]), e[0])
+        np.testing.assert_array_equal(host(got.cv[1][0]), e[1])
+        dec = client.decrypt(got).reshape(dim, lanes).T
+        np.testing.assert_allclose(dec, x @ w.T, atol=2e-8 * 50, rtol=2e-6)
+    ctx.close()
 
 
 def test_linear_operator_ext_normal_bitexact_and_decodes():

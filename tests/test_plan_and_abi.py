@@ -71,13 +71,10 @@ def test_config_validation(kwargs):
         LN.LinearOperatorConfig(**kwargs)
 
 
-@pytest.mark.parametrize("strategy", ["ext_double_hoist"])
-def test_extended_basis_strategies_are_refused_at_apply(strategy):
-    """The config accepts the reference's three names; ext_double_hoist is not built and fails before any work."""
-    cfg = LN.LinearOperatorConfig(hoist_strategy=strategy)
-    op = LN.LinearOperator(crypto_context=object(), token_lanes=8, config=cfg)
-    with pytest.raises(NotImplementedError):
-        op.apply([object()], object())
+def test_unknown_strategies_are_refused():
+    """The config accepts the reference's three names and nothing else."""
+    with pytest.raises(ValueError):
+        LN.LinearOperatorConfig(hoist_strategy="double")
 
 
 def test_plan_validation():
