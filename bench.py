@@ -607,9 +607,55 @@ def run_bootstrap(args) -> None:
     ctx.close()
 
 
+def run_silu(args) -> None:
+    """SiLU of the model's MLP as the reference evaluates it (operators/nonlinear/polynomial.py:469-562): a degree-236
+    Chebyshev series on [-8, 8] (k = 16, m = 4: 8 levels + 1 for the map) over ``--inputs`` ciphertexts at once,
+    N = 2^16, entering at 18 limbs (a refresh's output level) of the production 38-limb chain.  Decoded against the
+    float64 series."""
+    import torch
+    from numpy.polynomial import chebyshev as npcheb
+
+    from holmes_b200 import _lib
+    from holmes_b200 import fhe as F
+    from holmes_b200 import polynomial as P
+
+    spec = F.CKKSContextSpec(depth=DEPTH, log_n=LOG_N, dnum=DNUM, dcrt_bits=DCRT, first_mod=FIRST, special_bits=60,
+                             hamming_weight=192, seed=0, auto_load_keys=False)
+    client, ctx = F.generate_client_context(spec)
+    a, b, degree, limbs = -8.0, 8.0, 236, 18
+    std = npcheb.chebinterpolate(lambda y: (v := (y * (b - a) + (a + b)) / 2) / (1 + np.exp(-v)), degree)
+    ref = std.copy()
+    ref[0] *= 2.0
+    rng = np.random.default_rng(0)
+    xs = [rng.uniform(a, b, size=ctx.max_slots) for _ in range(args.inputs)]
+    batch = F.pack_cipher_batch([client.encrypt(x, cur_limbs=limbs, counter=i) for i, x in enumerate(xs)])
+    for _ in range(max(1, args.warmup)):
+        P.eval_chebyshev_series_cipher(batch, ref, lower_bound=a, upper_bound=b, crypto_context=ctx)
+    torch.cuda.synchronize()
+    count0 = _lib.ctypes.c_ulonglong()
+    _lib.call("holmes_launch_count", _lib.ctypes.byref(count0))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        out = P.eval_chebyshev_series_cipher(batch, ref, lower_bound=a, upper_bound=b, crypto_context=ctx)
+    e1.record()
+    torch.cuda.synchronize()
+    count1 = _lib.ctypes.c_ulonglong()
+    _lib.call("holmes_launch_count", _lib.ctypes.byref(count1))
+    ms = e0.elapsed_time(e1) / args.steps
+    err = max(float(np.abs(client.decrypt(out, item=i).real - npcheb.chebval((2 * x - a - b) / (b - a), std)).max())
+              for i, x in enumerate(xs[:2]))
+    print(json.dumps({"metric": "SiLU (degree-236 Chebyshev, Paterson-Stockmeyer) latency per ciphertext, N=2^16",
+                      "value": round(ms / 1e3 / args.inputs, 6), "unit": "s", "batch": args.inputs,
+                      "ms_per_batch": round(ms, 2), "steps": args.steps, "higher_is_better": False,
+                      "input_limbs": limbs, "output_limbs": int(out.state.cur_limbs), "max_abs_err_vs_series": err,
+                      "gpu_launches": int((count1.value - count0.value) // max(1, args.steps))}), flush=True)
+    ctx.close()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--workload", choices=("linear", "bootstrap", "primitives"), default="linear")
+    ap.add_argument("--workload", choices=("linear", "bootstrap", "primitives", "silu"), default="linear")
     ap.add_argument("--boot-batch", type=int, default=8)
     ap.add_argument("--boot-iterations", type=int, default=1, help="2 = Meta-BTS correction")
     ap.add_argument("--kernel", default=None, help="profile one kernel family (see run_kernel)")
@@ -630,6 +676,8 @@ def main() -> None:
         run_bootstrap(args)
     elif args.workload == "primitives":
         run_primitives(args)
+    elif args.workload == "silu":
+        run_silu(args)
     elif args.impl == "reference":
         run_reference(args)
     else:
