@@ -417,9 +417,11 @@ __global__ void __launch_bounds__(256) k_ks_inner(KsInnerArgs a, int log_n, cons
     }
   }
   const size_t roff = (size_t)r << log_n;
-  // Software pipeline over the items (MAXB > 0): the next item's digit words and addends are loaded before this
-  // item's products and stores, so two items' loads are in flight (the stores would otherwise keep the compiler
-  // from moving the loads up, the outputs not being declared distinct from the inputs).
+  // Software pipeline over the items (MAXB = 2, the linear path's beta): the next item's digit words and addends are
+  // loaded before this item's products and stores, so two items' loads are in flight (the stores would otherwise
+  // keep the compiler from moving the loads up, the outputs not being declared distinct from the inputs).  At
+  // MAXB = 5 the prefetched words would take the kernel from 70 to 110 registers, so it keeps the plain loop.
+  constexpr bool PIPE = MAXB == 2;
   u64 dnext[KB];
   u64 anext0 = 0, anext1 = 0;
   auto fetch = [&](int item) {
@@ -433,22 +435,24 @@ __global__ void __launch_bounds__(256) k_ks_inner(KsInnerArgs a, int log_n, cons
       anext1 = a.add1 ? a.add1[ao] : 0;
     }
   };
-  if constexpr (MAXB > 0) fetch(0);
+  if constexpr (PIPE) fetch(0);
   for (int item = 0; item < a.items; ++item) {
     const u64* d = a.digits + item * a.dig_item + roff + src;
     Split4 s0{0, 0, 0, 0}, s1{0, 0, 0, 0};
     u64 acur0 = 0, acur1 = 0;
     if constexpr (MAXB > 0) {
       u64 dcur[KB];
+      if constexpr (PIPE) {
 #pragma unroll
-      for (int j = 0; j < KB; ++j) dcur[j] = dnext[j];
-      acur0 = anext0;
-      acur1 = anext1;
-      if (item + 1 < a.items) fetch(item + 1);
+        for (int j = 0; j < KB; ++j) dcur[j] = dnext[j];
+        acur0 = anext0;
+        acur1 = anext1;
+        if (item + 1 < a.items) fetch(item + 1);
+      }
 #pragma unroll
       for (int j = 0; j < MAXB; ++j) {
         if (j < a.beta) {
-          const u64 dv = dcur[j];
+          const u64 dv = PIPE ? dcur[j] : d[j * dstep];
           const uint32_t d0 = (uint32_t)dv & ((1u << 30) - 1), d1 = (uint32_t)(dv >> 30);
           s0.s00 += (u64)d0 * kb[j].x;
           s0.sa += (u64)d0 * kb[j].y;
@@ -469,7 +473,7 @@ __global__ void __launch_bounds__(256) k_ks_inner(KsInnerArgs a, int log_n, cons
     }
     if (qlimb) {
       u64 u0 = fold_split(s0, m), u1 = fold_split(s1, m);
-      if constexpr (MAXB > 0) {
+      if constexpr (PIPE) {
         if (a.add0) u0 = add_mod(u0, acur0, m.q);
         if (a.add1) u1 = add_mod(u1, acur1, m.q);
       } else {
