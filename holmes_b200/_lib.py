@@ -47,6 +47,9 @@ SIGNATURES = {
     "holmes_mul_const": [p, p, p, p, i32, i32, i64, i64, p],
     "holmes_weighted_acc": [p, p, i64, i32, p, p, i64, i32, i32, p],
     "holmes_rescale": [p, p, i64, p, i64, i32, i32, p, p],
+    "holmes_rotate_scratch_words": [p, i32, i32, p],
+    "holmes_rotate": [p, p, p, i64, i32, p, i32, u64, p, p, i64, i32, p, p],
+    "holmes_encode_diag_rows": [p, p, i32, i32, i32, i32, i32, i32, i32, i32, d, i32, p, i64, p, p, p],
     "holmes_rescale_postop": [p, p, i64, p, i64, i32, i32, p, i32, p, i64, p, p],
     "holmes_modraise": [p, p, i64, p, i64, i32, i32, p, p],
     "holmes_add_const": [p, p, p, p, i32, i32, i64, i64, p],

@@ -238,6 +238,50 @@ int holmes_keyswitch(void* ctx, const uint64_t* digits, long long digit_item, in
   return ks_apply(*C(ctx), a, S(stream));
 }
 
+int holmes_rotate_scratch_words(void* ctx, int cur, int items, long long* words) {
+  if (!ctx || !words || cur < 1 || items < 1) return -1;
+  const HolmesCtx& c = *C(ctx);
+  if (cur > c.L) return -2;
+  const long long n = c.n, rows = (long long)cur + c.K;
+  const long long digits = (long long)items * c.beta(cur) * rows * n;
+  const long long work = (long long)items * 2 * rows * n;  // >= the ModUp's items * cur * N as well
+  *words = digits + work;
+  return 0;
+}
+
+int holmes_rotate(void* ctx, const uint64_t* c0, const uint64_t* c1, long long in_item, int cur, const uint64_t* key,
+                  int key_cap, uint64_t galois, uint64_t* out0, uint64_t* out1, long long out_item, int items,
+                  uint64_t* scratch, void* stream) {
+  if (!ctx || !c0 || !c1 || !key || !out0 || !out1 || !scratch) return -1;
+  if (cur < 1 || items < 1) return -2;
+  if (galois <= 1 || !(galois & 1)) return -3;
+  const HolmesCtx& c = *C(ctx);
+  if (cur > c.L) return -2;
+  const long long digit_item = (long long)c.beta(cur) * (cur + c.K) * c.n;
+  uint64_t* digits = scratch;
+  uint64_t* work = scratch + (size_t)items * digit_item;
+  const int e = modup(c, c1, in_item, cur, items, digits, digit_item, work, S(stream));
+  if (e) return e;
+  KsArgs a{digits, digit_item, cur,     key,  key_cap, galois, c0,    nullptr, in_item,
+           nullptr, nullptr,   0,       out0, out1,    out_item, items, work};
+  return ks_apply(c, a, S(stream));
+}
+
+int holmes_encode_diag_rows(void* ctx, const double* weight, int weight_complex, int dim, int lanes, int baby,
+                            int giant_base, int giant_count, int lane_shift, int slots, double scale, int cur,
+                            uint64_t* out, long long out_row_stride, double* rows_scratch, int* flag, void* stream) {
+  if (!ctx || !weight || !out || !rows_scratch || !flag) return -1;
+  if (baby < 1 || giant_count < 1) return -2;
+  const long long row_stride = 2LL * slots;
+  int e = pack_diagonals(weight, weight_complex, dim, lanes, baby, giant_base, giant_count, lane_shift, slots,
+                         rows_scratch, row_stride, S(stream));
+  if (e) return e;
+  e = fft_special_inv(*C(ctx), rows_scratch, row_stride, giant_count * baby, slots, S(stream));
+  if (e) return e;
+  return encode_rows(*C(ctx), rows_scratch, row_stride, giant_count * baby, slots, scale, cur, out, out_row_stride,
+                     flag, S(stream));
+}
+
 int holmes_bsgs_mac(void* ctx, uint64_t* res, const uint64_t* const* c0s, const uint64_t* const* c1s, long long bstride,
                     int nb, int inputs, const uint64_t* pts, long long pstride, int groups, int limbs, void* stream) {
   if (!ctx || !res || !c0s || !c1s || !pts) return -1;

@@ -84,6 +84,13 @@ int holmes_encode_fft(void* ctx, const double* u, long long row_stride, int rows
  * (plaintexts for holmes_bsgs_mac_ext; EasyFHE's is_ext constants) */
 int holmes_encode_fft_ext(void* ctx, const double* u, long long row_stride, int rows, int slots, double scale, int cur,
                           uint64_t* out, long long out_row_stride, int* flag, void* stream);
+/* one BSGS chunk's plaintexts from the weight page in one call (LinearWeight.plaintext, weight.py:471-582:
+ * pack, special FFT, rounding, NTT): holmes_pack_diagonals into rows_scratch ([giant_count * baby][slots][2]
+ * doubles), holmes_fft_special_inv on them in place, then holmes_encode_fft into out[giant_count * baby][cur][N] at
+ * `scale` */
+int holmes_encode_diag_rows(void* ctx, const double* weight, int weight_complex, int dim, int lanes, int baby,
+                            int giant_base, int giant_count, int lane_shift, int slots, double scale, int cur,
+                            uint64_t* out, long long out_row_stride, double* rows_scratch, int* flag, void* stream);
 /* diagonal rows of one BSGS chunk (weight.py:122-154 _cpu_packer / gpu_packer.py:48-200):
  * out[giant_count * baby][slots][2] complex; weight [dim][dim] float64 or complex128 (weight_complex = 1) */
 int holmes_pack_diagonals(const double* weight, int weight_complex, int dim, int lanes, int baby, int giant_base,
@@ -150,6 +157,15 @@ int holmes_rescale_noalloc(void* ctx, const uint64_t* in, long long in_stride, u
  * scratch >= items * cur * N words */
 int holmes_modup(void* ctx, const uint64_t* c1, long long c1_item, int cur, int items, uint64_t* digits,
                  long long digit_item, uint64_t* scratch, void* stream);
+/* homo_rotate of `items` ciphertexts sharing one key (fhe.homo_rotate, operator.py:447; qkv_kernel.py:832 for the
+ * conjugation galois 2N - 1): holmes_modup then holmes_keyswitch with add0 = c0, in one call.  c0 and c1 share the
+ * item stride in_item; galois must be odd and > 1 (holmes_galois); key / key_cap as holmes_keyswitch takes them;
+ * scratch >= holmes_rotate_scratch_words(ctx, cur, items) words (the digits, then the ModUp's and the key switch's
+ * work area). */
+int holmes_rotate_scratch_words(void* ctx, int cur, int items, long long* words);
+int holmes_rotate(void* ctx, const uint64_t* c0, const uint64_t* c1, long long in_item, int cur, const uint64_t* key,
+                  int key_cap, uint64_t galois, uint64_t* out0, uint64_t* out1, long long out_item, int items,
+                  uint64_t* scratch, void* stream);
 /* for `items` ciphertexts sharing one key:
  *   out0 = perm(add0) + ModDown(sum_j perm(digit_j) key_b[j]) + post0
  *   out1 = perm(add1) + ModDown(sum_j perm(digit_j) key_a[j]) + post1

@@ -530,3 +530,55 @@ def test_reference_mac_gather_abi(ti):
                             assert int(got[c, k, i, l, j]) == want
     finally:
         ctx.close()
+
+
+def test_composed_rotate_and_encode_entry_points():
+    """holmes_rotate (ModUp and key switch in one C call, two ciphertexts) equals fhe.homo_rotate word for word, and
+    holmes_encode_diag_rows (pack and encode in one C call) equals the linear operator's plaintexts for a chunk."""
+    import ctypes
+
+    from holmes_b200 import _lib as L
+    from holmes_b200 import fhe as F
+    from holmes_b200 import linear as LN
+
+    o, client, ctx = make_pair(log_n=11, limbs=4, dnum=2, dcrt=45, first=55, special=55)
+    try:
+        rng = np.random.default_rng(33)
+        cur, N = 3, ctx.N
+        cts = [client.encrypt(rng.normal(size=ctx.max_slots) * 0.5, cur_limbs=cur, counter=70 + i) for i in range(2)]
+        batch = F.pack_cipher_batch(cts)
+        for r in (5, 2 * N - 1):
+            g = ctx.galois(r)
+            key, cap = ctx.switch_key(g, cur)
+            words = ctypes.c_longlong()
+            L.call("holmes_rotate_scratch_words", ctx.handle, cur, 2, ctypes.byref(words))
+            scratch = torch.empty(words.value, dtype=torch.uint64, device=ctx.device)
+            out = torch.empty((2, 2, cur, N), dtype=torch.uint64, device=ctx.device)
+            L.call("holmes_rotate", ctx.handle, batch.cv[0].data_ptr(), batch.cv[1].data_ptr(),
+                   int(batch.cv[0].stride(0)), cur, key.data_ptr(), cap, g, out[0].data_ptr(), out[1].data_ptr(),
+                   cur * N, 2, scratch.data_ptr(), 0)
+            for i, ct in enumerate(cts):
+                want = F.homo_rotate(ct, r, ctx)
+                for c in range(2):
+                    np.testing.assert_array_equal(host(out[c, i]), host(want.cv[c][0]))
+        session = LN.Session(client, ctx)
+        dim, lanes = 64, 16
+        cfg = LN.LinearOperatorConfig(baby_steps=8, baby_anchor_step=8, max_plaintext_rows=16)
+        plan = cfg.plan(dimension=dim, token_lanes=lanes)
+        w = rng.normal(scale=0.02, size=(dim, dim))
+        chunk = plan.chunks[1]
+        rows = chunk.giant_count * plan.baby_steps
+        slots = int(session.max_slots)
+        with LN.LinearWeight(w, dtype=w.dtype, crypto_context=session) as lw:
+            want = lw.plaintext(plan, chunk, level=ctx.L - cur, operator_config=cfg)
+            wd = torch.from_numpy(w).to(ctx.device)
+            out = torch.empty((rows, cur, N), dtype=torch.uint64, device=ctx.device)
+            scratch = torch.empty((rows, slots, 2), dtype=torch.float64, device=ctx.device)
+            flag = torch.zeros(1, dtype=torch.int32, device=ctx.device)
+            L.call("holmes_encode_diag_rows", ctx.handle, wd.data_ptr(), 0, dim, lanes, plan.baby_steps,
+                   chunk.giant_base, chunk.giant_count, plan.lane_shift, slots, float(ctx.scale_at(cur)), cur,
+                   out.data_ptr(), cur * N, scratch.data_ptr(), flag.data_ptr(), 0)
+            np.testing.assert_array_equal(host(out), host(want.cv[0][:, :cur]))
+            assert int(flag.item()) == 0
+    finally:
+        ctx.close()
