@@ -49,6 +49,8 @@ SIGNATURES = {
     "holmes_rescale": [p, p, i64, p, i64, i32, i32, p, p],
     "holmes_rotate_scratch_words": [p, i32, i32, p],
     "holmes_rotate": [p, p, p, i64, i32, p, i32, u64, p, p, i64, i32, p, p],
+    "holmes_hoisted_rotations": [p, p, p, i64, i32, i32, i32, p, p, p, p, p, i64, i64, p, p],
+    "holmes_giant_sum": [p, p, p, i64, i64, i32, i32, i32, p, i32, u64, p, p, i64, p, p],
     "holmes_encode_diag_rows": [p, p, i32, i32, i32, i32, i32, i32, i32, i32, d, i32, p, i64, p, p, p],
     "holmes_rescale_postop": [p, p, i64, p, i64, i32, i32, p, i32, p, i64, p, p],
     "holmes_modraise": [p, p, i64, p, i64, i32, i32, p, p],

@@ -267,6 +267,93 @@ int holmes_rotate(void* ctx, const uint64_t* c0, const uint64_t* c1, long long i
   return ks_apply(c, a, S(stream));
 }
 
+int holmes_hoisted_rotations(void* ctx, const uint64_t* c0, const uint64_t* c1, long long in_item, int cur, int items,
+                             int count, const uint64_t* const* keys, const int* key_caps, const uint64_t* galois,
+                             uint64_t* out0, uint64_t* out1, long long out_item, long long out_rot, uint64_t* scratch,
+                             void* stream) {
+  if (!ctx || !c0 || !c1 || !keys || !key_caps || !galois || !out0 || !out1 || !scratch) return -1;
+  if (cur < 1 || items < 1 || count < 1) return -2;
+  const HolmesCtx& c = *C(ctx);
+  if (cur > c.L) return -2;
+  const long long digit_item = (long long)c.beta(cur) * (cur + c.K) * c.n;
+  uint64_t* digits = scratch;
+  uint64_t* work = scratch + (size_t)items * digit_item;
+  bool up = false;
+  for (int r = 0; r < count; ++r) {
+    uint64_t* o0 = out0 + (size_t)r * out_rot;
+    uint64_t* o1 = out1 + (size_t)r * out_rot;
+    if (galois[r] <= 1) {  // offset 0: the ciphertext itself
+      for (int i = 0; i < items; ++i) {
+        cudaError_t e = cudaMemcpyAsync(o0 + (size_t)i * out_item, c0 + (size_t)i * in_item,
+                                        (size_t)cur * c.n * sizeof(uint64_t), cudaMemcpyDeviceToDevice, S(stream));
+        if (e == cudaSuccess)
+          e = cudaMemcpyAsync(o1 + (size_t)i * out_item, c1 + (size_t)i * in_item,
+                              (size_t)cur * c.n * sizeof(uint64_t), cudaMemcpyDeviceToDevice, S(stream));
+        if (e != cudaSuccess) return (int)e;
+      }
+      continue;
+    }
+    if (!(galois[r] & 1) || !keys[r]) return -3;
+    if (!up) {
+      const int e = modup(c, c1, in_item, cur, items, digits, digit_item, work, S(stream));
+      if (e) return e;
+      up = true;
+    }
+    KsArgs a{digits, digit_item, cur,  keys[r], key_caps[r], galois[r], c0,    nullptr, in_item,
+             nullptr, nullptr,   0,    o0,      o1,          out_item,  items, work};
+    const int e = ks_apply(c, a, S(stream));
+    if (e) return e;
+  }
+  return 0;
+}
+
+int holmes_giant_sum(void* ctx, const uint64_t* p0, const uint64_t* p1, long long part_item, long long part_giant,
+                     int cur, int items, int giants, const uint64_t* key, int key_cap, uint64_t galois, uint64_t* out0,
+                     uint64_t* out1, long long out_item, uint64_t* scratch, void* stream) {
+  if (!ctx || !p0 || !p1 || !key || !out0 || !out1 || !scratch) return -1;
+  if (cur < 1 || items < 1 || giants < 1) return -2;
+  if (galois <= 1 || !(galois & 1)) return -3;
+  const HolmesCtx& c = *C(ctx);
+  if (cur > c.L) return -2;
+  const long long digit_item = (long long)c.beta(cur) * (cur + c.K) * c.n;
+  const size_t poly = (size_t)cur * c.n;
+  uint64_t* digits = scratch;
+  uint64_t* work = digits + (size_t)items * digit_item;
+  uint64_t* tmp0 = work + (size_t)items * 2 * (cur + c.K) * c.n;  // the other accumulator: [items][cur][N] x 2
+  uint64_t* tmp1 = tmp0 + (size_t)items * poly;
+  // acc = partial[G - 1]; acc = rot(acc) + partial[g] for g = G - 2 .. 0, ping-ponging so the last lands in out
+  const uint64_t* a0 = p0 + (size_t)(giants - 1) * part_giant;
+  const uint64_t* a1 = p1 + (size_t)(giants - 1) * part_giant;
+  long long a_item = part_item;
+  if (giants == 1) {
+    for (int i = 0; i < items; ++i) {
+      cudaError_t e = cudaMemcpyAsync(out0 + (size_t)i * out_item, a0 + (size_t)i * a_item, poly * sizeof(uint64_t),
+                                      cudaMemcpyDeviceToDevice, S(stream));
+      if (e == cudaSuccess)
+        e = cudaMemcpyAsync(out1 + (size_t)i * out_item, a1 + (size_t)i * a_item, poly * sizeof(uint64_t),
+                            cudaMemcpyDeviceToDevice, S(stream));
+      if (e != cudaSuccess) return (int)e;
+    }
+    return 0;
+  }
+  for (int g = giants - 2; g >= 0; --g) {
+    const bool to_out = ((giants - 2 - g) & 1) == ((giants - 2) & 1);  // the step g = 0 writes out
+    uint64_t* d0 = to_out ? out0 : tmp0;
+    uint64_t* d1 = to_out ? out1 : tmp1;
+    const long long d_item = to_out ? out_item : (long long)poly;
+    int e = modup(c, a1, a_item, cur, items, digits, digit_item, work, S(stream));
+    if (e) return e;
+    KsArgs ks{digits, digit_item, cur, key, key_cap, galois, a0, nullptr, a_item, p0 + (size_t)g * part_giant,
+              p1 + (size_t)g * part_giant, part_item, d0, d1, d_item, items, work};
+    e = ks_apply(c, ks, S(stream));
+    if (e) return e;
+    a0 = d0;
+    a1 = d1;
+    a_item = d_item;
+  }
+  return 0;
+}
+
 int holmes_encode_diag_rows(void* ctx, const double* weight, int weight_complex, int dim, int lanes, int baby,
                             int giant_base, int giant_count, int lane_shift, int slots, double scale, int cur,
                             uint64_t* out, long long out_row_stride, double* rows_scratch, int* flag, void* stream) {

@@ -166,6 +166,20 @@ int holmes_rotate_scratch_words(void* ctx, int cur, int items, long long* words)
 int holmes_rotate(void* ctx, const uint64_t* c0, const uint64_t* c1, long long in_item, int cur, const uint64_t* key,
                   int key_cap, uint64_t galois, uint64_t* out0, uint64_t* out1, long long out_item, int items,
                   uint64_t* scratch, void* stream);
+/* prepare_hoisted_baby_rotations (operator.py:113-119) in one call: one ModUp of the `items` ciphertexts, then
+ * rotation r < count by keys[r] / key_caps[r] / galois[r] (host arrays; galois <= 1 copies the input) into
+ * out_c + r * out_rot (item stride out_item); scratch as holmes_rotate's */
+int holmes_hoisted_rotations(void* ctx, const uint64_t* c0, const uint64_t* c1, long long in_item, int cur, int items,
+                             int count, const uint64_t* const* keys, const int* key_caps, const uint64_t* galois,
+                             uint64_t* out0, uint64_t* out1, long long out_item, long long out_rot, uint64_t* scratch,
+                             void* stream);
+/* the giant Horner chain of hoisted_mac_sum (bench/cmp/holmes_multi_mac.py:148-194) in one call: acc = partial[G-1];
+ * acc = rot(acc, giant offset) + partial[g] for g = G-2 .. 0, partial g of item i at p_c + g * part_giant +
+ * i * part_item, one key (galois of the giant offset); result in out_c; scratch >= holmes_rotate_scratch_words(ctx,
+ * cur, items) + 2 * items * cur * N words */
+int holmes_giant_sum(void* ctx, const uint64_t* p0, const uint64_t* p1, long long part_item, long long part_giant,
+                     int cur, int items, int giants, const uint64_t* key, int key_cap, uint64_t galois, uint64_t* out0,
+                     uint64_t* out1, long long out_item, uint64_t* scratch, void* stream);
 /* for `items` ciphertexts sharing one key:
  *   out0 = perm(add0) + ModDown(sum_j perm(digit_j) key_b[j]) + post0
  *   out1 = perm(add1) + ModDown(sum_j perm(digit_j) key_a[j]) + post1

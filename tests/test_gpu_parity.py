@@ -561,6 +561,34 @@ def test_composed_rotate_and_encode_entry_points():
                 want = F.homo_rotate(ct, r, ctx)
                 for c in range(2):
                     np.testing.assert_array_equal(host(out[c, i]), host(want.cv[c][0]))
+        # hoisted rotations (offsets 0, 3, 9): one ModUp, three keys
+        offs = (0, 3, 9)
+        gal = [ctx.galois(r) for r in offs]
+        keys = [ctx.switch_key(g, cur) if g > 1 else (torch.empty(1, dtype=torch.uint64, device=ctx.device), 0)
+                for g in gal]
+        hout = torch.empty((2, len(offs), 2, cur, N), dtype=torch.uint64, device=ctx.device)
+        kp = (ctypes.c_void_p * 3)(*[k[0].data_ptr() for k in keys])
+        caps = (ctypes.c_int * 3)(*[k[1] for k in keys])
+        gals = (ctypes.c_uint64 * 3)(*gal)
+        L.call("holmes_hoisted_rotations", ctx.handle, batch.cv[0].data_ptr(), batch.cv[1].data_ptr(),
+               int(batch.cv[0].stride(0)), cur, 2, 3, kp, caps, gals, hout[0].data_ptr(), hout[1].data_ptr(), cur * N,
+               2 * cur * N, scratch.data_ptr(), 0)
+        for b, r in enumerate(offs):
+            for i, ct in enumerate(cts):
+                want = F.homo_rotate(ct, r, ctx)
+                for c in range(2):
+                    np.testing.assert_array_equal(host(hout[c, b, i]), host(want.cv[c][0]))
+        # giant sum over 3 partials (the hoisted outputs) with offset 16: the Python Horner chain
+        g16 = ctx.galois(16)
+        key16, cap16 = ctx.switch_key(g16, cur)
+        L.call("holmes_rotate_scratch_words", ctx.handle, cur, 2, ctypes.byref(words))
+        gs = torch.empty(words.value + 2 * 2 * cur * N, dtype=torch.uint64, device=ctx.device)
+        gout = torch.empty((2, 2, cur, N), dtype=torch.uint64, device=ctx.device)
+        L.call("holmes_giant_sum", ctx.handle, hout[0].data_ptr(), hout[1].data_ptr(), cur * N, 2 * cur * N, cur, 2, 3,
+               key16.data_ptr(), cap16, g16, gout[0].data_ptr(), gout[1].data_ptr(), cur * N, gs.data_ptr(), 0)
+        h0, h1 = F.giant_horner(ctx, hout.clone(), 16)
+        np.testing.assert_array_equal(host(gout[0]), host(h0))
+        np.testing.assert_array_equal(host(gout[1]), host(h1))
         session = LN.Session(client, ctx)
         dim, lanes = 64, 16
         cfg = LN.LinearOperatorConfig(baby_steps=8, baby_anchor_step=8, max_plaintext_rows=16)
