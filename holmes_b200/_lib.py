@@ -51,6 +51,7 @@ SIGNATURES = {
     "holmes_rotate": [p, p, p, i64, i32, p, i32, u64, p, p, i64, i32, p, p],
     "holmes_hoisted_rotations": [p, p, p, i64, i32, i32, i32, p, p, p, p, p, i64, i64, p, p],
     "holmes_giant_sum": [p, p, p, i64, i64, i32, i32, i32, p, i32, u64, p, p, i64, p, p],
+    "holmes_mul_relin": [p, p, p, p, p, i64, i32, i32, p, i32, p, p, i64, p, p],
     "holmes_encode_diag_rows": [p, p, i32, i32, i32, i32, i32, i32, i32, i32, d, i32, p, i64, p, p, p],
     "holmes_rescale_postop": [p, p, i64, p, i64, i32, i32, p, i32, p, i64, p, p],
     "holmes_modraise": [p, p, i64, p, i64, i32, i32, p, p],

@@ -354,6 +354,33 @@ int holmes_giant_sum(void* ctx, const uint64_t* p0, const uint64_t* p1, long lon
   return 0;
 }
 
+int holmes_mul_relin(void* ctx, const uint64_t* a0, const uint64_t* a1, const uint64_t* b0, const uint64_t* b1,
+                     long long in_item, int cur, int items, const uint64_t* key, int key_cap, uint64_t* out0,
+                     uint64_t* out1, long long out_item, uint64_t* scratch, void* stream) {
+  if (!ctx || !a0 || !a1 || !b0 || !b1 || !key || !out0 || !out1 || !scratch) return -1;
+  if (cur < 1 || items < 1) return -2;
+  const HolmesCtx& c = *C(ctx);
+  if (cur > c.L) return -2;
+  const long long poly = (long long)cur * c.n;
+  const long long digit_item = (long long)c.beta(cur) * (cur + c.K) * c.n;
+  uint64_t* digits = scratch;
+  uint64_t* work = digits + (size_t)items * digit_item;
+  uint64_t* d0 = work + (size_t)items * 2 * (cur + c.K) * c.n;  // the tensor product, [items][cur][N] each
+  uint64_t* d1 = d0 + (size_t)items * poly;
+  uint64_t* d2 = d1 + (size_t)items * poly;
+  uint64_t* t = d2 + (size_t)items * poly;
+  int e = elementwise(c, EW_MUL, a0, b0, d0, items, cur, in_item, in_item, poly, S(stream));
+  if (!e) e = elementwise(c, EW_MUL, a0, b1, d1, items, cur, in_item, in_item, poly, S(stream));
+  if (!e) e = elementwise(c, EW_MUL, a1, b0, t, items, cur, in_item, in_item, poly, S(stream));
+  if (!e) e = elementwise(c, EW_ADD, d1, t, d1, items, cur, poly, poly, poly, S(stream));
+  if (!e) e = elementwise(c, EW_MUL, a1, b1, d2, items, cur, in_item, in_item, poly, S(stream));
+  if (!e) e = modup(c, d2, poly, cur, items, digits, digit_item, work, S(stream));
+  if (e) return e;
+  KsArgs ks{digits, digit_item, cur, key, key_cap, 1, d0, d1, poly, nullptr, nullptr, 0, out0, out1, out_item, items,
+            work};
+  return ks_apply(c, ks, S(stream));
+}
+
 int holmes_encode_diag_rows(void* ctx, const double* weight, int weight_complex, int dim, int lanes, int baby,
                             int giant_base, int giant_count, int lane_shift, int slots, double scale, int cur,
                             uint64_t* out, long long out_row_stride, double* rows_scratch, int* flag, void* stream) {

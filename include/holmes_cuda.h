@@ -180,6 +180,13 @@ int holmes_hoisted_rotations(void* ctx, const uint64_t* c0, const uint64_t* c1, 
 int holmes_giant_sum(void* ctx, const uint64_t* p0, const uint64_t* p1, long long part_item, long long part_giant,
                      int cur, int items, int giants, const uint64_t* key, int key_cap, uint64_t galois, uint64_t* out0,
                      uint64_t* out1, long long out_item, uint64_t* scratch, void* stream);
+/* homo_mul_relin (llama3fhe/operators/primitives.py:21-37) of `items` pairs in one call: the tensor product
+ * (d0, d1, d2) = (a0 b0, a0 b1 + a1 b0, a1 b1), then the relinearisation key switch of d2 added to (d0, d1); key /
+ * key_cap the relinearisation key (holmes_keygen with galois 0); the four inputs share the item stride in_item;
+ * scratch >= holmes_rotate_scratch_words(ctx, cur, items) + 4 * items * cur * N words.  Not rescaled. */
+int holmes_mul_relin(void* ctx, const uint64_t* a0, const uint64_t* a1, const uint64_t* b0, const uint64_t* b1,
+                     long long in_item, int cur, int items, const uint64_t* key, int key_cap, uint64_t* out0,
+                     uint64_t* out1, long long out_item, uint64_t* scratch, void* stream);
 /* for `items` ciphertexts sharing one key:
  *   out0 = perm(add0) + ModDown(sum_j perm(digit_j) key_b[j]) + post0
  *   out1 = perm(add1) + ModDown(sum_j perm(digit_j) key_a[j]) + post1

@@ -578,6 +578,17 @@ def test_composed_rotate_and_encode_entry_points():
                 want = F.homo_rotate(ct, r, ctx)
                 for c in range(2):
                     np.testing.assert_array_equal(host(hout[c, b, i]), host(want.cv[c][0]))
+        # relinearised product of the two ciphertexts with themselves (items 0, 1)
+        rkey, rcap = ctx.switch_key(0, cur)
+        ms = torch.empty(words.value + 4 * 2 * cur * N, dtype=torch.uint64, device=ctx.device)
+        mout = torch.empty((2, 2, cur, N), dtype=torch.uint64, device=ctx.device)
+        L.call("holmes_mul_relin", ctx.handle, batch.cv[0].data_ptr(), batch.cv[1].data_ptr(), batch.cv[0].data_ptr(),
+               batch.cv[1].data_ptr(), int(batch.cv[0].stride(0)), cur, 2, rkey.data_ptr(), rcap, mout[0].data_ptr(),
+               mout[1].data_ptr(), cur * N, ms.data_ptr(), 0)
+        for i, ct in enumerate(cts):
+            want = F.homo_mul_relin(ct, ct, ctx)
+            for c in range(2):
+                np.testing.assert_array_equal(host(mout[c, i]), host(want.cv[c][0]))
         # giant sum over 3 partials (the hoisted outputs) with offset 16: the Python Horner chain
         g16 = ctx.galois(16)
         key16, cap16 = ctx.switch_key(g16, cur)
