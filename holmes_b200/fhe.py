@@ -284,6 +284,7 @@ class Context:
             torch.cuda.synchronize(self.device)
             self._keys.clear()
             self._work.clear()
+            self.__dict__.pop("_ones_rows", None)
             _lib.call("holmes_ctx_destroy", self.handle)
             self.handle = None
 
@@ -790,7 +791,10 @@ def giant_double_hoist(ctx: Context, res: torch.Tensor, giant_offset: int) -> tu
                   c0.data_ptr(), _item_stride(c0), ext[0, g].data_ptr(), ext[1, g].data_ptr(), (cur + K) * N, items,
                   _stream())
         OPTIMER.stop(tok, items * (ctx.beta(cur) * (cur + K) + 3 * cur + 2 * K) * N * 8)
-    ones = torch.ones((G, cur + K, N), dtype=torch.uint64, device=ctx.device)
+    cache = ctx.__dict__.setdefault("_ones_rows", {})   # the all-ones plaintext, kept per (G, limbs)
+    ones = cache.get((G, cur + K))
+    if ones is None:
+        ones = cache[(G, cur + K)] = torch.ones((G, cur + K, N), dtype=torch.uint64, device=ctx.device)
     summed = torch.empty((2, 1, items, cur + K, N), dtype=torch.uint64, device=ctx.device)
     c0s = _lib.ptr_array([ext[0, 0, i].data_ptr() for i in range(items)])
     c1s = _lib.ptr_array([ext[1, 0, i].data_ptr() for i in range(items)])
