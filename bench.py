@@ -492,6 +492,172 @@ def run_kernel(args) -> None:
     ctx.close()
 
 
+def _ref_kernel_lib(name: str):
+    """The reference's own in-tree CUDA kernel library (bench/cmp/kernels/*.cu compiled unchanged for sm_100a by
+    ``make -C oracle ref``): the bar the engine's kernels are measured against.  None when not built."""
+    import ctypes
+
+    path = os.path.join(ROOT, "oracle", "_ref", name)
+    return ctypes.CDLL(path) if os.path.exists(path) else None
+
+
+def _root_tables_from_engine(ctx, limbs: int):
+    """power_of_roots / power_of_roots_shoup in the reference's layout ([limbs][N], psi^bitrev(k)) for the engine's
+    own primes.  psi is read back from the engine: the NTT of the monomial X has psi^(2 bitrev(0) + 1) = psi in
+    word 0."""
+    import torch
+
+    from holmes_b200 import _lib as L
+
+    N = ctx.N
+    x = torch.zeros((1, limbs, N), dtype=torch.uint64, device=ctx.device)
+    x[0, :, 1] = 1
+    L.call("holmes_ntt", ctx.handle, x.data_ptr(), 1, limbs, limbs * N, 0, 0, 0)
+    psis = [int(v) for v in x[0, :, 0].cpu().numpy()]
+    bits = ctx.logN
+    rev = np.array([int(format(k, f"0{bits}b")[::-1], 2) for k in range(N)])
+    roots = np.empty((limbs, N), dtype=np.uint64)
+    shoup = np.empty((limbs, N), dtype=np.uint64)
+    for li in range(limbs):
+        q, psi = ctx.moduli[li], psis[li]
+        pw = [1] * N
+        for k in range(1, N):
+            pw[k] = pw[k - 1] * psi % q
+        r = [pw[int(j)] for j in rev]
+        roots[li] = np.array(r, dtype=np.uint64)
+        shoup[li] = np.array([(v << 64) // q for v in r], dtype=np.uint64)
+    return roots, shoup
+
+
+def run_vs_ref(args) -> None:
+    """The engine's kernels against the reference's own in-tree kernels on the same B200, same inputs, bench shape
+    (N = 2^16, 13 limbs of the production chain):
+
+    * ``--kernel mac``: one BSGS chunk (8 giants x 64 babies, 16 inputs) -- the reference's ``holmes_mac_multi`` at its
+      production tile ``ti = 10108`` (lazy 1 x 8, bench/cmp/holmes_multi_mac.py:57-58; kernel
+      bench/cmp/kernels/holmes_mac.cu:196-274) against the engine's ``holmes_bsgs_mac`` (``k_bsgs_mac3``);
+    * ``--kernel encode``: encode stage 2 of one chunk's 512 rows (llround, per-limb reduction, NTT) -- the reference's
+      ``holmes_encode_stage2`` with its default launch (bench/cmp/holmes_fast_stage2.py:43-49; kernels
+      bench/cmp/kernels/holmes_encode.cu:115-285) against the engine's ``holmes_encode_fft`` on the same doubles.
+
+    Both outputs are compared word for word before timing; each side is timed with CUDA events over ``--steps``
+    launches after ``--warmup`` launches, the clocks sampled during the timed launches."""
+    import ctypes
+
+    import torch
+
+    from holmes_b200 import _lib as L
+    from holmes_b200 import fhe as F
+
+    spec, _, _ = spec_for(CUR_LIMBS)
+    _, ctx = F.generate_client_context(spec)
+    N, cur, I = ctx.N, int(args.limbs), int(args.inputs)
+    gen = torch.Generator(device=ctx.device).manual_seed(0)
+
+    def rand(items, limbs):
+        out = torch.empty((items, limbs, N), dtype=torch.uint64, device=ctx.device)
+        for li in range(limbs):
+            r = torch.randint(0, 2 ** 62, (items, N), device=ctx.device, dtype=torch.int64, generator=gen)
+            out[:, li] = (r % ctx.moduli[li]).to(torch.uint64)
+        return out
+
+    p, i32, ll, d = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong, ctypes.c_double
+    if args.kernel == "mac":
+        lib = _ref_kernel_lib("libholmes_mac_ref.so")
+        if lib is None:
+            raise SystemExit("oracle/_ref/libholmes_mac_ref.so is not built (make -C oracle ref)")
+        lib.holmes_mac_multi.argtypes = [p, p, p, ll, i32, i32, p, ll, i32, i32, i32, p, p, p, p]
+        lib.holmes_mac_multi.restype = i32
+        nb, G = 64, 8
+        pts = rand(G * nb, cur)
+        bab = rand(2 * nb * I, cur).reshape(2, nb, I, cur, N)
+        c0s = L.ptr_array([bab[0, :, i].data_ptr() for i in range(I)])
+        c1s = L.ptr_array([bab[1, :, i].data_ptr() for i in range(I)])
+        res_ref = torch.empty((2, G, I, cur, N), dtype=torch.uint64, device=ctx.device)
+        res_eng = torch.empty_like(res_ref)
+        tabs = (ctx.primes.data_ptr(), ctx.barret_ratio.data_ptr(), ctx.barret_k.data_ptr())
+
+        def ref():
+            rc = lib.holmes_mac_multi(res_ref.data_ptr(), c0s, c1s, I * cur * N, nb, I, pts.data_ptr(), cur * N, G,
+                                      10108, cur, *tabs, None)
+            if rc:
+                raise RuntimeError(f"reference holmes_mac_multi returned {rc}")
+
+        def eng():
+            L.call("holmes_bsgs_mac", ctx.handle, res_eng.data_ptr(), c0s, c1s, I * cur * N, nb, I, pts.data_ptr(),
+                   cur * N, G, cur, 0)
+        nbytes = (G * nb * cur + I * nb * 2 * cur + 2 * G * I * cur) * N * 8
+        outs = (res_ref, res_eng)
+        what = "BSGS MAC chunk: 8 giants x 64 babies x 16 inputs, 13 limbs"
+    elif args.kernel == "encode":
+        lib = _ref_kernel_lib("libholmes_encode_ref.so")
+        if lib is None:
+            raise SystemExit("oracle/_ref/libholmes_encode_ref.so is not built (make -C oracle ref)")
+        lib.holmes_encode_stage2.argtypes = [p, p, ll, i32, d, i32, p, p, p, p, p, p, p, i32, i32, i32]
+        lib.holmes_encode_stage2.restype = i32
+        rows = 512
+        z = torch.randn((rows, ctx.max_slots), dtype=torch.complex128, device=ctx.device, generator=gen) * 0.02
+        mid = F.fft_special_inv_rows(ctx, z, ctx.max_slots)
+        zr = torch.view_as_real(mid).contiguous()            # the stage-1 doubles: [rows][N/2][re, im]
+        roots, shoup = _root_tables_from_engine(ctx, cur)
+        k_max64 = 9223372036854775295                         # Encode.cu MAX_64BIT_VALUE (holmes_encode.cu:14)
+        diffs = torch.tensor([k_max64 % q for q in ctx.moduli[:cur]], dtype=torch.uint64, device=ctx.device)
+        rt = torch.from_numpy(roots).to(ctx.device)
+        st = torch.from_numpy(shoup).to(ctx.device)
+        out_ref = torch.empty((rows, cur, N), dtype=torch.uint64, device=ctx.device)
+        out_eng = torch.empty_like(out_ref)
+        flag = torch.zeros(1, dtype=torch.int32, device=ctx.device)
+        scale = float(ctx.scale)
+
+        def ref():
+            rc = lib.holmes_encode_stage2(out_ref.data_ptr(), zr.data_ptr(), N, rows, scale, cur,
+                                          ctx.primes.data_ptr(), diffs.data_ptr(), ctx.barret_ratio.data_ptr(),
+                                          ctx.barret_k.data_ptr(), rt.data_ptr(), st.data_ptr(),
+                                          torch.cuda.current_stream().cuda_stream, 0, 3, 0)
+            if rc:
+                raise RuntimeError(f"reference holmes_encode_stage2 returned {rc}")
+
+        def eng():
+            L.call("holmes_encode_fft", ctx.handle, zr.data_ptr(), N, rows, ctx.max_slots, scale, cur,
+                   out_eng.data_ptr(), cur * N, flag.data_ptr(), 0)
+        nbytes = rows * (N * 8 + cur * N * 8)
+        outs = (out_ref, out_eng)
+        what = "encode stage 2: 512 rows (one BSGS chunk), 13 limbs"
+    else:
+        raise SystemExit("--vs-ref covers --kernel mac and --kernel encode")
+    ref()
+    eng()
+    torch.cuda.synchronize()
+    if not torch.equal(outs[0], outs[1]):
+        raise SystemExit(f"{args.kernel}: engine and reference outputs differ")
+
+    def timed(fn):
+        for _ in range(max(1, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(max(1, args.steps)):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / max(1, args.steps)
+
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    clocks.ready()
+    t_ref = timed(ref)
+    t_eng = timed(eng)
+    ck = clocks.stop()
+    peak, kind = peaks()
+    print(json.dumps({"kernel": args.kernel, "vs_ref": what, "bit_identical": True, "ref_ms": round(t_ref, 4),
+                      "engine_ms": round(t_eng, 4), "speedup": round(t_ref / t_eng, 3),
+                      "algorithmic_bytes": nbytes, "engine_hbm_frac": round(nbytes / (t_eng * 1e-3) / 1e9 / peak, 4),
+                      "ref_hbm_frac": round(nbytes / (t_ref * 1e-3) / 1e9 / peak, 4), "peak_gbs": peak,
+                      "peak_kind": kind, "clocks": ck}), flush=True)
+    ctx.close()
+
+
 def run_primitives(args) -> None:
     """BASELINE config 2, the RNS-CKKS primitive sweep: N = 2^16, ~50-bit primes, dnum 3 (alpha = K = 12),
     L = 1..36 active limbs, residues uniform in [0, q_i) (seed 0).  Per L: batched forward / inverse NTT,
@@ -669,8 +835,12 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--cpu-rows", type=int, default=128, help="diagonal rows in the CPU baseline's sample")
     ap.add_argument("--no-check", dest="check", action="store_false")
+    ap.add_argument("--vs-ref", action="store_true",
+                    help="with --kernel mac|encode: time the reference's in-tree kernel beside the engine's")
     args = ap.parse_args()
-    if args.kernel:
+    if args.kernel and args.vs_ref:
+        run_vs_ref(args)
+    elif args.kernel:
         run_kernel(args)
     elif args.workload == "bootstrap":
         run_bootstrap(args)

@@ -41,6 +41,8 @@ SIGNATURES = {
     "holmes_encode_fft_ext": [p, p, i64, i32, i32, d, i32, p, i64, p, p],
     "holmes_encode_stage2": [p, p, i64, i32, d, i32, p, p, p, p, p, p, p, i32, i32, i32],
     "holmes_pack_diagonals":[p, i32, i32, i32, i32, i32, i32, i32, i32, p, i64, p],
+    "holmes_pack_structured": [p, p, p, i32, i32, p, p, p, p, p, p, p, p, p, i32, i32, i32, i32, i32, i32, i32, p,
+                               i64, p],
     "holmes_elementwise": [p, i32, p, p, p, i32, i32, i64, i64, i64, p],
     "holmes_mul_i": [p, p, p, i32, i32, i64, i64, p],
     "holmes_automorph": [p, p, p, u64, i32, i32, i64, i64, p],
@@ -48,6 +50,7 @@ SIGNATURES = {
     "holmes_weighted_acc": [p, p, i64, i32, p, p, i64, i32, i32, p],
     "holmes_rescale": [p, p, i64, p, i64, i32, i32, p, p],
     "holmes_rotate_scratch_words": [p, i32, i32, p],
+    "holmes_scratch_words": [p, i32, i32, i32, p],
     "holmes_rotate": [p, p, p, i64, i32, p, i32, u64, p, p, i64, i32, p, p],
     "holmes_hoisted_rotations": [p, p, p, i64, i32, i32, i32, p, p, p, p, p, i64, i64, p, p],
     "holmes_giant_sum": [p, p, p, i64, i64, i32, i32, i32, p, i32, u64, p, p, i64, p, p],

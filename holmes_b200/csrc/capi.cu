@@ -165,6 +165,32 @@ int holmes_pack_diagonals(const double* weight, int weight_complex, int dim, int
                         row_stride, S(stream));
 }
 
+int holmes_pack_structured(const void* const* sources, const long long* row_strides, const long long* col_strides,
+                           int source_count, int source_fp32, const long long* real_source, const long long* real_row,
+                           const double* real_scale, const long long* imag_source, const long long* imag_row,
+                           const double* imag_scale, const long long* real_column, const long long* imag_column,
+                           const double* column_scale, int dim, int lanes, int baby, int giant_base, int giant_count,
+                           int lane_shift, int slots, double* out, long long row_stride, void* stream) {
+  if (!sources || !row_strides || !col_strides || !real_source || !real_row || !real_scale || !imag_source ||
+      !imag_row || !imag_scale || !real_column || !imag_column || !column_scale || !out)
+    return -1;
+  if (source_count < 1 || source_count > 3) return -2;
+  StructSources src{};
+  for (int i = 0; i < 3; ++i) {
+    const int k = i < source_count ? i : 0;
+    if (!sources[k]) return -1;
+    src.p[i] = sources[k];
+    src.row_stride[i] = row_strides[k];
+    src.col_stride[i] = col_strides[k];
+  }
+  src.count = source_count;
+  src.fp32 = source_fp32 ? 1 : 0;
+  StructMaps M{real_source, real_row, imag_source, imag_row, real_column, imag_column, real_scale, imag_scale,
+               column_scale};
+  return pack_structured(src, M, dim, lanes, baby, giant_base, giant_count, lane_shift, slots, out, row_stride,
+                         S(stream));
+}
+
 int holmes_elementwise(void* ctx, int op, const uint64_t* a, const uint64_t* b, uint64_t* out, int items, int limbs,
                        long long a_item, long long b_item, long long out_item, void* stream) {
   if (!ctx || !a || !out || (op != EW_NEG && !b) || op < 0 || op > 3) return -1;
@@ -247,6 +273,20 @@ int holmes_rotate_scratch_words(void* ctx, int cur, int items, long long* words)
   const long long work = (long long)items * 2 * rows * n;  // >= the ModUp's items * cur * N as well
   *words = digits + work;
   return 0;
+}
+
+int holmes_scratch_words(void* ctx, int op, int cur, int items, long long* words) {
+  long long base = 0;
+  const int e = holmes_rotate_scratch_words(ctx, cur, items, &base);
+  if (e) return e;
+  const HolmesCtx& c = *C(ctx);
+  const long long poly = (long long)items * cur * c.n;
+  switch (op) {
+    case HOLMES_OP_ROTATE: *words = base; return 0;
+    case HOLMES_OP_GIANT_SUM: *words = base + 2 * poly; return 0;   // the ping-pong accumulator
+    case HOLMES_OP_MUL_RELIN: *words = base + 4 * poly; return 0;   // d0, d1, d2 and one product
+    default: return -4;
+  }
 }
 
 int holmes_rotate(void* ctx, const uint64_t* c0, const uint64_t* c1, long long in_item, int cur, const uint64_t* key,

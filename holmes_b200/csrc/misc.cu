@@ -833,7 +833,8 @@ int fft_special_inv(const HolmesCtx& c, double* z, long long row_stride, int row
 // gpu_packer.py:157-200): row(g, b)[s] = W[(f - g B) mod D, (f + b + lane_shift lane) mod D],
 // f = s / lanes, lane = s % lanes, g = giant_base + row / B, b = row % B.  Output complex
 // interleaved [rows][slots][2]; a real weight gives zero imaginary parts.
-__global__ void k_pack(const double* __restrict__ w, int cplx, int dim, int lanes, int baby, int giant_base,
+// weight kind: 0 float64 real, 1 complex128, 2 float32 real (widened exactly to double)
+__global__ void k_pack(const double* __restrict__ w, int kind, int dim, int lanes, int baby, int giant_base,
                        int lane_shift, int slots, double* __restrict__ out, long long row_stride) {
   const int row = blockIdx.y;
   const int g = giant_base + row / baby, b = row % baby;
@@ -844,16 +845,61 @@ __global__ void k_pack(const double* __restrict__ w, int cplx, int dim, int lane
     if (of < 0) of += dim;
     const int inf = (int)(((long long)f + b + (long long)lane_shift * lane) % dim);
     const long long idx = (long long)of * dim + inf;
-    o[s] = cplx ? reinterpret_cast<const double2*>(w)[idx] : make_double2(w[idx], 0.0);
+    if (kind == 1)
+      o[s] = reinterpret_cast<const double2*>(w)[idx];
+    else if (kind == 2)
+      o[s] = make_double2((double)reinterpret_cast<const float*>(w)[idx], 0.0);
+    else
+      o[s] = make_double2(w[idx], 0.0);
   }
 }
 int pack_diagonals(const double* weight, int weight_complex, int dim, int lanes, int baby, int giant_base,
                    int giant_count, int lane_shift, int slots, double* out, long long row_stride, cudaStream_t st) {
   if (dim < 1 || lanes < 1 || baby < 1 || giant_count < 1 || giant_base < 0) return -2;
+  if (weight_complex < 0 || weight_complex > 2) return -2;
   dim3 grid((unsigned)((slots + 255) / 256 < 64 ? (slots + 255) / 256 : 64), (unsigned)(giant_count * baby));
   count_launch();
   k_pack<<<grid, 256, 0, st>>>(weight, weight_complex, dim, lanes, baby, giant_base, lane_shift, slots, out,
                                row_stride);
+  return (int)cudaGetLastError();
+}
+
+// Structured diagonal rows: the physical square map is never built.  Output row r = physical row `of` of the
+// square matrix takes its real part from source real_source[of] at logical row real_row[of] (scaled by
+// real_scale[of]) and its imaginary part likewise; physical column `inf` reads logical columns real_column[inf] /
+// imag_column[inf] (negative = zero) scaled by column_scale[inf].  Sources are float32 or float64 matrices with
+// element strides.
+__device__ __forceinline__ double struct_load(const StructSources& S, long long src, long long row, long long col) {
+  if (src < 0 || src >= S.count || col < 0) return 0.0;
+  const long long off = row * S.row_stride[src] + col * S.col_stride[src];
+  return S.fp32 ? (double)reinterpret_cast<const float*>(S.p[src])[off]
+                : reinterpret_cast<const double*>(S.p[src])[off];
+}
+__global__ void k_pack_structured(StructSources S, StructMaps M, int dim, int lanes, int baby, int giant_base,
+                                  int lane_shift, int slots, double* __restrict__ out, long long row_stride) {
+  const int row = blockIdx.y;
+  const int g = giant_base + row / baby, b = row % baby;
+  double2* o = reinterpret_cast<double2*>(out + row * row_stride);
+  for (int s = blockIdx.x * blockDim.x + threadIdx.x; s < slots; s += gridDim.x * blockDim.x) {
+    const int f = s / lanes, lane = s - f * lanes;
+    int of = (f - g * baby) % dim;
+    if (of < 0) of += dim;
+    const int inf = (int)(((long long)f + b + (long long)lane_shift * lane) % dim);
+    const double cs = M.column_scale[inf];
+    double re = struct_load(S, M.real_source[of], M.real_row[of], M.real_column[inf]);
+    double im = struct_load(S, M.imag_source[of], M.imag_row[of], M.imag_column[inf]);
+    re = __dmul_rn(re, __dmul_rn(M.real_scale[of], cs));
+    im = __dmul_rn(im, __dmul_rn(M.imag_scale[of], cs));
+    o[s] = make_double2(re, im);
+  }
+}
+int pack_structured(const StructSources& S, const StructMaps& M, int dim, int lanes, int baby, int giant_base,
+                    int giant_count, int lane_shift, int slots, double* out, long long row_stride, cudaStream_t st) {
+  if (dim < 1 || lanes < 1 || baby < 1 || giant_count < 1 || giant_base < 0) return -2;
+  if (S.count < 1 || S.count > 3) return -2;
+  dim3 grid((unsigned)((slots + 255) / 256 < 64 ? (slots + 255) / 256 : 64), (unsigned)(giant_count * baby));
+  count_launch();
+  k_pack_structured<<<grid, 256, 0, st>>>(S, M, dim, lanes, baby, giant_base, lane_shift, slots, out, row_stride);
   return (int)cudaGetLastError();
 }
 

@@ -11,7 +11,9 @@
 // loads the library holds those 2 MiB until the process exits.  A kernel cannot be handed the host-side
 // name of the array (that is only a host stand-in for the symbol), so the first call on each device, with
 // that device current, looks up its device address with cudaGetSymbolAddress and caches it; that first
-// call should therefore happen before any stream capture.  All calls share the one array: two calls that
+// call should therefore happen before any stream capture.  The cached address assumes one primary-context
+// lifetime per device and process: after cudaDeviceReset the array lives at an address this cache does not
+// know, so the library must not be called again in that process.  All calls share the one array: two calls that
 // overlap on the GPU (different streams, no ordering between them) race on it.  The inverse NTT writes
 // every scratch word it later reads, so stale contents from an earlier call are never used and nothing
 // needs clearing.

@@ -98,6 +98,17 @@ int fft_special_inv(const HolmesCtx& c, double* z, long long row_stride, int row
 
 int pack_diagonals(const double* weight, int weight_complex, int dim, int lanes, int baby, int giant_base,
                    int giant_count, int lane_shift, int slots, double* out, long long row_stride, cudaStream_t st);
+struct StructSources {
+  const void* p[3];
+  long long row_stride[3], col_stride[3];
+  int count, fp32;
+};
+struct StructMaps {
+  const long long *real_source, *real_row, *imag_source, *imag_row, *real_column, *imag_column;
+  const double *real_scale, *imag_scale, *column_scale;
+};
+int pack_structured(const StructSources& S, const StructMaps& M, int dim, int lanes, int baby, int giant_base,
+                    int giant_count, int lane_shift, int slots, double* out, long long row_stride, cudaStream_t st);
 
 int decrypt_coef(const HolmesCtx& c, const u64* c0, const u64* c1, int cur, u64* out, cudaStream_t st);
 int secret_ntt(HolmesCtx& c, cudaStream_t st);

@@ -92,9 +92,22 @@ int holmes_encode_diag_rows(void* ctx, const double* weight, int weight_complex,
                             int giant_base, int giant_count, int lane_shift, int slots, double scale, int cur,
                             uint64_t* out, long long out_row_stride, double* rows_scratch, int* flag, void* stream);
 /* diagonal rows of one BSGS chunk (weight.py:122-154 _cpu_packer / gpu_packer.py:48-200):
- * out[giant_count * baby][slots][2] complex; weight [dim][dim] float64 or complex128 (weight_complex = 1) */
+ * out[giant_count * baby][slots][2] complex; weight [dim][dim] float64 (weight_complex = 0), complex128 (1) or
+ * float32 (2, widened exactly) */
 int holmes_pack_diagonals(const double* weight, int weight_complex, int dim, int lanes, int baby, int giant_base,
                           int giant_count, int lane_shift, int slots, double* out, long long row_stride, void* stream);
+/* diagonal rows of one BSGS chunk from a structured weight, replacing the reference's Triton
+ * pack_structured_token_lane_bsgs_weight_chunk_triton_gpu (llama3fhe/operators/linear/gpu_packer.py:201-476;
+ * map semantics llama3fhe/operators/linear/structured_weight.py:52-140): one to three real source matrices (host
+ * array of device pointers, element strides, float32 when source_fp32) and device maps of `dim` entries --
+ * int64 real/imag source and row per physical row, int64 real/imag column per physical column (negative = zero),
+ * float64 real/imag scale per row and column_scale per column; value = source * (row scale * column scale) */
+int holmes_pack_structured(const void* const* sources, const long long* row_strides, const long long* col_strides,
+                           int source_count, int source_fp32, const long long* real_source, const long long* real_row,
+                           const double* real_scale, const long long* imag_source, const long long* imag_row,
+                           const double* imag_scale, const long long* real_column, const long long* imag_column,
+                           const double* column_scale, int dim, int lanes, int baby, int giant_base, int giant_count,
+                           int lane_shift, int slots, double* out, long long row_stride, void* stream);
 
 /* ---- ciphertext arithmetic (fhe.homo_add / homo_sub / homo_mul_pt / homo_mul_i / rescale,
  *      llama3fhe/operators/primitives.py:21-190) */
@@ -144,8 +157,10 @@ int holmes_add_const(void* ctx, const uint64_t* a, const uint64_t* consts, uint6
  * counterpart in the reference.  Scratch comes from a 2 MiB array compiled into the library (held by every
  * GPU that loads it): comps * N must not exceed 4 * 2^16 words (-6 otherwise), and the calling thread's
  * current device must be the context's (-7 otherwise).  The first call on a device looks up the array's
- * device address, so make it before any stream capture.  Calls that overlap on the GPU race on the shared
- * array; nothing needs clearing between calls. */
+ * device address, so make it before any stream capture.  That address is kept for the rest of the process:
+ * it assumes one primary-context lifetime per device, so do not call this after cudaDeviceReset (or any other
+ * teardown and re-creation of the device's primary context) in the same process.  Calls that overlap on the
+ * GPU race on the shared array; nothing needs clearing between calls. */
 int holmes_rescale_noalloc(void* ctx, const uint64_t* in, long long in_stride, uint64_t* out, long long out_stride,
                            int cur, int comps, void* stream);
 
@@ -187,6 +202,13 @@ int holmes_giant_sum(void* ctx, const uint64_t* p0, const uint64_t* p1, long lon
 int holmes_mul_relin(void* ctx, const uint64_t* a0, const uint64_t* a1, const uint64_t* b0, const uint64_t* b1,
                      long long in_item, int cur, int items, const uint64_t* key, int key_cap, uint64_t* out0,
                      uint64_t* out1, long long out_item, uint64_t* scratch, void* stream);
+/* exact scratch words of a composed entry point for `items` ciphertexts at `cur` limbs:
+ * op HOLMES_OP_ROTATE (holmes_rotate, holmes_hoisted_rotations), HOLMES_OP_GIANT_SUM (holmes_giant_sum),
+ * HOLMES_OP_MUL_RELIN (holmes_mul_relin); -4 for an unknown op.  Same sizing rules as the comments above. */
+#define HOLMES_OP_ROTATE 0
+#define HOLMES_OP_GIANT_SUM 1
+#define HOLMES_OP_MUL_RELIN 2
+int holmes_scratch_words(void* ctx, int op, int cur, int items, long long* words);
 /* for `items` ciphertexts sharing one key:
  *   out0 = perm(add0) + ModDown(sum_j perm(digit_j) key_b[j]) + post0
  *   out1 = perm(add1) + ModDown(sum_j perm(digit_j) key_a[j]) + post1

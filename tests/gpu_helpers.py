@@ -7,7 +7,10 @@ import torch
 from oracle.oracle import Oracle, OracleParams
 
 
-def make_pair(log_n=10, limbs=4, dnum=2, dcrt=40, first=50, special=50, K=None, hamming=32, seed=0, scale_bits=None):
+def make_pair(log_n=10, limbs=4, dnum=2, dcrt=40, first=50, special=50, K=None, hamming=32, seed=0, scale_bits=None,
+              key_limits=None):
+    """``key_limits``: rotation -> the largest limb count its key serves (keys trimmed to that many Q limbs, as the
+    reference's key tiers do, ``llama3fhe/parallel/prefill/keys.py:118-140``)."""
     from holmes_b200 import fhe as F
 
     op = OracleParams(log_n=log_n, limbs=limbs, dnum=dnum, dcrt_bits=dcrt, first_mod_bits=first, special_bits=special,
@@ -16,7 +19,7 @@ def make_pair(log_n=10, limbs=4, dnum=2, dcrt=40, first=50, special=50, K=None, 
                              special_bits=special, special_limbs=K, hamming_weight=hamming, seed=seed,
                              scale_bits=scale_bits,
                              secret_key_dist="SPARSE_TERNARY" if hamming else "UNIFORM_TERNARY",
-                             auto_load_keys=False)
+                             auto_load_keys=False, rotation_key_limb_limits=dict(key_limits or {}))
     client, ctx = F.generate_client_context(spec)
     return Oracle(op), client, ctx
 

@@ -424,8 +424,9 @@ def test_linear_operator_bitexact_and_decodes(complex_weight):
 
 
 def test_full_ring_rotation_round_trip_and_linearity():
-    """N = 2^16 with the reference's production primes (59/60-bit, dnum 5 at 13 limbs): rotation by r then -r and
-    conjugation twice return the message; rotation is linear (size-independent properties)."""
+    """N = 2^16 with 59/60-bit primes on a 13-limb chain with dnum 2 (alpha 7, K 7): rotation by r then -r and
+    conjugation twice return the message; rotation is linear (size-independent properties).  The production chain
+    itself (38 limbs, dnum 5, keys trimmed to 13 limbs) is pinned in tests/test_gpu_production_chain.py."""
     from holmes_b200 import fhe as F
 
     o, client, ctx = make_pair(log_n=16, limbs=13, dnum=2, dcrt=59, first=60, special=60, K=7, hamming=192)
@@ -619,5 +620,64 @@ def test_composed_rotate_and_encode_entry_points():
                    out.data_ptr(), cur * N, scratch.data_ptr(), flag.data_ptr(), 0)
             np.testing.assert_array_equal(host(out), host(want.cv[0][:, :cur]))
             assert int(flag.item()) == 0
+    finally:
+        ctx.close()
+
+
+@pytest.mark.parametrize("giants", [1, 2, 4])
+def test_giant_sum_abi_giant_counts_and_mul_relin_distinct(giants):
+    """holmes_giant_sum with an odd and even number of Horner steps (the ping-pong's two parities, and the single-giant
+    copy) against fhe.giant_horner; holmes_mul_relin of two DIFFERENT ciphertext batches against fhe.homo_mul_relin;
+    scratch sized by holmes_scratch_words."""
+    import ctypes
+
+    from holmes_b200 import _lib as L
+    from holmes_b200 import fhe as F
+
+    o, client, ctx = make_pair(log_n=11, limbs=4, dnum=2, dcrt=45, first=55, special=55)
+    try:
+        rng = np.random.default_rng(50 + giants)
+        cur, N, items = 3, ctx.N, 2
+        part = np.stack([np.stack([np.stack([residues(o.pr.q, cur, N, rng) for _ in range(items)])
+                                   for _ in range(giants)]) for _ in range(2)])   # [2][G][items][cur][N]
+        pd = dev(part)
+        g16 = ctx.galois(16)
+        key16, cap16 = ctx.switch_key(g16, cur)
+        words = ctypes.c_longlong()
+        L.call("holmes_scratch_words", ctx.handle, 1, cur, items, ctypes.byref(words))
+        gs = torch.empty(words.value, dtype=torch.uint64, device=ctx.device)
+        gout = torch.empty((2, items, cur, N), dtype=torch.uint64, device=ctx.device)
+        L.call("holmes_giant_sum", ctx.handle, pd[0].data_ptr(), pd[1].data_ptr(), cur * N, items * cur * N, cur, items,
+               giants, key16.data_ptr(), cap16, g16, gout[0].data_ptr(), gout[1].data_ptr(), cur * N, gs.data_ptr(), 0)
+        h0, h1 = F.giant_horner(ctx, pd.clone(), 16)
+        np.testing.assert_array_equal(host(gout[0]), host(h0))
+        np.testing.assert_array_equal(host(gout[1]), host(h1))
+        for i in range(items):
+            w0, w1 = o.giant_horner((part[0, :, i], part[1, :, i]), 16)
+            np.testing.assert_array_equal(host(gout[0, i]), w0)
+            np.testing.assert_array_equal(host(gout[1, i]), w1)
+        # relinearised products a_i * b_i of two different batches
+        a = F.pack_cipher_batch([client.encrypt(rng.normal(size=ctx.max_slots) * 0.5, cur_limbs=cur, counter=90 + i)
+                                 for i in range(items)])
+        b = F.pack_cipher_batch([client.encrypt(rng.normal(size=ctx.max_slots) * 0.5, cur_limbs=cur, counter=95 + i)
+                                 for i in range(items)])
+        assert a.cv[0].stride(0) == b.cv[0].stride(0)
+        rkey, rcap = ctx.switch_key(0, cur)
+        L.call("holmes_scratch_words", ctx.handle, 2, cur, items, ctypes.byref(words))
+        ms = torch.empty(words.value, dtype=torch.uint64, device=ctx.device)
+        mout = torch.empty((2, items, cur, N), dtype=torch.uint64, device=ctx.device)
+        L.call("holmes_mul_relin", ctx.handle, a.cv[0].data_ptr(), a.cv[1].data_ptr(), b.cv[0].data_ptr(),
+               b.cv[1].data_ptr(), int(a.cv[0].stride(0)), cur, items, rkey.data_ptr(), rcap, mout[0].data_ptr(),
+               mout[1].data_ptr(), cur * N, ms.data_ptr(), 0)
+        want = F.homo_mul_relin(a, b, ctx)
+        np.testing.assert_array_equal(host(mout[0]), host(want.cv[0]))
+        np.testing.assert_array_equal(host(mout[1]), host(want.cv[1]))
+        for i in range(items):
+            ra = (host(a.cv[0][i]), host(a.cv[1][i]))
+            rb = (host(b.cv[0][i]), host(b.cv[1][i]))
+            w0, w1 = o.mul_relin(ra, rb)
+            np.testing.assert_array_equal(host(mout[0, i]), w0)
+            np.testing.assert_array_equal(host(mout[1, i]), w1)
+        assert L.load().holmes_scratch_words(ctx.handle, 7, cur, items, ctypes.byref(words)) == -4
     finally:
         ctx.close()
