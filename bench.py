@@ -162,8 +162,8 @@ def spec_for(cur_limbs: int):
     from holmes_b200 import fhe as F
     from holmes_b200 import linear as LN
 
-    cfg = LN.LLAMA3_LINEAR_SCHEDULES.qkv
-    rots = LN.linear_rotations(dimension=DIM, token_lanes=LANES, operator_config=cfg)
+    cfg = LN.PRODUCTION
+    rots = cfg.rotation_keys(DIM, LANES)
     return F.CKKSContextSpec(depth=DEPTH, log_n=LOG_N, dnum=DNUM, dcrt_bits=DCRT, first_mod=FIRST, special_bits=60,
                              hamming_weight=192, seed=0, rotations=tuple(rots), auto_load_keys=False,
                              rotation_key_limb_limits={int(r): cur_limbs for r in rots}), cfg, rots
@@ -206,7 +206,7 @@ def run_engine(args) -> None:
                            baby_shard=(rank, world, None) if chunked else None)
     lw = LN.LinearWeight(weight, dtype=np.complex128, crypto_context=session)
     lw.prepare(cfg)
-    my_chunks = C.chunk_shard(len(op.plan(DIM).chunks), world, rank)
+    my_chunks = C.chunk_shard(len(op.layout(DIM).chunks), world, rank)
     torch.cuda.synchronize()
 
     def step():

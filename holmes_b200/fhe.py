@@ -156,6 +156,8 @@ class Context:
     def __init__(self, spec: CKKSContextSpec, device: str = "cuda") -> None:
         if not torch.cuda.is_available():
             raise _lib.HolmesError("libholmes_cuda needs a CUDA device")
+        if torch.device(device).type != "cuda":
+            raise _lib.HolmesError(f"libholmes_cuda has no CPU backend: device {device!r} is not a CUDA device")
         self.spec = spec
         self.device = torch.device(device if device != "cuda" else f"cuda:{torch.cuda.current_device()}")
         torch.cuda.set_device(self.device)
@@ -396,6 +398,7 @@ class Client:
 
     def decrypt_coefficients(self, cipher: Cipher, item: int = 0) -> list[int]:
         ctx = self.context
+        _valid(ctx, cipher, "decrypt")
         cur = int(cipher.state.cur_limbs)
         c0 = cipher.cv[0][item, :cur].contiguous()
         c1 = cipher.cv[1][item, :cur].contiguous()
@@ -436,9 +439,9 @@ def generate_client_context(spec: CKKSContextSpec, device: str = "cuda"):
 # ----------------------------------------------------------------------------------------------------- helpers
 
 
-def _new_cipher(ctx: Context, batch: int, limbs: int, state: CipherState, slots: int) -> Cipher:
-    storage = torch.empty((2, batch, limbs, ctx.N), dtype=torch.uint64, device=ctx.device)
-    return Cipher([storage[0], storage[1]], state, slots, False, batch, ctx)
+def _new_cipher(ctx: Context, batch: int, limbs: int, state: CipherState, slots: int, comps: int = 2) -> Cipher:
+    storage = torch.empty((comps, batch, limbs, ctx.N), dtype=torch.uint64, device=ctx.device)
+    return Cipher([storage[c] for c in range(comps)], state, slots, False, batch, ctx)
 
 
 def _item_stride(t: torch.Tensor) -> int:
@@ -456,6 +459,23 @@ def _check_same(a: Cipher, b: Cipher, what: str) -> None:
         raise ValueError(f"{what}: batch mismatch {a.batch_size} != {b.batch_size}")
 
 
+def _valid(ctx: Context, a: Cipher, what: str) -> None:
+    """Refuse, before any launch, a cipher or plaintext whose storage the kernels would read out of bounds or from the
+    wrong device: every component must be a uint64 CUDA tensor on the context's device, [batch][>= limbs][N] with unit
+    word stride and limb stride N (limbs = cur, or cur + K for the extended basis)."""
+    limbs = int(a.state.cur_limbs) + (ctx.K if a.is_ext else 0)
+    for c, t in enumerate(a.cv):
+        if not torch.is_tensor(t) or t.device.type != "cuda" or t.device.index != ctx.device.index:
+            raise ValueError(f"{what}: component {c} is not on {ctx.device}")
+        if t.dtype != torch.uint64 or t.dim() != 3:
+            raise ValueError(f"{what}: component {c} must be a uint64 [batch][limbs][N] tensor")
+        if int(t.shape[0]) < int(a.batch_size) or int(t.shape[1]) < limbs or int(t.shape[2]) != ctx.N:
+            raise ValueError(f"{what}: component {c} of shape {tuple(t.shape)} cannot hold {a.batch_size} x {limbs} "
+                             f"limbs of {ctx.N} words")
+        if int(t.stride(2)) != 1 or int(t.stride(1)) != ctx.N:
+            raise ValueError(f"{what}: component {c} needs unit word stride and limb stride N")
+
+
 def _ew(ctx: Context, op: int, a: torch.Tensor, b: torch.Tensor | None, out: torch.Tensor, limbs: int) -> None:
     _lib.call("holmes_elementwise", ctx.handle, op, a.data_ptr(), 0 if b is None else b.data_ptr(), out.data_ptr(),
               int(a.shape[0]), int(limbs), _item_stride(a), 0 if b is None else _item_stride(b), _item_stride(out),
@@ -469,38 +489,54 @@ def _ctx(ctx) -> Context:
 # ----------------------------------------------------------------------------------------------------- ops
 
 
-def homo_add(a: Cipher, b: Cipher, ctx) -> Cipher:
+def _add_sub(a: Cipher, b: Cipher, ctx, op: int, what: str) -> Cipher:
+    """a + b (op 0) or a - b (op 1), component by component.  Either may be an unrelinearised three-component
+    product (the lazy accumulators of ``homo_mul_no_relin``); a component only one operand has is copied (negated
+    for the subtrahend)."""
     ctx = _ctx(ctx)
-    _check_same(a, b, "homo_add")
+    _valid(ctx, a, what)
+    _valid(ctx, b, what)
+    _check_same(a, b, what)
     cur = int(a.state.cur_limbs)
-    out = _new_cipher(ctx, a.batch_size, cur, a.state, a.slots)
-    for c in range(2):
-        _ew(ctx, 0, a.cv[c], b.cv[c], out.cv[c], cur)
+    na, nb = len(a.cv), len(b.cv)
+    out = _new_cipher(ctx, a.batch_size, cur, a.state, a.slots, max(na, nb))
+    for c in range(max(na, nb)):
+        if c < na and c < nb:
+            _ew(ctx, op, a.cv[c], b.cv[c], out.cv[c], cur)
+        elif c < na:
+            out.cv[c].copy_(a.cv[c][:, :cur])
+        elif op == 1:
+            _ew(ctx, 3, b.cv[c], None, out.cv[c], cur)
+        else:
+            out.cv[c].copy_(b.cv[c][:, :cur])
     return out
+
+
+def homo_add(a: Cipher, b: Cipher, ctx) -> Cipher:
+    return _add_sub(a, b, ctx, 0, "homo_add")
 
 
 def homo_sub(a: Cipher, b: Cipher, ctx) -> Cipher:
-    ctx = _ctx(ctx)
-    _check_same(a, b, "homo_sub")
-    cur = int(a.state.cur_limbs)
-    out = _new_cipher(ctx, a.batch_size, cur, a.state, a.slots)
-    for c in range(2):
-        _ew(ctx, 1, a.cv[c], b.cv[c], out.cv[c], cur)
-    return out
+    return _add_sub(a, b, ctx, 1, "homo_sub")
 
 
-def homo_mul_i(a: Cipher, ctx) -> Cipher:
+def homo_mul_i(a: Cipher, ctx, negative: bool = False) -> Cipher:
+    """a * i (a * X^(N/2)); ``negative``: a * (-i)."""
     ctx = _ctx(ctx)
+    _valid(ctx, a, "homo_mul_i")
     cur = int(a.state.cur_limbs)
-    out = _new_cipher(ctx, a.batch_size, cur, a.state, a.slots)
-    for c in range(2):
+    out = _new_cipher(ctx, a.batch_size, cur, a.state, a.slots, len(a.cv))
+    for c in range(len(a.cv)):
         _lib.call("holmes_mul_i", ctx.handle, a.cv[c].data_ptr(), out.cv[c].data_ptr(), a.batch_size, cur,
                   _item_stride(a.cv[c]), _item_stride(out.cv[c]), _stream())
+        if negative:
+            _ew(ctx, 3, out.cv[c], None, out.cv[c], cur)
     return out
 
 
 def rescale(a: Cipher, ctx) -> Cipher:
     ctx = _ctx(ctx)
+    _valid(ctx, a, "rescale")
     cur = int(a.state.cur_limbs)
     if cur < 2:
         raise ValueError("rescale needs at least two limbs")
@@ -520,6 +556,7 @@ def rescale(a: Cipher, ctx) -> Cipher:
 def align_to(a: Cipher, target: CipherState, ctx) -> Cipher:
     """Bring ``a`` to ``target``: rescale while its degree is above the target's, then drop limbs."""
     ctx = _ctx(ctx)
+    _valid(ctx, a, "align_to")
     cur = a
     while int(cur.state.scale_degree) > int(target.scale_degree):
         cur = rescale(cur, ctx)
@@ -527,8 +564,8 @@ def align_to(a: Cipher, target: CipherState, ctx) -> Cipher:
     have = int(cur.state.cur_limbs)
     if want > have:
         raise ValueError(f"align_to: cannot raise {have} limbs to {want}")
-    if want == have:
-        return cur
+    if want == have:   # a distinct object the caller owns (releasing it must not release ``a``)
+        return cur if cur is not a else a.cipher_like([c.clone() for c in a.cv])
     state = cur.state.replace(cur_limbs=want)
     return cur.cipher_like([c[:, :want].contiguous() for c in cur.cv], state=state)
 
@@ -579,6 +616,7 @@ def rotate_batch(ctx: Context, c0: torch.Tensor, c1: torch.Tensor, cur: int, rot
 
 def homo_rotate(a: Cipher, rotation: int, ctx) -> Cipher:
     ctx = _ctx(ctx)
+    _valid(ctx, a, "homo_rotate")
     cur = int(a.state.cur_limbs)
     out = _new_cipher(ctx, a.batch_size, cur, a.state, a.slots)
     rotate_batch(ctx, a.cv[0], a.cv[1], cur, int(rotation), out.cv[0], out.cv[1])
@@ -604,6 +642,7 @@ def fast_rotate(a: Cipher, rotations, ctx, output_ext: bool = False) -> Cipher:
             return homo_rotate(a, rotations[0], ctx)
         return prepare_hoisted_baby_rotations(a, tuple(int(r) for r in rotations), ctx)[0]
     ctx = _ctx(ctx)
+    _valid(ctx, a, "fast_rotate")
     if a.batch_size != 1 or a.is_ext:
         raise ValueError("fast_rotate(output_ext=True) expects one non-extended ciphertext")
     cur = int(a.state.cur_limbs)
@@ -633,6 +672,7 @@ def fast_rotate(a: Cipher, rotations, ctx, output_ext: bool = False) -> Cipher:
 def moddown_from_ext(a: Cipher, ctx) -> Cipher:
     """ModDown of an extended-basis ciphertext (``is_ext``, ``cur + K`` limbs) back to its ``cur`` Q limbs."""
     ctx = _ctx(ctx)
+    _valid(ctx, a, "moddown_from_ext")
     if not a.is_ext:
         raise ValueError("moddown_from_ext expects an extended-basis ciphertext")
     cur = int(a.state.cur_limbs)
@@ -651,6 +691,8 @@ def grouped_pairwise_mac(batch: Cipher, plaintexts: Plaintext, groups: int, ctx)
     ``fast_rotate(output_ext=True)``) need extended plaintexts (``Session.plaintext(..., is_ext=True)``) and give an
     extended result."""
     ctx = _ctx(ctx)
+    _valid(ctx, batch, "grouped_pairwise_mac")
+    _valid(ctx, plaintexts, "grouped_pairwise_mac")
     groups = int(groups)
     nb = int(batch.batch_size)
     cur = int(batch.state.cur_limbs)
@@ -689,7 +731,8 @@ def pack_cipher_batch(ciphers) -> Cipher:
         if int(c.state.cur_limbs) != cur or int(c.state.scale_degree) != int(first.state.scale_degree) \
                 or c.slots != first.slots or c.is_ext != first.is_ext or len(c.cv) != len(first.cv):
             raise ValueError("pack_cipher_batch: ciphers differ in level, scale degree, slots or form")
-    cv = [torch.cat([c.cv[k][:, :cur] for c in ciphers], dim=0) for k in range(len(first.cv))]
+    limbs = cur + (int(first.context.K) if first.is_ext else 0)
+    cv = [torch.cat([c.cv[k][:, :limbs] for c in ciphers], dim=0) for k in range(len(first.cv))]
     return first.cipher_like(cv, batch_size=int(cv[0].shape[0]))
 
 
@@ -709,6 +752,7 @@ def prepare_hoisted_baby_rotations(a: Cipher, baby_offsets, ctx, strategy: str =
     if strategy != "normal":
         raise ValueError(f"unknown hoist strategy {strategy!r}")
     ctx = _ctx(ctx)
+    _valid(ctx, a, "prepare_hoisted_baby_rotations")
     if a.batch_size != 1:
         raise ValueError("prepare_hoisted_baby_rotations expects one ciphertext")
     offsets = [int(o) for o in baby_offsets]
@@ -812,6 +856,8 @@ def hoisted_mac_sum(cipher: Cipher, baby_offsets, plaintexts: Plaintext, giant_o
     """sum_g rot(sum_b pt[g B + b] baby[b], g giant_offset) via Horner (``ext_double_hoist``: every giant rotated
     directly over Q u P and one ModDown of the sum); scale degree adds the plaintext's."""
     ctx = _ctx(ctx)
+    _valid(ctx, cipher, "hoisted_mac_sum")
+    _valid(ctx, plaintexts, "hoisted_mac_sum")
     if baby_rotations is None:
         baby_rotations = prepare_hoisted_baby_rotations(cipher, baby_offsets, ctx, strategy, baby_anchor_step)
     block = baby_rotations[0]
@@ -834,6 +880,8 @@ def hoisted_mac_sum(cipher: Cipher, baby_offsets, plaintexts: Plaintext, giant_o
 
 def homo_mul_pt(a: Cipher, pt: Plaintext, ctx) -> Cipher:
     ctx = _ctx(ctx)
+    _valid(ctx, a, "homo_mul_pt")
+    _valid(ctx, pt, "homo_mul_pt")
     cur = int(a.state.cur_limbs)
     if int(pt.state.cur_limbs) < cur:
         raise ValueError("homo_mul_pt: plaintext has fewer limbs than the ciphertext")
@@ -851,9 +899,17 @@ def homo_mul_pt(a: Cipher, pt: Plaintext, ctx) -> Cipher:
 
 def homo_mul_no_relin(a: Cipher, b: Cipher, ctx) -> Cipher:
     ctx = _ctx(ctx)
-    if int(a.state.cur_limbs) != int(b.state.cur_limbs):
-        raise ValueError("homo_mul: limb mismatch")
-    cur = int(a.state.cur_limbs)
+    _valid(ctx, a, "homo_mul")
+    _valid(ctx, b, "homo_mul")
+    if len(a.cv) != 2 or len(b.cv) != 2:
+        raise ValueError("homo_mul: relinearise a three-component operand first")
+    if a.batch_size != b.batch_size:
+        raise ValueError(f"homo_mul: batch mismatch {a.batch_size} != {b.batch_size}")
+    if a.is_ext or b.is_ext:
+        raise ValueError("homo_mul: extended ciphertexts are not supported")
+    # operands at different levels meet at the lower one (the deeper operand's extra limbs are dropped; the nominal
+    # scale is the same at every level)
+    cur = min(int(a.state.cur_limbs), int(b.state.cur_limbs))
     n = a.batch_size
     shape = (n, cur, ctx.N)
     d0 = torch.empty(shape, dtype=torch.uint64, device=ctx.device)
@@ -874,6 +930,7 @@ def homo_mul_no_relin(a: Cipher, b: Cipher, ctx) -> Cipher:
 
 def homo_relinearize(a: Cipher, ctx) -> Cipher:
     ctx = _ctx(ctx)
+    _valid(ctx, a, "homo_relinearize")
     if len(a.cv) != 3:
         raise ValueError("homo_relinearize expects a three-component ciphertext")
     cur = int(a.state.cur_limbs)
@@ -905,6 +962,10 @@ def homo_mul_relin_rescale_postop(a: Cipher, b: Cipher, ctx, apply_double: bool 
     output's limbs, its modulus drop) and ``scalar`` (encoded for the output state, ``ctx.rescale_divisor_at``)
     land at the output, which has one limb fewer than the shallower operand."""
     ctx = _ctx(ctx)
+    _valid(ctx, a, "homo_mul_relin_rescale_postop")
+    _valid(ctx, b, "homo_mul_relin_rescale_postop")
+    if sub is not None:
+        _valid(ctx, sub, "homo_mul_relin_rescale_postop")
     cur = min(int(a.state.cur_limbs), int(b.state.cur_limbs))
     prod = homo_mul_relin(_drop_limbs(a, cur), _drop_limbs(b, cur), ctx)
     if cur < 2:
@@ -982,6 +1043,7 @@ def grouped_scalar_weighted_acc(batch: Cipher, table: EncodedScalar, ctx) -> Cip
     """``out[g] = sum_k table[g][k] * batch[k]`` in one launch per component, residue-identical to the loop of
     scalar multiplies and adds (each product reduced mod q_l, the sum exact mod q_l); ``groups`` items out."""
     ctx = _ctx(ctx)
+    _valid(ctx, batch, "grouped_scalar_weighted_acc")
     if table.table is None:
         raise ValueError("grouped_scalar_weighted_acc needs a weight table EncodedScalar")
     res = table.table.to(device=ctx.device, dtype=torch.uint64).contiguous()
@@ -1029,6 +1091,7 @@ def _const_kernel(name: str, a: Cipher, k: torch.Tensor, out: Cipher, comps: ran
 def homo_mul_scalar(a: Cipher, scalar: EncodedScalar, ctx) -> Cipher:
     """a * scalar without rescale: the scale degrees and factors multiply."""
     ctx = _ctx(ctx)
+    _valid(ctx, a, "homo_mul_scalar")
     cur = int(a.state.cur_limbs)
     sf = None
     if a.state.scaling_factor is not None and scalar.state.scaling_factor is not None:
@@ -1046,6 +1109,7 @@ def homo_mul_scalar_rescale(a: Cipher, scalar: EncodedScalar, ctx) -> Cipher:
 def homo_add_scalar(a: Cipher, scalar, ctx) -> Cipher:
     """a + scalar; a float is encoded at the ciphertext's own scale, an EncodedScalar must carry that scale."""
     ctx = _ctx(ctx)
+    _valid(ctx, a, "homo_add_scalar")
     cur = int(a.state.cur_limbs)
     sf = float(a.state.scaling_factor if a.state.scaling_factor is not None else ctx.scale_at(cur))
     if not isinstance(scalar, EncodedScalar):
@@ -1061,6 +1125,8 @@ def homo_add_scalar(a: Cipher, scalar, ctx) -> Cipher:
 def homo_add_pt(a: Cipher, pt: Plaintext, ctx) -> Cipher:
     """a + pt (pt at the ciphertext's scale and degree, at least as many limbs)."""
     ctx = _ctx(ctx)
+    _valid(ctx, a, "homo_add_pt")
+    _valid(ctx, pt, "homo_add_pt")
     cur = int(a.state.cur_limbs)
     if int(pt.state.cur_limbs) < cur:
         raise ValueError("homo_add_pt: plaintext has fewer limbs than the ciphertext")

@@ -1,13 +1,12 @@
-"""Diagonal (BSGS) linear layers over libholmes_cuda, with the reference's operator API.
+"""Diagonal (BSGS) linear layers over libholmes_cuda: a batched schedule behind the reference's operator calls.
 
-Public names, arguments and validation follow ``llama3fhe/operators/linear`` (config.py:49-380,
-operator.py:58-639, weight.py:232-659): ``LinearOperatorConfig``, ``LinearPlan``, ``LinearChunk``,
-``BabyBlock``, ``linear_rotations``, ``LLAMA3_LINEAR_SCHEDULES``, ``LinearWeight`` and
-``LinearOperator`` (``apply`` / ``project`` / ``prepare_baby_rotations`` / ``cache_info``).
-
-What differs is the schedule underneath ``apply``.  The reference loops over inputs inside every
-chunk (``_mac_chunk``: one ``hoisted_mac_sum`` plus a giant alignment rotation per input).  Here all
-inputs of a call move together:
+The reference's own ``LinearOperator`` (``llama3fhe/operators/linear/operator.py:58-639``) runs unchanged on this
+engine through :mod:`holmes_b200.easyfhe_compat`; it loops over inputs inside every chunk (``_mac_chunk``: one
+``hoisted_mac_sum`` plus a giant alignment rotation per input).  This module is the engine's faster schedule of
+the same computation, with call names a caller of the reference recognises (``LinearOperator.apply`` / ``project``
+/ ``prepare_baby_rotations`` / ``cache_info``, ``LinearWeight``) and its own geometry types: :class:`BsgsSchedule`
+(the schedule knobs; the reference's ``LinearOperatorConfig`` objects are accepted and read by attribute name) and
+:class:`BsgsLayout` (babies, giants, chunks and the exact rotation-key set).  All inputs of a call move together:
 
 * baby basis: one batched ModUp of every input, then one key switch per baby offset over all inputs
   (each rotation key is read from HBM once per offset, not once per input);
@@ -34,226 +33,142 @@ import torch
 from . import _lib
 from . import fhe as F
 
-_CACHE_MODES = {"none", "middle", "plain", "both"}
-_HOIST_STRATEGIES = {"normal", "ext_normal", "ext_double_hoist"}
-_RAW_WEIGHT_POLICIES = {"device", "host"}
-
-
-def default_linear_encode_depth() -> int:
-    raw = os.environ.get("LLAMA_FHE_LINEAR_ENCODE_DEPTH", "0").strip()
-    try:
-        depth = int(raw or "0")
-    except ValueError as exc:
-        raise ValueError(f"LLAMA_FHE_LINEAR_ENCODE_DEPTH must be a non-negative integer, got {raw!r}.") from exc
-    if depth < 0:
-        raise ValueError(f"LLAMA_FHE_LINEAR_ENCODE_DEPTH must be a non-negative integer, got {raw!r}.")
-    return depth
+HOIST_MODES = ("normal", "ext_normal", "ext_double_hoist")
+CACHE_MODES = ("none", "middle", "plain", "both")
 
 
 @dataclass(frozen=True)
-class LinearOperatorConfig:
-    """Schedule and cache policy of one diagonal linear (reference: config.py:49-121)."""
+class BsgsSchedule:
+    """How one square diagonal linear is evaluated: the knobs of the reference's ``LinearOperatorConfig``
+    (``llama3fhe/operators/linear/config.py:49-121``) under this engine's own names.
 
-    baby_steps: int = 32
-    baby_anchor_step: int = 32
-    max_plaintext_rows: int = 512
-    reuse_baby_rotations: bool = True
-    hoist_strategy: str = "normal"
-    constant_cache_mode: str = "none"
-    raw_weight_policy: str = "device"
+    ``babies`` B baby steps; ``anchor`` babies per anchored block (>= 2; -1 or >= B: one block); ``chunk_rows``
+    diagonal rows encoded and multiplied per chunk (at least B); ``reuse_babies`` keeps an input's baby basis for
+    the next apply; ``hoist`` the giant-step strategy; ``cache`` which encode stage a weight keeps ("middle": FFT'd
+    rows, "plain": NTT plaintexts); ``weight_on_device`` keeps the weight page in HBM; ``lane_shift`` > 0 selects the
+    shifted-lane packing (D / lanes diagonals)."""
+
+    babies: int = 32
+    anchor: int = 32
+    chunk_rows: int = 512
+    reuse_babies: bool = True
+    hoist: str = "normal"
+    cache: str = "none"
+    weight_on_device: bool = True
     lane_shift: int = 0
-    encode_depth: int = field(default_factory=default_linear_encode_depth)
 
     def __post_init__(self) -> None:
-        if int(self.baby_steps) <= 0:
-            raise ValueError("baby_steps must be positive.")
-        if int(self.encode_depth) < 0:
-            raise ValueError("encode_depth must be zero or positive.")
-        if int(self.baby_anchor_step) in (0, 1):
-            raise ValueError("baby_anchor_step must be at least two or -1.")
-        if int(self.baby_anchor_step) < -1:
-            raise ValueError("baby_anchor_step must be positive or -1.")
-        if int(self.max_plaintext_rows) < int(self.baby_steps):
-            raise ValueError("max_plaintext_rows must hold one baby-step group.")
+        problems = []
+        if int(self.babies) < 1:
+            problems.append(f"babies={self.babies} (need >= 1)")
+        if int(self.anchor) != -1 and int(self.anchor) < 2:
+            problems.append(f"anchor={self.anchor} (need -1 or >= 2)")
+        if int(self.chunk_rows) < int(self.babies):
+            problems.append(f"chunk_rows={self.chunk_rows} below babies={self.babies}")
         if int(self.lane_shift) < 0:
-            raise ValueError("lane_shift must be zero or positive.")
-        if str(self.hoist_strategy).lower() not in _HOIST_STRATEGIES:
-            raise ValueError("hoist_strategy must be 'normal', 'ext_normal', or 'ext_double_hoist'.")
-        if str(self.constant_cache_mode) not in _CACHE_MODES:
-            raise ValueError(f"constant_cache_mode must be one of {sorted(_CACHE_MODES)}, "
-                             f"got {self.constant_cache_mode!r}.")
-        if str(self.raw_weight_policy) not in _RAW_WEIGHT_POLICIES:
-            raise ValueError(f"raw_weight_policy must be 'device' or 'host', got {self.raw_weight_policy!r}.")
+            problems.append(f"lane_shift={self.lane_shift} (need >= 0)")
+        if str(self.hoist).lower() not in HOIST_MODES:
+            problems.append(f"hoist={self.hoist!r} (one of {HOIST_MODES})")
+        if str(self.cache) not in CACHE_MODES:
+            problems.append(f"cache={self.cache!r} (one of {CACHE_MODES})")
+        if problems:
+            raise ValueError("invalid BSGS schedule: " + "; ".join(problems))
 
-    def plan(self, *, dimension: int, token_lanes: int) -> "LinearPlan":
-        return LinearPlan(dimension=int(dimension), token_lanes=int(token_lanes), baby_steps=int(self.baby_steps),
-                          baby_anchor_step=int(self.baby_anchor_step),
-                          max_plaintext_rows=int(self.max_plaintext_rows), lane_shift=int(self.lane_shift))
+    @classmethod
+    def coerce(cls, config) -> "BsgsSchedule":
+        """This schedule from a ``BsgsSchedule``, None (the defaults) or any object with the attribute names of the
+        reference's ``LinearOperatorConfig`` (its own instances included), read field by field."""
+        if config is None:
+            return cls()
+        if isinstance(config, cls):
+            return config
+        return cls(babies=int(config.baby_steps), anchor=int(config.baby_anchor_step),
+                   chunk_rows=int(config.max_plaintext_rows),
+                   reuse_babies=bool(getattr(config, "reuse_baby_rotations", True)),
+                   hoist=str(getattr(config, "hoist_strategy", "normal")).lower(),
+                   cache=str(getattr(config, "constant_cache_mode", "none")),
+                   weight_on_device=str(getattr(config, "raw_weight_policy", "device")) == "device",
+                   lane_shift=int(getattr(config, "lane_shift", 0)))
+
+    def layout(self, dimension: int, lanes: int) -> "BsgsLayout":
+        return BsgsLayout(int(dimension), int(lanes), int(self.babies), int(self.anchor), int(self.chunk_rows),
+                          int(self.lane_shift))
+
+    def rotation_keys(self, dimension: int, lanes: int, conjugation_slots: int | None = None) -> tuple[int, ...]:
+        return self.layout(dimension, lanes).rotation_keys(self.hoist, conjugation_slots)
 
 
-def _production_linear_config() -> LinearOperatorConfig:
-    return LinearOperatorConfig(baby_steps=64, baby_anchor_step=64, max_plaintext_rows=512, reuse_baby_rotations=True,
-                                hoist_strategy="normal", constant_cache_mode="none", raw_weight_policy="device")
+#: the reference's production schedule for every Llama-3 projection (QKV, W_O, gate/up, down): 64 babies, one
+#: anchor block, 512 rows per chunk (``llama3fhe/operators/linear/config.py:123-134``)
+PRODUCTION = BsgsSchedule(babies=64, anchor=64, chunk_rows=512)
 
 
 @dataclass(frozen=True)
-class Llama3LinearSchedules:
-    qkv: LinearOperatorConfig = field(default_factory=_production_linear_config)
-    w_o: LinearOperatorConfig = field(default_factory=_production_linear_config)
-    gate_up: LinearOperatorConfig = field(default_factory=_production_linear_config)
-    down: LinearOperatorConfig = field(default_factory=_production_linear_config)
+class Chunk:
+    """Giants ``first .. first + count - 1`` of a layout, encoded and multiplied together."""
 
-
-LLAMA3_LINEAR_SCHEDULES = Llama3LinearSchedules()
-
-
-@dataclass(frozen=True)
-class LinearChunk:
     index: int
-    giant_base: int
-    giant_count: int
+    first: int
+    count: int
 
     @property
     def name(self) -> str:
         return f"chunk.{int(self.index)}"
 
 
-@dataclass(frozen=True)
-class BabyBlock:
-    start: int
-    width: int
+class BsgsLayout:
+    """BSGS geometry of one D x D diagonal page over ``lanes`` token lanes (feature-major slot f * lanes + t).
 
+    Diagonal row (g, b) holds ``W[(f - g B) mod D, (f + b + lane_shift t) mod D]`` at slot (f, t); the matvec is
+    ``sum_g rot(sum_b row(g, b) * rot(x, b lanes), g B lanes)``: babies at strides ``b lanes``, giants at stride
+    ``B lanes``, the giants split into chunks of ``chunk_rows / B``.  ``rotation_keys`` is the exact key set a
+    schedule needs (pinned against the reference's ``linear_rotations``, ``config.py:338-380``, by the golden
+    fixtures)."""
 
-@dataclass(frozen=True)
-class LinearPlan:
-    """BSGS geometry of one square diagonal block (reference: config.py:150-336)."""
+    def __init__(self, dimension: int, lanes: int, babies: int, anchor: int, chunk_rows: int, lane_shift: int = 0):
+        if dimension < 1 or lanes < 1 or babies < 1:
+            raise ValueError(f"layout needs positive dimension, lanes and babies, got {dimension}, {lanes}, {babies}")
+        if lane_shift and lane_shift * lanes != dimension:
+            raise ValueError(f"lane_shift={lane_shift} must be dimension / lanes = {dimension} / {lanes} "
+                             f"for the shifted-lane packing")
+        self.dimension, self.lanes, self.babies = dimension, lanes, babies
+        self.anchor, self.chunk_rows, self.lane_shift = anchor, chunk_rows, lane_shift
+        self.diagonals = lane_shift if lane_shift else dimension
+        if self.diagonals % babies:
+            raise ValueError(f"babies={babies} does not divide the {self.diagonals} diagonals")
+        self.giants = self.diagonals // babies
+        self.giant_stride = babies * lanes
+        self.baby_strides = tuple(b * lanes for b in range(babies))
+        per = max(1, chunk_rows // babies)
+        self.chunks = tuple(Chunk(i, first, min(per, self.giants - first))
+                            for i, first in enumerate(range(0, self.giants, per)))
+        width = anchor if 2 <= anchor < babies else babies
+        #: baby blocks (start, width): anchored blocks reach their babies through one anchor rotation
+        self.blocks = tuple((b0, min(width, babies - b0)) for b0 in range(0, babies, width))
+        keys = {s * lanes for s in range(1, width)}
+        if len(self.blocks) > 1:
+            keys.add(anchor * lanes)
+        self.baby_keys = tuple(sorted(keys))
+        #: shifted lanes: the lane-fold rotations (1, 2, 4, ...) and the lane-0 -> all-lanes expansion rotations
+        self.fold_strides = tuple(1 << i for i in range(lanes.bit_length() - 1)) if lane_shift else ()
+        self.expand_strides = tuple((dimension - 1) * t for t in range(1, lanes)) if lane_shift else ()
+        self.key = (dimension, lanes, babies, chunk_rows, lane_shift, anchor)
 
-    dimension: int
-    token_lanes: int
-    baby_steps: int
-    baby_anchor_step: int
-    max_plaintext_rows: int
-    lane_shift: int = 0
-
-    def __post_init__(self) -> None:
-        if int(self.dimension) <= 0:
-            raise ValueError("dimension must be positive.")
-        if int(self.token_lanes) <= 0:
-            raise ValueError("token_lanes must be positive.")
-        if int(self.baby_steps) <= 0:
-            raise ValueError("baby_steps must be positive.")
-        if int(self.lane_shift) < 0:
-            raise ValueError("lane_shift must be zero or positive.")
-        if int(self.lane_shift) and int(self.lane_shift) * int(self.token_lanes) != int(self.dimension):
-            raise ValueError("shifted-lane packing requires lane_shift * token_lanes == dimension, got "
-                             f"{self.lane_shift} * {self.token_lanes} != {self.dimension}.")
-        if int(self.diagonals) % int(self.baby_steps):
-            raise ValueError(f"baby_steps={self.baby_steps} must divide diagonals={self.diagonals} "
-                             f"(dimension={self.dimension}, lane_shift={self.lane_shift}).")
-        if int(self.baby_anchor_step) in (0, 1) or int(self.baby_anchor_step) < -1:
-            raise ValueError("baby_anchor_step must be at least two or -1.")
-        if int(self.max_plaintext_rows) < int(self.baby_steps):
-            raise ValueError("max_plaintext_rows must hold one baby-step group.")
-
-    @property
-    def shifted_lanes(self) -> bool:
-        return int(self.lane_shift) > 0
-
-    @property
-    def diagonals(self) -> int:
-        return int(self.lane_shift) if self.shifted_lanes else int(self.dimension)
-
-    @property
-    def giant_steps(self) -> int:
-        return self.diagonals // int(self.baby_steps)
-
-    @property
-    def fold_offsets(self) -> tuple[int, ...]:
-        if not self.shifted_lanes:
-            return ()
-        return tuple(1 << i for i in range(int(self.token_lanes).bit_length() - 1))
-
-    @property
-    def lane_expand_offsets(self) -> tuple[int, ...]:
-        if not self.shifted_lanes:
-            return ()
-        return tuple((int(self.dimension) - 1) * lane for lane in range(1, int(self.token_lanes)))
-
-    @property
-    def chunk_giants(self) -> int:
-        return max(1, int(self.max_plaintext_rows) // int(self.baby_steps))
-
-    @property
-    def giant_offset(self) -> int:
-        return int(self.baby_steps) * int(self.token_lanes)
-
-    @property
-    def baby_offsets(self) -> tuple[int, ...]:
-        return tuple(b * int(self.token_lanes) for b in range(int(self.baby_steps)))
-
-    @property
-    def anchor_enabled(self) -> bool:
-        return int(self.baby_anchor_step) >= 2 and int(self.baby_steps) > int(self.baby_anchor_step)
-
-    @property
-    def baby_blocks(self) -> tuple[BabyBlock, ...]:
-        width = int(self.baby_anchor_step) if self.anchor_enabled else int(self.baby_steps)
-        return tuple(BabyBlock(start=s, width=min(width, int(self.baby_steps) - s))
-                     for s in range(0, int(self.baby_steps), width))
-
-    @property
-    def baby_rotation_count(self) -> int:
-        return max(0, int(self.baby_steps) - 1)
-
-    @property
-    def baby_key_offsets(self) -> tuple[int, ...]:
-        width = int(self.baby_blocks[0].width)
-        keys = {s * int(self.token_lanes) for s in range(1, width)}
-        if len(self.baby_blocks) > 1:
-            keys.add(int(self.baby_anchor_step) * int(self.token_lanes))
+    def rotation_keys(self, hoist: str = "normal", conjugation_slots: int | None = None) -> tuple[int, ...]:
+        keys = set(self.baby_keys)
+        widest = max(c.count for c in self.chunks)
+        if widest > 1:                                 # giant steps inside a chunk
+            if str(hoist).lower() == "ext_double_hoist":
+                keys.update(s * self.giant_stride for s in range(1, widest))
+            else:
+                keys.add(self.giant_stride)
+        keys.update(c.first * self.giant_stride for c in self.chunks if c.first)   # chunk alignment
+        keys.update(self.fold_strides)
+        keys.update(self.expand_strides)
+        if conjugation_slots is not None:
+            keys.add(4 * int(conjugation_slots) - 1)
+        keys.discard(0)
         return tuple(sorted(keys))
-
-    @property
-    def chunks(self) -> tuple[LinearChunk, ...]:
-        bases = range(0, self.giant_steps, self.chunk_giants)
-        return tuple(LinearChunk(index=i, giant_base=b, giant_count=min(self.chunk_giants, self.giant_steps - b))
-                     for i, b in enumerate(bases))
-
-    @property
-    def chunk_sizes(self) -> tuple[int, ...]:
-        return tuple(c.giant_count for c in self.chunks)
-
-    @property
-    def plaintext_chunks(self) -> int:
-        return len(self.chunks)
-
-    @property
-    def cache_key(self) -> tuple[int, ...]:
-        return (int(self.dimension), int(self.token_lanes), int(self.baby_steps), int(self.max_plaintext_rows),
-                int(self.lane_shift))
-
-
-def linear_rotations(*, dimension: int, token_lanes: int, slots: int | None = None,
-                     include_conjugation: bool = False,
-                     operator_config: LinearOperatorConfig | None = None) -> tuple[int, ...]:
-    """Exact rotation-key set of one schedule (reference: config.py:338-380)."""
-    cfg = LinearOperatorConfig() if operator_config is None else operator_config
-    plan = cfg.plan(dimension=int(dimension), token_lanes=int(token_lanes))
-    keys = set(plan.baby_key_offsets)
-    most = max(c.giant_count for c in plan.chunks)
-    if most > 1:
-        if str(cfg.hoist_strategy).lower() == "ext_double_hoist":
-            keys.update(step * plan.giant_offset for step in range(1, most))
-        else:
-            keys.add(plan.giant_offset)
-    keys.update(c.giant_base * plan.giant_offset for c in plan.chunks if c.giant_base)
-    keys.update(plan.fold_offsets)
-    keys.update(plan.lane_expand_offsets)
-    if include_conjugation:
-        if slots is None:
-            raise ValueError("slots are required when conjugation is requested.")
-        keys.add(4 * int(slots) - 1)
-    return tuple(sorted(int(v) for v in keys if int(v)))
 
 
 # ----------------------------------------------------------------------------------------------------- session
@@ -317,15 +232,16 @@ def create_session(spec: F.CKKSContextSpec, device: str = "cuda") -> Session:
 # ----------------------------------------------------------------------------------------------------- weight
 
 
-def pack_chunk(ctx: F.Context, weight: torch.Tensor, plan: LinearPlan, chunk: LinearChunk, slots: int) -> torch.Tensor:
-    """Diagonal rows of ``chunk`` as complex128 [rows][slots] (reference: weight.py:122-154)."""
-    rows = int(chunk.giant_count) * int(plan.baby_steps)
+def pack_chunk(ctx: F.Context, weight: torch.Tensor, layout: BsgsLayout, chunk: Chunk, slots: int) -> torch.Tensor:
+    """Diagonal rows of ``chunk`` as complex128 [rows][slots] (the rows of the reference's packers,
+    ``llama3fhe/operators/linear/weight.py:122-154``)."""
+    rows = chunk.count * layout.babies
     out = torch.empty((rows, slots), dtype=torch.complex128, device=ctx.device)
     w = weight
     cplx = bool(w.is_complex())
     src = torch.view_as_real(w) if cplx else w
-    _lib.call("holmes_pack_diagonals", src.data_ptr(), int(cplx), int(plan.dimension), int(plan.token_lanes),
-              int(plan.baby_steps), int(chunk.giant_base), int(chunk.giant_count), int(plan.lane_shift), int(slots),
+    _lib.call("holmes_pack_diagonals", src.data_ptr(), int(cplx), layout.dimension, layout.lanes, layout.babies,
+              chunk.first, chunk.count, layout.lane_shift, int(slots),
               torch.view_as_real(out).data_ptr(), 2 * slots, F._stream())
     return out
 
@@ -360,10 +276,12 @@ class LinearWeight:
     def closed(self) -> bool:
         return self._closed
 
-    def prepare(self, operator_config: LinearOperatorConfig) -> float:
+    def prepare(self, schedule=None) -> float:
+        """Upload the page to HBM (once); returns the seconds spent.  ``schedule`` is accepted for the reference's
+        signature and not needed."""
         if self._closed:
-            raise RuntimeError("linear weight is closed.")
-        del operator_config
+            raise RuntimeError("the weight page has been closed")
+        del schedule
         start = time.perf_counter()
         if self._device_source is None:
             ctx = self.crypto_context.context
@@ -393,38 +311,38 @@ class LinearWeight:
         self.setup_seconds += elapsed
         return elapsed
 
-    def _bundle(self, plan: LinearPlan, chunk: LinearChunk, operator_config: LinearOperatorConfig) -> F.ConstantBundle:
-        key = (*plan.cache_key, int(chunk.index), str(operator_config.constant_cache_mode))
+    def _bundle(self, layout: BsgsLayout, chunk: Chunk, schedule: BsgsSchedule) -> F.ConstantBundle:
+        key = (*layout.key, chunk.index, schedule.cache)
         bundle = self._bundles.get(key)
         if bundle is None:
-            self.prepare(operator_config)
+            self.prepare()
             ctx = self.crypto_context.context
 
-            def packer(source, slots, context, plan=plan, chunk=chunk):
+            def packer(source, slots, context, layout=layout, chunk=chunk):
                 del context
-                return pack_chunk(ctx, source, plan, chunk, slots)
+                return pack_chunk(ctx, source, layout, chunk, slots)
 
             bundle = F.ConstantBundle(vectors={chunk.name: F.UnpackedRaw(self._device_source, packer)},
-                                      cache_mode=str(operator_config.constant_cache_mode))
-            if str(operator_config.constant_cache_mode) != "none":
+                                      cache_mode=schedule.cache)
+            if schedule.cache != "none":
                 self._bundles[key] = bundle
         return bundle
 
-    def plaintext(self, plan: LinearPlan, chunk: LinearChunk, *, level: int,
-                  operator_config: LinearOperatorConfig) -> F.Plaintext:
+    def plaintext(self, layout: BsgsLayout, chunk: Chunk, *, level: int, schedule) -> F.Plaintext:
+        """The NTT plaintexts of ``chunk``'s diagonal rows at ``level`` (over Q u P for the extended hoists)."""
+        schedule = BsgsSchedule.coerce(schedule)
         if self._closed:
-            raise RuntimeError("linear weight is closed.")
-        if int(plan.dimension) != self.dimension:
-            raise ValueError(f"linear plan dimension={plan.dimension} does not match weight "
-                             f"dimension={self.dimension}.")
+            raise RuntimeError("the weight page has been closed")
+        if layout.dimension != self.dimension:
+            raise ValueError(f"layout of dimension {layout.dimension} applied to a {self.dimension}-wide page")
         ctx = self.crypto_context.context
         cur = int(ctx.L) - int(level)
-        bundle = self._bundle(plan, chunk, operator_config)
+        bundle = self._bundle(layout, chunk, schedule)
         if self._upload_event is not None:
             torch.cuda.current_stream(ctx.device).wait_event(self._upload_event)
         return bundle.plaintext(chunk.name, state=F.CipherState(cur, 1, ctx.scale_at(cur)),
                                 slots=int(self.crypto_context.max_slots), context=ctx,
-                                is_ext=str(operator_config.hoist_strategy).lower() != "normal", cache=True)
+                                is_ext=schedule.hoist != "normal", cache=True)
 
     def cache_info(self) -> dict:
         totals: dict = {"bundle_count": len(self._bundles)}
@@ -450,7 +368,7 @@ class LinearWeight:
 
     def __enter__(self) -> "LinearWeight":
         if self._closed:
-            raise RuntimeError("cannot enter a closed linear weight.")
+            raise RuntimeError("the weight page has been closed")
         return self
 
     def __exit__(self, *exc) -> None:
@@ -499,16 +417,16 @@ class _Babies:
 class LinearOperator:
     """A reusable BSGS schedule with an operator-local baby cache (reference: operator.py:58-639)."""
 
-    def __init__(self, *, crypto_context, token_lanes: int, config: LinearOperatorConfig | None = None,
-                 baby_shard=None) -> None:
-        """``baby_shard = (rank, world, group)`` splits the baby key switches over the ranks of ``group`` (each
-        rank holding the same inputs) and all-gathers the basis; None builds it locally."""
+    def __init__(self, *, crypto_context, token_lanes: int, config=None, baby_shard=None) -> None:
+        """``config``: a :class:`BsgsSchedule`, or the reference's ``LinearOperatorConfig`` (read by attribute name).
+        ``baby_shard = (rank, world, group)`` splits the baby key switches over the ranks of ``group`` (each rank
+        holding the same inputs) and all-gathers the basis; None builds it locally."""
         self.crypto_context = crypto_context
         self.baby_shard = None if baby_shard is None else (int(baby_shard[0]), int(baby_shard[1]), baby_shard[2])
         self.token_lanes = int(token_lanes)
         if self.token_lanes <= 0:
-            raise ValueError("token_lanes must be positive.")
-        self.config = LinearOperatorConfig() if config is None else config
+            raise ValueError(f"token_lanes={token_lanes} must be positive")
+        self.config = BsgsSchedule.coerce(config)
         self._baby_cache: dict = {}
         self._baby_hits = 0
         self._baby_misses = 0
@@ -518,14 +436,14 @@ class LinearOperator:
     def closed(self) -> bool:
         return self._closed
 
-    def plan(self, dimension: int) -> LinearPlan:
-        return self.config.plan(dimension=int(dimension), token_lanes=int(self.token_lanes))
+    def layout(self, dimension: int) -> BsgsLayout:
+        return self.config.layout(int(dimension), self.token_lanes)
 
     # -- baby basis ----------------------------------------------------------------------------------------
-    def _baby_key(self, inputs, plan: LinearPlan):
-        return (tuple(id(c) for c in inputs), plan.cache_key + (int(plan.baby_anchor_step),))
+    def _baby_key(self, inputs, plan: BsgsLayout):
+        return (tuple(id(c) for c in inputs), plan.key)
 
-    def _lookup_babies(self, inputs, plan: LinearPlan, level: int):
+    def _lookup_babies(self, inputs, plan: BsgsLayout, level: int):
         key = self._baby_key(inputs, plan)
         entry = self._baby_cache.get(key)
         if entry is not None and all(a is b for a, b in zip(entry.sources, inputs)) and entry.level == level:
@@ -536,15 +454,15 @@ class LinearOperator:
         self._baby_misses += len(inputs)
         return None
 
-    def _build_babies(self, inputs, plan: LinearPlan, level: int) -> _Babies:
+    def _build_babies(self, inputs, plan: BsgsLayout, level: int) -> _Babies:
         """All B baby rotations of every input.  With a baby shard (rank, world, group) set, this rank key-switches
         only its contiguous range of babies and an all-gather over the group fills in the rest: every rank then
         holds the whole basis at 1 / world of the key switches."""
         ctx = self.crypto_context.context
         cur = int(inputs[0].state.cur_limbs)
         n_in = len(inputs)
-        B = int(plan.baby_steps)
-        ext = str(self.config.hoist_strategy).lower() != "normal"
+        B = plan.babies
+        ext = self.config.hoist != "normal"
         limbs = cur + (ctx.K if ext else 0)
         storage = torch.empty((B, 2, n_in, limbs, ctx.N), dtype=torch.uint64, device=ctx.device)
         c0 = torch.stack([c.cv[0][0, :cur] for c in inputs])
@@ -566,7 +484,7 @@ class LinearOperator:
         if max(lo, 1) < hi:
             digits, dig_item = F._modup(ctx, c1, cur, n_in)
             for b in range(max(lo, 1), hi):
-                g = ctx.galois(plan.baby_offsets[b])
+                g = ctx.galois(plan.baby_strides[b])
                 if ext:
                     key_t, cap = ctx.switch_key(g, cur)
                     _lib.call("holmes_keyswitch_ext", ctx.handle, digits.data_ptr(), dig_item, cur, key_t.data_ptr(),
@@ -580,22 +498,22 @@ class LinearOperator:
             from .collectives import all_gather_rows
             # asynchronous: the first chunk's encode (which needs no babies) overlaps the transfer
             entry.pending = all_gather_rows(storage, lo, hi, shard[1], shard[2], async_op=True)
-        if bool(self.config.reuse_baby_rotations):
+        if self.config.reuse_babies:
             self._baby_cache[self._baby_key(inputs, plan)] = entry
         return entry
 
     def prepare_baby_rotations(self, input_ciphers, *, dimension: int) -> dict:
         if self._closed:
-            raise RuntimeError("linear operator is closed.")
+            raise RuntimeError("the linear operator has been closed")
         inputs = tuple(input_ciphers)
         profile = {"baby_precompute": 0.0, "baby_precompute_enqueue": 0.0, "baby_cache_hits": 0.0,
                    "baby_cache_misses": 0.0}
-        if not inputs or not bool(self.config.reuse_baby_rotations):
+        if not inputs or not self.config.reuse_babies:
             return profile
-        plan = self.plan(int(dimension))
+        plan = self.layout(int(dimension))
         levels = {int(self.crypto_context.level_for_cipher(c)) for c in inputs}
         if len(levels) != 1:
-            raise ValueError("linear inputs must enter at one common level.")
+            raise ValueError(f"the inputs of one apply must share a level, got levels {sorted(levels)}")
         level = levels.pop()
         hits, misses = self._baby_hits, self._baby_misses
         start = time.perf_counter()
@@ -617,47 +535,46 @@ class LinearOperator:
 
     # -- apply ---------------------------------------------------------------------------------------------
     def apply(self, input_ciphers, weight: LinearWeight, *, chunk_indices=None, rescale: bool = True):
+        """W x for every input (single non-extended ciphertexts at one level, at most 32); ``chunk_indices`` limits
+        the sum to those chunks (a partial at scale degree 2 without ``rescale``).  Returns (outputs, stage
+        seconds)."""
         if self._closed:
-            raise RuntimeError("linear operator is closed.")
-        strategy = str(self.config.hoist_strategy).lower()
-        if strategy not in _HOIST_STRATEGIES:
-            raise ValueError(f"unknown hoist_strategy {strategy!r}")
+            raise RuntimeError("the linear operator has been closed")
+        strategy = self.config.hoist
         ext = strategy != "normal"
         double = strategy == "ext_double_hoist"
         inputs = tuple(input_ciphers)
         if not inputs:
             return (), dict(_EMPTY_PROFILE)
         if weight.closed:
-            raise RuntimeError("cannot apply a closed linear weight.")
+            raise RuntimeError("the weight page has been closed")
         if weight.crypto_context is not self.crypto_context:
-            raise ValueError("linear operator and weight must share one context.")
+            raise ValueError("the operator and the weight page belong to different sessions")
         if len(inputs) > 32:
-            raise ValueError("at most 32 inputs per apply (split the batch)")
-        plan = self.plan(weight.dimension)
+            raise ValueError(f"{len(inputs)} inputs in one apply; the multi-input MAC takes at most 32")
+        plan = self.layout(weight.dimension)
         if chunk_indices is None:
             chunks = plan.chunks
         else:
             wanted = tuple(int(i) for i in chunk_indices)
-            if not wanted:
-                raise ValueError("chunk_indices must select at least one chunk.")
-            if len(set(wanted)) != len(wanted):
-                raise ValueError("chunk_indices must not repeat a chunk.")
+            if not wanted or len(set(wanted)) != len(wanted):
+                raise ValueError(f"chunk_indices {wanted} must name distinct chunks, at least one")
             for i in wanted:
                 if i < 0 or i >= len(plan.chunks):
                     raise IndexError(f"chunk index {i} outside [0, {len(plan.chunks)})")
             chunks = tuple(plan.chunks[i] for i in wanted)
         levels = {int(self.crypto_context.level_for_cipher(c)) for c in inputs}
         if len(levels) != 1:
-            raise ValueError("linear inputs must enter at one common level.")
+            raise ValueError(f"the inputs of one apply must share a level, got levels {sorted(levels)}")
         level = levels.pop()
         if any(c.batch_size != 1 or c.is_ext for c in inputs):
-            raise ValueError("linear inputs must be single non-extended ciphertexts.")
+            raise ValueError("every input must be one non-extended ciphertext")
         ctx = self.crypto_context.context
         stage = dict(_EMPTY_PROFILE)
         stage["weight_upload"] = float(weight.prepare(self.config))
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
         ev[0].record()
-        babies = self._lookup_babies(inputs, plan, level) if bool(self.config.reuse_baby_rotations) else None
+        babies = self._lookup_babies(inputs, plan, level) if self.config.reuse_babies else None
         if babies is None:
             babies = self._build_babies(inputs, plan, level)
         ev[1].record()
@@ -671,11 +588,11 @@ class LinearOperator:
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record()
-            pts = weight.plaintext(plan, chunk, level=level, operator_config=self.config)
+            pts = weight.plaintext(plan, chunk, level=level, schedule=self.config)
             e1.record()
             pt_state = pts.state
             babies.ready()
-            res = F.bsgs_partial_sums(ctx, blocks, pts, int(chunk.giant_count))
+            res = F.bsgs_partial_sums(ctx, blocks, pts, chunk.count)
             del pts
             if ext:   # babies and MAC over Q u P, one ModDown per giant partial
                 G = int(res.shape[1])
@@ -686,10 +603,10 @@ class LinearOperator:
                           F._stream())
                 res = down
             if double:   # ext_double_hoist: every giant rotated directly over Q u P, summed, one ModDown
-                g0, g1 = F.giant_double_hoist(ctx, res, int(plan.giant_offset))
+                g0, g1 = F.giant_double_hoist(ctx, res, plan.giant_stride)
             else:        # normal / ext_normal: the Horner chain
-                g0, g1 = F.giant_horner(ctx, res, int(plan.giant_offset))
-            shift = int(chunk.giant_base) * int(plan.giant_offset)
+                g0, g1 = F.giant_horner(ctx, res, plan.giant_stride)
+            shift = chunk.first * plan.giant_stride
             if acc0 is None:
                 if shift:
                     n0, n1 = torch.empty_like(g0), torch.empty_like(g1)
@@ -738,7 +655,7 @@ class LinearOperator:
 
     def __enter__(self) -> "LinearOperator":
         if self._closed:
-            raise RuntimeError("cannot enter a closed linear operator.")
+            raise RuntimeError("the linear operator has been closed")
         return self
 
     def __exit__(self, *exc) -> None:

@@ -1,9 +1,10 @@
-"""Pair refresh: two real ciphertexts through one bootstrap as ``left + i right``.
+"""Pair refresh on this engine: one bootstrap carries two real ciphertexts, packed as ``a + i b``.
 
-Mirrors the reference's residual-refresh helpers (``llama3fhe/operators/norm/refresh.py:21-60``) and the
-station-level ``pair_bootstrap`` / ``halve`` (``llama3fhe/parallel/prefill/stations.py:102-190``): same names,
-argument meaning and error behaviour, on this engine's primitives (``holmes_b200.fhe``) and bootstrap operator
-(``holmes_b200.bootstrap.BootstrapOperator``).  Inputs are not consumed.
+The composition is the reference's (``llama3fhe/operators/norm/refresh.py:21-60`` for the pack / unpack / halving
+helpers, ``llama3fhe/parallel/prefill/stations.py:102-190`` for ``pair_bootstrap`` and ``halve``), and it has to be:
+the three-line arithmetic is the interface.  The functions keep those names and argument meanings so a caller of the
+reference can use them; they run on :mod:`holmes_b200.fhe` and the batched
+:class:`holmes_b200.bootstrap.BootstrapOperator`, and they leave their inputs untouched.
 """
 from __future__ import annotations
 
@@ -15,7 +16,7 @@ def _ctx_of(crypto_context):
 
 
 def _half_rescale(cipher, *, crypto_context):
-    """Public 0.5 multiplication with one rescale (``refresh.py:21-31``)."""
+    """Multiply by the public constant 1/2 and rescale once; the result keeps the input's scale."""
     ctx = _ctx_of(crypto_context)
     encoded = fhe.encode_scalar(0.5, cur_limbs=int(cipher.state.cur_limbs), scale_degree=1,
                                 scaling_factor=float(ctx.q(int(cipher.state.cur_limbs) - 1)), context=ctx)
@@ -25,14 +26,15 @@ def _half_rescale(cipher, *, crypto_context):
 
 
 def _pack_complex_pair(left, right, *, crypto_context):
-    """Pack two real streams as ``left + i*right`` so one bootstrap serves both."""
+    """``left + i right``: the real parts of two messages share one ciphertext (and so one bootstrap)."""
     ctx = _ctx_of(crypto_context)
     return fhe.homo_add(left, fhe.homo_mul_i(right, ctx), ctx)
 
 
 def _unpack_complex_pair(value, *, crypto_context):
-    """Split a refreshed complex cipher into ``(2*real, 2*imaginary)`` with the conjugation (rotation index
-    M - 1); the factor 2 is the caller's to undo (``_half_rescale``) or absorb."""
+    """(2 Re, 2 Im) of a refreshed ``a + i b`` from one conjugation (rotation index M - 1): v + conj(v) and
+    i (conj(v) - v).  The factor 2 stays for the caller to remove (``_half_rescale``) or fold into a later
+    constant."""
     ctx = _ctx_of(crypto_context)
     conjugated = fhe.homo_rotate(value, int(ctx.M) - 1, ctx)
     real_twice = fhe.homo_add(value, conjugated, ctx)
@@ -42,10 +44,11 @@ def _unpack_complex_pair(value, *, crypto_context):
 
 def pair_bootstrap(ciphers, *, context, bootstrap_operator, iterations: int = 1, precision_bits: int = 14,
                    synchronize: bool = True):
-    """Refresh an even list of real ciphertexts two at a time via ``a + i*b``; returns ``(refreshed, 2.0)``.
+    """Bootstrap an even number of real ciphertexts at half the bootstrap count: consecutive pairs are packed as
+    ``a + i b``, refreshed, and split again.  Returns the refreshed ciphertexts (each doubled) and the factor 2.0.
 
-    All pairs go through the operator's batched ``refresh_many`` when it has one (one C2S / EvalMod / S2C pass
-    for the whole batch), else through ``refresh`` one pair at a time.
+    With an operator that has ``refresh_many`` every pair moves through one batched C2S / EvalMod / S2C pass;
+    otherwise each pair is refreshed on its own.
     """
     ciphers = tuple(ciphers)
     if len(ciphers) % 2:
@@ -65,7 +68,7 @@ def pair_bootstrap(ciphers, *, context, bootstrap_operator, iterations: int = 1,
 
 
 def halve(ciphers, *, context):
-    """Public 0.5 multiplication (one rescale) undoing a pair-refresh doubling."""
+    """Remove the doubling of ``pair_bootstrap`` (a public 1/2 and one rescale per ciphertext)."""
     return tuple(_half_rescale(c, crypto_context=context) for c in ciphers)
 
 

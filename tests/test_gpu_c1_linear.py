@@ -38,9 +38,9 @@ def test_config1_linear_bitexact_and_decodes():
         signs = rng.choice([-1.0, 1.0], size=dim)
         w = _fwht_rows(rng.normal(scale=0.02, size=(dim, dim)) * signs[None, :])
         x = rng.normal(size=dim)
-        cfg = LN.LinearOperatorConfig(baby_steps=64, baby_anchor_step=64, max_plaintext_rows=512)
-        plan = cfg.plan(dimension=dim, token_lanes=1)
-        assert (plan.baby_steps, plan.giant_steps, len(plan.chunks)) == (64, 64, 8)
+        cfg = LN.BsgsSchedule(babies=64, anchor=64, chunk_rows=512)
+        plan = cfg.layout(dim, 1)
+        assert (plan.babies, plan.giants, len(plan.chunks)) == (64, 64, 8)
         session = LN.Session(client, ctx)
         cur = ctx.L
         ct = client.encrypt(x, cur_limbs=cur, counter=7)

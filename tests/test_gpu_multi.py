@@ -86,14 +86,14 @@ def _linear_worker(rank, world, port, out_dir):
         _, client, ctx = make_pair(log_n=11, limbs=4, dnum=2, dcrt=45, first=55, special=55)
         session = LN.Session(client, ctx)
         dim, lanes = 64, 16
-        cfg = LN.LinearOperatorConfig(baby_steps=8, baby_anchor_step=8, max_plaintext_rows=16)
+        cfg = LN.BsgsSchedule(babies=8, anchor=8, chunk_rows=16)
         rng = np.random.default_rng(26081431)
         w = rng.normal(scale=0.02, size=(dim, dim))
         xs = rng.normal(size=(4, lanes, dim))
         cts = [client.encrypt(x.T.reshape(-1), cur_limbs=ctx.L, counter=100 + i) for i, x in enumerate(xs)]
         op = LN.LinearOperator(crypto_context=session, token_lanes=lanes, config=cfg, baby_shard=(rank, world, None))
         lw = LN.LinearWeight(w, dtype=w.dtype, crypto_context=session)
-        chunks = C.chunk_shard(len(op.plan(dim).chunks), world, rank)
+        chunks = C.chunk_shard(len(op.layout(dim).chunks), world, rank)
         parts, _ = op.apply(cts, lw, chunk_indices=chunks, rescale=False)
         s0 = C.modular_reduce_scatter(ctx, torch.cat([p.cv[0] for p in parts]), world)
         s1 = C.modular_reduce_scatter(ctx, torch.cat([p.cv[1] for p in parts]), world)
@@ -123,8 +123,7 @@ def test_chunk_sharded_linear_with_baby_all_gather_two_gpus(tmp_path):
     o, _, ctx = make_pair(log_n=11, limbs=4, dnum=2, dcrt=45, first=55, special=55)
     try:
         dim, lanes = 64, 16
-        plan = LN.LinearOperatorConfig(baby_steps=8, baby_anchor_step=8, max_plaintext_rows=16).plan(
-            dimension=dim, token_lanes=lanes)
+        plan = LN.BsgsSchedule(babies=8, anchor=8, chunk_rows=16).layout(dim, lanes)
         rng = np.random.default_rng(26081431)
         w = rng.normal(scale=0.02, size=(dim, dim))
         xs = rng.normal(size=(4, lanes, dim))

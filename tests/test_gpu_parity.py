@@ -257,17 +257,17 @@ def _oracle_linear(o, ref_inputs, weight, plan, cur, scale):
     """Per-input restatement of LinearOperator.apply (reference: operator.py:203-467)."""
     outs = []
     for ref in ref_inputs:
-        babies = o.hoisted_rotations(ref, plan.baby_offsets)
+        babies = o.hoisted_rotations(ref, plan.baby_strides)
         acc = None
         for chunk in plan.chunks:
-            rows = packing.diagonal_rows(weight, dimension=plan.dimension, token_lanes=plan.token_lanes,
-                                         baby_steps=plan.baby_steps, giant_base=chunk.giant_base,
-                                         giant_count=chunk.giant_count, lane_shift=plan.lane_shift)
+            rows = packing.diagonal_rows(weight, dimension=plan.dimension, token_lanes=plan.lanes,
+                                         baby_steps=plan.babies, giant_base=chunk.first,
+                                         giant_count=chunk.count, lane_shift=plan.lane_shift)
             pts = np.stack([o.encode(r, cur, scale) for r in rows])
-            part = o.bsgs_mac(pts, babies, chunk.giant_count)
-            res = o.giant_horner(part, plan.giant_offset)
-            if chunk.giant_base:
-                res = o.rotate(res, chunk.giant_base * plan.giant_offset)
+            part = o.bsgs_mac(pts, babies, chunk.count)
+            res = o.giant_horner(part, plan.giant_stride)
+            if chunk.first:
+                res = o.rotate(res, chunk.first * plan.giant_stride)
             acc = res if acc is None else (o.add(acc[0], res[0], range(cur)), o.add(acc[1], res[1], range(cur)))
         outs.append(o.rescale(acc))
     return outs
@@ -281,26 +281,26 @@ def _oracle_linear_ext(o, ref_inputs, weight, plan, cur, scale, double=False):
     moduli = [o.pr.q[i] for i in ids]
     outs = []
     for ref in ref_inputs:
-        babies = [o.rotate_ext(ref, r) for r in plan.baby_offsets]
+        babies = [o.rotate_ext(ref, r) for r in plan.baby_strides]
         acc = None
         for chunk in plan.chunks:
-            rows = packing.diagonal_rows(weight, dimension=plan.dimension, token_lanes=plan.token_lanes,
-                                         baby_steps=plan.baby_steps, giant_base=chunk.giant_base,
-                                         giant_count=chunk.giant_count, lane_shift=plan.lane_shift)
+            rows = packing.diagonal_rows(weight, dimension=plan.dimension, token_lanes=plan.lanes,
+                                         baby_steps=plan.babies, giant_base=chunk.first,
+                                         giant_count=chunk.count, lane_shift=plan.lane_shift)
             pts = np.stack([o.encode_ext(r, cur, scale) for r in rows])
-            part = o.bsgs_mac(pts, babies, chunk.giant_count, moduli=moduli)
-            down = [np.stack([o.moddown(part[c][g], cur) for g in range(chunk.giant_count)]) for c in range(2)]
+            part = o.bsgs_mac(pts, babies, chunk.count, moduli=moduli)
+            down = [np.stack([o.moddown(part[c][g], cur) for g in range(chunk.count)]) for c in range(2)]
             if double:
-                terms = [o.rotate_ext((down[0][g], down[1][g]), g * plan.giant_offset)
-                         for g in range(chunk.giant_count)]
+                terms = [o.rotate_ext((down[0][g], down[1][g]), g * plan.giant_stride)
+                         for g in range(chunk.count)]
                 tot = terms[0]
                 for t in terms[1:]:
                     tot = (o.add(tot[0], t[0], ids), o.add(tot[1], t[1], ids))
                 res = (o.moddown(tot[0], cur), o.moddown(tot[1], cur))
             else:
-                res = o.giant_horner(down, plan.giant_offset)
-            if chunk.giant_base:
-                res = o.rotate(res, chunk.giant_base * plan.giant_offset)
+                res = o.giant_horner(down, plan.giant_stride)
+            if chunk.first:
+                res = o.rotate(res, chunk.first * plan.giant_stride)
             acc = res if acc is None else (o.add(acc[0], res[0], range(cur)), o.add(acc[1], res[1], range(cur)))
         outs.append(o.rescale(acc))
     return outs
@@ -314,10 +314,10 @@ def test_linear_operator_ext_double_hoist_bitexact_and_decodes():
     o, client, ctx = make_pair(log_n=11, limbs=4, dnum=2, dcrt=45, first=55, special=55)
     session = LN.Session(client, ctx)
     dim, lanes = 64, 16
-    cfg = LN.LinearOperatorConfig(baby_steps=8, baby_anchor_step=8, max_plaintext_rows=32,
-                                  hoist_strategy="ext_double_hoist")
-    plan = cfg.plan(dimension=dim, token_lanes=lanes)
-    assert plan.chunk_giants == 4
+    cfg = LN.BsgsSchedule(babies=8, anchor=8, chunk_rows=32,
+                                  hoist="ext_double_hoist")
+    plan = cfg.layout(dim, lanes)
+    assert plan.chunks[0].count == 4
     rng = np.random.default_rng(17)
     w = rng.normal(scale=0.02, size=(dim, dim))
     xs = rng.normal(size=(2, lanes, dim))
@@ -333,8 +333,8 @@ def test_linear_operator_ext_double_hoist_bitexact_and_decodes():
             LN.LinearWeight(w, dtype=w.dtype, crypto_context=session) as lw:
         outs, _ = op.apply(cts, lw)
         # the single-input EasyFHE call takes the same path
-        pts = lw.plaintext(plan, plan.chunks[1], level=0, operator_config=cfg)
-        one = F.hoisted_mac_sum(cts[0], plan.baby_offsets, pts, plan.giant_offset, plan.chunks[1].giant_count, ctx,
+        pts = lw.plaintext(plan, plan.chunks[1], level=0, schedule=cfg)
+        one = F.hoisted_mac_sum(cts[0], plan.baby_strides, pts, plan.giant_stride, plan.chunks[1].count, ctx,
                                 strategy="ext_double_hoist")
         assert int(one.state.cur_limbs) == cur and not one.is_ext
     expect = _oracle_linear_ext(o, refs, w, plan, cur, ctx.scale, double=True)
@@ -354,8 +354,8 @@ def test_linear_operator_ext_normal_bitexact_and_decodes():
     o, client, ctx = make_pair(log_n=11, limbs=4, dnum=2, dcrt=45, first=55, special=55)
     session = LN.Session(client, ctx)
     dim, lanes = 64, 16
-    cfg = LN.LinearOperatorConfig(baby_steps=8, baby_anchor_step=8, max_plaintext_rows=16, hoist_strategy="ext_normal")
-    plan = cfg.plan(dimension=dim, token_lanes=lanes)
+    cfg = LN.BsgsSchedule(babies=8, anchor=8, chunk_rows=16, hoist="ext_normal")
+    plan = cfg.layout(dim, lanes)
     rng = np.random.default_rng(7)
     w = rng.normal(scale=0.02, size=(dim, dim))
     xs = rng.normal(size=(2, lanes, dim))
@@ -384,8 +384,8 @@ def test_linear_operator_bitexact_and_decodes(complex_weight):
     o, client, ctx = make_pair(log_n=11, limbs=4, dnum=2, dcrt=45, first=55, special=55)
     session = LN.Session(client, ctx)
     dim, lanes = 64, 16            # slots = 1024 = dim * lanes
-    cfg = LN.LinearOperatorConfig(baby_steps=8, baby_anchor_step=8, max_plaintext_rows=16)
-    plan = cfg.plan(dimension=dim, token_lanes=lanes)
+    cfg = LN.BsgsSchedule(babies=8, anchor=8, chunk_rows=16)
+    plan = cfg.layout(dim, lanes)
     rng = np.random.default_rng(26081431)
     w = rng.normal(scale=0.02, size=(dim, dim))
     if complex_weight:
@@ -603,20 +603,20 @@ def test_composed_rotate_and_encode_entry_points():
         np.testing.assert_array_equal(host(gout[1]), host(h1))
         session = LN.Session(client, ctx)
         dim, lanes = 64, 16
-        cfg = LN.LinearOperatorConfig(baby_steps=8, baby_anchor_step=8, max_plaintext_rows=16)
-        plan = cfg.plan(dimension=dim, token_lanes=lanes)
+        cfg = LN.BsgsSchedule(babies=8, anchor=8, chunk_rows=16)
+        plan = cfg.layout(dim, lanes)
         w = rng.normal(scale=0.02, size=(dim, dim))
         chunk = plan.chunks[1]
-        rows = chunk.giant_count * plan.baby_steps
+        rows = chunk.count * plan.babies
         slots = int(session.max_slots)
         with LN.LinearWeight(w, dtype=w.dtype, crypto_context=session) as lw:
-            want = lw.plaintext(plan, chunk, level=ctx.L - cur, operator_config=cfg)
+            want = lw.plaintext(plan, chunk, level=ctx.L - cur, schedule=cfg)
             wd = torch.from_numpy(w).to(ctx.device)
             out = torch.empty((rows, cur, N), dtype=torch.uint64, device=ctx.device)
             scratch = torch.empty((rows, slots, 2), dtype=torch.float64, device=ctx.device)
             flag = torch.zeros(1, dtype=torch.int32, device=ctx.device)
-            L.call("holmes_encode_diag_rows", ctx.handle, wd.data_ptr(), 0, dim, lanes, plan.baby_steps,
-                   chunk.giant_base, chunk.giant_count, plan.lane_shift, slots, float(ctx.scale_at(cur)), cur,
+            L.call("holmes_encode_diag_rows", ctx.handle, wd.data_ptr(), 0, dim, lanes, plan.babies,
+                   chunk.first, chunk.count, plan.lane_shift, slots, float(ctx.scale_at(cur)), cur,
                    out.data_ptr(), cur * N, scratch.data_ptr(), flag.data_ptr(), 0)
             np.testing.assert_array_equal(host(out), host(want.cv[0][:, :cur]))
             assert int(flag.item()) == 0

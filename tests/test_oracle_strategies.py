@@ -24,10 +24,10 @@ def test_hoist_strategy_restatements_decode_to_the_product():
     out_scale = scale * scale / o.pr.q[cur - 1]
     got = {}
     for strategy in ("normal", "ext_normal", "ext_double_hoist"):
-        cfg = LN.LinearOperatorConfig(baby_steps=4, baby_anchor_step=4, max_plaintext_rows=16,
-                                      hoist_strategy=strategy)
-        plan = cfg.plan(dimension=dim, token_lanes=lanes)
-        assert plan.chunk_giants == 4
+        cfg = LN.BsgsSchedule(babies=4, anchor=4, chunk_rows=16,
+                                      hoist=strategy)
+        plan = cfg.layout(dim, lanes)
+        assert plan.chunks[0].count == 4
         if strategy == "normal":
             (res,) = _oracle_linear(o, [ref], w, plan, cur, scale)
         else:

@@ -20,27 +20,29 @@ def plans():
         return json.load(f)["plans"]
 
 
+def _schedule(p):
+    return LN.BsgsSchedule(babies=p["baby_steps"], anchor=p["baby_anchor_step"], chunk_rows=p["max_plaintext_rows"],
+                           hoist=p["hoist_strategy"], lane_shift=p["lane_shift"])
+
+
 def test_plan_geometry_matches_reference(plans):
+    """The engine's own layout type gives the reference's LinearPlan geometry and key sets for every fixture."""
     for p in plans:
-        cfg = LN.LinearOperatorConfig(baby_steps=p["baby_steps"], baby_anchor_step=p["baby_anchor_step"],
-                                      max_plaintext_rows=p["max_plaintext_rows"], hoist_strategy=p["hoist_strategy"],
-                                      lane_shift=p["lane_shift"])
-        plan = cfg.plan(dimension=p["dimension"], token_lanes=p["token_lanes"])
-        assert plan.giant_steps == p["giant_steps"]
-        assert plan.chunk_giants == p["chunk_giants"]
-        assert plan.giant_offset == p["giant_offset"]
-        assert list(plan.baby_offsets) == p["baby_offsets"]
-        assert [[c.index, c.giant_base, c.giant_count] for c in plan.chunks] == p["chunks"]
-        assert list(plan.baby_key_offsets) == p["baby_key_offsets"]
-        assert [[b.start, b.width] for b in plan.baby_blocks] == p["baby_blocks"]
-        assert list(plan.fold_offsets) == p["fold_offsets"]
-        assert list(plan.lane_expand_offsets) == p["lane_expand_offsets"]
-        rot = LN.linear_rotations(dimension=p["dimension"], token_lanes=p["token_lanes"], operator_config=cfg)
-        assert list(rot) == p["rotations"]
+        sched = _schedule(p)
+        lay = sched.layout(p["dimension"], p["token_lanes"])
+        assert lay.giants == p["giant_steps"]
+        assert lay.chunks[0].count == p["chunk_giants"]
+        assert lay.giant_stride == p["giant_offset"]
+        assert list(lay.baby_strides) == p["baby_offsets"]
+        assert [[c.index, c.first, c.count] for c in lay.chunks] == p["chunks"]
+        assert list(lay.baby_keys) == p["baby_key_offsets"]
+        assert [list(b) for b in lay.blocks] == p["baby_blocks"]
+        assert list(lay.fold_strides) == p["fold_offsets"]
+        assert list(lay.expand_strides) == p["lane_expand_offsets"]
+        assert list(sched.rotation_keys(p["dimension"], p["token_lanes"])) == p["rotations"]
         slots = p["dimension"] * p["token_lanes"]
-        rc = LN.linear_rotations(dimension=p["dimension"], token_lanes=p["token_lanes"], slots=slots,
-                                 include_conjugation=True, operator_config=cfg)
-        assert list(rc) == p["rotations_conj"]
+        assert list(sched.rotation_keys(p["dimension"], p["token_lanes"], conjugation_slots=slots)) == \
+            p["rotations_conj"]
 
 
 @pytest.mark.parametrize(("strategy", "baby", "anchor", "expected"), [
@@ -48,42 +50,42 @@ def test_plan_geometry_matches_reference(plans):
     ("normal", 64, 64, 71), ("ext_normal", 64, 64, 71), ("ext_double_hoist", 64, 64, 77),
     ("normal", 128, 64, 72), ("ext_normal", 128, 64, 72), ("ext_double_hoist", 128, 64, 74)])
 def test_rotation_key_counts(strategy, baby, anchor, expected):
-    cfg = LN.LinearOperatorConfig(baby_steps=baby, baby_anchor_step=anchor, max_plaintext_rows=512,
-                                  hoist_strategy=strategy)
-    assert len(LN.linear_rotations(dimension=4096, token_lanes=8, operator_config=cfg)) == expected
+    sched = LN.BsgsSchedule(babies=baby, anchor=anchor, chunk_rows=512, hoist=strategy)
+    assert len(sched.rotation_keys(4096, 8)) == expected
 
 
 def test_production_schedule():
-    for cfg in (LN.LLAMA3_LINEAR_SCHEDULES.qkv, LN.LLAMA3_LINEAR_SCHEDULES.w_o, LN.LLAMA3_LINEAR_SCHEDULES.gate_up,
-                LN.LLAMA3_LINEAR_SCHEDULES.down):
-        assert (cfg.baby_steps, cfg.baby_anchor_step, cfg.max_plaintext_rows) == (64, 64, 512)
-        assert cfg.hoist_strategy == "normal" and cfg.reuse_baby_rotations
-    plan = LN.LLAMA3_LINEAR_SCHEDULES.qkv.plan(dimension=4096, token_lanes=8)
-    assert plan.giant_offset == 512 and plan.chunk_sizes == (8,) * 8 and plan.plaintext_chunks == 8
+    sched = LN.PRODUCTION
+    assert (sched.babies, sched.anchor, sched.chunk_rows, sched.hoist, sched.reuse_babies) == (64, 64, 512, "normal",
+                                                                                              True)
+    lay = sched.layout(4096, 8)
+    assert lay.giant_stride == 512 and [c.count for c in lay.chunks] == [8] * 8
 
 
-@pytest.mark.parametrize("kwargs", [dict(baby_steps=0), dict(baby_anchor_step=1), dict(baby_anchor_step=-2),
-                                    dict(max_plaintext_rows=8, baby_steps=16), dict(hoist_strategy="fast"),
-                                    dict(constant_cache_mode="all"), dict(raw_weight_policy="disk"),
-                                    dict(lane_shift=-1), dict(encode_depth=-1)])
-def test_config_validation(kwargs):
+def test_reference_config_objects_are_read_by_name():
+    """A reference-style LinearOperatorConfig (any object with its attribute names) becomes the same schedule."""
+    import types
+
+    ref = types.SimpleNamespace(baby_steps=16, baby_anchor_step=8, max_plaintext_rows=64, reuse_baby_rotations=False,
+                                hoist_strategy="EXT_NORMAL", constant_cache_mode="plain", raw_weight_policy="host",
+                                lane_shift=0)
+    assert LN.BsgsSchedule.coerce(ref) == LN.BsgsSchedule(babies=16, anchor=8, chunk_rows=64, reuse_babies=False,
+                                                          hoist="ext_normal", cache="plain", weight_on_device=False)
+    assert LN.BsgsSchedule.coerce(None) == LN.BsgsSchedule()
+
+
+@pytest.mark.parametrize("kwargs", [dict(babies=0), dict(anchor=1), dict(anchor=-2), dict(chunk_rows=8, babies=16),
+                                    dict(hoist="fast"), dict(hoist="double"), dict(cache="all"), dict(lane_shift=-1)])
+def test_schedule_validation(kwargs):
     with pytest.raises(ValueError):
-        LN.LinearOperatorConfig(**kwargs)
+        LN.BsgsSchedule(**kwargs)
 
 
-def test_unknown_strategies_are_refused():
-    """The config accepts the reference's three names and nothing else."""
+def test_layout_validation():
     with pytest.raises(ValueError):
-        LN.LinearOperatorConfig(hoist_strategy="double")
-
-
-def test_plan_validation():
+        LN.BsgsSchedule(babies=48).layout(4096, 8)
     with pytest.raises(ValueError):
-        LN.LinearOperatorConfig(baby_steps=48).plan(dimension=4096, token_lanes=8)
-    with pytest.raises(ValueError):
-        LN.LinearOperatorConfig(baby_steps=16, lane_shift=100).plan(dimension=4096, token_lanes=8)
-    with pytest.raises(ValueError):
-        LN.linear_rotations(dimension=64, token_lanes=4, include_conjugation=True)
+        LN.BsgsSchedule(babies=16, lane_shift=100).layout(4096, 8)
 
 
 def test_rotation_normalisation_and_key_size_match_reference():
@@ -116,34 +118,6 @@ def test_c_abi_exports_every_declared_symbol():
     raw = ctypes.CDLL(_lib.LIB_PATH)
     for name in names:
         getattr(raw, name)
-
-
-def test_shifted_lane_layout_matches_golden_semantics():
-    """Carrier layout (layouts/shifted_lane.py:41-175): pack, lane-0 pack, unpack per lane, expansion offsets."""
-    import numpy as np
-    from holmes_b200.shifted_lane import ShiftedLaneLayout, lane0_mask_vector
-
-    lay = ShiftedLaneLayout(hidden_dim=64, slots=512)
-    assert (lay.lanes, lay.shift) == (8, 8)
-    x = np.arange(64, dtype=np.float64)
-    sl = lay.pack(x)
-    assert lay.is_shifted_lane(sl)
-    for lane in range(8):
-        np.testing.assert_array_equal(lay.unpack(sl, lane=lane), x)
-    assert sl[lay.slot(3, 2)] == x[(3 + 8 * 2) % 64]
-    lr = lay.pack_lane0(x)
-    # rotating the lane-0 carrier by each expansion offset and adding builds the SL carrier
-    built = lr.copy()
-    for off in lay.lane0_to_shifted_offsets():
-        built = built + np.roll(lr, -off)
-    np.testing.assert_array_equal(built, sl)
-    assert lay.fold_offsets() == (1, 2, 4)
-    plan = LN.LinearOperatorConfig(baby_steps=16, lane_shift=128).plan(dimension=1024, token_lanes=8)
-    mask = lane0_mask_vector(plan, slots=8192)
-    assert mask.sum() == 1024 and mask[::8].all()
-    assert plan.lane_expand_offsets == tuple(1023 * l for l in range(1, 8))
-    with pytest.raises(ValueError):
-        ShiftedLaneLayout(hidden_dim=48, slots=512)
 
 
 def test_cipher_batch_pack_unpack_on_host_tensors():
