@@ -61,6 +61,14 @@ SIGNATURES = {
     "holmes_add_const": [p, p, p, p, i32, i32, i64, i64, p],
     "holmes_rescale_noalloc":[p, p, i64, p, i64, i32, i32, p],
     "holmes_modup": [p, p, i64, i32, i32, p, i64, p, p],
+    "holmes_peer_alloc": [ctypes.c_ulonglong, p],
+    "holmes_peer_free": [p],
+    "holmes_ipc_export": [p, p],
+    "holmes_ipc_import": [p, p],
+    "holmes_ipc_close": [p],
+    "holmes_peer_signal": [p, i32, u64, p],
+    "holmes_peer_wait": [p, i32, u64, i64, p, p],
+    "holmes_modreduce_scatter": [p, p, i32, p, i32, i32, i64, p, p],
     "holmes_keyswitch": [p, p, i64, i32, p, i32, u64, p, p, i64, p, p, i64, p, p, i64, i32, p, p],
     "holmes_bsgs_mac": [p, p, p, p, i64, i32, i32, p, i64, i32, i32, p],
     "holmes_mac_gather": [p, p, p, i64, p, p, p, i32, i32, p, i64, i32, i32, p, p, p, p],

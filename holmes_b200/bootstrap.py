@@ -177,8 +177,26 @@ class BootstrapProgram:
     cheb: np.ndarray
     rotations: tuple
     gap: int = 1             # N / (2 n): sparse slots when > 1
+    s2c_int: int = 1         # exact integer factor applied before SlotsToCoeffs (keeps its diagonals encodable)
     _plain: dict = field(default_factory=dict)
     setup_seconds: float = 0.0
+    cache_mode: str = "plain"   # "plain": keep encoded diagonals across refreshes; "none": encode per use
+
+    @property
+    def constants(self) -> "BootstrapProgram":
+        """The program's constant store (EasyFHE ``program.constants``; ``set_cache_mode`` / ``clear_cache``)."""
+        return self
+
+    def set_cache_mode(self, mode: str, clear: bool = False) -> None:
+        mode = str(mode)
+        if mode not in ("none", "middle", "plain", "both"):
+            raise ValueError(f"unknown bootstrap constant cache mode {mode!r}")
+        self.cache_mode = mode
+        if clear:
+            self._plain.clear()
+
+    def clear_cache(self) -> None:
+        self._plain.clear()
 
     @property
     def output_state(self) -> F.CipherState:
@@ -198,10 +216,16 @@ class BootstrapProgram:
         rows = np.stack([mat[r] * factor for r in offsets])
         scale = float(ctx.q(cur - 1))
         pv = F.encode_rows(ctx, torch.from_numpy(rows).to(ctx.device), cur, scale, self.n)
-        ctx.check_encode_range()
+        try:
+            ctx.check_encode_range()
+        except ValueError as exc:
+            raise ValueError(f"{which} level {level} of the {self.n}-slot bootstrap: diagonals up to "
+                             f"{float(np.max(np.abs(rows))):.4g} at scale 2^{math.log2(scale):.2f} "
+                             f"(factor {factor:.4g}, adjust {float(adjust):.4g}): {exc}") from None
         pt = F.Plaintext([pv], F.CipherState(cur, 1, scale), self.n, False, len(offsets), ctx)
-        self._plain[key] = (offsets, pt)
-        return self._plain[key]
+        if self.cache_mode in ("plain", "both"):
+            self._plain[key] = (offsets, pt)
+        return offsets, pt
 
 
 def requirements(specs, log_n: int) -> Requirements:
@@ -217,6 +241,23 @@ def requirements(specs, log_n: int) -> Requirements:
         rots.update(n << i for i in range(int(log_n) - 1 - int(spec.log_slots)))  # sparse-slot subsum
         depth = max(depth, spec.depth)
     return Requirements(tuple(sorted(rots)), depth)
+
+
+#: largest |diagonal value| a transform level may hold: plaintexts are encoded at the scale of the limb the next
+#: rescale drops (~2^59), and the encoder's range is 2^61
+DIAGONAL_LIMIT = 3.0
+
+
+def s2c_integer_factor(levels: list[dict], total: float) -> int:
+    """The power of two c that SlotsToCoeffs takes as an exact integer multiply (no level) so that its remaining
+    constant total / c, spread evenly over the levels, keeps every diagonal below DIAGONAL_LIMIT.  Small level
+    budgets (the sparse-slot programs clamp the budget to log2 of their slots) would otherwise put more than the
+    encoder's range on each level: q0 2^cf / (2 pi Delta) ~ 163 over 3 levels is 5.5 per level."""
+    peak = max(float(np.max(np.abs(np.stack(list(m.values()))))) for m in levels)
+    c = 1
+    while peak * (total / c) ** (1.0 / len(levels)) > DIAGONAL_LIMIT and c < (1 << 20):
+        c *= 2
+    return c
 
 
 def generate(context, spec: BootstrapSpec) -> BootstrapProgram:
@@ -243,9 +284,11 @@ def generate(context, spec: BootstrapSpec) -> BootstrapProgram:
     s2c_total = q0 * (2.0 ** cf) / (2.0 * math.pi * delta)
     cheb = chebyshev_cos(B, int(spec.double_angles), int(spec.cheb_degree))
     req = requirements([spec], ctx.logN)
+    s2c_int = s2c_integer_factor(s2c, s2c_total)
     prog = BootstrapProgram(spec=spec, context=ctx, n=n, raise_to_limbs=raise_to, output_limbs=out_limbs, cf=cf, B=B,
                             c2s=c2s, s2c=s2c, c2s_scale=c2s_total ** (1.0 / len(c2s)),
-                            s2c_scale=s2c_total ** (1.0 / len(s2c)), cheb=cheb, rotations=req.rotations, gap=gap)
+                            s2c_scale=(s2c_total / s2c_int) ** (1.0 / len(s2c)), cheb=cheb, rotations=req.rotations,
+                            gap=gap, s2c_int=s2c_int)
     prog.setup_seconds = time.perf_counter() - start
     return prog
 
@@ -267,6 +310,18 @@ def scale_table(top_limbs: int, top_scale: float, ctx) -> dict:
     for lv in range(int(top_limbs), 1, -1):
         S[lv - 1] = S[lv] * S[lv] / float(ctx.q(lv - 1))
     return S
+
+
+def mul_int(ct: F.Cipher, k: int) -> F.Cipher:
+    """ct * k for an integer k, no rescale: the message is multiplied by k at the same declared scale."""
+    ctx = ct.context
+    cur = int(ct.state.cur_limbs)
+    res = torch.tensor([int(k) % ctx.q(i) for i in range(cur)], dtype=torch.uint64, device=ctx.device)
+    out = F._new_cipher(ctx, ct.batch_size, cur, ct.state, ct.slots)
+    for c in range(2):
+        _lib.call("holmes_mul_const", ctx.handle, ct.cv[c].data_ptr(), res.data_ptr(), out.cv[c].data_ptr(),
+                  ct.batch_size, cur, F._item_stride(ct.cv[c]), F._item_stride(out.cv[c]), _stream())
+    return out
 
 
 def int_mul_rescale(ct: F.Cipher, k: int, new_scale: float) -> F.Cipher:
@@ -451,6 +506,15 @@ def bootstrap(ct: F.Cipher, ctx, program: BootstrapProgram) -> F.Cipher:
     # input's own scale s_in (rho is within a few 2^-20 of 1; the diagonals absorb it, no level is spent).
     m_scale = s_in * k_pre * 2.0 ** program.cf / float(ctx.q(1))
     rho = s_in / (float(z.state.scaling_factor) * float(ctx.scale) / m_scale)
+    # exact integer part of the SlotsToCoeffs constant, applied without a level (message and noise alike): the
+    # program's share, and the power of two that keeps rho * (per-level factor) encodable when the input arrives at a
+    # scale well above its nominal one
+    k_int = int(program.s2c_int)
+    while rho * program.s2c_scale > DIAGONAL_LIMIT and k_int < (1 << 40):
+        rho /= 2.0
+        k_int *= 2
+    if k_int > 1:
+        z = mul_int(z, k_int)
     for lvl in range(len(program.s2c)):
         offsets, pt = program.diagonal_plaintexts("s2c", lvl, int(z.state.cur_limbs), rho if lvl == 0 else 1.0)
         z = linear_level(z, offsets, pt)

@@ -21,7 +21,7 @@ NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 FLAGS = ["-O3", "-std=c++17", "-lineinfo", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC", "-Xcompiler",
          "-O2", "-Xptxas", "-warn-spills"]
-SOURCES = ["context.cu", "nttk.cu", "misc.cu", "mac_tc.cu", "capi.cu", "noalloc.cu"]
+SOURCES = ["context.cu", "nttk.cu", "misc.cu", "mac_tc.cu", "capi.cu", "noalloc.cu", "peer.cu"]
 
 
 def _deps() -> list[str]:

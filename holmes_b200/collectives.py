@@ -90,3 +90,132 @@ def modular_reduce_scatter(ctx, partials: torch.Tensor, world: int, group=None) 
     on each rank (the rank's token shard of the items)."""
     recv = exchange_partials(partials, world, group)
     return modsum(ctx, recv, int(partials.shape[1]))
+
+
+# ----------------------------------------------------------------------------------------------------- peer memory
+
+
+class PeerReduceScatter:
+    """Modular reduce-scatter of token-sharded partial sums over peer memory, one kernel per step.
+
+    Every rank owns a ``partials`` buffer [n_items][limbs][N] that the other ranks map once at construction (CUDA IPC
+    handles travel through ``group`` with ``all_gather_object``; each rank opens its peers' handles with its own device
+    current).  ``reduce()`` is device-side only, on the current stream:
+
+    1. signal "my partials of this epoch are written" (flag 0 of this rank's flag block);
+    2. wait (bounded) until every rank's flag 0 reaches the epoch;
+    3. sum every rank's partials of this rank's token shard modulo q into ``out`` -- plain loads from peer memory;
+    4. signal "I have read your partials" into every peer's flag 2 + rank, and wait (bounded) until every peer has
+       done the same in this rank's block, so the next step may overwrite ``partials``.
+
+    A wait that runs out sets a device status word and the sum is skipped; ``check()`` (one device read) raises
+    ``TimeoutError`` naming the flag.  The reference's partial reduces are host-staged sends plus an owner-side
+    ``homo_add`` (``parallel/prefill/stations.py:1565-1596``, ``parallel/decode/decode_collectives.py:59-195``)."""
+
+    FLAGS_PER_RANK = 2
+
+    def __init__(self, ctx, n_items: int, limbs: int, world: int, rank: int, group=None,
+                 timeout_s: float = 2.0, clock_hz: float = 1.965e9) -> None:
+        if world < 1 or world > 16 or not 0 <= rank < world:
+            raise ValueError(f"rank {rank} of world {world} (1 .. 16 ranks)")
+        if n_items % world:
+            raise ValueError(f"{n_items} items do not split evenly over {world} ranks")
+        self.ctx, self.world, self.rank, self.group = ctx, int(world), int(rank), group
+        self.n_items, self.limbs, self.per = int(n_items), int(limbs), int(n_items) // int(world)
+        self.budget = int(timeout_s * clock_hz)
+        self.timeout_s = float(timeout_s)
+        dev = ctx.device
+        self._owned: list[int] = []
+        self._mapped: list[int] = []
+        self.partials = self._alloc((self.n_items, self.limbs, ctx.N))
+        self.flags = self._alloc((self.FLAGS_PER_RANK + self.world,))
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.epoch = 0
+        handles = (self._export(self.partials), self._export(self.flags))
+        if self.world > 1:
+            every = [None] * self.world
+            dist.all_gather_object(every, handles, group=group)
+        else:
+            every = [handles]
+        torch.cuda.synchronize(dev)
+        self.peer_partials, self.peer_flags = [], []
+        for r, (hp, hf) in enumerate(every):
+            if r == self.rank:
+                self.peer_partials.append(self.partials.data_ptr())
+                self.peer_flags.append(self.flags.data_ptr())
+            else:
+                self.peer_partials.append(self._import(hp))
+                self.peer_flags.append(self._import(hf))
+
+    def _alloc(self, shape) -> torch.Tensor:
+        """A zeroed uint64 tensor on its own cudaMalloc allocation (IPC handles name whole allocations)."""
+        n = 1
+        for d in shape:
+            n *= int(d)
+        ptr = _lib.ctypes.c_void_p()
+        _lib.call("holmes_peer_alloc", n * 8, _lib.ctypes.byref(ptr))
+        self._owned.append(int(ptr.value))
+
+        class _View:
+            __cuda_array_interface__ = {"shape": tuple(int(d) for d in shape), "typestr": "<u8",
+                                        "data": (int(ptr.value), False), "version": 3, "strides": None}
+
+        return torch.as_tensor(_View(), device=self.ctx.device)
+
+    @staticmethod
+    def _export(t: torch.Tensor) -> bytes:
+        buf = (_lib.ctypes.c_ubyte * 64)()
+        _lib.call("holmes_ipc_export", t.data_ptr(), buf)
+        return bytes(buf)
+
+    def _import(self, handle: bytes) -> int:
+        ptr = _lib.ctypes.c_void_p()
+        _lib.call("holmes_ipc_import", (_lib.ctypes.c_ubyte * 64).from_buffer_copy(handle), _lib.ctypes.byref(ptr))
+        self._mapped.append(int(ptr.value))
+        return int(ptr.value)
+
+    def _ptrs(self, ptrs) -> "_lib.ctypes.Array":
+        return _lib.ptr_array([int(p) for p in ptrs])
+
+    def reduce(self, out: torch.Tensor | None = None) -> torch.Tensor:
+        """Sum of every rank's ``partials`` rows of this rank's token shard, modulo q -> [n_items / world][limbs][N]."""
+        ctx, N, L = self.ctx, self.ctx.N, self.limbs
+        item = L * N
+        if out is None:
+            out = torch.empty((self.per, L, N), dtype=torch.uint64, device=ctx.device)
+        if tuple(out.shape) != (self.per, L, N) or not out.is_contiguous():
+            raise ValueError(f"out must be a contiguous [{self.per}][{L}][{N}] tensor")
+        self.epoch += 1
+        e, s = self.epoch, torch.cuda.current_stream().cuda_stream
+        F = self.FLAGS_PER_RANK
+        own = self.flags.data_ptr()
+        _lib.call("holmes_peer_signal", self._ptrs([own]), 1, e, s)
+        _lib.call("holmes_peer_wait", self._ptrs(self.peer_flags), self.world, e, self.budget, self.status.data_ptr(), s)
+        off = self.rank * self.per * item * 8
+        srcs = self._ptrs([p + off for p in self.peer_partials])
+        _lib.call("holmes_modreduce_scatter", ctx.handle, srcs, self.world, out.data_ptr(), self.per, L, item,
+                  self.status.data_ptr(), s)
+        done = [p + 8 * (F + self.rank) for p in self.peer_flags]
+        _lib.call("holmes_peer_signal", self._ptrs(done), self.world, e, s)
+        mine = [own + 8 * (F + r) for r in range(self.world)]
+        _lib.call("holmes_peer_wait", self._ptrs(mine), self.world, e, self.budget, self.status.data_ptr(), s)
+        return out
+
+    def check(self) -> None:
+        """Raise if a wait of an earlier step ran out (one device read)."""
+        st = int(self.status.item())
+        if st:
+            self.status.zero_()
+            raise TimeoutError(f"peer reduce-scatter: a flag wait of rank {self.rank} ran out after "
+                               f"{self.timeout_s:.1f} s (flag {st - 1}); a peer did not reach epoch {self.epoch}")
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (every rank must have finished its last step)."""
+        torch.cuda.synchronize(self.ctx.device)
+        for p in self._mapped:
+            _lib.call("holmes_ipc_close", p)
+        self._mapped.clear()
+        self.partials = self.flags = None
+        for p in self._owned:
+            _lib.call("holmes_peer_free", p)
+        self._owned.clear()

@@ -108,7 +108,7 @@ static int upload(HolmesCtx& c, T** dst, const std::vector<T>& src) {
 int build_context(HolmesCtx& c, int log_n, int limbs, int dnum, int dcrt_bits, int first_mod_bits, int special_bits,
                   int special_limbs, int hamming, u64 seed) {
   if (log_n < 10 || log_n > 16) return -1;
-  if (limbs < 1 || limbs > 64 || dnum < 1 || dnum > limbs) return -2;
+  if (limbs < 1 || limbs > 128 || dnum < 1 || dnum > limbs) return -2;
   if (dcrt_bits < 20 || dcrt_bits > 60 || first_mod_bits < 20 || first_mod_bits > 60 || special_bits < 20 ||
       special_bits > 60)
     return -3;
@@ -118,7 +118,7 @@ int build_context(HolmesCtx& c, int log_n, int limbs, int dnum, int dcrt_bits, i
   c.dnum = dnum;
   c.alpha = (limbs + dnum - 1) / dnum;
   c.K = special_limbs > 0 ? special_limbs : c.alpha;
-  if (c.K > 64) return -2;
+  if (c.K > 128) return -2;
   c.T = c.L + c.K;
   c.beta_max = c.beta(c.L);
   c.hamming = hamming;

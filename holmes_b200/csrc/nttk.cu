@@ -31,7 +31,7 @@
 
 namespace holmes {
 
-constexpr int MAXA = 16;  // largest digit width (alpha) and special-limb count K supported
+constexpr int MAXA = 24;  // largest digit width (alpha) and special-limb count K supported
 
 #define HOLMES_LOGN_SWITCH(logn, MACRO) \
   switch (logn) {                       \
@@ -127,7 +127,8 @@ static int ntt16_inverse(NttTables T, MOD mo, SC sc, LD ld, IM im, ST st, int po
 // Target t is limb r = t (t < skip_lo) or t + w (above), of modulus index mi = r (r < cur) or L + r - cur.  One
 // thread reads the w source words of one coefficient once, splits them into 30-bit halves, and produces every
 // target from constants pre-split in shared memory (four fused wide multiply-adds per product, w <= 16 products
-// per 64-bit sum), then one Barrett fold per output, left lazy in [0, 8 q) for the forward NTT that follows.
+// per 64-bit sum; wider digits fold once after the 16th product), then one Barrett fold per output, left lazy in
+// [0, 8 q) for the forward NTT that follows.
 // Used by the key switch (P -> Q) and ModUp (digit -> complement), whose NTTs then load plainly.  With `own`
 // set (ModUp) the same thread also writes the skipped rows skip_lo + a: own_a * own_scale[a] mod q_(skip_lo + a).
 struct ConvArgs {
@@ -176,17 +177,21 @@ __global__ void __launch_bounds__(256) k_conv(ConvArgs a, int log_n, const Mod* 
     }
     for (int t = 0; t < a.ntgt; ++t) {
       const uint2* h = hs + t * W;
+      const int r = t < a.skip_lo ? t : t + W;
+      const int mi = r < a.cur ? r : a.L + r - a.cur;
       Split4 s{0, 0, 0, 0};
 #pragma unroll
       for (int k = 0; k < W; ++k) {
+        if (k == 16) {  // 16 products of 30-bit halves fill the 64-bit sums: fold lazily and restart from the split
+          const u64 v = fold_split_lazy(s, mods[mi]);
+          s = Split4{v & ((1ull << 30) - 1), v >> 30, 0, 0};
+        }
         const uint2 c = h[k];
         s.s00 += (u64)ys[k].x * c.x;
         s.sa += (u64)ys[k].x * c.y;
         s.sb += (u64)ys[k].y * c.x;
         s.s11 += (u64)ys[k].y * c.y;
       }
-      const int r = t < a.skip_lo ? t : t + W;
-      const int mi = r < a.cur ? r : a.L + r - a.cur;
       op[(size_t)r << log_n] = fold_split_lazy(s, mods[mi]);
     }
   }
@@ -220,6 +225,14 @@ static int conv_launch(const HolmesCtx& c, const ConvArgs& a, cudaStream_t st) {
     case 14: return conv_launch_w<14>(c, a, st);
     case 15: return conv_launch_w<15>(c, a, st);
     case 16: return conv_launch_w<16>(c, a, st);
+    case 17: return conv_launch_w<17>(c, a, st);
+    case 18: return conv_launch_w<18>(c, a, st);
+    case 19: return conv_launch_w<19>(c, a, st);
+    case 20: return conv_launch_w<20>(c, a, st);
+    case 21: return conv_launch_w<21>(c, a, st);
+    case 22: return conv_launch_w<22>(c, a, st);
+    case 23: return conv_launch_w<23>(c, a, st);
+    case 24: return conv_launch_w<24>(c, a, st);
     default: return -3;
   }
 }
@@ -560,6 +573,7 @@ struct ModKsQ {
 
 static int ks_inner_launch(const HolmesCtx& c, const KsInnerArgs& ia, cudaStream_t st) {
   if (c.n < 256) return -5;
+  if (ia.beta > 16) return -3;   // the split sums hold 16 products
   count_launch();
   const dim3 grid((unsigned)(c.n / 256), (unsigned)(ia.cur + ia.K));
   if (ia.beta <= 2) k_ks_inner<2><<<grid, 256, 0, st>>>(ia, c.log_n, c.d_mod);

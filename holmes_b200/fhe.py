@@ -19,6 +19,7 @@ device buffers.  There is no CPU path: without the library or a CUDA device thes
 from __future__ import annotations
 
 import dataclasses
+import gc
 import math
 import types
 from dataclasses import dataclass, field
@@ -104,9 +105,6 @@ class Cipher:
     def deep_copy(self) -> "Cipher":
         return self.cipher_like([c.clone() for c in self.cv])
 
-    def release(self) -> None:
-        self.cv = []
-
     @property
     def device(self):
         return self.cv[0].device
@@ -158,6 +156,9 @@ class Context:
             raise _lib.HolmesError("libholmes_cuda needs a CUDA device")
         if torch.device(device).type != "cuda":
             raise _lib.HolmesError(f"libholmes_cuda has no CPU backend: device {device!r} is not a CUDA device")
+        # contexts (keys, workspaces) that are no longer referenced may sit in reference cycles; free their device
+        # memory before this one allocates (a caller that builds many contexts in one process relies on it)
+        gc.collect()
         self.spec = spec
         self.device = torch.device(device if device != "cuda" else f"cuda:{torch.cuda.current_device()}")
         torch.cuda.set_device(self.device)
@@ -246,19 +247,27 @@ class Context:
         self.key_bytes += key.numel() * 8
         return key
 
-    def switch_key(self, galois: int, cur_limbs: int):
-        """(key tensor, cap) for X -> X^galois (0 = relinearisation) usable at ``cur_limbs``."""
-        entry = self._keys.get(galois)
-        if entry is not None and entry[1] >= cur_limbs:
-            return entry
+    def key_limit(self, galois: int) -> int | None:
+        """The configured limb cap of a rotation's key (``rotation_key_limb_limits``), or None."""
         if self._caps is None:
             limits = self.spec.rotation_key_limb_limits or {}
             self._caps = {self.galois(int(r)): int(c) for r, c in limits.items()}
-        cap_default = self._caps.get(galois, self.L) if galois else self.L
-        if entry is None or entry[1] < cur_limbs:
-            cap = max(cap_default, int(cur_limbs))
-            entry = (self._make_key(galois, min(cap, self.L)), min(cap, self.L))
-            self._keys[galois] = entry
+        return self._caps.get(galois) if galois else None
+
+    def switch_key(self, galois: int, cur_limbs: int):
+        """(key tensor, cap) for X -> X^galois (0 = relinearisation) usable at ``cur_limbs``.  A key is generated on
+        first use, trimmed to the Q limbs it serves: the larger of ``cur_limbs`` and the rotation's configured limit
+        (the key's rows for limbs below any cap are the same words, so a trimmed key gives the same residues).  A
+        request above the cached key's cap replaces it with a wider one."""
+        entry = self._keys.get(galois)
+        if entry is not None and entry[1] >= cur_limbs:
+            return entry
+        limit = self.key_limit(galois)
+        cap = min(self.L, max(int(cur_limbs), int(limit) if limit else int(cur_limbs)))
+        if entry is not None:
+            self.key_bytes -= entry[0].numel() * 8
+        entry = (self._make_key(galois, cap), cap)
+        self._keys[galois] = entry
         return entry
 
     def get_rotation_key_for_limbs(self, rotation: int, cur_limbs: int):
@@ -428,9 +437,10 @@ class Client:
 
 def generate_client_context(spec: CKKSContextSpec, device: str = "cuda"):
     ctx = Context(spec, device)
-    if spec.auto_load_keys:
+    if spec.auto_load_keys:   # eager: every requested key now, at its configured limit (else the full chain)
         for r in spec.rotations:
-            ctx.switch_key(ctx.galois(int(r)), ctx.L)
+            g = ctx.galois(int(r))
+            ctx.switch_key(g, ctx.key_limit(g) or ctx.L)
         if spec.relinearization:
             ctx.switch_key(0, ctx.L)
     return Client(ctx), ctx
@@ -496,10 +506,13 @@ def _add_sub(a: Cipher, b: Cipher, ctx, op: int, what: str) -> Cipher:
     ctx = _ctx(ctx)
     _valid(ctx, a, what)
     _valid(ctx, b, what)
-    _check_same(a, b, what)
-    cur = int(a.state.cur_limbs)
+    # operands at different levels meet at the lower one (the deeper operand's extra limbs are dropped; at a
+    # fixed nominal scale per level that is exact), as EasyFHE's adds do
+    cur = min(int(a.state.cur_limbs), int(b.state.cur_limbs))
+    low = a if int(a.state.cur_limbs) == cur else b
+    _check_same(_drop_limbs(a, cur), _drop_limbs(b, cur), what)
     na, nb = len(a.cv), len(b.cv)
-    out = _new_cipher(ctx, a.batch_size, cur, a.state, a.slots, max(na, nb))
+    out = _new_cipher(ctx, a.batch_size, cur, low.state, a.slots, max(na, nb))
     for c in range(max(na, nb)):
         if c < na and c < nb:
             _ew(ctx, op, a.cv[c], b.cv[c], out.cv[c], cur)
@@ -539,7 +552,7 @@ def rescale(a: Cipher, ctx) -> Cipher:
     _valid(ctx, a, "rescale")
     cur = int(a.state.cur_limbs)
     if cur < 2:
-        raise ValueError("rescale needs at least two limbs")
+        raise ValueError(f"rescale: cur_limbs must be > 1, got {cur}")
     ql = ctx.q(cur - 1)
     sf = None if a.state.scaling_factor is None else float(a.state.scaling_factor) / ql
     state = CipherState(cur - 1, max(1, int(a.state.scale_degree) - 1), sf)

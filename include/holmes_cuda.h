@@ -248,6 +248,33 @@ int holmes_bsgs_mac(void* ctx, uint64_t* res, const uint64_t* const* c0s, const 
 int holmes_modsum(void* ctx, const uint64_t* const* srcs, int nsrc, uint64_t* out, int items, int limbs,
                   long long item_stride, void* stream);
 
+/* ---- modular reduce-scatter over peer memory (the modreduce_scatter export; replaces the reference's owner-side
+ *      reduce of host-staged partials, parallel/prefill/stations.py:1565-1596, parallel/decode/decode_collectives.py:
+ *      59-195, operators/linear/shard/mlp_feature_shard.py:536-575).  One process per GPU.
+ * holmes_ipc_export: the 64-byte CUDA IPC handle of a device allocation, for the other ranks;
+ * holmes_ipc_import: map a peer's handle into the CALLING device (make the reading device current first; peer access
+ *   is enabled lazily); holmes_ipc_close: unmap. */
+/* holmes_peer_alloc / holmes_peer_free: a zeroed device allocation of its own (an IPC handle names a whole
+ * allocation, so buffers shared with peers are allocated here, not carved from a caching allocator's pool) */
+int holmes_peer_alloc(unsigned long long bytes, void** ptr_out);
+int holmes_peer_free(void* ptr);
+int holmes_ipc_export(const void* dev_ptr, void* handle_out);
+int holmes_ipc_import(const void* handle, void** ptr_out);
+int holmes_ipc_close(void* ptr);
+/* store `epoch` into each of `count` (<= 16) 64-bit flags (host array of device pointers, local or peer-mapped) after a
+ * system-scope fence: every earlier write on `stream` is visible to the peers before the flag is */
+int holmes_peer_signal(uint64_t* const* flags, int count, uint64_t epoch, void* stream);
+/* wait on `stream` until every flag (host array of device pointers, local or peer-mapped) is >= epoch; a flag that
+ * is still below after budget_cycles SM clocks makes the kernel write its index + 1 into *status (device int) and
+ * return -- bounded, never a hang; the host reads *status after the stream's work */
+int holmes_peer_wait(const uint64_t* const* flags, int count, uint64_t epoch, long long budget_cycles, int* status,
+                     void* stream);
+/* out = sum_k srcs[k] mod q over [items][limbs][N] (item stride item_stride words in every source and in out; srcs a
+ * host array of nsrc <= 16 device pointers, this rank's own and peer-mapped ones, read with plain loads); does
+ * nothing when *status is nonzero (a wait before it gave up) */
+int holmes_modreduce_scatter(void* ctx, const uint64_t* const* srcs, int nsrc, uint64_t* out, int items, int limbs,
+                             long long item_stride, const int* status, void* stream);
+
 /* kernels launched by this library since it was loaded (all streams, all contexts) */
 int holmes_launch_count(unsigned long long* count_out);
 

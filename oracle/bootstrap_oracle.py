@@ -170,6 +170,14 @@ class OracleBootstrap:
         z = self._add(re, (j0, j1, im[2]))
         m_scale = s_in * k_pre * 2.0 ** prog.cf / float(self.pr.q[1])
         rho = s_in / (float(z[2]) * self.delta / m_scale)
+        c_int = int(getattr(prog, "s2c_int", 1))
+        while rho * prog.s2c_scale > 3.0 and c_int < (1 << 40):   # holmes_b200.bootstrap.DIAGONAL_LIMIT
+            rho /= 2.0
+            c_int *= 2
+        if c_int > 1:   # the exact integer part of the SlotsToCoeffs constant (holmes_b200.bootstrap.mul_int)
+            ids = self._ids(z[0].shape[0])
+            r = [c_int % self.pr.q[i] for i in ids]
+            z = (o.mul_scalar(z[0], r, ids), o.mul_scalar(z[1], r, ids), z[2])
         for k, lvl in enumerate(prog.s2c):
             z = self.linear(z, lvl, prog.s2c_scale * (rho if k == 0 else 1.0))
         z = self.drop(z, prog.output_limbs)

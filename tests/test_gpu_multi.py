@@ -1,5 +1,5 @@
 """Two GPUs over NCCL: the modular reduce-scatter of partial sums (raw limbs over all_to_all, owner-side mod-q sum
-with holmes_modsum) equals the oracle's sum.  Skipped with fewer than two GPUs."""
+with holmes_modsum, and the peer-memory PeerReduceScatter) equals the exact sum.  Skipped with fewer than two GPUs."""
 import os
 import socket
 
@@ -42,6 +42,17 @@ def _worker(rank, world, port, out_dir):
         torch.cuda.synchronize()
         np.save(os.path.join(out_dir, f"s{rank}.npy"), got.cpu().numpy())
         np.save(os.path.join(out_dir, "q.npy"), np.array(ctx.moduli[:limbs], dtype=np.uint64))
+        # the same reduce over peer memory (IPC-mapped partials, flag waits, one summing kernel), two epochs
+        prs = C.PeerReduceScatter(ctx, items, limbs, world, rank, timeout_s=10.0)
+        for step, data in enumerate((parts, parts[::-1].copy())):
+            prs.partials.copy_(torch.from_numpy(data).cuda())
+            out = prs.reduce()
+            torch.cuda.synchronize()
+            prs.check()
+            np.save(os.path.join(out_dir, f"peer{step}_{rank}.npy"), out.cpu().numpy())
+            np.save(os.path.join(out_dir, f"pin{step}_{rank}.npy"), data)
+        dist.barrier()
+        prs.close()
         dist.barrier()
         ctx.close()
     finally:
@@ -64,6 +75,15 @@ def test_modular_reduce_scatter_two_gpus(tmp_path):
         want = sum(p[owned].astype(object) for p in parts)
         for li, ql in enumerate(q):
             assert np.array_equal(got[:, li].astype(object), want[:, li] % ql)
+    # peer-memory reduce-scatter: word for word the same sums, on both epochs
+    for step in range(2):
+        ins = [np.load(tmp_path / f"pin{step}_{r}.npy") for r in range(world)]
+        for r in range(world):
+            got = np.load(tmp_path / f"peer{step}_{r}.npy")
+            owned = list(C.token_shard(4, world, r))
+            want = sum(p[owned].astype(object) for p in ins)
+            for li, ql in enumerate(q):
+                assert np.array_equal(got[:, li].astype(object), want[:, li] % ql), (step, r, li)
 
 
 def _linear_worker(rank, world, port, out_dir):
