@@ -658,6 +658,183 @@ def run_vs_ref(args) -> None:
     ctx.close()
 
 
+LAYER_METRIC = "encrypted Llama-3-8B prefill-128 one-decoder-layer latency (1 B200)"
+
+
+def _reference_application():
+    """Put the reference's own llama3fhe (installed unchanged in baseline/_ref by tests/install_reference.py) on the
+    path with this engine registered as its ``easyfhe``."""
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "llama3fhe")):
+        raise SystemExit("--workload layer drives the reference's own layer graph on this engine; install the "
+                         "reference first: python tests/install_reference.py <checkout of the reference>")
+    if ref not in sys.path:
+        sys.path.insert(0, ref)
+    from holmes_b200 import easyfhe_compat
+
+    easyfhe_compat.install()
+
+
+class _LayerSetup:
+    """BASELINE config 3 through the reference's own one-layer application path (the synthetic preset of its
+    ``run_layer0.py``: ``llama3fhe/application/runner.py:158-470``): Llama-3-8B geometry (hidden 4096, 32 query / 8
+    KV heads of 128, MLP 14336), 128 prefill tokens feature-major packed into 16 ciphertexts at N = 2^16, the
+    production chain (38 limbs, dnum 5), the reference's polynomial tables and its layer schedule, RoPE theta 5e5,
+    bootstraps where the schedule places them.  Everything above the engine -- layer graph, operators, attention,
+    bootstrap policy -- is the reference's code, unchanged; every FHE operation runs on libholmes_cuda."""
+
+    def __init__(self, seed: int) -> None:
+        _reference_application()
+        import numpy as _np
+
+        from llama3fhe import Llama3CKKSConfig
+        from llama3fhe.application.approx_config import ApproximationConfig
+        from llama3fhe.application.args import build_parser, resolve_poly_paths
+        from llama3fhe.application.inputs import _synthetic_inputs
+        from llama3fhe.application.layer_stream import DoubleBufferedLayerStream
+        from llama3fhe.application.session import _create_context, _encrypt_hidden
+        from llama3fhe.application.settings import layer_schedule, resolve_settings
+        from llama3fhe.backend import set_stage_sync
+        from llama3fhe.layouts import AttentionPairLayout, FeatureMajorPrefillLayout
+        from llama3fhe.model import Llama3Model, prepare_bootstrap_operator
+
+        set_stage_sync(False)   # the operators' stage-timer device synchronisations (profiling only) off
+        t0 = time.perf_counter()
+        ref_args = resolve_poly_paths(build_parser(layer0_preset=True).parse_args(
+            ["--key-mode", "host", "--seed", str(seed)]))
+        self.feature, self.attention = FeatureMajorPrefillLayout(), AttentionPairLayout()
+        self.config = Llama3CKKSConfig.from_json(ref_args.config)
+        settings = resolve_settings(ref_args, self.config)
+        self.schedule = layer_schedule(ref_args, settings)
+        self.approx = ApproximationConfig(rmsnorm_path=ref_args.rms_coeffs, silu_path=ref_args.silu_coeffs,
+                                          softmax_path=ref_args.softmax_coeffs)
+        self.model = Llama3Model(config=self.config, num_layers=1, feature_layout=self.feature,
+                                 attention_layout=self.attention)
+        self.hidden, self.weights = _synthetic_inputs(int(ref_args.seed), layout=self.feature,
+                                                      attention_layout=self.attention)
+        self.rope_theta = float(getattr(ref_args, "rope_theta", 500000.0) or 500000.0)
+        rotations = self.model.required_rotations(
+            self.schedule, bootstrap_deep_level_budget=(3, 3) if self.schedule.softmax_main_deep_bootstrap else None)
+        self.context = _create_context(self.config, rotations, auto_load_keys=settings.auto_load_keys)
+        self.inputs = _encrypt_hidden(self.hidden, context=self.context, layout=self.feature,
+                                      input_level=settings.input_level)
+        self.bootstrap = prepare_bootstrap_operator(self.context, self.schedule)
+        self.mask = _np.ones(int(self.feature.seq_len), dtype=bool)
+        self._stream_cls = DoubleBufferedLayerStream
+        self.rotation_keys = len(rotations)
+        self.setup_seconds = time.perf_counter() - t0
+
+    def layers(self):
+        return self._stream_cls(loader=None, synthetic_weights=self.weights, approx_config=self.approx,
+                                config=self.config, feature_layout=self.feature, attention_layout=self.attention,
+                                num_layers=1, rope_theta=self.rope_theta)
+
+    def forward(self, inputs=None):
+        return self.model.forward(self.hidden, crypto_context=self.context,
+                                  input_ciphers=self.inputs if inputs is None else inputs, layers=self.layers(),
+                                  bootstrap_operator=self.bootstrap, schedule=self.schedule, refresh_first_layer=False,
+                                  attention_token_valid_mask=self.mask)
+
+    def check(self, result) -> dict:
+        """Decrypted layer output against the reference's own plaintext model of the same layer (its polynomial
+        approximations, Alg2 softmax; ``llama3fhe/approx/layer.py:592-767``)."""
+        from llama3fhe.application.client import decrypt_hidden
+        from llama3fhe.approx.layer import poly_prefill_layer_numpy
+
+        fhe = decrypt_hidden(result.ciphers, crypto_context=self.context, layout=self.feature)
+        layer = next(iter(self.layers()))
+        want = poly_prefill_layer_numpy(self.hidden, weights=layer.weights, approximations=layer.approximations,
+                                        attention_layout=self.attention, layer_idx=0, rope_theta=self.rope_theta,
+                                        use_alg2_softmax=True, token_valid_mask=self.mask).hidden
+        err = np.abs(np.asarray(fhe, dtype=np.float64) - np.asarray(want, dtype=np.float64))
+        scale = float(np.max(np.abs(want)))
+        return {"max_abs_err": float(err.max()), "mean_abs_err": float(err.mean()), "max_abs_ref": scale,
+                "max_rel_err": float(err.max() / scale) if scale else None}
+
+
+def run_layer(args) -> None:
+    """BASELINE config 3 (see _LayerSetup): ``value`` = device seconds of one encrypted decoder layer with the 16
+    input ciphertexts resident in HBM (CUDA events around each step on the launching stream, synchronised on both
+    sides); ``e2e`` = the same through the public call with the input ciphertexts copied from pinned host memory and
+    the output ciphertexts copied back inside every timed step.  The working set (keys, encoded weight chunks of
+    GB each) is far above the 126 MB L2."""
+    import torch
+
+    from holmes_b200 import _lib
+    from holmes_b200 import fhe as F
+
+    torch.cuda.set_device(0)
+    setup = _LayerSetup(seed=int(args.seed))
+    steps, warm = max(1, args.steps), max(0, args.warmup)
+    F.OPTIMER.enabled = False
+    for _ in range(warm):
+        setup.forward()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    clocks.ready()
+    n0 = ctypes_launches(_lib)
+    times, result = [], None
+    for _ in range(steps):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        a.record()
+        result = setup.forward()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b) / 1e3)
+    launches = (ctypes_launches(_lib) - n0) // steps
+    ck = clocks.stop()
+    # end to end: input ciphertexts from pinned host memory, outputs back to pinned host memory, every step
+    host_in = [[c.cv[k].cpu().pin_memory() for k in range(2)] for c in setup.inputs]
+    dev_in = tuple(c.cipher_like([torch.empty_like(c.cv[0]), torch.empty_like(c.cv[1])]) for c in setup.inputs)
+    h2d = sum(int(t.numel()) * 8 for pair in host_in for t in pair)
+    e2e_steps = max(1, min(steps, args.e2e_steps))
+    e2e_times, d2h = [], 0
+    for _ in range(e2e_steps):
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for src, dst in zip(host_in, dev_in):
+            dst.cv[0].copy_(src[0], non_blocking=True)
+            dst.cv[1].copy_(src[1], non_blocking=True)
+        out = setup.forward(dev_in)
+        outs = [c.cv[k][:, :int(c.state.cur_limbs)].to("cpu", non_blocking=False) for c in out.ciphers
+                for k in range(2)]
+        b.record()
+        torch.cuda.synchronize()
+        d2h = sum(int(t.numel()) * 8 for t in outs)
+        e2e_times.append(a.elapsed_time(b) / 1e3)
+    check = setup.check(result) if args.check else None
+    v = statistics.median(times)
+    line = {"metric": LAYER_METRIC, "value": round(v, 4), "unit": "s", "n_gpus": 1, "steps": steps, "warmup": warm,
+            "ms_per_step": round(v * 1e3, 1), "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+            "dtype": "u64 (RNS residues, 59/60-bit primes)",
+            "data": "synthetic (the reference's seeded one-layer preset: weights ~N(0, 0.002^2), hidden ~N(0, 0.01^2))",
+            "config": {"workload": "BASELINE config 3: one Llama-3-8B decoder layer, encrypted prefill of 128 tokens, "
+                                   "1 B200 -- the reference's own layer graph (llama3fhe TransformerLayer.forward / "
+                                   "graph.prefill.evaluate, run_layer0 synthetic preset) on libholmes_cuda",
+                       "geometry": "hidden 4096, 32 q / 8 kv heads x 128, MLP 14336, 128 tokens in 16 FM ciphertexts",
+                       "ckks": f"N=2^16, {setup.context.context.L} limbs, dnum 5, 59/60-bit",
+                       "rotation_keys": setup.rotation_keys, "keys": "generated on first use, trimmed to their level",
+                       "l2": "working set (keys, encoded weight chunks, bootstrap constants) >> 126 MB L2"},
+            "gpu_launches": int(launches), "clocks": ck,
+            "e2e": {"value": round(statistics.median(e2e_times), 4), "unit": "s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+            "setup_s": round(setup.setup_seconds, 1), "step_times_s": [round(t, 3) for t in times]}
+    if check is not None:
+        line["parity_vs_reference_poly_model"] = check
+    print(json.dumps(line), flush=True)
+
+
+def ctypes_launches(lib) -> int:
+    import ctypes as _ct
+
+    n = _ct.c_ulonglong()
+    lib.call("holmes_launch_count", _ct.byref(n))
+    return int(n.value)
+
+
 def run_primitives(args) -> None:
     """BASELINE config 2, the RNS-CKKS primitive sweep: N = 2^16, ~50-bit primes, dnum 3 (alpha = K = 12),
     L = 1..36 active limbs, residues uniform in [0, q_i) (seed 0).  Per L: batched forward / inverse NTT,
@@ -821,7 +998,7 @@ def run_silu(args) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--workload", choices=("linear", "bootstrap", "primitives", "silu"), default="linear")
+    ap.add_argument("--workload", choices=("linear", "layer", "bootstrap", "primitives", "silu"), default="linear")
     ap.add_argument("--boot-batch", type=int, default=8)
     ap.add_argument("--boot-iterations", type=int, default=1, help="2 = Meta-BTS correction")
     ap.add_argument("--kernel", default=None, help="profile one kernel family (see run_kernel)")
@@ -835,6 +1012,8 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
     ap.add_argument("--cpu-rows", type=int, default=128, help="diagonal rows in the CPU baseline's sample")
     ap.add_argument("--no-check", dest="check", action="store_false")
+    ap.add_argument("--seed", type=int, default=26081461, help="seed of the layer workload's synthetic preset")
+    ap.add_argument("--e2e-steps", type=int, default=3, help="end-to-end steps of the layer workload")
     ap.add_argument("--vs-ref", action="store_true",
                     help="with --kernel mac|encode: time the reference's in-tree kernel beside the engine's")
     args = ap.parse_args()
@@ -842,6 +1021,8 @@ def main() -> None:
         run_vs_ref(args)
     elif args.kernel:
         run_kernel(args)
+    elif args.workload == "layer" and args.impl != "reference":
+        run_layer(args)
     elif args.workload == "bootstrap":
         run_bootstrap(args)
     elif args.workload == "primitives":

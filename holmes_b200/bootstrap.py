@@ -495,6 +495,7 @@ def bootstrap(ct: F.Cipher, ctx, program: BootstrapProgram) -> F.Cipher:
     for lvl in range(len(program.c2s)):
         offsets, pt = program.diagonal_plaintexts("c2s", lvl, int(y.state.cur_limbs))
         y = linear_level(y, offsets, pt)
+    x_c2s_scale = y.state.scaling_factor
     conj = F.homo_rotate(y, ctx.M - 1, ctx)
     re = F.homo_add(y, conj, ctx)
     im = F.homo_mul_i(F.homo_sub(conj, y, ctx), ctx)
@@ -502,10 +503,18 @@ def bootstrap(ct: F.Cipher, ctx, program: BootstrapProgram) -> F.Cipher:
     im = eval_mod(im, program)
     z = F.homo_add(re, F.homo_mul_i(im, ctx), ctx)
     # S2C's constant assumes the message at the nominal scale: z carries the input's message at scale
-    # S_z Delta / m_scale.  The first S2C level also multiplies by rho = s_in / that, so the output lands on the
-    # input's own scale s_in (rho is within a few 2^-20 of 1; the diagonals absorb it, no level is spent).
+    # S_z Delta / m_scale.  The first S2C level also multiplies by rho = Delta / that, so the output lands exactly on
+    # the context's fixed scale Delta, whatever scale the input arrived at (the reference's fixed-scale contexts,
+    # scale_mode "fixed": every refresh restarts the scale bookkeeping at Delta, so the small per-level drift of
+    # exactly tracked scales -- it doubles with every squaring -- cannot pile up from one refresh to the next).  For an
+    # input at Delta, rho is within a few 2^-20 of 1; the diagonals absorb it, no level is spent.
+    target = float(ctx.scale)
     m_scale = s_in * k_pre * 2.0 ** program.cf / float(ctx.q(1))
-    rho = s_in / (float(z.state.scaling_factor) * float(ctx.scale) / m_scale)
+    rho = target / (float(z.state.scaling_factor) * float(ctx.scale) / m_scale)
+    if not (math.isfinite(rho) and rho > 0):
+        raise ValueError(f"bootstrap scale bookkeeping failed for the {program.n}-slot program: input scale {s_in!r} "
+                         f"at {int(ct.state.cur_limbs)} limbs, CoeffsToSlots output scale {x_c2s_scale!r}, EvalMod "
+                         f"output scale {z.state.scaling_factor!r} at {int(z.state.cur_limbs)} limbs")
     # exact integer part of the SlotsToCoeffs constant, applied without a level (message and noise alike): the
     # program's share, and the power of two that keeps rho * (per-level factor) encodable when the input arrives at a
     # scale well above its nominal one
@@ -519,7 +528,7 @@ def bootstrap(ct: F.Cipher, ctx, program: BootstrapProgram) -> F.Cipher:
         offsets, pt = program.diagonal_plaintexts("s2c", lvl, int(z.state.cur_limbs), rho if lvl == 0 else 1.0)
         z = linear_level(z, offsets, pt)
     z = drop_to(z, program.output_limbs)
-    z.state = F.CipherState(int(z.state.cur_limbs), 1, s_in)
+    z.state = F.CipherState(int(z.state.cur_limbs), 1, target)
     return z
 
 
@@ -554,7 +563,7 @@ def with_correction(cipher: F.Cipher, ctx, once, iterations: int, precision_bits
     inv = F.encode_scalar(1.0 / float(1 << int(precision_bits)), cur_limbs=cur, scale_degree=1,
                           scaling_factor=float(ctx.q(cur - 1)), context=ctx)
     out = F.homo_mul_scalar_rescale(corrected, inv, ctx)
-    out.state = out.state.replace(scaling_factor=cipher.state.scaling_factor)
+    out.state = out.state.replace(scaling_factor=first.state.scaling_factor)
     return out
 
 

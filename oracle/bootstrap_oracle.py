@@ -169,7 +169,7 @@ class OracleBootstrap:
         j0, j1 = o.mul_i(im[:2])
         z = self._add(re, (j0, j1, im[2]))
         m_scale = s_in * k_pre * 2.0 ** prog.cf / float(self.pr.q[1])
-        rho = s_in / (float(z[2]) * self.delta / m_scale)
+        rho = self.delta / (float(z[2]) * self.delta / m_scale)   # output at the fixed scale Delta
         c_int = int(getattr(prog, "s2c_int", 1))
         while rho * prog.s2c_scale > 3.0 and c_int < (1 << 40):   # holmes_b200.bootstrap.DIAGONAL_LIMIT
             rho /= 2.0
@@ -181,7 +181,7 @@ class OracleBootstrap:
         for k, lvl in enumerate(prog.s2c):
             z = self.linear(z, lvl, prog.s2c_scale * (rho if k == 0 else 1.0))
         z = self.drop(z, prog.output_limbs)
-        return z[0], z[1], s_in
+        return z[0], z[1], self.delta
 
     def refresh(self, ct, s_in, iterations=1, precision_bits=8):
         """One bootstrap or the Meta-BTS correction (same steps as holmes_b200.bootstrap.with_correction)."""
@@ -205,7 +205,7 @@ class OracleBootstrap:
             err = self.bootstrap(sub(first_down, (ct[0][:cur_in], ct[1][:cur_in])), s_in)
             lim = err[0].shape[0]
             d0, d1 = sub((first[0][:lim], first[1][:lim]), err)
-            return d0, d1, s_in
+            return d0, d1, self.delta
         f = 1 << int(precision_bits)
         fs = mul_int(first, f)
         first_down = (fs[0][:cur_in], fs[1][:cur_in])
@@ -215,7 +215,7 @@ class OracleBootstrap:
         c0, c1 = sub((fs[0][:lim], fs[1][:lim]), (err[0][:lim], err[1][:lim]))
         k = int(round(1.0 / float(f) * float(self.pr.q[lim - 1])))
         d0, d1 = o.rescale(mul_int((c0, c1), k))
-        return d0, d1, s_in
+        return d0, d1, self.delta
 
 
 __all__ = ["OracleBootstrap"]
