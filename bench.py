@@ -752,27 +752,83 @@ class _LayerSetup:
                 "max_rel_err": float(err.max() / scale) if scale else None}
 
 
+def layer_cpu_rates(rows: int = 16, hoisted: int = 2, rotations: int = 1) -> dict:
+    """CPU seconds per algorithmic byte of each kernel family, from the CPU restatement (oracle/, OpenMP, all host
+    cores) on a bounded sample at the production chain's 13-limb linear level: the bytes of a sampled operation are
+    counted with the same formulas the engine's per-family timers use (holmes_b200.fhe.OPTIMER)."""
+    cpu = cpu_baseline(rows=rows, hoisted=hoisted, rotations=rotations)
+    po = cpu["per_op_s"]
+    N, cur, K, beta, slots = 1 << LOG_N, CUR_LIMBS, 8, 2, 1 << (LOG_N - 1)
+    ks_bytes = (1 * (beta * (cur + K) + 2 * cur) + 2 * beta * (cur + K) + cur) * N * 8
+    modup_bytes = (cur + beta * (cur + K)) * N * 8
+    enc_bytes = 2 * slots * 16 + slots * 16 + cur * N * 8
+    mac_bytes = (1 + 2 + 2) * cur * N * 8
+    rates = {"keyswitch": po["hoisted_ks"] / ks_bytes, "modup": po["modup"] / modup_bytes,
+             "encode_ntt": po["encode_row"] / enc_bytes, "fft_special": po["encode_row"] / enc_bytes,
+             "bsgs_mac": po["mac_row_input"] / mac_bytes}
+    rates["rescale"] = rates["keyswitch"]
+    return {"rates_s_per_byte": rates, "cores": cpu["cores"], "per_op_s": po,
+            "sample": f"{rows} rows encoded + MAC'd, 1 ModUp, {hoisted} hoisted + {rotations} full key switches at "
+                      f"N=2^16 / 13 of 38 limbs"}
+
+
+def layer_cpu_estimate(volume: dict, rates: dict) -> float:
+    """Seconds of the CPU restatement for one layer: every family's algorithmic bytes in the layer times that
+    family's CPU seconds per byte (families without a sampled rate use the key switch's)."""
+    r = rates["rates_s_per_byte"]
+    return float(sum(v["bytes"] * r.get(name, r["keyswitch"]) for name, v in volume.items()))
+
+
+LAYER_VOLUME = os.path.join(ROOT, "profiles", "layer_op_volume.json")
+
+
 def run_layer(args) -> None:
     """BASELINE config 3 (see _LayerSetup): ``value`` = device seconds of one encrypted decoder layer with the 16
     input ciphertexts resident in HBM (CUDA events around each step on the launching stream, synchronised on both
     sides); ``e2e`` = the same through the public call with the input ciphertexts copied from pinned host memory and
     the output ciphertexts copied back inside every timed step.  The working set (keys, encoded weight chunks of
-    GB each) is far above the 126 MB L2."""
+    GB each) is far above the 126 MB L2.  After the timed steps, one more step runs with the engine's per-family
+    CUDA-event timers on (untimed) for the kernel breakdown and the roofline line.
+
+    With N > 1 GPUs (torchrun) every rank runs its own replica of the layer on its own GPU: the reference's one-layer
+    graph is a single-process program (its multi-GPU layer is the station chain of bench/t2_layer.py), so the N-GPU
+    line reports the slowest replica's latency with per-GPU work fixed ("scaling": "weak", replicas only)."""
     import torch
+    import torch.distributed as dist
 
     from holmes_b200 import _lib
     from holmes_b200 import fhe as F
 
-    torch.cuda.set_device(0)
-    setup = _LayerSetup(seed=int(args.seed))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=900), device_id=torch.device("cuda", local))
+    setup = _LayerSetup(seed=int(args.seed) + rank)
     steps, warm = max(1, args.steps), max(0, args.warmup)
     F.OPTIMER.enabled = False
     for _ in range(warm):
         setup.forward()
     torch.cuda.synchronize()
-    clocks = ClockSampler(torch.cuda.current_device())
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def slowest(seconds: float) -> float:
+        if world == 1:
+            return seconds
+        t = torch.tensor([seconds], dtype=torch.float64, device=f"cuda:{local}")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    clocks = ClockSampler(local)
     clocks.start()
     clocks.ready()
+    barrier()
     n0 = ctypes_launches(_lib)
     times, result = [], None
     for _ in range(steps):
@@ -782,7 +838,7 @@ def run_layer(args) -> None:
         result = setup.forward()
         b.record()
         torch.cuda.synchronize()
-        times.append(a.elapsed_time(b) / 1e3)
+        times.append(slowest(a.elapsed_time(b) / 1e3))
     launches = (ctypes_launches(_lib) - n0) // steps
     ck = clocks.stop()
     # end to end: input ciphertexts from pinned host memory, outputs back to pinned host memory, every step
@@ -791,6 +847,7 @@ def run_layer(args) -> None:
     h2d = sum(int(t.numel()) * 8 for pair in host_in for t in pair)
     e2e_steps = max(1, min(steps, args.e2e_steps))
     e2e_times, d2h = [], 0
+    barrier()
     for _ in range(e2e_steps):
         torch.cuda.synchronize()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -804,11 +861,45 @@ def run_layer(args) -> None:
         b.record()
         torch.cuda.synchronize()
         d2h = sum(int(t.numel()) * 8 for t in outs)
-        e2e_times.append(a.elapsed_time(b) / 1e3)
-    check = setup.check(result) if args.check else None
+        e2e_times.append(slowest(a.elapsed_time(b) / 1e3))
+    # kernel-family breakdown: one more (untimed) step with the per-family CUDA-event timers
+    F.OPTIMER.reset()
+    F.OPTIMER.enabled = True
+    setup.forward()
+    F.OPTIMER.enabled = False
+    ops = F.OPTIMER.summary()
+    check = setup.check(result) if args.check and rank == 0 else None
+    barrier()
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
     v = statistics.median(times)
-    line = {"metric": LAYER_METRIC, "value": round(v, 4), "unit": "s", "n_gpus": 1, "steps": steps, "warmup": warm,
-            "ms_per_step": round(v * 1e3, 1), "higher_is_better": False, "scaling": "strong", "vs_baseline": None,
+    hbm, kind = peaks()
+    dominant = max(ops.items(), key=lambda kv: kv[1]["ms"]) if ops else None
+    roofline = None
+    if dominant:
+        name, d = dominant
+        per_launch_s = d["ms"] / 1e3 / d["launches"]
+        achieved = d["bytes"] / d["launches"] / per_launch_s / 1e9
+        roofline = {"bound": "hbm", "kernel": name, "achieved": round(achieved, 1), "peak": hbm, "peak_kind": kind,
+                    "unit": "GB/s", "frac": round(achieved / hbm, 4), "traffic": measured_traffic(name),
+                    "algorithmic_bytes_per_launch": d["bytes"] // d["launches"],
+                    "avg_launch_ms": round(d["ms"] / d["launches"], 4),
+                    "share_of_step": round(d["ms"] / 1e3 / v, 4)}
+    volume = {k: {"launches": val["launches"], "bytes": val["bytes"], "ms": round(val["ms"], 2)}
+              for k, val in ops.items()}
+    cpu = None
+    if args.cpu_baseline and world == 1:
+        rates = layer_cpu_rates()
+        cpu = {"value": round(layer_cpu_estimate(volume, rates), 1), "unit": "s", "cores": rates["cores"],
+               "kind": "port",
+               "sample": rates["sample"] + "; scaled to the layer by every kernel family's algorithmic bytes in one "
+                                           "layer (CPU seconds per byte of that family times its bytes)",
+               "per_op_s": rates["per_op_s"]}
+    line = {"metric": LAYER_METRIC, "value": round(v, 4), "unit": "s", "n_gpus": world, "steps": steps,
+            "warmup": warm, "ms_per_step": round(v * 1e3, 1), "higher_is_better": False,
+            "scaling": "weak" if world > 1 else "strong", "vs_baseline": None,
             "dtype": "u64 (RNS residues, 59/60-bit primes)",
             "data": "synthetic (the reference's seeded one-layer preset: weights ~N(0, 0.002^2), hidden ~N(0, 0.01^2))",
             "config": {"workload": "BASELINE config 3: one Llama-3-8B decoder layer, encrypted prefill of 128 tokens, "
@@ -816,14 +907,51 @@ def run_layer(args) -> None:
                                    "graph.prefill.evaluate, run_layer0 synthetic preset) on libholmes_cuda",
                        "geometry": "hidden 4096, 32 q / 8 kv heads x 128, MLP 14336, 128 tokens in 16 FM ciphertexts",
                        "ckks": f"N=2^16, {setup.context.context.L} limbs, dnum 5, 59/60-bit",
+                       "parallelism": f"replicas x{world} (one independent layer per GPU)" if world > 1 else "1 GPU",
                        "rotation_keys": setup.rotation_keys, "keys": "generated on first use, trimmed to their level",
                        "l2": "working set (keys, encoded weight chunks, bootstrap constants) >> 126 MB L2"},
-            "gpu_launches": int(launches), "clocks": ck,
+            "roofline": roofline,
+            "kernels": {k: {"launches": val["launches"], "ms_per_step": round(val["ms"], 2)} for k, val in ops.items()},
+            "cpu_baseline": cpu, "gpu_launches": int(launches), "clocks": ck,
             "e2e": {"value": round(statistics.median(e2e_times), 4), "unit": "s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps},
             "setup_s": round(setup.setup_seconds, 1), "step_times_s": [round(t, 3) for t in times]}
     if check is not None:
         line["parity_vs_reference_poly_model"] = check
+    if args.write_volume:
+        with open(LAYER_VOLUME, "w", encoding="utf-8") as f:
+            json.dump({"what": "per kernel family of one config-3 layer on the engine: launches, algorithmic bytes "
+                               "and device ms (holmes_b200.fhe.OPTIMER)", "families": volume}, f, indent=1)
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_reference_layer(args) -> None:
+    """The reference arm for the layer workload: EasyFHE (the reference's engine) is not distributed, so the CPU
+    restatement stands in -- sampled per-family CPU rates (all host cores) times the per-family algorithmic bytes of
+    one layer (profiles/layer_op_volume.json, recorded from the engine's run of the same layer)."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    with open(LAYER_VOLUME, encoding="utf-8") as f:
+        volume = json.load(f)["families"]
+    for _ in range(min(1, args.warmup)):
+        layer_cpu_rates(rows=2, hoisted=1, rotations=1)
+    vals, rates = [], None
+    for _ in range(max(1, min(args.steps, 3))):
+        rates = layer_cpu_rates()
+        vals.append(layer_cpu_estimate(volume, rates))
+    v = round(statistics.median(vals), 1)
+    line = {"impl": "reference", "metric": LAYER_METRIC, "value": v, "unit": "s",
+            "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "u64 (RNS residues)",
+            "data": "synthetic (seeded)",
+            "config": {"workload": "BASELINE config 3 layer, estimated on the CPU restatement of the reference's "
+                                   "engine (EasyFHE is not distributed and cannot run here)"},
+            "cpu_baseline": {"value": v, "unit": "s", "cores": rates["cores"], "kind": "port",
+                             "sample": rates["sample"] + "; scaled by the layer's per-family algorithmic bytes "
+                                                         "(profiles/layer_op_volume.json)"},
+            "e2e": {"value": v, "unit": "s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
 
@@ -1014,6 +1142,8 @@ def main() -> None:
     ap.add_argument("--no-check", dest="check", action="store_false")
     ap.add_argument("--seed", type=int, default=26081461, help="seed of the layer workload's synthetic preset")
     ap.add_argument("--e2e-steps", type=int, default=3, help="end-to-end steps of the layer workload")
+    ap.add_argument("--write-volume", action="store_true",
+                    help="layer workload: record the per-family volume of one layer in profiles/layer_op_volume.json")
     ap.add_argument("--vs-ref", action="store_true",
                     help="with --kernel mac|encode: time the reference's in-tree kernel beside the engine's")
     args = ap.parse_args()
@@ -1021,8 +1151,8 @@ def main() -> None:
         run_vs_ref(args)
     elif args.kernel:
         run_kernel(args)
-    elif args.workload == "layer" and args.impl != "reference":
-        run_layer(args)
+    elif args.workload == "layer":
+        run_reference_layer(args) if args.impl == "reference" else run_layer(args)
     elif args.workload == "bootstrap":
         run_bootstrap(args)
     elif args.workload == "primitives":

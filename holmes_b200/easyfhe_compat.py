@@ -223,9 +223,34 @@ def _build() -> dict:
             "easyfhe.bs.openfhe": openfhe, "easyfhe.cuda": torch.cuda, "easyfhe.multiprocessing": torch.multiprocessing}
 
 
-def install(replace_packers: bool = True) -> types.ModuleType:
+def batched_bootstrap(ciphers, crypto_context, program) -> list:
+    """The reference's batched-refresh hook (``BootstrapOperator.batch_backend``, ``callable(ciphers, crypto_context,
+    program) -> list``; ``llama3fhe/operators/nonlinear/bootstrap.py:183-188, 484-560``): ciphertexts of one state go
+    through one bootstrap as a batch, so every key switch of C2S / EvalMod / S2C is shared (each key read once per
+    batch, not once per ciphertext).  Per ciphertext the arithmetic is the single refresh's, word for word."""
+    ciphers = list(ciphers)
+    batch = _fhe.pack_cipher_batch(ciphers)
+    out = _bootstrap.bootstrap(batch, crypto_context, program)
+    return list(_fhe.unpack_cipher_batch(out))
+
+
+def _install_batch_backend() -> None:
+    """Set the reference's ``BootstrapOperator.batch_backend`` when its package is importable (the reference's own
+    GPU benches install theirs the same way, ``bench/cmp/holmes_batch_bs.py``)."""
+    try:
+        import importlib
+
+        mod = importlib.import_module("llama3fhe.operators.nonlinear.bootstrap")
+    except ImportError:
+        return
+    if getattr(mod.BootstrapOperator, "batch_backend", None) is None:
+        mod.BootstrapOperator.batch_backend = staticmethod(batched_bootstrap)
+
+
+def install(replace_packers: bool = True, batch_bootstrap: bool = True) -> types.ModuleType:
     """Register the engine as ``easyfhe`` (and, with ``replace_packers``, the CUDA packers in place of the
-    reference's Triton module).  Idempotent; returns the ``easyfhe`` module object."""
+    reference's Triton module; with ``batch_bootstrap``, :func:`batched_bootstrap` as the reference's batched-refresh
+    hook once its package is importable).  Idempotent; returns the ``easyfhe`` module object."""
     current = sys.modules.get("easyfhe")
     if current is not None and getattr(current, "__holmes_b200__", False):
         return current
@@ -242,6 +267,8 @@ def install(replace_packers: bool = True) -> types.ModuleType:
         parent = sys.modules.get("llama3fhe.operators.linear")
         if parent is not None:
             parent.gpu_packer = sys.modules[_PACKER]
+    if batch_bootstrap:
+        _install_batch_backend()
     return mods["easyfhe"]
 
 
