@@ -724,6 +724,17 @@ class _LayerSetup:
         self.rotation_keys = len(rotations)
         self.setup_seconds = time.perf_counter() - t0
 
+    def release_transients(self) -> None:
+        """Dead temporaries back to the allocator between steps (the reference runner's
+        ``_release_transient_device_memory``, ``llama3fhe/application/session.py``)."""
+        import gc
+
+        import torch
+
+        gc.collect()
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+
     def layers(self):
         return self._stream_cls(loader=None, synthetic_weights=self.weights, approx_config=self.approx,
                                 config=self.config, feature_layout=self.feature, attention_layout=self.attention,
@@ -833,7 +844,8 @@ def run_layer(args) -> None:
     times, result = [], None
     for _ in range(steps):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        torch.cuda.synchronize()
+        result = None
+        setup.release_transients()      # outside the timed interval, as the reference's runner does between samples
         a.record()
         result = setup.forward()
         b.record()
@@ -849,7 +861,7 @@ def run_layer(args) -> None:
     e2e_times, d2h = [], 0
     barrier()
     for _ in range(e2e_steps):
-        torch.cuda.synchronize()
+        setup.release_transients()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         for src, dst in zip(host_in, dev_in):
@@ -1147,6 +1159,9 @@ def main() -> None:
     ap.add_argument("--vs-ref", action="store_true",
                     help="with --kernel mac|encode: time the reference's in-tree kernel beside the engine's")
     args = ap.parse_args()
+    if args.workload == "layer":
+        # the layer's many short-lived multi-GB temporaries fragment a fixed-segment pool
+        os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
     if args.kernel and args.vs_ref:
         run_vs_ref(args)
     elif args.kernel:

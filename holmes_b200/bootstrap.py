@@ -223,7 +223,9 @@ class BootstrapProgram:
                              f"{float(np.max(np.abs(rows))):.4g} at scale 2^{math.log2(scale):.2f} "
                              f"(factor {factor:.4g}, adjust {float(adjust):.4g}): {exc}") from None
         pt = F.Plaintext([pv], F.CipherState(cur, 1, scale), self.n, False, len(offsets), ctx)
-        if self.cache_mode in ("plain", "both"):
+        # a level carrying a per-call factor (SlotsToCoeffs' rho) is encoded per call: caching it would keep one
+        # entry per refresh
+        if self.cache_mode in ("plain", "both") and float(adjust) == 1.0:
             self._plain[key] = (offsets, pt)
         return offsets, pt
 

@@ -10,8 +10,9 @@ check their decoded outputs against the reference's NumPy oracles at the referen
 
 Deselected: ``test_linear.py::test_linear_weight_uses_constant_bundle_cache_stage`` builds an EasyFHE context on
 ``device="cpu"``; this engine has no CPU backend and refuses such a context.  Eight decode tests of
-``test_decode_fm.py`` stop inside the reference's own decode graph, before any engine call (its production PairFold
-decode refuses their small layouts and legacy KV caches).
+``test_decode_fm.py`` fail in the reference's own code: six are refused by its production PairFold decode (small
+layouts, legacy KV caches) before any engine call, and two read a legacy C-form KV cache that a prefill with the
+default PairFold packing does not emit.
 """
 import os
 import subprocess
@@ -34,15 +35,17 @@ FILES = [
 ]
 DESELECT = {
     "test_linear.py": ["test_linear_weight_uses_constant_bundle_cache_stage"],
-    # these stop in the reference's own decode graph before any engine call: the production PairFold decode
-    # refuses the tests' small layouts and legacy KV caches (llama3fhe/graph/decode.py:398, model.py:475)
+    # these fail in the reference's own code: its production PairFold decode refuses the tests' small layouts and
+    # legacy KV caches (llama3fhe/graph/decode.py:398, model.py:475), and a prefill with the default PairFold decode
+    # packing emits no legacy C-form cache for the two emit tests to read
     "test_decode_fm.py": ["test_decode_layer_with_attention_matches_numpy",
                           "test_decode_model_next_token_kv_cache_matches_numpy",
                           "test_decode_model_prefix_bundle_matches_poly_reference",
                           "test_decode_model_next_n_tokens_kv_cache_matches_numpy",
                           "test_prefill128_decode_n_tokens_kv_cache_matches_numpy",
                           "test_prefill128_decode_hidden4096_with_bootstrap",
-                          "test_prefill_layer0_emits_c_cache_for_decode"],
+                          "test_prefill_layer0_emits_c_cache_for_decode",
+                          "test_prefill_two_layer_emits_c_cache_for_decode"],
 }
 
 
@@ -58,6 +61,8 @@ def test_reference_gpu_file_passes_on_engine(name):
     for test in DESELECT.get(name, []):
         cmd += ["--deselect", f"{rel}::{test}"]
     res = subprocess.run(cmd, cwd=ROOT, capture_output=True, text=True, timeout=900)
-    tail = "\n".join((res.stdout + res.stderr).strip().splitlines()[-30:])
+    lines = (res.stdout + res.stderr).strip().splitlines()
+    errors = [ln for ln in lines if ln.startswith("E ")][:20]
+    tail = "\n".join(errors + lines[-12:])
     assert res.returncode == 0, f"{name}:\n{tail}"
     assert " passed" in tail and " failed" not in tail, tail
