@@ -47,15 +47,17 @@ CUR_LIMBS = 13
 DIM, LANES, INPUTS = 4096, 8, 16
 
 
-def measured_traffic(family: str):
-    """DRAM bytes per launch of a kernel family from the committed ncu summary (profiles/traffic.txt), or None."""
+def measured_traffic(family: str, algorithmic_bytes: int):
+    """DRAM bytes per launch of a kernel family: the committed ncu capture (profiles/traffic.txt: measured bytes and
+    algorithmic bytes of the captured launch) scaled by this run's algorithmic bytes per launch (the family's traffic
+    grows in proportion to the items and limbs it processes), or None."""
     try:
         with open(os.path.join(ROOT, "profiles", "traffic.txt"), encoding="utf-8") as f:
             for line in f:
                 parts = line.split()
-                if len(parts) >= 2 and not line.startswith("#") and parts[0] == family:
-                    return int(parts[1])
-    except OSError:
+                if len(parts) >= 3 and not line.startswith("#") and parts[0] == family:
+                    return int(round(int(parts[1]) / int(parts[2]) * int(algorithmic_bytes)))
+    except (OSError, ValueError, ZeroDivisionError):
         pass
     return None
 
@@ -315,7 +317,7 @@ def run_engine(args) -> None:
             achieved = d["bytes"] / d["launches"] / per_launch_s / 1e9
             roofline = {"bound": "hbm", "kernel": name, "achieved": round(achieved, 1), "peak": hbm,
                         "peak_kind": kind, "unit": "GB/s", "frac": round(achieved / hbm, 4),
-                        "traffic": measured_traffic(name),
+                        "traffic": measured_traffic(name, d["bytes"] // d["launches"]),
                         "algorithmic_bytes_per_launch": d["bytes"] // d["launches"],
                         "avg_launch_ms": round(d["ms"] / d["launches"], 4),
                         "share_of_step": round(d["ms"] / args.steps / ms, 4)}
@@ -841,6 +843,7 @@ def run_layer(args) -> None:
     clocks.ready()
     barrier()
     n0 = ctypes_launches(_lib)
+    mem0 = torch.cuda.memory_stats()
     times, result = [], None
     for _ in range(steps):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -852,6 +855,11 @@ def run_layer(args) -> None:
         torch.cuda.synchronize()
         times.append(slowest(a.elapsed_time(b) / 1e3))
     launches = (ctypes_launches(_lib) - n0) // steps
+    mem1 = torch.cuda.memory_stats()
+    memory = {"peak_allocated_gb": round(mem1.get("allocated_bytes.all.peak", 0) / 1e9, 1),
+              "peak_reserved_gb": round(mem1.get("reserved_bytes.all.peak", 0) / 1e9, 1),
+              **{k: (mem1.get(k, 0) - mem0.get(k, 0)) // steps
+                 for k in ("num_alloc_retries", "num_device_alloc", "num_device_free", "num_sync_all_streams")}}
     ck = clocks.stop()
     # end to end: input ciphertexts from pinned host memory, outputs back to pinned host memory, every step
     host_in = [[c.cv[k].cpu().pin_memory() for k in range(2)] for c in setup.inputs]
@@ -895,7 +903,8 @@ def run_layer(args) -> None:
         per_launch_s = d["ms"] / 1e3 / d["launches"]
         achieved = d["bytes"] / d["launches"] / per_launch_s / 1e9
         roofline = {"bound": "hbm", "kernel": name, "achieved": round(achieved, 1), "peak": hbm, "peak_kind": kind,
-                    "unit": "GB/s", "frac": round(achieved / hbm, 4), "traffic": measured_traffic(name),
+                    "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                    "traffic": measured_traffic(name, d["bytes"] // d["launches"]),
                     "algorithmic_bytes_per_launch": d["bytes"] // d["launches"],
                     "avg_launch_ms": round(d["ms"] / d["launches"], 4),
                     "share_of_step": round(d["ms"] / 1e3 / v, 4)}
@@ -927,7 +936,8 @@ def run_layer(args) -> None:
             "cpu_baseline": cpu, "gpu_launches": int(launches), "clocks": ck,
             "e2e": {"value": round(statistics.median(e2e_times), 4), "unit": "s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps},
-            "setup_s": round(setup.setup_seconds, 1), "step_times_s": [round(t, 3) for t in times]}
+            "setup_s": round(setup.setup_seconds, 1), "step_times_s": [round(t, 3) for t in times],
+            "device_memory_per_step": memory}
     if check is not None:
         line["parity_vs_reference_poly_model"] = check
     if args.write_volume:

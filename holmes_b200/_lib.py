@@ -59,6 +59,7 @@ SIGNATURES = {
     "holmes_rescale_postop": [p, p, i64, p, i64, i32, i32, p, i32, p, i64, p, p],
     "holmes_modraise": [p, p, i64, p, i64, i32, i32, p, p],
     "holmes_add_const": [p, p, p, p, i32, i32, i64, i64, p],
+    "holmes_const_op": [p, i32, p, p, p, i32, i32, i64, i64, p],
     "holmes_rescale_noalloc":[p, p, i64, p, i64, i32, i32, p],
     "holmes_modup": [p, p, i64, i32, i32, p, i64, p, p],
     "holmes_peer_alloc": [ctypes.c_ulonglong, p],
@@ -112,8 +113,16 @@ def check(rc: int, what: str) -> None:
         raise HolmesError(f"{what} failed: {kind} {rc}")
 
 
+_FNS: dict = {}
+
+
 def call(name: str, *args) -> None:
-    check(getattr(load(), name)(*args), name)
+    fn = _FNS.get(name)
+    if fn is None:
+        fn = _FNS[name] = getattr(load(), name)
+    rc = fn(*args)
+    if rc != 0:
+        check(rc, name)
 
 
 def ptr_array(ptrs) -> ctypes.Array:

@@ -303,8 +303,7 @@ def generate(context, spec: BootstrapSpec) -> BootstrapProgram:
 # N = 2^16, and EvalMod multiplies that by the q0 * I overflow term it removes.)
 
 
-def _stream():
-    return torch.cuda.current_stream().cuda_stream
+_stream = F._stream
 
 
 def scale_table(top_limbs: int, top_scale: float, ctx) -> dict:
@@ -318,11 +317,8 @@ def mul_int(ct: F.Cipher, k: int) -> F.Cipher:
     """ct * k for an integer k, no rescale: the message is multiplied by k at the same declared scale."""
     ctx = ct.context
     cur = int(ct.state.cur_limbs)
-    res = torch.tensor([int(k) % ctx.q(i) for i in range(cur)], dtype=torch.uint64, device=ctx.device)
     out = F._new_cipher(ctx, ct.batch_size, cur, ct.state, ct.slots)
-    for c in range(2):
-        _lib.call("holmes_mul_const", ctx.handle, ct.cv[c].data_ptr(), res.data_ptr(), out.cv[c].data_ptr(),
-                  ct.batch_size, cur, F._item_stride(ct.cv[c]), F._item_stride(out.cv[c]), _stream())
+    F.const_cv(ctx, F.CONST_MUL, ct.cv[:2], ctx.residues(k, cur), out.cv, ct.batch_size, cur)
     return out
 
 
@@ -330,11 +326,8 @@ def int_mul_rescale(ct: F.Cipher, k: int, new_scale: float) -> F.Cipher:
     """ct * k (an integer) then rescale; the result is declared at ``new_scale``."""
     ctx = ct.context
     cur = int(ct.state.cur_limbs)
-    res = torch.tensor([int(k) % ctx.q(i) for i in range(cur)], dtype=torch.uint64, device=ctx.device)
     out = F._new_cipher(ctx, ct.batch_size, cur, F.CipherState(cur, 2, None), ct.slots)
-    for c in range(2):
-        _lib.call("holmes_mul_const", ctx.handle, ct.cv[c].data_ptr(), res.data_ptr(), out.cv[c].data_ptr(),
-                  ct.batch_size, cur, F._item_stride(ct.cv[c]), F._item_stride(out.cv[c]), _stream())
+    F.const_cv(ctx, F.CONST_MUL, ct.cv[:2], ctx.residues(k, cur), out.cv, ct.batch_size, cur)
     r = F.rescale(out, ctx)
     r.state = F.CipherState(cur - 1, 1, float(new_scale))
     return r
@@ -347,23 +340,49 @@ def mul_scalar_to(ct: F.Cipher, value: float, target: float) -> F.Cipher:
     return int_mul_rescale(ct, k, target)
 
 
+def _drop_view(ct: F.Cipher, limbs: int) -> F.Cipher:
+    """The first ``limbs`` limbs of ``ct`` (a view, scale kept): a modulus drop costs no copy."""
+    if int(ct.state.cur_limbs) == int(limbs):
+        return ct
+    return F.Cipher([c[:, :int(limbs)] for c in ct.cv[:2]], ct.state.replace(cur_limbs=int(limbs)), ct.slots, False,
+                    ct.batch_size, ct.context)
+
+
 def adjust(ct: F.Cipher, limbs: int, S: dict) -> F.Cipher:
-    """Drop ``ct`` to ``limbs`` limbs, landing on the canonical scale S[limbs]."""
-    while int(ct.state.cur_limbs) > int(limbs):
-        cur = int(ct.state.cur_limbs)
-        ct = mul_scalar_to(ct, 1.0, S[cur - 1])
-    return ct
+    """Drop ``ct`` to ``limbs`` limbs, landing on the canonical scale S[limbs]: a modulus drop to ``limbs`` + 1 limbs
+    (no arithmetic), then one integer multiply and rescale by q_limbs, k = round(S[limbs] q_limbs / scale)."""
+    if int(ct.state.cur_limbs) <= int(limbs):
+        return ct
+    return mul_scalar_to(_drop_view(ct, int(limbs) + 1), 1.0, S[int(limbs)])
+
+
+def lin_comb(terms: list, S: dict) -> F.Cipher:
+    """sum_i c_i t_i over (ciphertext, coefficient) pairs on canonical scales, with ONE rescale: every t_i is dropped
+    (modulus only) to lim + 1 limbs, lim = the lowest term's limbs - 1, and multiply-accumulated with the integer
+    k_i = round(c_i S[lim] q_lim / scale_i), so that the rescale by q_lim lands the sum on S[lim]."""
+    first = terms[0][0]
+    ctx = first.context
+    lim = min(int(t.state.cur_limbs) for t, _ in terms) - 1
+    target = S[lim]
+    q = float(ctx.q(lim))
+    batch = first.batch_size
+    acc = F._new_cipher(ctx, batch, lim + 1, F.CipherState(lim + 1, 2, None), first.slots)
+    for i, (t, c) in enumerate(terms):
+        k = int(round(float(c) * target * q / float(t.state.scaling_factor)))
+        F.const_cv(ctx, F.CONST_MUL if i == 0 else F.CONST_AXPY, [x[:, :lim + 1] for x in t.cv[:2]],
+                   ctx.residues(k, lim + 1), acc.cv, batch, lim + 1)
+    r = F.rescale(acc, ctx)
+    r.state = F.CipherState(lim, 1, target)
+    return r
 
 
 def add_scalar(ct: F.Cipher, value: float) -> F.Cipher:
     ctx = ct.context
     cur = int(ct.state.cur_limbs)
     v = int(round(float(value) * float(ct.state.scaling_factor)))
-    k = torch.tensor([v % ctx.q(i) for i in range(cur)], dtype=torch.uint64, device=ctx.device)
-    out = F.Cipher([torch.empty_like(ct.cv[0][:, :cur]), ct.cv[1][:, :cur].clone()], ct.state, ct.slots, False,
-                   ct.batch_size, ctx)
-    _lib.call("holmes_add_const", ctx.handle, ct.cv[0].data_ptr(), k.data_ptr(), out.cv[0].data_ptr(), ct.batch_size,
-              cur, F._item_stride(ct.cv[0]), F._item_stride(out.cv[0]), _stream())
+    out = F._new_cipher(ctx, ct.batch_size, cur, ct.state, ct.slots)
+    F.const_cv(ctx, F.CONST_ADD, ct.cv[:1], ctx.residues(v, cur), out.cv[:1], ct.batch_size, cur)
+    out.cv[1].copy_(ct.cv[1][:, :cur])
     return out
 
 
@@ -421,7 +440,8 @@ def linear_level(ct: F.Cipher, offsets, pt: F.Plaintext) -> F.Cipher:
 
 
 def _chebyshev(w: F.Cipher, coeffs: np.ndarray, S: dict) -> F.Cipher:
-    """sum_k c_k T_k(w) with T_2k = 2 T_k^2 - 1, T_2k+1 = 2 T_k T_k+1 - T_1 (canonical scales throughout)."""
+    """sum_k c_k T_k(w) with T_2k = 2 T_k^2 - 1, T_2k+1 = 2 T_k T_k+1 - T_1 (canonical scales throughout); the sum
+    over k is one multiply-accumulate chain and one rescale (``lin_comb``)."""
     d = len(coeffs) - 1
     T: dict = {1: w}
     low: dict = {}
@@ -442,17 +462,8 @@ def _chebyshev(w: F.Cipher, coeffs: np.ndarray, S: dict) -> F.Cipher:
             T[k] = F.homo_sub(p, t1_at(int(p.state.cur_limbs)), p.context)
         return T[k]
 
-    terms = []
-    for k in range(1, d + 1):
-        if abs(coeffs[k]) < 1e-18:
-            continue
-        tk = get(k)
-        terms.append(mul_scalar_to(tk, float(coeffs[k]), S[int(tk.state.cur_limbs) - 1]))
-    lim = min(int(t.state.cur_limbs) for t in terms)
-    acc = adjust(terms[0], lim, S)
-    for t in terms[1:]:
-        acc = F.homo_add(acc, adjust(t, lim, S), acc.context)
-    return add_scalar(acc, float(coeffs[0]))
+    terms = [(get(k), float(coeffs[k])) for k in range(1, d + 1) if abs(coeffs[k]) >= 1e-18]
+    return add_scalar(lin_comb(terms, S), float(coeffs[0]))
 
 
 def eval_mod(x: F.Cipher, program: BootstrapProgram) -> F.Cipher:
@@ -482,10 +493,10 @@ def bootstrap(ct: F.Cipher, ctx, program: BootstrapProgram) -> F.Cipher:
     raise_to = program.raise_to_limbs
     items = x.batch_size
     raised = F._new_cipher(ctx, items, raise_to, F.CipherState(raise_to, 1, float(ctx.scale)), x.slots)
-    scratch = ctx.workspace("modraise", items * ctx.N)
-    for c in range(2):
-        _lib.call("holmes_modraise", ctx.handle, x.cv[c].data_ptr(), F._item_stride(x.cv[c]), raised.cv[c].data_ptr(),
-                  F._item_stride(raised.cv[c]), raise_to, items, scratch.data_ptr(), _stream())
+    scratch = ctx.workspace("modraise", 2 * items * ctx.N)
+    for (src, n_src, si), (dst, _, so) in F._runs(items, x.cv[:2], raised.cv):
+        _lib.call("holmes_modraise", ctx.handle, src.data_ptr(), si, dst.data_ptr(), so, raise_to, n_src,
+                  scratch.data_ptr(), _stream())
     y = raised
     # Sparse slots (n < N/2): after ModRaise the overflow q0 I fills every coefficient, not only the multiples of
     # gap = N/(2n) that carry the n-slot message.  Summing the rotations by n j (j < gap), the automorphisms that

@@ -241,6 +241,12 @@ int holmes_modraise(void* ctx, const uint64_t* in, long long in_stride, uint64_t
   return modraise(*C(ctx), in, in_stride, out, out_stride, raise, comps, scratch, S(stream));
 }
 
+int holmes_const_op(void* ctx, int op, const uint64_t* a, const uint64_t* host_consts, uint64_t* out, int items,
+                    int limbs, long long a_item, long long out_item, void* stream) {
+  if (!ctx || !a || !host_consts || !out) return -1;
+  return const_op(*C(ctx), op, a, host_consts, out, items, limbs, a_item, out_item, S(stream));
+}
+
 int holmes_add_const(void* ctx, const uint64_t* a, const uint64_t* consts, uint64_t* out, int items, int limbs,
                      long long a_item, long long out_item, void* stream) {
   if (!ctx || !a || !consts || !out) return -1;

@@ -17,6 +17,9 @@
 #pragma once
 #include <atomic>
 #include <cstdint>
+#include <map>
+#include <mutex>
+#include <utility>
 #include <cuda_runtime.h>
 
 namespace holmes {
@@ -27,6 +30,22 @@ inline std::atomic<unsigned long long>& launch_counter() {
   return c;
 }
 inline void count_launch() { launch_counter().fetch_add(1, std::memory_order_relaxed); }
+
+// Raise a kernel's dynamic shared memory limit once per device: the attribute stays set on the function for the
+// context, so later launches skip the driver call.
+inline cudaError_t set_smem_once(const void* fn, int bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<int, const void*>, int> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> g(mu);
+  auto it = done.find({dev, fn});
+  if (it != done.end() && it->second >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) done[{dev, fn}] = bytes;
+  return e;
+}
 
 typedef uint64_t u64;
 typedef int64_t i64;

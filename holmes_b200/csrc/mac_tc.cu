@@ -385,7 +385,7 @@ int bsgs_mac_tc(ModSrc ms, u64* res, const InPtrs& in, long long bstride, int nb
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   const int spi = (nb + kKS - 1) / kKS;
   auto go = [&](auto kernel) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, TcGeom::SMEM);
+    cudaError_t e = set_smem_once((const void*)kernel, TcGeom::SMEM);
     if (e != cudaSuccess) return (int)e;
     count_launch();
     kernel<<<sms, TcGeom::THREADS, TcGeom::SMEM, st>>>(res, in, bstride, nb, inputs, groups, pts, pstride, limbs,

@@ -166,6 +166,49 @@ int add_const(const HolmesCtx& c, const u64* a, const u64* consts, u64* out, int
   return (int)cudaGetLastError();
 }
 
+// Per-limb constants passed by value in the launch's parameter space: a scalar product or sum needs no device
+// copy of its residues (an upload from pageable host memory would make the host wait for the stream).
+struct ConstRow {
+  u64 v[HOLMES_CONST_LIMBS];
+};
+// op CONST_ADD: o = a + k; CONST_MUL: o = a * k; CONST_AXPY: o = o + a * k (mod q_limb); two words per thread.
+__global__ void k_const_op(int op, const u64* __restrict__ a, u64* __restrict__ o, int items, int limbs, long long ai,
+                           long long oi, int log_n, const Mod* __restrict__ mods, const __grid_constant__ ConstRow k) {
+  const size_t per_item = (size_t)limbs << log_n;
+  const size_t total = (size_t)items * per_item / 2;
+  for (size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x; t < total; t += (size_t)gridDim.x * blockDim.x) {
+    const size_t w = 2 * t;
+    const unsigned wl = (unsigned)(w >> log_n);
+    const int item = (int)(wl / (unsigned)limbs), limb = (int)(wl - (unsigned)item * limbs);
+    const size_t r = ((size_t)limb << log_n) | (w & (((size_t)1 << log_n) - 1));
+    const Mod m = mods[limb];
+    const u64 c = k.v[limb];
+    const ulonglong2 x = *reinterpret_cast<const ulonglong2*>(a + item * ai + r);
+    ulonglong2* dst = reinterpret_cast<ulonglong2*>(o + item * oi + r);
+    ulonglong2 z;
+    if (op == CONST_ADD) {
+      z = make_ulonglong2(add_mod(x.x, c, m.q), add_mod(x.y, c, m.q));
+    } else if (op == CONST_MUL) {
+      z = make_ulonglong2(mul_mod(x.x, c, m), mul_mod(x.y, c, m));
+    } else {
+      const ulonglong2 y = *dst;
+      z = make_ulonglong2(add_mod(y.x, mul_mod(x.x, c, m), m.q), add_mod(y.y, mul_mod(x.y, c, m), m.q));
+    }
+    *dst = z;
+  }
+}
+int const_op(const HolmesCtx& c, int op, const u64* a, const u64* host_consts, u64* out, int items, int limbs,
+             long long a_item, long long o_item, cudaStream_t st) {
+  if (op < CONST_ADD || op > CONST_AXPY || limbs < 1 || limbs > c.T || limbs > HOLMES_CONST_LIMBS || items < 1)
+    return -2;
+  if ((a_item | o_item) & 1) return -2;   // 16-byte accesses
+  ConstRow k;
+  for (int l = 0; l < limbs; ++l) k.v[l] = host_consts[l];
+  const size_t work = (size_t)items * limbs * c.n / 2;
+  k_const_op<<<grid_for(work, 256), 256, 0, st>>>(op, a, out, items, limbs, a_item, o_item, c.log_n, c.d_mod, k);
+  return (int)cudaGetLastError();
+}
+
 // --------------------------------------------------------------------------------------------- BSGS MAC
 // res[c][g][i][limb][j] = sum_b pts[g nb + b][limb][j] * baby_i[b][c][limb][j]  (mod q_limb)
 // (semantics of the reference's mac_multi, bench/cmp/kernels/holmes_mac.cu:1-13, 116-190).
@@ -592,7 +635,7 @@ template <int IW, int GPT>
 static int launch_mac3(u64* res, const InPtrs& in, long long bstride, int nb, int inputs, int groups, const u64* pts,
                        long long pstride, int limbs, const ModSrc& ms, int log_n, int n, cudaStream_t st) {
   using Geo = M3Geom<IW, GPT>;
-  cudaError_t e = cudaFuncSetAttribute(k_bsgs_mac3<IW, GPT>, cudaFuncAttributeMaxDynamicSharedMemorySize, Geo::SMEM);
+  cudaError_t e = set_smem_once((const void*)k_bsgs_mac3<IW, GPT>, Geo::SMEM);
   if (e != cudaSuccess) return (int)e;
   dim3 grid((unsigned)((n / 32) * ((inputs + IW - 1) / IW)), (unsigned)limbs, (unsigned)((groups + kMacGG - 1) / kMacGG));
   count_launch();
@@ -640,7 +683,7 @@ int bsgs_mac(ModSrc ms, u64* res, const u64* const* c0s, const u64* const* c1s,
   for (int i = 0; i < inputs; ++i) aligned = aligned && ((uintptr_t)in.c0[i] % 16 == 0) && ((uintptr_t)in.c1[i] % 16 == 0);
   if (!aligned || getenv("HOLMES_MAC_V2")) {
     const int smem = 2 * kMacStageWords * 8;
-    cudaError_t e = cudaFuncSetAttribute(k_bsgs_mac2, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = set_smem_once((const void*)k_bsgs_mac2, smem);
     if (e != cudaSuccess) return (int)e;
     count_launch();
     k_bsgs_mac2<<<grid, 256, smem, st>>>(res, in, bstride, nb, inputs, groups, pts, pstride, limbs, ms, log_n);
@@ -821,7 +864,7 @@ int fft_special_inv(const HolmesCtx& c, double* z, long long row_stride, int row
   const int bs = slots < kFftBlock ? slots : kFftBlock;
   const int threads = bs / 2 < 512 ? (bs / 2 < 32 ? 32 : bs / 2) : 512;
   const size_t smem = (size_t)bs * sizeof(double2);
-  HOLMES_CUDA_TRY(cudaFuncSetAttribute(k_fft_special_inv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  HOLMES_CUDA_TRY(set_smem_once((const void*)k_fft_special_inv, (int)smem));
   count_launch();
   k_fft_special_inv<<<rows, threads, smem, st>>>(z, row_stride, slots, log_slots,
                                                  reinterpret_cast<const double2*>(c.d_fft_tw));

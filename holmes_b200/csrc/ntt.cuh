@@ -290,7 +290,7 @@ template <class K, class... Args>
 inline cudaError_t launch_ntt(K kernel, int logn_cl, int threads, int smem, int polys, cudaStream_t st,
                               Args... args) {
   if (polys <= 0) return cudaSuccess;
-  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  cudaError_t e = set_smem_once((const void*)kernel, smem);
   if (e != cudaSuccess) return e;
   const int cl = 1 << logn_cl;
   cudaLaunchConfig_t cfg = {};

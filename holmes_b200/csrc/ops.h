@@ -83,6 +83,11 @@ int modraise(const HolmesCtx& c, const u64* in, long long in_stride, u64* out, l
              int comps, u64* scratch, cudaStream_t st);
 
 // out[item][l][n] = a[item][l][n] + consts[l] (a constant polynomial added in the NTT domain)
+// scalar op with per-limb constants read from HOST memory (passed by value to the kernel)
+constexpr int HOLMES_CONST_LIMBS = 64;
+enum { CONST_ADD = 0, CONST_MUL = 1, CONST_AXPY = 2 };
+int const_op(const HolmesCtx& c, int op, const u64* a, const u64* host_consts, u64* out, int items, int limbs,
+             long long a_item, long long o_item, cudaStream_t st);
 int add_const(const HolmesCtx& c, const u64* a, const u64* consts, u64* out, int items, int limbs, long long a_item,
               long long o_item, cudaStream_t st);
 

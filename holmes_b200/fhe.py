@@ -18,6 +18,7 @@ device buffers.  There is no CPU path: without the library or a CUDA device thes
 """
 from __future__ import annotations
 
+import collections
 import dataclasses
 import gc
 import math
@@ -144,7 +145,13 @@ class CKKSContextSpec:
     relinearization: bool = True
 
 
+_RAW_STREAM = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def _stream() -> int:
+    """The current CUDA stream of the current device, as the C ABI's ``void* stream``."""
+    if _RAW_STREAM is not None:
+        return _RAW_STREAM(torch._C._cuda_getDevice())
     return torch.cuda.current_stream().cuda_stream
 
 
@@ -198,6 +205,7 @@ class Context:
         self._requested = set(int(r) for r in spec.rotations)
         self._work: dict = {}
         self._flag = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._consts: collections.OrderedDict = collections.OrderedDict()
         self._enc_counter = 0
         self.key_bytes = 0
 
@@ -217,6 +225,32 @@ class Context:
         """P = product of the special primes, modulo q_0 .. q_{cur-1}."""
         P = math.prod(self.moduli[self.L:self.L + self.K])
         return [P % self.moduli[i] for i in range(int(cur))]
+
+    def device_u64(self, rows) -> torch.Tensor:
+        """A small uint64 table on this context's device, without a stream synchronisation: the copy starts from
+        pinned host memory, and tables seen before come from a bounded cache (per-level constants recur in every
+        bootstrap and polynomial)."""
+        arr = np.ascontiguousarray(np.asarray(rows, dtype=np.uint64))
+        key = (arr.shape, arr.tobytes()) if arr.nbytes <= 65536 else None
+        if key is not None:
+            hit = self._consts.get(key)
+            if hit is not None:
+                self._consts.move_to_end(key)
+                return hit
+        dev = torch.from_numpy(arr).pin_memory().to(self.device, non_blocking=True)
+        if key is not None:
+            self._consts[key] = dev
+            if len(self._consts) > 8192:
+                self._consts.popitem(last=False)
+        return dev
+
+    def p_mod_q_dev(self, cur: int) -> torch.Tensor:
+        return self.device_u64(self.p_mod_q(cur))
+
+    def residues(self, value: int, cur: int) -> list:
+        """Canonical residues of an integer modulo q_0 .. q_{cur-1}."""
+        v = int(value)
+        return [v % q for q in self.moduli[:int(cur)]]
 
     def beta(self, cur: int) -> int:
         return -(-int(cur) // self.alpha)
@@ -295,6 +329,7 @@ class Context:
             torch.cuda.synchronize(self.device)
             self._keys.clear()
             self._work.clear()
+            self._consts.clear()
             self.__dict__.pop("_ones_rows", None)
             _lib.call("holmes_ctx_destroy", self.handle)
             self.handle = None
@@ -492,6 +527,63 @@ def _ew(ctx: Context, op: int, a: torch.Tensor, b: torch.Tensor | None, out: tor
               _stream())
 
 
+def _run(cv, batch: int):
+    """(first component, items, item stride) when the components lie one after another at one item stride (a cipher
+    from ``_new_cipher``, or limb views of one), so that one launch over ``len(cv) * batch`` items serves them all;
+    else None."""
+    t0 = cv[0]
+    st = int(t0.stride(0))
+    base = t0.data_ptr()
+    for c in range(1, len(cv)):
+        t = cv[c]
+        if int(t.stride(0)) != st or t.data_ptr() != base + c * batch * st * 8:
+            return None
+    return t0, len(cv) * batch, st
+
+
+def _runs(batch: int, *cvs):
+    """Per launch, one (tensor, items, item stride) per operand: a single launch when every operand's components
+    form a run (``_run``), else one launch per component."""
+    runs = [_run(cv, batch) for cv in cvs]
+    if all(r is not None for r in runs):
+        return [runs]
+    return [[(cv[c], batch, int(cv[c].stride(0))) for cv in cvs] for c in range(len(cvs[0]))]
+
+
+def _ew_cv(ctx: Context, op: int, a_cv, b_cv, out_cv, batch: int, limbs: int) -> None:
+    """``_ew`` over every component (op 3, negation, takes no ``b_cv``)."""
+    if b_cv is None:
+        for (a, items, ai), (o, _, oi) in _runs(batch, a_cv, out_cv):
+            _lib.call("holmes_elementwise", ctx.handle, op, a.data_ptr(), 0, o.data_ptr(), items, int(limbs), ai, 0, oi,
+                      _stream())
+        return
+    for (a, items, ai), (b, _, bi), (o, _, oi) in _runs(batch, a_cv, b_cv, out_cv):
+        _lib.call("holmes_elementwise", ctx.handle, op, a.data_ptr(), b.data_ptr(), o.data_ptr(), items, int(limbs), ai,
+                  bi, oi, _stream())
+
+
+CONST_ADD, CONST_MUL, CONST_AXPY = 0, 1, 2
+_CONST_LIMBS = 64
+
+
+def const_cv(ctx: Context, op: int, a_cv, residues, out_cv, batch: int, limbs: int) -> None:
+    """Per-limb scalar op over every component: CONST_ADD out = a + k, CONST_MUL out = a * k, CONST_AXPY out += a * k
+    (``residues`` the host list k[0 .. limbs-1]; passed by value to the kernel, no device copy)."""
+    limbs = int(limbs)
+    if limbs > _CONST_LIMBS:   # beyond the launch-parameter table: the device-table kernels
+        if op == CONST_AXPY:
+            raise ValueError(f"scalar multiply-accumulate supports at most {_CONST_LIMBS} limbs")
+        k = ctx.device_u64(list(residues)[:limbs])
+        name = "holmes_add_const" if op == CONST_ADD else "holmes_mul_const"
+        for (a, items, ai), (o, _, oi) in _runs(batch, a_cv, out_cv):
+            _lib.call(name, ctx.handle, a.data_ptr(), k.data_ptr(), o.data_ptr(), items, limbs, ai, oi, _stream())
+        return
+    host = (_lib.ctypes.c_uint64 * limbs)(*[int(v) for v in list(residues)[:limbs]])
+    for (a, items, ai), (o, _, oi) in _runs(batch, a_cv, out_cv):
+        _lib.call("holmes_const_op", ctx.handle, int(op), a.data_ptr(), host, o.data_ptr(), items, limbs, ai, oi,
+                  _stream())
+
+
 def _ctx(ctx) -> Context:
     return ctx.context if hasattr(ctx, "context") and isinstance(ctx.context, Context) else ctx
 
@@ -513,6 +605,9 @@ def _add_sub(a: Cipher, b: Cipher, ctx, op: int, what: str) -> Cipher:
     _check_same(_drop_limbs(a, cur), _drop_limbs(b, cur), what)
     na, nb = len(a.cv), len(b.cv)
     out = _new_cipher(ctx, a.batch_size, cur, low.state, a.slots, max(na, nb))
+    if na == nb:
+        _ew_cv(ctx, op, a.cv, b.cv, out.cv, a.batch_size, cur)
+        return out
     for c in range(max(na, nb)):
         if c < na and c < nb:
             _ew(ctx, op, a.cv[c], b.cv[c], out.cv[c], cur)
@@ -539,11 +634,10 @@ def homo_mul_i(a: Cipher, ctx, negative: bool = False) -> Cipher:
     _valid(ctx, a, "homo_mul_i")
     cur = int(a.state.cur_limbs)
     out = _new_cipher(ctx, a.batch_size, cur, a.state, a.slots, len(a.cv))
-    for c in range(len(a.cv)):
-        _lib.call("holmes_mul_i", ctx.handle, a.cv[c].data_ptr(), out.cv[c].data_ptr(), a.batch_size, cur,
-                  _item_stride(a.cv[c]), _item_stride(out.cv[c]), _stream())
-        if negative:
-            _ew(ctx, 3, out.cv[c], None, out.cv[c], cur)
+    for (x, items, xi), (o, _, oi) in _runs(a.batch_size, a.cv, out.cv):
+        _lib.call("holmes_mul_i", ctx.handle, x.data_ptr(), o.data_ptr(), items, cur, xi, oi, _stream())
+    if negative:
+        _ew_cv(ctx, 3, out.cv, None, out.cv, a.batch_size, cur)
     return out
 
 
@@ -557,11 +651,11 @@ def rescale(a: Cipher, ctx) -> Cipher:
     sf = None if a.state.scaling_factor is None else float(a.state.scaling_factor) / ql
     state = CipherState(cur - 1, max(1, int(a.state.scale_degree) - 1), sf)
     out = _new_cipher(ctx, a.batch_size, cur - 1, state, a.slots)
-    scratch = ctx.workspace("rescale", a.batch_size * ctx.N)
+    scratch = ctx.workspace("rescale", 2 * a.batch_size * ctx.N)
     tok = OPTIMER.start("rescale")
-    for c in range(2):
-        _lib.call("holmes_rescale", ctx.handle, a.cv[c].data_ptr(), _item_stride(a.cv[c]), out.cv[c].data_ptr(),
-                  _item_stride(out.cv[c]), cur, a.batch_size, scratch.data_ptr(), _stream())
+    for (x, items, xi), (o, _, oi) in _runs(a.batch_size, a.cv[:2], out.cv):
+        _lib.call("holmes_rescale", ctx.handle, x.data_ptr(), xi, o.data_ptr(), oi, cur, items, scratch.data_ptr(),
+                  _stream())
     OPTIMER.stop(tok, 2 * a.batch_size * (2 * cur - 1) * ctx.N * 8)
     return out
 
@@ -666,7 +760,7 @@ def fast_rotate(a: Cipher, rotations, ctx, output_ext: bool = False) -> Cipher:
     for b, off in enumerate(offsets):
         g = ctx.galois(off)
         if g == 1:   # (P c0, P c1): P is 0 modulo the special primes
-            pm = torch.tensor(ctx.p_mod_q(cur), dtype=torch.uint64, device=ctx.device)
+            pm = ctx.p_mod_q_dev(cur)
             for c in range(2):
                 block.cv[c][b, cur:].zero_()
                 _lib.call("holmes_mul_const", ctx.handle, a.cv[c][:1, :cur].data_ptr(), pm.data_ptr(),
@@ -745,8 +839,14 @@ def pack_cipher_batch(ciphers) -> Cipher:
                 or c.slots != first.slots or c.is_ext != first.is_ext or len(c.cv) != len(first.cv):
             raise ValueError("pack_cipher_batch: ciphers differ in level, scale degree, slots or form")
     limbs = cur + (int(first.context.K) if first.is_ext else 0)
-    cv = [torch.cat([c.cv[k][:, :limbs] for c in ciphers], dim=0) for k in range(len(first.cv))]
-    return first.cipher_like(cv, batch_size=int(cv[0].shape[0]))
+    total = sum(int(c.batch_size) for c in ciphers)
+    first_t = first.cv[0]
+    # the components one after another in one storage: later element-wise launches cover them in one go
+    storage = torch.empty((len(first.cv), total, limbs, int(first_t.shape[2])), dtype=first_t.dtype,
+                          device=first_t.device)
+    for k in range(len(first.cv)):
+        torch.cat([c.cv[k][:int(c.batch_size), :limbs] for c in ciphers], dim=0, out=storage[k])
+    return first.cipher_like([storage[k] for k in range(len(first.cv))], batch_size=total)
 
 
 def unpack_cipher_batch(batch: Cipher) -> tuple:
@@ -833,7 +933,7 @@ def giant_double_hoist(ctx: Context, res: torch.Tensor, giant_offset: int) -> tu
     G, items, cur = int(res.shape[1]), int(res.shape[2]), int(res.shape[3])
     K, N = ctx.K, ctx.N
     ext = torch.empty((2, G, items, cur + K, N), dtype=torch.uint64, device=ctx.device)
-    pm = torch.tensor(ctx.p_mod_q(cur), dtype=torch.uint64, device=ctx.device)
+    pm = ctx.p_mod_q_dev(cur)
     for c in range(2):
         ext[c, 0, :, cur:].zero_()
         _lib.call("holmes_mul_const", ctx.handle, res[c, 0].data_ptr(), pm.data_ptr(), ext[c, 0].data_ptr(), items,
@@ -1048,8 +1148,12 @@ class EncodedScalar:
     def residues(self, ctx, limbs: int) -> torch.Tensor:
         if self.table is not None:
             raise ValueError("a weight table has no single residue vector")
-        return torch.tensor([self.integer % ctx.q(i) for i in range(int(limbs))], dtype=torch.uint64,
-                            device=ctx.device)
+        return ctx.device_u64(self.residue_list(ctx, limbs))
+
+    def residue_list(self, ctx, limbs: int) -> list:
+        if self.table is not None:
+            raise ValueError("a weight table has no single residue vector")
+        return ctx.residues(self.integer, limbs)
 
 
 def grouped_scalar_weighted_acc(batch: Cipher, table: EncodedScalar, ctx) -> Cipher:
@@ -1094,13 +1198,6 @@ def encode_scalar(value, cur_limbs: int, scale_degree: int = 1, scaling_factor: 
     return EncodedScalar(float(value), int(round(float(value) * sf)), CipherState(int(cur_limbs), int(scale_degree), sf))
 
 
-def _const_kernel(name: str, a: Cipher, k: torch.Tensor, out: Cipher, comps: range, ctx: Context) -> None:
-    cur = int(a.state.cur_limbs)
-    for c in comps:
-        _lib.call(name, ctx.handle, a.cv[c].data_ptr(), k.data_ptr(), out.cv[c].data_ptr(), a.batch_size, cur,
-                  _item_stride(a.cv[c]), _item_stride(out.cv[c]), _stream())
-
-
 def homo_mul_scalar(a: Cipher, scalar: EncodedScalar, ctx) -> Cipher:
     """a * scalar without rescale: the scale degrees and factors multiply."""
     ctx = _ctx(ctx)
@@ -1111,7 +1208,7 @@ def homo_mul_scalar(a: Cipher, scalar: EncodedScalar, ctx) -> Cipher:
         sf = float(a.state.scaling_factor) * float(scalar.state.scaling_factor)
     out = _new_cipher(ctx, a.batch_size, cur,
                       CipherState(cur, int(a.state.scale_degree) + int(scalar.state.scale_degree), sf), a.slots)
-    _const_kernel("holmes_mul_const", a, scalar.residues(ctx, cur), out, range(len(a.cv)), ctx)
+    const_cv(ctx, CONST_MUL, a.cv, scalar.residue_list(ctx, cur), out.cv, a.batch_size, cur)
     return out
 
 
@@ -1131,7 +1228,7 @@ def homo_add_scalar(a: Cipher, scalar, ctx) -> Cipher:
         raise ValueError("homo_add_scalar: the scalar's scale differs from the ciphertext's")
     out = a.cipher_like([torch.empty_like(a.cv[0][:, :cur])] + [c[:, :cur].clone() for c in a.cv[1:]],
                         state=a.state)
-    _const_kernel("holmes_add_const", a, scalar.residues(ctx, cur), out, range(1), ctx)
+    const_cv(ctx, CONST_ADD, a.cv[:1], scalar.residue_list(ctx, cur), out.cv[:1], a.batch_size, cur)
     return out
 
 
@@ -1237,8 +1334,7 @@ class ConstantBundle:
         cur = int(cur_limbs)
         sf = float(scaling_factor) if scaling_factor is not None else ctx.scale_at(cur)
         ints = [int(round(self.scalars[str(nm)] * sf)) for nm in names]
-        residues = torch.tensor([[v % ctx.q(i) for i in range(cur)] for v in ints], dtype=torch.uint64,
-                                device=ctx.device)
+        residues = ctx.device_u64([ctx.residues(v, cur) for v in ints])
         return types.SimpleNamespace(residues=residues, cur_limbs=cur, scale_degree=int(scale_degree),
                                      scaling_factor=sf)
 

@@ -473,7 +473,7 @@ class LinearOperator:
             lo, hi = shard[0] * B // shard[1], (shard[0] + 1) * B // shard[1]
         if lo == 0:
             if ext:   # baby 0 over Q u P: (P c0, P c1), zero on the special limbs
-                pm = torch.tensor(ctx.p_mod_q(cur), dtype=torch.uint64, device=ctx.device)
+                pm = ctx.p_mod_q_dev(cur)
                 for c, src in ((0, c0), (1, c1)):
                     storage[0, c, :, cur:].zero_()
                     _lib.call("holmes_mul_const", ctx.handle, src.data_ptr(), pm.data_ptr(), storage[0, c].data_ptr(),

@@ -202,7 +202,7 @@ def _leaf_table(leaves: list, basis_limbs: int, scale: float, ctx) -> "fhe.torch
     for leaf in leaves:
         ints = [int(round(float(w) * scale)) for w in leaf.weights]
         rows.append([[v % q for q in qs] for v in ints])
-    return fhe.torch.tensor(np.array(rows, dtype=np.uint64), dtype=fhe.torch.uint64, device=ctx.device)
+    return ctx.device_u64(np.array(rows, dtype=np.uint64))
 
 
 def _leaves(T: list, leaves: list, ctx) -> list:

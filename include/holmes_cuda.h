@@ -151,6 +151,13 @@ int holmes_modraise(void* ctx, const uint64_t* in, long long in_stride, uint64_t
  * (fhe.homo_add_scalar, operators/nonlinear/polynomial.py) */
 int holmes_add_const(void* ctx, const uint64_t* a, const uint64_t* consts, uint64_t* out, int items, int limbs,
                      long long a_item, long long out_item, void* stream);
+/* the same scalar arithmetic with the per-limb constants read from HOST memory at the call (copied into the
+ * launch's parameters, so no device copy and no stream synchronisation): op 0 out = a + k, op 1 out = a * k,
+ * op 2 out = out + a * k (mod q_l), k[l] canonical residues.  The scalar products and sums of EvalMod and of
+ * the polynomial evaluators (fhe.homo_mul_scalar / homo_add_scalar, operators/nonlinear/polynomial.py).
+ * limbs <= 64; a_item and out_item even.  Returns -2 on a bad op or size. */
+int holmes_const_op(void* ctx, int op, const uint64_t* a, const uint64_t* host_consts, uint64_t* out, int items,
+                    int limbs, long long a_item, long long out_item, void* stream);
 
 /* holmes_rescale without caller scratch, for callers that cannot allocate device memory (a runtime that
  * owns the whole pool, or a loop where cudaMalloc's device synchronisation is unacceptable).  No

@@ -49,9 +49,27 @@ class OracleBootstrap:
         return self.int_mul_rescale(ct, int(round(float(value) * target * q / float(ct[2]))), target)
 
     def adjust(self, ct, lim, S):
-        while ct[0].shape[0] > lim:
-            ct = self.mul_scalar_to(ct, 1.0, S[ct[0].shape[0] - 1])
-        return ct
+        # a modulus drop to lim + 1 limbs, then one integer multiply and rescale onto S[lim]
+        if ct[0].shape[0] <= lim:
+            return ct
+        return self.mul_scalar_to(self.drop(ct, lim + 1), 1.0, S[lim])
+
+    def lin_comb(self, terms, S):
+        # sum c_i t_i: every t_i dropped to lim + 1 limbs and multiplied by k_i = round(c_i S[lim] q_lim / s_i), the
+        # products summed, one rescale onto S[lim]
+        o = self.o
+        lim = min(t[0].shape[0] for t, _ in terms) - 1
+        target = S[lim]
+        q = float(self.pr.q[lim])
+        ids = self._ids(lim + 1)
+        acc = None
+        for t, c in terms:
+            k = int(round(float(c) * target * q / float(t[2])))
+            r = [k % self.pr.q[i] for i in range(lim + 1)]
+            m = (o.mul_scalar(t[0][:lim + 1], r, ids), o.mul_scalar(t[1][:lim + 1], r, ids))
+            acc = m if acc is None else (o.add(acc[0], m[0], ids), o.add(acc[1], m[1], ids))
+        d0, d1 = o.rescale(acc)
+        return d0, d1, target
 
     def add_scalar(self, ct, value):
         c0, c1, sf = ct
@@ -113,17 +131,8 @@ class OracleBootstrap:
                 T[k] = self._add(self._add(p, p), t1_at(p[0].shape[0]), sub=True)
             return T[k]
 
-        terms = []
-        for k in range(1, len(coeffs)):
-            if abs(coeffs[k]) < 1e-18:
-                continue
-            tk = get(k)
-            terms.append(self.mul_scalar_to(tk, float(coeffs[k]), S[tk[0].shape[0] - 1]))
-        lim = min(t[0].shape[0] for t in terms)
-        acc = self.adjust(terms[0], lim, S)
-        for t in terms[1:]:
-            acc = self._add(acc, self.adjust(t, lim, S))
-        return self.add_scalar(acc, float(coeffs[0]))
+        terms = [(get(k), float(coeffs[k])) for k in range(1, len(coeffs)) if abs(coeffs[k]) >= 1e-18]
+        return self.add_scalar(self.lin_comb(terms, S), float(coeffs[0]))
 
     def eval_mod(self, x):
         S = self.scale_table(x[0].shape[0], x[2])

@@ -81,3 +81,53 @@ def test_grouped_scalar_weighted_acc_matches_the_loop():
                 np.testing.assert_array_equal(host(acc.cv[c][g]), host(loop.cv[c][0, :cur]))
     finally:
         ctx.close()
+
+
+def test_const_op_abi_host_constants(env):
+    """holmes_const_op (per-limb constants by value from host memory): add, multiply and multiply-accumulate against the
+    oracle's modular arithmetic, over both components in one launch (a run of 2 x batch items) and component by
+    component (separate storages); limbs beyond the parameter table are refused."""
+    import ctypes
+
+    from holmes_b200 import _lib
+    from holmes_b200 import fhe as F
+
+    o, client, ctx = env
+    rng = np.random.default_rng(7)
+    cts = [client.encrypt(rng.normal(size=ctx.max_slots) * 0.3, cur_limbs=5, counter=40 + i) for i in range(3)]
+    src = F.pack_cipher_batch(cts)
+    n = src.batch_size
+    assert F._run(src.cv, n) is not None       # a packed batch is one run of 2 x n items
+    apart = F.Cipher([src.cv[0].clone(), src.cv[1].clone()], src.state, src.slots, False, n, ctx)
+    assert F._run(apart.cv, n) is None
+    ids = list(range(5))
+    k1 = [int(v) for v in rng.integers(0, 2 ** 62, 5, dtype=np.uint64)]
+    k1 = [v % ctx.q(i) for i, v in enumerate(k1)]
+    k2 = [(3 * v + 11) % ctx.q(i) for i, v in enumerate(k1)]
+    run = F._new_cipher(ctx, n, 5, src.state, src.slots)
+    F.const_cv(ctx, F.CONST_MUL, src.cv, k1, run.cv, n, 5)
+    split = F.Cipher([torch.empty_like(run.cv[0]), torch.empty_like(run.cv[1])], run.state, run.slots, False, n, ctx)
+    F.const_cv(ctx, F.CONST_MUL, apart.cv, k1, split.cv, n, 5)
+    F.const_cv(ctx, F.CONST_AXPY, src.cv, k2, run.cv, n, 5)
+    added = F._new_cipher(ctx, n, 5, src.state, src.slots)
+    F.const_cv(ctx, F.CONST_ADD, src.cv, k2, added.cv, n, 5)
+    for c in range(2):
+        for i in range(n):
+            x = host(src.cv[c][i, :5])
+            m1 = o.mul_scalar(x, k1, ids)
+            np.testing.assert_array_equal(host(split.cv[c][i]), m1)
+            np.testing.assert_array_equal(host(run.cv[c][i]), o.add(m1, o.mul_scalar(x, k2, ids), ids))
+            want = np.stack([(x[l].astype(object) + k2[l]) % ctx.q(l) for l in ids]).astype(np.uint64)
+            np.testing.assert_array_equal(host(added.cv[c][i]), want)
+    # rescale, add and multiply-by-i: one launch over the run and one per component give the same words
+    for fn in (lambda x: F.rescale(x, ctx), lambda x: F.homo_add(x, x, ctx), lambda x: F.homo_mul_i(x, ctx, True)):
+        a, b = fn(src), fn(apart)
+        for c in range(2):
+            np.testing.assert_array_equal(host(a.cv[c]), host(b.cv[c]))
+    r = F.rescale(src, ctx)
+    for c in range(2):
+        np.testing.assert_array_equal(host(r.cv[c][1]), o.rescale((host(src.cv[0][1, :5]), host(src.cv[1][1, :5])))[c])
+    host_k = (ctypes.c_uint64 * 65)(*([1] * 65))
+    rc = _lib.load().holmes_const_op(ctx.handle, 1, src.cv[0].data_ptr(), host_k, run.cv[0].data_ptr(), 1, 65,
+                                     F._item_stride(src.cv[0]), F._item_stride(run.cv[0]), F._stream())
+    assert rc == -2
