@@ -1,27 +1,28 @@
 #!/usr/bin/env python
-"""Benchmark of the Holmes linear hot path on B200.
+"""Benchmark of the Holmes hot path on B200.
 
-Workload (one "step"): one encrypted 4096 x 4096 complex weight page applied to the 16 input ciphertexts of a
+Default workload (``--workload layer``, BASELINE config 3; one "step"): one encrypted Llama-3-8B decoder layer, a
+128-token prefill on one B200 -- the reference's own one-layer application (``llama3fhe`` TransformerLayer.forward /
+graph.prefill.evaluate with the synthetic preset of its ``run_layer0.py``, installed unchanged in baseline/_ref) with
+every FHE operation on libholmes_cuda through the ``easyfhe`` compatibility layer: QKV / W_O / MLP projections (BSGS
+linear), attention with its softmax, RMSNorm and SiLU polynomials, and the bootstraps the reference's schedule places,
+at the production CKKS parameters (N = 2^16, 38 limbs of 59/60-bit primes, dnum 5).  ``value`` = device seconds per
+layer with the input ciphertexts resident in HBM; ``e2e`` = the same with the inputs copied from pinned host memory
+and the outputs copied back inside every timed step.  Under torchrun every rank runs its own replica (the reference's
+one-layer graph is a single-process program): replicas only.  Without baseline/_ref the default falls back to the
+linear workload below.
+
+``--workload linear``: one encrypted 4096 x 4096 complex weight page applied to the 16 input ciphertexts of a
 128-token prefill -- the QKV projection of one Llama-3-8B layer in the reference's feature-major layout
-(llama3fhe/operators/linear/prefill/qkv_kernel.py:678-940: 8 complex FM pairs and their conjugates, 8 token
-lanes, one page) -- through ``LinearOperator.apply`` with the production schedule (baby 64, 8 chunks of
-8 giants, llama3fhe/operators/linear/config.py:123-134), the production CKKS parameters (N = 2^16,
-59/60-bit primes, depth 37, dnum 5 -> alpha 8, K 8; llama3fhe/parallel/presets.py:63-127) at the linear
-entry level of 13 limbs (parallel/prefill/stations.py:190).  Every step rebuilds the 64-rotation baby
-basis, re-encodes all 4096 diagonal rows online (pack -> special FFT -> round -> NTT) and rescales, as the
-reference does per projection.  Weights ~ N(0, 0.02^2) (complex), pre-multiplied by a seeded +-1 Walsh-
-Hadamard rotation (QuaRot); inputs ~ N(0, 1); all synthetic and seeded.
-
-Multi-GPU (torchrun), default ``--parallelism chunk``: rank r key-switches 1 / W of the 64 baby rotations of all 16
-inputs and an NCCL all-gather completes the basis on every rank, then the rank encodes, MACs and runs the giant
-Horner chain of its 8 / W BSGS chunks (the reference's decode-style chunk ownership,
-parallel/decode/decode_ownership.py), and a modular reduce-scatter (all-to-all of raw limbs + the engine's mod-q
-sum) delivers each rank its token shard (16 / W outputs, parallel/prefill/ownership.py:1-44) to rescale.
-``--parallelism token`` instead gives each rank 16 / W inputs end to end with no data-path collective, which
-repeats the page's encode on every rank.
+(llama3fhe/operators/linear/prefill/qkv_kernel.py:678-940) -- through ``LinearOperator.apply`` with the production
+schedule (baby 64, 8 chunks of 8 giants) at the linear entry level of 13 limbs; every step rebuilds the baby basis,
+re-encodes all 4096 diagonal rows online (pack -> special FFT -> round -> NTT) and rescales.  Multi-GPU
+(``--parallelism chunk``): rank r key-switches 1 / W of the baby rotations, an NCCL all-gather completes the basis,
+each rank MACs its 8 / W BSGS chunks, and a modular reduce-scatter delivers each rank its token shard;
+``--parallelism token`` gives each rank 16 / W inputs end to end with no data-path collective.
 
 ``--impl reference`` times the CPU restatement of the same path (``oracle/``) on the host cores, on a bounded
-sample scaled to one page.  EasyFHE, the reference's engine, is not distributed with the reference and
+sample scaled to the workload.  EasyFHE, the reference's engine, is not distributed with the reference and
 cannot run here.
 """
 from __future__ import annotations
@@ -795,6 +796,18 @@ def layer_cpu_estimate(volume: dict, rates: dict) -> float:
 LAYER_VOLUME = os.path.join(ROOT, "profiles", "layer_op_volume.json")
 
 
+def layer_cpu_rates_threads(threads: int, rows: int = 4):
+    """``layer_cpu_rates`` measured in a child process limited to ``threads`` OpenMP threads (the thread count is
+    fixed when the oracle's library first runs, so the parent's all-core library cannot be reused), or None."""
+    env = dict(os.environ, OMP_NUM_THREADS=str(int(threads)), CUDA_VISIBLE_DEVICES="")
+    try:
+        res = subprocess.run([sys.executable, os.path.abspath(__file__), "--cpu-rates-json", "--cpu-rows", str(rows)],
+                             env=env, capture_output=True, text=True, timeout=600)
+        return json.loads(res.stdout.strip().splitlines()[-1]) if res.returncode == 0 else None
+    except (subprocess.TimeoutExpired, ValueError, IndexError):
+        return None
+
+
 def run_layer(args) -> None:
     """BASELINE config 3 (see _LayerSetup): ``value`` = device seconds of one encrypted decoder layer with the 16
     input ciphertexts resident in HBM (CUDA events around each step on the launching stream, synchronised on both
@@ -918,6 +931,10 @@ def run_layer(args) -> None:
                "sample": rates["sample"] + "; scaled to the layer by every kernel family's algorithmic bytes in one "
                                            "layer (CPU seconds per byte of that family times its bytes)",
                "per_op_s": rates["per_op_s"]}
+        one = layer_cpu_rates_threads(1, rows=16)
+        if one is not None:
+            cpu["one_thread"] = {"value": round(layer_cpu_estimate(volume, one), 1), "unit": "s", "cores": 1,
+                                 "sample": one["sample"], "per_op_s": one["per_op_s"]}
     line = {"metric": LAYER_METRIC, "value": round(v, 4), "unit": "s", "n_gpus": world, "steps": steps,
             "warmup": warm, "ms_per_step": round(v * 1e3, 1), "higher_is_better": False,
             "scaling": "weak" if world > 1 else "strong", "vs_baseline": None,
@@ -1148,7 +1165,9 @@ def run_silu(args) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--workload", choices=("linear", "layer", "bootstrap", "primitives", "silu"), default="linear")
+    ap.add_argument("--workload", choices=("linear", "layer", "bootstrap", "primitives", "silu"), default=None,
+                    help="default: layer (BASELINE config 3) when the reference's application is installed in "
+                         "baseline/_ref, else linear (one QKV page)")
     ap.add_argument("--boot-batch", type=int, default=8)
     ap.add_argument("--boot-iterations", type=int, default=1, help="2 = Meta-BTS correction")
     ap.add_argument("--kernel", default=None, help="profile one kernel family (see run_kernel)")
@@ -1168,7 +1187,13 @@ def main() -> None:
                     help="layer workload: record the per-family volume of one layer in profiles/layer_op_volume.json")
     ap.add_argument("--vs-ref", action="store_true",
                     help="with --kernel mac|encode: time the reference's in-tree kernel beside the engine's")
+    ap.add_argument("--cpu-rates-json", action="store_true", help=argparse.SUPPRESS)
     args = ap.parse_args()
+    if args.cpu_rates_json:    # one bounded CPU sample in this process's thread count (OMP_NUM_THREADS)
+        print(json.dumps(layer_cpu_rates(rows=args.cpu_rows)), flush=True)
+        return
+    if args.workload is None:
+        args.workload = "layer" if os.path.isdir(os.path.join(ROOT, "baseline", "_ref", "llama3fhe")) else "linear"
     if args.workload == "layer":
         # the layer's many short-lived multi-GB temporaries fragment a fixed-segment pool
         os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")

@@ -179,6 +179,7 @@ class BootstrapProgram:
     gap: int = 1             # N / (2 n): sparse slots when > 1
     s2c_int: int = 1         # exact integer factor applied before SlotsToCoeffs (keeps its diagonals encodable)
     _plain: dict = field(default_factory=dict)
+    _diag: dict = field(default_factory=dict)
     setup_seconds: float = 0.0
     cache_mode: str = "plain"   # "plain": keep encoded diagonals across refreshes; "none": encode per use
 
@@ -213,14 +214,24 @@ class BootstrapProgram:
         factor = (self.c2s_scale if which == "c2s" else self.s2c_scale) * float(adjust)
         mat = mats[level]
         offsets = sorted(mat)
-        rows = np.stack([mat[r] * factor for r in offsets])
+        # the level's diagonals stay on the device; the factor is applied there (the same double products as
+        # mat[r] * factor on the host), so a per-call factor costs no host-to-device copy
+        dkey = (which, level)
+        raw = self._diag.get(dkey)
+        if raw is None:
+            host = torch.from_numpy(np.stack([mat[r] for r in offsets]).astype(np.complex128)).pin_memory()
+            raw = self._diag[dkey] = host.to(ctx.device, non_blocking=True)
+        rows = raw * factor
         scale = float(ctx.q(cur - 1))
-        pv = F.encode_rows(ctx, torch.from_numpy(rows).to(ctx.device), cur, scale, self.n)
+        pv = F.encode_rows(ctx, rows, cur, scale, self.n)
         try:
-            ctx.check_encode_range()
+            # a level encoded once (cached) is checked now; a per-call level (SlotsToCoeffs' rho, which the host-side
+            # DIAGONAL_LIMIT bound already keeps in range) is checked without draining the stream
+            ctx.check_encode_range(wait=float(adjust) == 1.0)
         except ValueError as exc:
             raise ValueError(f"{which} level {level} of the {self.n}-slot bootstrap: diagonals up to "
-                             f"{float(np.max(np.abs(rows))):.4g} at scale 2^{math.log2(scale):.2f} "
+                             f"{float(np.max(np.abs(np.stack(list(mat.values()))))) * factor:.4g} at scale "
+                             f"2^{math.log2(scale):.2f} "
                              f"(factor {factor:.4g}, adjust {float(adjust):.4g}): {exc}") from None
         pt = F.Plaintext([pv], F.CipherState(cur, 1, scale), self.n, False, len(offsets), ctx)
         # a level carrying a per-call factor (SlotsToCoeffs' rho) is encoded per call: caching it would keep one

@@ -210,12 +210,18 @@ class PeerReduceScatter:
                                f"{self.timeout_s:.1f} s (flag {st - 1}); a peer did not reach epoch {self.epoch}")
 
     def close(self) -> None:
-        """Unmap the peers' buffers and free this rank's (every rank must have finished its last step)."""
+        """Unmap the peers' buffers, then (after every rank has unmapped this one's: a barrier over ``group``) free
+        this rank's.  Collective: every rank calls it once, after its last step."""
         torch.cuda.synchronize(self.ctx.device)
         for p in self._mapped:
             _lib.call("holmes_ipc_close", p)
         self._mapped.clear()
         self.partials = self.flags = None
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        for p in self._owned:
+            _lib.call("holmes_peer_free", _lib.ctypes.c_void_p(p))
+        self._owned.clear()
         for p in self._owned:
             _lib.call("holmes_peer_free", p)
         self._owned.clear()

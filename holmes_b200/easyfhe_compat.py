@@ -197,6 +197,30 @@ def _packer_module() -> types.ModuleType:
     return mod
 
 
+# ------------------------------------------------------------------------------------------- host arrays
+
+
+class HostTensor(torch.Tensor):
+    """What ``easyfhe.from_numpy`` returns: a CPU tensor over the array whose ``.to(cuda)`` copies through pinned
+    memory without waiting for the device (a plain ``Tensor.to`` from host memory synchronises the stream, which
+    drains the GPU's queue at every constant upload).  The device tensor is ordered after everything already queued on
+    the current stream, as the synchronous copy was; the pinned staging buffer is held until the copy has run."""
+
+    def to(self, *args, **kwargs):
+        plain = self.as_subclass(torch.Tensor)
+        target = kwargs.get("device", args[0] if args else None)
+        if isinstance(target, (str, torch.device)) and torch.device(target).type == "cuda" and \
+                not kwargs.get("non_blocking", False) and not any(isinstance(a, torch.dtype) for a in args) and \
+                "dtype" not in kwargs and "copy" not in kwargs and "memory_format" not in kwargs:
+            return plain.pin_memory().to(torch.device(target), non_blocking=True)
+        return plain.to(*args, **kwargs)
+
+
+def from_numpy(array) -> torch.Tensor:
+    """``easyfhe.from_numpy``: the array as a CPU tensor (a ``HostTensor``; see there)."""
+    return torch.from_numpy(array).as_subclass(HostTensor)
+
+
 # ------------------------------------------------------------------------------------------- registration
 
 
@@ -216,7 +240,7 @@ def _build() -> dict:
     bs.openfhe = openfhe
     bs.__path__ = []
     top = _forwarding("easyfhe", torch, fhe=fhe, bs=bs, cuda=torch.cuda, multiprocessing=torch.multiprocessing,
-                      from_numpy=torch.from_numpy, get_device_module=get_device_module)
+                      from_numpy=from_numpy, get_device_module=get_device_module)
     top.__path__ = []
     return {"easyfhe": top, "easyfhe.fhe": fhe, "easyfhe.fhe.ciphertext": ciphertext, "easyfhe.fhe.ops": ops,
             "easyfhe.fhe.ops.layout": layout, "easyfhe.fhe.constants": constants, "easyfhe.bs": bs,

@@ -318,11 +318,29 @@ class Context:
                 self.key_bytes -= self._keys[g][0].numel() * 8
                 del self._keys[g]
 
-    def check_encode_range(self) -> None:
-        """One device read: raise if any encode since the last check reached the 2^61 limit."""
-        if int(self._flag.item()):
-            self._flag.zero_()
-            raise ValueError("encoded value exceeds the 2^61 encoder range")
+    def check_encode_range(self, wait: bool = True) -> None:
+        """Raise if any encode since the last check reached the 2^61 limit.  ``wait``: one device read now (the host
+        waits for the stream); else the flag is copied back without waiting and the copy started by the previous
+        such call is read if it has landed, so an overflow is reported one check late but the queue never drains."""
+        if wait:
+            if int(self._flag.item()):
+                self._flag.zero_()
+                raise ValueError("encoded value exceeds the 2^61 encoder range")
+            return
+        pending = getattr(self, "_flag_pending", None)
+        if pending is not None:
+            host, done = pending
+            if not done.query():
+                return
+            self._flag_pending = None
+            if int(host[0]):
+                self._flag.zero_()
+                raise ValueError("encoded value exceeds the 2^61 encoder range")
+        host = torch.zeros(1, dtype=torch.int32).pin_memory()
+        host.copy_(self._flag, non_blocking=True)
+        done = torch.cuda.Event()
+        done.record()
+        self._flag_pending = (host, done)
 
     def close(self) -> None:
         if getattr(self, "handle", None) is not None:
