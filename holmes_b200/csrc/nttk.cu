@@ -571,83 +571,11 @@ struct ModKsQ {
   __device__ int operator()(int p) const { return (p % (2 * cur)) % cur; }
 };
 
-// Key switch, P limbs, computed where the P-limb inverse NTT loads them (N = 2^16): word n of limb k of component c
-// of item i is sum_j digit_j[i][cur + k][src(n)] * key_{c,j}[cap + k][n] mod p_k, canonical -- the words k_ks_inner
-// would otherwise write to scratch for this pass to read back.  Polynomials run over [items][2][K].
-struct LdKsInnerP {
-  const u64* digits;
-  long long dig_item;
-  const u64* key;
-  const Mod* mods;
-  u64 galois;
-  int cur, cap, K, L, beta, key_beta, log_n;
-  struct S {
-    const u64* d;
-    const u64* k;
-    size_t dstep, kstep;
-    Mod m;
-  };
-  __device__ S prep(int p) const {
-    const int item = p / (2 * K), c = (p / K) & 1, k = p % K;
-    S s;
-    s.dstep = (size_t)(cur + K) << log_n;
-    s.kstep = (size_t)(cap + K) << log_n;
-    s.d = digits + item * dig_item + ((size_t)(cur + k) << log_n);
-    s.k = key + (size_t)c * key_beta * s.kstep + ((size_t)(cap + k) << log_n);
-    s.m = mods[L + k];
-    return s;
-  }
-  __device__ u64 load(const S& s, int n) const {
-    const u32 src = galois > 1 ? automorph_src((u32)n, galois, log_n) : (u32)n;
-    Split4 acc{0, 0, 0, 0};
-    for (int j = 0; j < beta; ++j) split_mac(acc, s.d[j * s.dstep + src], s.k[j * s.kstep + n]);
-    return fold_split(acc, s.m);
-  }
-};
-
-// Key switch, Q limbs: the P -> Q conversion computed where the Q-limb forward NTT loads it (N = 2^16): word n of
-// limb i of component c of item it is sum_k y[it][c][k][n] H[k][i] mod q_i as k_conv forms it (radix-2^30 split
-// sums, a lazy fold after every 16 products), a representative below 8 q -- the words k_conv would otherwise write for
-// this pass to read back.  y = the P limbs after their inverse NTT, scratch [items][2][K][N]; polynomials run over
-// [items][2][cur].  The 13-odd target polynomials of one (item, component) are neighbours in the grid, so their
-// reads of the same K source rows meet in L2.
-struct LdConvQ {
-  const u64* y;
-  const u64* H;  // H[k * h_row + i]
-  const Mod* mods;
-  int h_row, cur, K, log_n;
-  struct S {
-    const u64* y;
-    const u64* h;
-    Mod m;
-  };
-  __device__ S prep(int p) const {
-    const int item = p / (2 * cur), c = (p / cur) & 1, i = p % cur;
-    S s;
-    s.y = y + ((size_t)(item * 2 + c) * K << log_n);
-    s.h = H + i;
-    s.m = mods[i];
-    return s;
-  }
-  __device__ u64 load(const S& s, int n) const {
-    Split4 acc{0, 0, 0, 0};
-    for (int k = 0; k < K; ++k) {
-      if (k == 16) {
-        const u64 v = fold_split_lazy(acc, s.m);
-        acc = Split4{v & ((1ull << 30) - 1), v >> 30, 0, 0};
-      }
-      split_mac(acc, s.y[((size_t)k << log_n) + n], s.h[(size_t)k * h_row]);
-    }
-    return fold_split_lazy(acc, s.m);
-  }
-};
-
-// rows: the limb rows k_ks_inner computes (cur + K; cur when the P rows are left to LdKsInnerP)
-static int ks_inner_launch(const HolmesCtx& c, const KsInnerArgs& ia, cudaStream_t st, int rows = -1) {
+static int ks_inner_launch(const HolmesCtx& c, const KsInnerArgs& ia, cudaStream_t st) {
   if (c.n < 256) return -5;
   if (ia.beta > 16) return -3;   // the split sums hold 16 products
   count_launch();
-  const dim3 grid((unsigned)(c.n / 256), (unsigned)(rows > 0 ? rows : ia.cur + ia.K));
+  const dim3 grid((unsigned)(c.n / 256), (unsigned)(ia.cur + ia.K));
   if (ia.beta <= 2) k_ks_inner<2><<<grid, 256, 0, st>>>(ia, c.log_n, c.d_mod);
   else if (ia.beta <= 5) k_ks_inner<5><<<grid, 256, 0, st>>>(ia, c.log_n, c.d_mod);
   else k_ks_inner<0><<<grid, 256, 0, st>>>(ia, c.log_n, c.d_mod);
@@ -658,7 +586,7 @@ static int ks_inner_launch(const HolmesCtx& c, const KsInnerArgs& ia, cudaStream
 // out_c already holding what the conversion is subtracted from.  P iNTT in place, P -> Q conversion into
 // scratch + items 2 K N, Q NTT with "out -= conversion".
 static int moddown_tail(const HolmesCtx& c, u64* scratch, u64* out0, u64* out1, long long out_item, int cur, int items,
-                        cudaStream_t st, const LdKsInnerP* inner_p = nullptr) {
+                        cudaStream_t st) {
   const int K = c.K;
   {
     NttTables T{c.d_itw, c.d_mod};
@@ -666,10 +594,8 @@ static int moddown_tail(const HolmesCtx& c, u64* scratch, u64* out0, u64* out1, 
     StScratch ss{scratch, c.log_n};
     const int polys = items * 2 * K;
     if (c.log_n == 16) {
-      const int e = inner_p ? ntt16_inverse<HOLMES_KS16_MINB>(T, ModKsP{c.L, K}, ScKsP{c.d_md_scale, K}, *inner_p,
-                                                              IMRows{scratch}, ss, polys, st)
-                            : ntt16_inverse<HOLMES_KS16_MINB>(T, ModKsP{c.L, K}, ScKsP{c.d_md_scale, K}, ld,
-                                                              IMRows{scratch}, ss, polys, st);
+      const int e = ntt16_inverse<HOLMES_KS16_MINB>(T, ModKsP{c.L, K}, ScKsP{c.d_md_scale, K}, ld, IMRows{scratch},
+                                                    ss, polys, st);
       if (e) return e;
     } else {
 #define L_(LG)                                                                                                   \
@@ -685,13 +611,6 @@ static int moddown_tail(const HolmesCtx& c, u64* scratch, u64* out0, u64* out1, 
     }
   }
   u64* conv = scratch + (size_t)items * 2 * K * c.n;  // [items][2][cur][N], coefficient form
-  if (c.log_n == 16) {
-    // the conversion is formed in the Q forward NTT's loads; `conv` only holds that NTT's intermediate
-    NttTables T{c.d_tw, c.d_mod};
-    const LdConvQ lc{scratch, c.d_md_hat, c.d_mod, c.L, cur, K, c.log_n};
-    StKsSub sq{out0, out1, out_item, c.d_mod, cur, c.log_n};
-    return ntt16_forward<HOLMES_KS16_MINB>(T, ModKsQ{cur}, lc, IMRows{conv}, sq, items * 2 * cur, st);
-  }
   {
     ConvArgs ca{scratch, (long long)K * c.n, conv, (long long)cur * c.n, c.d_md_hat, c.L,
                 K, cur, cur, cur, c.L, items * 2, nullptr, 0, nullptr};
@@ -726,14 +645,6 @@ int ks_apply(const HolmesCtx& c, const KsArgs& a, cudaStream_t st) {
   KsInnerArgs ia{a.digits, a.dig_item, a.key, a.add0, a.add1, a.add_item, a.post0, a.post1, a.post_item, a.out0,
                  a.out1, a.out_item, a.scratch, a.scratch + (size_t)K * c.n, (long long)2 * K * c.n, nullptr, g,
                  a.cur, a.key_cap, K, c.L, beta, key_beta, a.items};
-  if (c.log_n == 16) {
-    // the P-limb inner products are formed inside the P inverse NTT's first pass: k_ks_inner does the Q rows only
-    const int e = ks_inner_launch(c, ia, st, a.cur);
-    if (e) return e;
-    const LdKsInnerP inner_p{a.digits, a.dig_item, a.key, c.d_mod, g, a.cur, a.key_cap, K, c.L, beta, key_beta,
-                             c.log_n};
-    return moddown_tail(c, a.scratch, a.out0, a.out1, a.out_item, a.cur, a.items, st, &inner_p);
-  }
   const int e = ks_inner_launch(c, ia, st);
   if (e) return e;
   return moddown_tail(c, a.scratch, a.out0, a.out1, a.out_item, a.cur, a.items, st);

@@ -109,7 +109,16 @@ class OracleBootstrap:
         d0, d1 = o.rescale(acc)
         return d0, d1, float(sf) * float(self.pr.q[cur - 1]) / self.pr.q[cur - 1]
 
+    def add_adj(self, a, b, S):
+        lim = min(a[0].shape[0], b[0].shape[0])
+        return self._add(self.adjust(a, lim, S), self.adjust(b, lim, S))
+
     def chebyshev(self, w, S):
+        # Paterson-Stockmeyer in the Chebyshev basis: babies T_1 .. T_(m-1), giants T_m, T_2m, ...; p = q T_n + r
+        # recursively down to leaves of m coefficients, each one lin_comb (the split arithmetic is the plan's,
+        # holmes_b200.bootstrap.ps_baby / cheb_split)
+        from holmes_b200.bootstrap import cheb_split, ps_baby
+
         coeffs = self.prog.cheb
         T = {1: w}
         low = {}
@@ -131,8 +140,20 @@ class OracleBootstrap:
                 T[k] = self._add(self._add(p, p), t1_at(p[0].shape[0]), sub=True)
             return T[k]
 
-        terms = [(get(k), float(coeffs[k])) for k in range(1, len(coeffs)) if abs(coeffs[k]) >= 1e-18]
-        return self.add_scalar(self.lin_comb(terms, S), float(coeffs[0]))
+        m = ps_baby(len(coeffs) - 1)
+
+        def leaf(c):
+            terms = [(get(k), float(c[k])) for k in range(1, len(c)) if abs(c[k]) >= 1e-18] or [(get(1), 0.0)]
+            return self.add_scalar(self.lin_comb(terms, S), float(c[0]))
+
+        def evalp(c):
+            if len(c) <= m:
+                return leaf(c)
+            n = 1 << (math.ceil(math.log2(len(c))) - 1)
+            q, r = cheb_split(c, n)
+            return self.add_adj(self.mul_rescale(evalp(q), get(n), S), evalp(r), S)
+
+        return evalp([float(v) for v in coeffs])
 
     def eval_mod(self, x):
         S = self.scale_table(x[0].shape[0], x[2])
