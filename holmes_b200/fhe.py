@@ -206,6 +206,8 @@ class Context:
         self._work: dict = {}
         self._flag = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._consts: collections.OrderedDict = collections.OrderedDict()
+        self._modup_cache: collections.OrderedDict = collections.OrderedDict()
+        self._modup_cache_bytes = 0
         self._enc_counter = 0
         self.key_bytes = 0
 
@@ -348,6 +350,8 @@ class Context:
             self._keys.clear()
             self._work.clear()
             self._consts.clear()
+            self._modup_cache.clear()
+            self._modup_cache_bytes = 0
             self.__dict__.pop("_ones_rows", None)
             _lib.call("holmes_ctx_destroy", self.handle)
             self.handle = None
@@ -696,14 +700,52 @@ def align_to(a: Cipher, target: CipherState, ctx) -> Cipher:
 
 
 def _modup(ctx: Context, c1: torch.Tensor, cur: int, items: int) -> tuple[torch.Tensor, int]:
+    """The ModUp digits of ``c1`` (its first ``cur`` limbs, ``items`` items).  Digits of a recent input are reused:
+    the reference rotates one ciphertext by many offsets one call at a time (attention's per-head rotations), and
+    every such rotation needs the same digits.  An input is the same when its memory, item stride, level, item count
+    and torch version counter (bumped by every in-place torch write, shared by all views) are; the cache holds the
+    input tensor, so its memory cannot be handed to another tensor while the entry lives, and the engine's own calls
+    that write into caller-provided buffers drop the entries they overlap (``_modup_forget``)."""
     dig_item = ctx.beta(cur) * (cur + ctx.K) * ctx.N
+    key = (c1.data_ptr(), int(c1._version), int(c1.stride(0)), int(cur), int(items))
+    hit = ctx._modup_cache.get(key)
+    if hit is not None and hit[0].untyped_storage().data_ptr() == c1.untyped_storage().data_ptr():
+        ctx._modup_cache.move_to_end(key)
+        return hit[1], dig_item
     digits = torch.empty(items * dig_item, dtype=torch.uint64, device=ctx.device)
     scratch = ctx.workspace("modup", items * cur * ctx.N)
     tok = OPTIMER.start("modup")
     _lib.call("holmes_modup", ctx.handle, c1.data_ptr(), _item_stride(c1), cur, items, digits.data_ptr(), dig_item,
               scratch.data_ptr(), _stream())
     OPTIMER.stop(tok, items * (cur + dig_item // ctx.N) * ctx.N * 8)
+    nbytes = int(digits.numel()) * 8
+    if nbytes <= MODUP_CACHE_BYTES // 4:
+        cache = ctx._modup_cache
+        cache[key] = (c1, digits, nbytes)
+        ctx._modup_cache_bytes += nbytes
+        while ctx._modup_cache_bytes > MODUP_CACHE_BYTES:
+            ctx._modup_cache_bytes -= cache.popitem(last=False)[1][2]
     return digits, dig_item
+
+
+#: device bytes of ModUp digits kept for reuse per context
+MODUP_CACHE_BYTES = 2 << 30
+
+
+def _modup_forget(ctx: Context, *tensors) -> None:
+    """Drop the cached digits of every input whose memory overlaps one of ``tensors`` (about to be written by a raw
+    kernel launch, which torch's version counter does not see)."""
+    cache = ctx._modup_cache
+    if not cache:
+        return
+    def span(t):   # the whole storage: conservative for views
+        st = t.untyped_storage()
+        return st.data_ptr(), st.data_ptr() + int(st.nbytes())
+
+    spans = [span(t) for t in tensors if t is not None]
+    for key in [k for k, (src, _, _) in cache.items()
+                if any(lo < hi2 and lo2 < hi for lo, hi in spans for lo2, hi2 in [span(src)])]:
+        ctx._modup_cache_bytes -= cache.pop(key)[2]
 
 
 def _keyswitch(ctx: Context, digits: torch.Tensor, dig_item: int, cur: int, galois: int, key, add0, add1, add_item,
@@ -726,6 +768,7 @@ def rotate_batch(ctx: Context, c0: torch.Tensor, c1: torch.Tensor, cur: int, rot
     """out = rot((c0, c1), rotation) [+ post] for a batch [items][>= cur][N] sharing one key."""
     items = int(c0.shape[0])
     g = ctx.galois(rotation)
+    _modup_forget(ctx, out0, out1)
     if g == 1:
         if post0 is None:
             out0.copy_(c0[:, :cur])

@@ -167,6 +167,34 @@ def test_rotation_and_conjugation_bitexact(pair, cur):
     assert np.abs(client.decrypt(F.homo_rotate(ct, 7, ctx)) - want).max() < 1e-5
 
 
+def test_modup_digit_reuse_follows_writes(pair):
+    """Rotations of one ciphertext by several offsets share its ModUp digits; a torch in-place write to the
+    ciphertext (version counter) and a raw write by rotate_batch into its memory both retire them."""
+    o, client, ctx = pair
+    from holmes_b200 import fhe as F
+
+    rng = np.random.default_rng(41)
+    ct, ref = _cipher(o, client, rng.normal(size=ctx.max_slots) * 0.5, 5, 21)
+    other, ref2 = _cipher(o, client, rng.normal(size=ctx.max_slots) * 0.5, 5, 22)
+    for r in (3, 5, 3):
+        out = F.homo_rotate(ct, r, ctx)
+        e0, e1 = o.rotate(ref, r)
+        np.testing.assert_array_equal(host(out.cv[0][0]), e0)
+        np.testing.assert_array_equal(host(out.cv[1][0]), e1)
+    assert any(v[0] is ct.cv[1] for v in ctx._modup_cache.values())
+    ct.cv[0].copy_(other.cv[0])
+    ct.cv[1].copy_(other.cv[1])
+    out = F.homo_rotate(ct, 3, ctx)
+    e0, e1 = o.rotate(ref2, 3)
+    np.testing.assert_array_equal(host(out.cv[0][0]), e0)
+    np.testing.assert_array_equal(host(out.cv[1][0]), e1)
+    F.rotate_batch(ctx, other.cv[0], other.cv[1], 5, 7, ct.cv[0], ct.cv[1])   # raw write into ct's memory
+    out = F.homo_rotate(ct, 3, ctx)
+    e0, e1 = o.rotate(o.rotate(ref2, 7), 3)
+    np.testing.assert_array_equal(host(out.cv[0][0]), e0)
+    np.testing.assert_array_equal(host(out.cv[1][0]), e1)
+
+
 @pytest.mark.parametrize("dnum", [7, 3])
 def test_rotation_bitexact_many_digits(dnum):
     """beta = ceil(cur / alpha) above the key-switch inner product's register-cached key counts (2 and 5): seven
