@@ -10,7 +10,7 @@
 // system scope after a system fence and read with acquire loads.  Every wait is bounded by a clock64 budget: a wait
 // that runs out writes the index of the flag it gave up on (plus one) into a device status word and returns, and the
 // summing kernel does nothing when the status is set, so a missing peer turns into an error the host reads rather
-// than a hung GPU.  No TMA and no multicast touch peer memory here.
+// than a hung GPU.  Only plain loads and stores touch peer memory here.
 #include <cuda_runtime.h>
 
 #include <cstring>

@@ -246,6 +246,16 @@ class Context:
                 self._consts.popitem(last=False)
         return dev
 
+    def forget_digits(self, *tensors) -> None:
+        """Retire reused ModUp digits: of the inputs overlapping ``tensors``, or all of them when none are given.  A
+        caller that overwrites a ciphertext's memory outside torch (its own kernel launches) calls this first; writes
+        through torch ops and through this engine are tracked already."""
+        if tensors:
+            _modup_forget(self, *tensors)
+        else:
+            self._modup_cache.clear()
+            self._modup_cache_bytes = 0
+
     def p_mod_q_dev(self, cur: int) -> torch.Tensor:
         return self.device_u64(self.p_mod_q(cur))
 
