@@ -809,6 +809,43 @@ def layer_cpu_rates_threads(threads: int, rows: int = 4):
         return None
 
 
+def write_kernel_list(setup, path: str) -> None:
+    """One more (untimed) layer under CUPTI (torch.profiler, CUDA activity only): every kernel and copy with its
+    launches, total device time and share, written to ``path`` as a markdown table.  The layer's ~360,000 launches
+    make a per-launch ncu list impractical (its CSV alone runs to hundreds of MB); these are the same per-launch
+    device durations, aggregated by kernel name."""
+    import collections
+
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+
+    setup.release_transients()
+    wall = time.perf_counter()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        setup.forward()
+        torch.cuda.synchronize()
+    wall = time.perf_counter() - wall
+    agg = collections.defaultdict(lambda: [0, 0.0])
+    first, last = None, None
+    for e in prof.events():
+        if e.device_type != torch.autograd.DeviceType.CUDA:
+            continue
+        rec = agg[e.name]
+        rec[0] += 1
+        rec[1] += float(getattr(e, "device_time_total", 0.0) or e.cuda_time_total)
+        first = e.time_range.start if first is None else min(first, e.time_range.start)
+        last = e.time_range.end if last is None else max(last, e.time_range.end)
+    total = sum(v[1] for v in agg.values())
+    lines = [f"device work {total / 1e6:.3f} s in a {((last or 0) - (first or 0)) / 1e6:.3f} s span "
+             f"({sum(v[0] for v in agg.values())} launches and copies; wall {wall:.2f} s under the profiler)", "",
+             "| kernel | launches | total ms | share |", "|---|---:|---:|---:|"]
+    for name, (n, us) in sorted(agg.items(), key=lambda kv: -kv[1][1]):
+        short = name if len(name) <= 110 else name[:107] + "..."
+        lines.append(f"| `{short}` | {n} | {us / 1e3:.1f} | {us / total:.3f} |")
+    with open(path, "w", encoding="utf-8") as f:
+        f.write("\n".join(lines) + "\n")
+
+
 def run_layer(args) -> None:
     """BASELINE config 3 (see _LayerSetup): ``value`` = device seconds of one encrypted decoder layer with the 16
     input ciphertexts resident in HBM (CUDA events around each step on the launching stream, synchronised on both
@@ -902,6 +939,8 @@ def run_layer(args) -> None:
     setup.forward()
     F.OPTIMER.enabled = False
     ops = F.OPTIMER.summary()
+    if args.kernel_list and rank == 0:
+        write_kernel_list(setup, args.kernel_list)
     check = setup.check(result) if args.check and rank == 0 else None
     barrier()
     if rank != 0:
@@ -1188,6 +1227,8 @@ def main() -> None:
                     help="layer workload: record the per-family volume of one layer in profiles/layer_op_volume.json")
     ap.add_argument("--vs-ref", action="store_true",
                     help="with --kernel mac|encode: time the reference's in-tree kernel beside the engine's")
+    ap.add_argument("--kernel-list", default=None,
+                    help="layer workload: write the per-kernel device time of one more (untimed) layer to this file")
     ap.add_argument("--cpu-rates-json", action="store_true", help=argparse.SUPPRESS)
     args = ap.parse_args()
     if args.cpu_rates_json:    # one bounded CPU sample in this process's thread count (OMP_NUM_THREADS)

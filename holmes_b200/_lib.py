@@ -44,6 +44,7 @@ SIGNATURES = {
     "holmes_pack_structured": [p, p, p, i32, i32, p, p, p, p, p, p, p, p, p, i32, i32, i32, i32, i32, i32, i32, p,
                                i64, p],
     "holmes_elementwise": [p, i32, p, p, p, i32, i32, i64, i64, i64, p],
+    "holmes_tensor_product": [p, p, p, i64, p, p, i64, p, p, p, i64, i32, i32, p],
     "holmes_mul_i": [p, p, p, i32, i32, i64, i64, p],
     "holmes_automorph": [p, p, p, u64, i32, i32, i64, i64, p],
     "holmes_mul_const": [p, p, p, p, i32, i32, i64, i64, p],

@@ -197,6 +197,13 @@ int holmes_elementwise(void* ctx, int op, const uint64_t* a, const uint64_t* b, 
   return elementwise(*C(ctx), op, a, b, out, items, limbs, a_item, b_item, out_item, S(stream));
 }
 
+int holmes_tensor_product(void* ctx, const uint64_t* a0, const uint64_t* a1, long long a_item, const uint64_t* b0,
+                          const uint64_t* b1, long long b_item, uint64_t* d0, uint64_t* d1, uint64_t* d2,
+                          long long d_item, int items, int limbs, void* stream) {
+  if (!ctx || !a0 || !a1 || !b0 || !b1 || !d0 || !d1 || !d2) return -1;
+  return tensor_product(*C(ctx), a0, a1, a_item, b0, b1, b_item, d0, d1, d2, d_item, items, limbs, S(stream));
+}
+
 int holmes_mul_i(void* ctx, const uint64_t* a, uint64_t* out, int items, int limbs, long long a_item, long long out_item,
                  void* stream) {
   if (!ctx || !a || !out) return -1;

@@ -40,6 +40,43 @@ __global__ void k_elementwise(int op, const u64* __restrict__ a, const u64* __re
   }
 }
 
+// Tensor product of two ciphertexts (before relinearisation): d0 = a0 b0, d1 = a0 b1 + a1 b0, d2 = a1 b1 (mod q_l),
+// two words per thread; each operand word is read once.
+__global__ void k_tensor(const u64* __restrict__ a0, const u64* __restrict__ a1, long long ai,
+                         const u64* __restrict__ b0, const u64* __restrict__ b1, long long bi, u64* __restrict__ d0,
+                         u64* __restrict__ d1, u64* __restrict__ d2, long long di, int items, int limbs, int log_n,
+                         const Mod* __restrict__ mods) {
+  const size_t per_item = (size_t)limbs << log_n;
+  const size_t total = (size_t)items * per_item / 2;
+  for (size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x; t < total; t += (size_t)gridDim.x * blockDim.x) {
+    const size_t w = 2 * t;
+    const unsigned wl = (unsigned)(w >> log_n);
+    const int item = (int)(wl / (unsigned)limbs), limb = (int)(wl - (unsigned)item * limbs);
+    const size_t r = ((size_t)limb << log_n) | (w & (((size_t)1 << log_n) - 1));
+    const Mod m = mods[limb];
+    const ulonglong2 x0 = *reinterpret_cast<const ulonglong2*>(a0 + item * ai + r);
+    const ulonglong2 x1 = *reinterpret_cast<const ulonglong2*>(a1 + item * ai + r);
+    const ulonglong2 y0 = *reinterpret_cast<const ulonglong2*>(b0 + item * bi + r);
+    const ulonglong2 y1 = *reinterpret_cast<const ulonglong2*>(b1 + item * bi + r);
+    const size_t o = item * di + r;
+    *reinterpret_cast<ulonglong2*>(d0 + o) = make_ulonglong2(mul_mod(x0.x, y0.x, m), mul_mod(x0.y, y0.y, m));
+    *reinterpret_cast<ulonglong2*>(d1 + o) =
+        make_ulonglong2(add_mod(mul_mod(x0.x, y1.x, m), mul_mod(x1.x, y0.x, m), m.q),
+                        add_mod(mul_mod(x0.y, y1.y, m), mul_mod(x1.y, y0.y, m), m.q));
+    *reinterpret_cast<ulonglong2*>(d2 + o) = make_ulonglong2(mul_mod(x1.x, y1.x, m), mul_mod(x1.y, y1.y, m));
+  }
+}
+int tensor_product(const HolmesCtx& c, const u64* a0, const u64* a1, long long a_item, const u64* b0, const u64* b1,
+                   long long b_item, u64* d0, u64* d1, u64* d2, long long d_item, int items, int limbs,
+                   cudaStream_t st) {
+  if (limbs < 1 || limbs > c.T || items < 1) return -2;
+  if ((a_item | b_item | d_item) & 1) return -2;
+  const size_t work = ((size_t)items * limbs * c.n) / 2;
+  k_tensor<<<grid_for(work, 256), 256, 0, st>>>(a0, a1, a_item, b0, b1, b_item, d0, d1, d2, d_item, items, limbs,
+                                                c.log_n, c.d_mod);
+  return (int)cudaGetLastError();
+}
+
 int elementwise(const HolmesCtx& c, int op, const u64* a, const u64* b, u64* out, int items, int limbs,
                 long long a_item, long long b_item, long long o_item, cudaStream_t st) {
   if (limbs < 1 || limbs > c.T || items < 1) return -2;

@@ -143,12 +143,17 @@ struct ConvArgs {
   long long own_item;
   const Tw* own_scale;
 };
+// Grid (blocks, groups): block row y takes targets [y tpg, (y + 1) tpg), so a conversion of few items (one
+// ciphertext: 256 blocks of coefficients) still spreads over every SM; each group re-reads its coefficients' W source
+// words (from L2) and computes the same sums, so the split changes nothing in the results.
 template <int W>
 __global__ void __launch_bounds__(256) k_conv(ConvArgs a, int log_n, const Mod* __restrict__ mods) {
-  extern __shared__ uint2 hs[];  // [ntgt][W]: the split constant of source a for target t
+  extern __shared__ uint2 hs[];  // [targets of this group][W]: the split constant of source a for target t
   const int N = 1 << log_n;
-  for (int e = threadIdx.x; e < a.ntgt * W; e += blockDim.x) {
-    const int t = e / W, k = e % W;
+  const int tpg = (a.ntgt + gridDim.y - 1) / gridDim.y;
+  const int t0 = blockIdx.y * tpg, t1 = min(a.ntgt, t0 + tpg);
+  for (int e = threadIdx.x; e < (t1 - t0) * W; e += blockDim.x) {
+    const int t = t0 + e / W, k = e % W;
     const int r = t < a.skip_lo ? t : t + W;
     const int mi = r < a.cur ? r : a.L + r - a.cur;
     const u64 h = a.H[(size_t)k * a.h_row + mi];
@@ -167,7 +172,7 @@ __global__ void __launch_bounds__(256) k_conv(ConvArgs a, int log_n, const Mod* 
       ys[k] = make_uint2((uint32_t)(v & ((1ull << 30) - 1)), (uint32_t)(v >> 30));
     }
     u64* op = a.out + item * a.out_item + n;
-    if (a.own) {
+    if (a.own && blockIdx.y == 0) {
       const u64* src = a.own + item * a.own_item + n;
 #pragma unroll
       for (int k = 0; k < W; ++k) {
@@ -175,8 +180,8 @@ __global__ void __launch_bounds__(256) k_conv(ConvArgs a, int log_n, const Mod* 
         op[(size_t)(a.skip_lo + k) << log_n] = shoup(src[(size_t)k << log_n], a.own_scale[k], m.q);
       }
     }
-    for (int t = 0; t < a.ntgt; ++t) {
-      const uint2* h = hs + t * W;
+    for (int t = t0; t < t1; ++t) {
+      const uint2* h = hs + (t - t0) * W;
       const int r = t < a.skip_lo ? t : t + W;
       const int mi = r < a.cur ? r : a.L + r - a.cur;
       Split4 s{0, 0, 0, 0};
@@ -198,12 +203,17 @@ __global__ void __launch_bounds__(256) k_conv(ConvArgs a, int log_n, const Mod* 
 }
 template <int W>
 static int conv_launch_w(const HolmesCtx& c, const ConvArgs& a, cudaStream_t st) {
-  const size_t smem = (size_t)a.ntgt * W * sizeof(uint2);
   const size_t work = (size_t)a.items << c.log_n;
   size_t blocks = (work + 255) / 256;
   if (blocks > 148 * 8) blocks = 148 * 8;
+  // target groups: enough blocks for every SM to hold several, at least 4 targets per group
+  int groups = (int)((148 * 8 + blocks - 1) / blocks);
+  groups = std::max(1, std::min(groups, a.ntgt / 4));
+  const int tpg = (a.ntgt + groups - 1) / groups;
+  groups = (a.ntgt + tpg - 1) / tpg;
+  const size_t smem = (size_t)tpg * W * sizeof(uint2);
   count_launch();
-  k_conv<W><<<(unsigned)blocks, 256, smem, st>>>(a, c.log_n, c.d_mod);
+  k_conv<W><<<dim3((unsigned)blocks, (unsigned)groups), 256, smem, st>>>(a, c.log_n, c.d_mod);
   return (int)cudaGetLastError();
 }
 static int conv_launch(const HolmesCtx& c, const ConvArgs& a, cudaStream_t st) {
@@ -576,6 +586,8 @@ static int ks_inner_launch(const HolmesCtx& c, const KsInnerArgs& ia, cudaStream
   if (ia.beta > 16) return -3;   // the split sums hold 16 products
   count_launch();
   const dim3 grid((unsigned)(c.n / 256), (unsigned)(ia.cur + ia.K));
+  // (the generic loop, k_ks_inner<0>, fits 5 CTAs per SM at 50 registers but measured 2% slower than these on the
+  // config-3 layer's single-ciphertext key switches)
   if (ia.beta <= 2) k_ks_inner<2><<<grid, 256, 0, st>>>(ia, c.log_n, c.d_mod);
   else if (ia.beta <= 5) k_ks_inner<5><<<grid, 256, 0, st>>>(ia, c.log_n, c.d_mod);
   else k_ks_inner<0><<<grid, 256, 0, st>>>(ia, c.log_n, c.d_mod);
@@ -771,6 +783,24 @@ int rescale(const HolmesCtx& c, const u64* in, long long in_stride, u64* out, lo
             u64* scratch, cudaStream_t st, int dbl, const u64* sub, long long sub_stride, const u64* cst) {
   if (cur < 2 || cur > c.L) return -2;
   const int N = c.n;
+  if (c.log_n == 16) {
+    // the two-pass NTTs: 16 CTAs per polynomial and pass instead of one 8-CTA cluster, so a rescale of one or two
+    // ciphertexts still spreads over the GPU; the forward NTT's intermediate lives in `out` (each second-pass CTA
+    // reads its rows before its store overwrites them)
+    const PolyMap pin = poly_map(1, in_stride, N, cur - 1);
+    const PolyMap pscr = poly_map(1, N, N, cur - 1);
+    {
+      NttTables T{c.d_itw, c.d_mod};
+      const int e = ntt16_inverse(T, ModPlain{pin}, ScLimb{c.d_ninv, 0, pin}, LdPlain{in + (size_t)(cur - 1) * N, pin},
+                                  IMPlain{scratch, pscr}, StPlain{scratch, pscr}, comps, st);
+      if (e) return e;
+    }
+    NttTables T{c.d_tw, c.d_mod};
+    const PolyMap pim = poly_map(cur - 1, out_stride, N, 0);
+    LdRescale ld{scratch, c.d_mod, c.q[cur - 1], cur, c.log_n};
+    StRescale sr{in, in_stride, out, out_stride, c.d_mod, c.rs_qinv(cur), cur, c.log_n, sub, sub_stride, cst, dbl};
+    return ntt16_forward(T, ModPlain{pim}, ld, IMPlain{out, pim}, sr, comps * (cur - 1), st);
+  }
   {
     NttTables T{c.d_itw, c.d_mod};
     PolyMap pin = poly_map(1, in_stride, N, cur - 1);

@@ -121,6 +121,9 @@ int keygen(const HolmesCtx& c, u64 galois, int cap, u64* key, cudaStream_t st);
 int encrypt(const HolmesCtx& c, const u64* m, int cur, u64 counter, u64* c0, u64* c1, cudaStream_t st);
 
 enum EwOp { EW_ADD = 0, EW_SUB = 1, EW_MUL = 2, EW_NEG = 3 };
+int tensor_product(const HolmesCtx& c, const u64* a0, const u64* a1, long long a_item, const u64* b0, const u64* b1,
+                   long long b_item, u64* d0, u64* d1, u64* d2, long long d_item, int items, int limbs,
+                   cudaStream_t st);
 int elementwise(const HolmesCtx& c, int op, const u64* a, const u64* b, u64* out, int items, int limbs,
                 long long a_item, long long b_item, long long o_item, cudaStream_t st);
 int mul_i(const HolmesCtx& c, const u64* a, u64* out, int items, int limbs, long long a_item, long long o_item,

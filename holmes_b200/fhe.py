@@ -207,6 +207,7 @@ class Context:
         self._flag = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._consts: collections.OrderedDict = collections.OrderedDict()
         self._modup_cache: collections.OrderedDict = collections.OrderedDict()
+        self._modup_by_storage: dict = {}
         self._modup_cache_bytes = 0
         self._enc_counter = 0
         self.key_bytes = 0
@@ -254,6 +255,7 @@ class Context:
             _modup_forget(self, *tensors)
         else:
             self._modup_cache.clear()
+            self._modup_by_storage.clear()
             self._modup_cache_bytes = 0
 
     def p_mod_q_dev(self, cur: int) -> torch.Tensor:
@@ -361,6 +363,7 @@ class Context:
             self._work.clear()
             self._consts.clear()
             self._modup_cache.clear()
+            self._modup_by_storage.clear()
             self._modup_cache_bytes = 0
             self.__dict__.pop("_ones_rows", None)
             _lib.call("holmes_ctx_destroy", self.handle)
@@ -709,13 +712,15 @@ def align_to(a: Cipher, target: CipherState, ctx) -> Cipher:
     return cur.cipher_like([c[:, :want].contiguous() for c in cur.cv], state=state)
 
 
-def _modup(ctx: Context, c1: torch.Tensor, cur: int, items: int) -> tuple[torch.Tensor, int]:
+def _modup(ctx: Context, c1: torch.Tensor, cur: int, items: int, reuse: bool = False) -> tuple[torch.Tensor, int]:
     """The ModUp digits of ``c1`` (its first ``cur`` limbs, ``items`` items).  Digits of a recent input are reused:
     the reference rotates one ciphertext by many offsets one call at a time (attention's per-head rotations), and
     every such rotation needs the same digits.  An input is the same when its memory, item stride, level, item count
     and torch version counter (bumped by every in-place torch write, shared by all views) are; the cache holds the
     input tensor, so its memory cannot be handed to another tensor while the entry lives, and the engine's own calls
-    that write into caller-provided buffers drop the entries they overlap (``_modup_forget``)."""
+    that write into caller-provided buffers drop the entries they overlap (``_modup_forget``).  ``reuse`` marks a
+    call whose digits are worth keeping (a rotation of a caller's ciphertext, which may be rotated again); the
+    third component of a product, relinearised once, is looked up but not kept."""
     dig_item = ctx.beta(cur) * (cur + ctx.K) * ctx.N
     key = (c1.data_ptr(), int(c1._version), int(c1.stride(0)), int(cur), int(items))
     hit = ctx._modup_cache.get(key)
@@ -729,13 +734,25 @@ def _modup(ctx: Context, c1: torch.Tensor, cur: int, items: int) -> tuple[torch.
               scratch.data_ptr(), _stream())
     OPTIMER.stop(tok, items * (cur + dig_item // ctx.N) * ctx.N * 8)
     nbytes = int(digits.numel()) * 8
-    if nbytes <= MODUP_CACHE_BYTES // 4:
+    if reuse and nbytes <= MODUP_CACHE_BYTES // 4:
         cache = ctx._modup_cache
-        cache[key] = (c1, digits, nbytes)
+        sp = c1.untyped_storage().data_ptr()
+        cache[key] = (c1, digits, nbytes, sp)
+        ctx._modup_by_storage.setdefault(sp, set()).add(key)
         ctx._modup_cache_bytes += nbytes
         while ctx._modup_cache_bytes > MODUP_CACHE_BYTES:
-            ctx._modup_cache_bytes -= cache.popitem(last=False)[1][2]
+            _modup_drop(ctx, next(iter(cache)))
     return digits, dig_item
+
+
+def _modup_drop(ctx: Context, key) -> None:
+    entry = ctx._modup_cache.pop(key)
+    ctx._modup_cache_bytes -= entry[2]
+    keys = ctx._modup_by_storage.get(entry[3])
+    if keys is not None:
+        keys.discard(key)
+        if not keys:
+            del ctx._modup_by_storage[entry[3]]
 
 
 #: device bytes of ModUp digits kept for reuse per context
@@ -743,19 +760,15 @@ MODUP_CACHE_BYTES = 2 << 30
 
 
 def _modup_forget(ctx: Context, *tensors) -> None:
-    """Drop the cached digits of every input whose memory overlaps one of ``tensors`` (about to be written by a raw
-    kernel launch, which torch's version counter does not see)."""
-    cache = ctx._modup_cache
-    if not cache:
+    """Drop the cached digits of every input that shares storage with one of ``tensors`` (about to be written by a raw
+    kernel launch, which torch's version counter does not see); memory of different storages never overlaps."""
+    if not ctx._modup_cache:
         return
-    def span(t):   # the whole storage: conservative for views
-        st = t.untyped_storage()
-        return st.data_ptr(), st.data_ptr() + int(st.nbytes())
-
-    spans = [span(t) for t in tensors if t is not None]
-    for key in [k for k, (src, _, _) in cache.items()
-                if any(lo < hi2 and lo2 < hi for lo, hi in spans for lo2, hi2 in [span(src)])]:
-        ctx._modup_cache_bytes -= cache.pop(key)[2]
+    for t in tensors:
+        if t is None:
+            continue
+        for key in list(ctx._modup_by_storage.get(t.untyped_storage().data_ptr(), ())):
+            _modup_drop(ctx, key)
 
 
 def _keyswitch(ctx: Context, digits: torch.Tensor, dig_item: int, cur: int, galois: int, key, add0, add1, add_item,
@@ -774,8 +787,9 @@ def _keyswitch(ctx: Context, digits: torch.Tensor, dig_item: int, cur: int, galo
 
 
 def rotate_batch(ctx: Context, c0: torch.Tensor, c1: torch.Tensor, cur: int, rotation: int, out0: torch.Tensor,
-                 out1: torch.Tensor, post0=None, post1=None) -> None:
-    """out = rot((c0, c1), rotation) [+ post] for a batch [items][>= cur][N] sharing one key."""
+                 out1: torch.Tensor, post0=None, post1=None, reuse: bool = True) -> None:
+    """out = rot((c0, c1), rotation) [+ post] for a batch [items][>= cur][N] sharing one key.  ``reuse``: keep the
+    input's ModUp digits for further rotations of it (off for one-off intermediates such as a Horner accumulator)."""
     items = int(c0.shape[0])
     g = ctx.galois(rotation)
     _modup_forget(ctx, out0, out1)
@@ -787,7 +801,7 @@ def rotate_batch(ctx: Context, c0: torch.Tensor, c1: torch.Tensor, cur: int, rot
             _ew(ctx, 0, c0, post0, out0, cur)
             _ew(ctx, 0, c1, post1, out1, cur)
         return
-    digits, dig_item = _modup(ctx, c1, cur, items)
+    digits, dig_item = _modup(ctx, c1, cur, items, reuse)
     _keyswitch(ctx, digits, dig_item, cur, g, ctx.switch_key(g, cur), c0, None, _item_stride(c0), out0, out1, items,
                post0, post1, 0 if post0 is None else _item_stride(post0))
 
@@ -839,7 +853,7 @@ def fast_rotate(a: Cipher, rotations, ctx, output_ext: bool = False) -> Cipher:
                           _stream())
             continue
         if digits is None:
-            digits, dig_item = _modup(ctx, a.cv[1], cur, 1)
+            digits, dig_item = _modup(ctx, a.cv[1], cur, 1, True)
         key_t, cap = ctx.switch_key(g, cur)
         _lib.call("holmes_keyswitch_ext", ctx.handle, digits.data_ptr(), dig_item, cur, key_t.data_ptr(), cap, int(g),
                   a.cv[0].data_ptr(), _item_stride(a.cv[0]), block.cv[0][b:b + 1].data_ptr(),
@@ -950,7 +964,7 @@ def prepare_hoisted_baby_rotations(a: Cipher, baby_offsets, ctx, strategy: str =
             block.cv[1][b].copy_(a.cv[1][0, :cur])
             continue
         if digits is None:
-            digits, dig_item = _modup(ctx, a.cv[1], cur, 1)
+            digits, dig_item = _modup(ctx, a.cv[1], cur, 1, True)
         _keyswitch(ctx, digits, dig_item, cur, g, ctx.switch_key(g, cur), a.cv[0], None, 0, block.cv[0][b:b + 1],
                    block.cv[1][b:b + 1], 1)
     return (block,)
@@ -990,7 +1004,7 @@ def giant_horner(ctx: Context, res: torch.Tensor, giant_offset: int) -> tuple[to
     for g in range(G - 2, -1, -1):
         n0 = torch.empty_like(acc0)
         n1 = torch.empty_like(acc1)
-        rotate_batch(ctx, acc0, acc1, cur, giant_offset, n0, n1, post0=res[0, g], post1=res[1, g])
+        rotate_batch(ctx, acc0, acc1, cur, giant_offset, n0, n1, post0=res[0, g], post1=res[1, g], reuse=False)
         acc0, acc1 = n0, n1
     return acc0, acc1
 
@@ -1095,16 +1109,19 @@ def homo_mul_no_relin(a: Cipher, b: Cipher, ctx) -> Cipher:
     # scale is the same at every level)
     cur = min(int(a.state.cur_limbs), int(b.state.cur_limbs))
     n = a.batch_size
-    shape = (n, cur, ctx.N)
-    d0 = torch.empty(shape, dtype=torch.uint64, device=ctx.device)
-    d1 = torch.empty_like(d0)
-    d2 = torch.empty_like(d0)
-    t = torch.empty_like(d0)
-    _ew(ctx, 2, a.cv[0], b.cv[0], d0, cur)
-    _ew(ctx, 2, a.cv[0], b.cv[1], d1, cur)
-    _ew(ctx, 2, a.cv[1], b.cv[0], t, cur)
-    _ew(ctx, 0, d1, t, d1, cur)
-    _ew(ctx, 2, a.cv[1], b.cv[1], d2, cur)
+    storage = torch.empty((3, n, cur, ctx.N), dtype=torch.uint64, device=ctx.device)
+    d0, d1, d2 = storage[0], storage[1], storage[2]
+    if _item_stride(a.cv[0]) != _item_stride(a.cv[1]) or _item_stride(b.cv[0]) != _item_stride(b.cv[1]):
+        t = torch.empty_like(d0)
+        _ew(ctx, 2, a.cv[0], b.cv[0], d0, cur)
+        _ew(ctx, 2, a.cv[0], b.cv[1], d1, cur)
+        _ew(ctx, 2, a.cv[1], b.cv[0], t, cur)
+        _ew(ctx, 0, d1, t, d1, cur)
+        _ew(ctx, 2, a.cv[1], b.cv[1], d2, cur)
+    else:
+        _lib.call("holmes_tensor_product", ctx.handle, a.cv[0].data_ptr(), a.cv[1].data_ptr(), _item_stride(a.cv[0]),
+                  b.cv[0].data_ptr(), b.cv[1].data_ptr(), _item_stride(b.cv[0]), d0.data_ptr(), d1.data_ptr(),
+                  d2.data_ptr(), cur * ctx.N, n, cur, _stream())
     sf = None
     if a.state.scaling_factor is not None and b.state.scaling_factor is not None:
         sf = float(a.state.scaling_factor) * float(b.state.scaling_factor)

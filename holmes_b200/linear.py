@@ -482,7 +482,7 @@ class LinearOperator:
                 storage[0, 0].copy_(c0)
                 storage[0, 1].copy_(c1)
         if max(lo, 1) < hi:
-            digits, dig_item = F._modup(ctx, c1, cur, n_in)
+            digits, dig_item = F._modup(ctx, c1, cur, n_in, True)
             for b in range(max(lo, 1), hi):
                 g = ctx.galois(plan.baby_strides[b])
                 if ext:
@@ -610,14 +610,14 @@ class LinearOperator:
             if acc0 is None:
                 if shift:
                     n0, n1 = torch.empty_like(g0), torch.empty_like(g1)
-                    F.rotate_batch(ctx, g0, g1, cur, shift, n0, n1)
+                    F.rotate_batch(ctx, g0, g1, cur, shift, n0, n1, reuse=False)
                     acc0, acc1 = n0, n1
                 else:
                     acc0, acc1 = g0.clone(), g1.clone()
             else:
                 n0, n1 = torch.empty_like(acc0), torch.empty_like(acc1)
                 if shift:
-                    F.rotate_batch(ctx, g0, g1, cur, shift, n0, n1, post0=acc0, post1=acc1)
+                    F.rotate_batch(ctx, g0, g1, cur, shift, n0, n1, post0=acc0, post1=acc1, reuse=False)
                 else:
                     F._ew(ctx, 0, g0, acc0, n0, cur)
                     F._ew(ctx, 0, g1, acc1, n1, cur)

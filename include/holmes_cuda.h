@@ -114,6 +114,11 @@ int holmes_pack_structured(const void* const* sources, const long long* row_stri
 /* op: 0 add, 1 sub, 2 multiply, 3 negate (b unused); limb l uses modulus l */
 int holmes_elementwise(void* ctx, int op, const uint64_t* a, const uint64_t* b, uint64_t* out, int items, int limbs,
                        long long a_item, long long b_item, long long out_item, void* stream);
+/* tensor product before relinearisation (fhe.homo_mul without relin, primitives.py:21-37): d0 = a0 b0,
+ * d1 = a0 b1 + a1 b0, d2 = a1 b1 (mod q_l), one launch; item strides even */
+int holmes_tensor_product(void* ctx, const uint64_t* a0, const uint64_t* a1, long long a_item, const uint64_t* b0,
+                          const uint64_t* b1, long long b_item, uint64_t* d0, uint64_t* d1, uint64_t* d2,
+                          long long d_item, int items, int limbs, void* stream);
 /* multiply by X^(N/2) (slot-wise i) */
 int holmes_mul_i(void* ctx, const uint64_t* a, uint64_t* out, int items, int limbs, long long a_item, long long out_item,
                  void* stream);

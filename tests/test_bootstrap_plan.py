@@ -105,3 +105,34 @@ def test_refresh_iterations_validated_on_host():
     with pytest.raises(ValueError):
         BS.with_correction(object(), None, lambda c: calls.append(c), 3, 8)
     assert not calls
+
+
+@pytest.mark.parametrize("degree", [7, 8, 31, 63, 64, 100])
+def test_paterson_stockmeyer_split_reproduces_the_series(degree):
+    """EvalMod's Chebyshev-basis split p = q T_n + r (bootstrap.cheb_split), applied recursively down to leaves of
+    ps_baby(degree) coefficients exactly as bootstrap._chebyshev / OracleBootstrap.chebyshev do, evaluates to the
+    series itself; and it never needs more than log2(degree + 1) + 1 levels."""
+    from numpy.polynomial import chebyshev as C
+
+    rng = np.random.default_rng(degree)
+    c = list(rng.normal(size=degree + 1) / (1 + np.arange(degree + 1)))
+    x = np.linspace(-1, 1, 257)
+    m = BS.ps_baby(degree)
+    T = lambda k: C.chebval(x, [0] * k + [1])  # noqa: E731
+
+    def depth_of(k):   # levels T_k costs in the power tree (T_2k = 2 T_k^2 - 1, T_2k+1 = 2 T_k T_k+1 - T_1)
+        return 0 if k <= 1 else int(np.ceil(np.log2(k)))
+
+    def evalp(cs):
+        if len(cs) <= m:
+            lvl = max(depth_of(k) for k in range(1, len(cs))) + 1 if len(cs) > 1 else 1
+            return C.chebval(x, cs), lvl
+        n = 1 << (int(np.ceil(np.log2(len(cs)))) - 1)
+        q, r = BS.cheb_split(cs, n)
+        (qv, ql), (rv, rl) = evalp(q), evalp(r)
+        return qv * T(n) + rv, max(max(ql, depth_of(n)) + 1, rl)
+
+    val, levels = evalp(c)
+    np.testing.assert_allclose(val, C.chebval(x, c), atol=1e-12)
+    assert levels <= int(np.ceil(np.log2(degree + 1))) + 1
+    assert m == 1 << max(1, int(np.ceil(np.log2(degree + 1) / 2)))
