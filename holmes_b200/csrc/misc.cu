@@ -538,29 +538,29 @@ __device__ __forceinline__ void split_words(u64* p) {
   *reinterpret_cast<ulonglong2*>(p) = o;
 }
 
-template <int IW, int GPT>
+template <int IW, int GPT, int GG = kMacGG>
 struct M3Geom {
-  static constexpr int THREADS = IW * (kMacGG / GPT) * 32;
-  static constexpr int PT_WORDS = kMacGG * kM3SB * 32;
+  static constexpr int THREADS = IW * (GG / GPT) * 32;
+  static constexpr int PT_WORDS = GG * kM3SB * 32;
   static constexpr int BB_WORDS = IW * 2 * kM3SB * 32;
   static constexpr int STAGE_WORDS = PT_WORDS + BB_WORDS;
   static constexpr int SMEM = kM3NS * STAGE_WORDS * 8;
   static constexpr int MINB = (228 * 1024) / (SMEM + 1024) < 4 ? (228 * 1024) / (SMEM + 1024) : 4;
 };
 
-template <int IW, int GPT>
-__global__ void __launch_bounds__(M3Geom<IW, GPT>::THREADS, M3Geom<IW, GPT>::MINB)
+template <int IW, int GPT, int GG = kMacGG>
+__global__ void __launch_bounds__(M3Geom<IW, GPT, GG>::THREADS, M3Geom<IW, GPT, GG>::MINB)
     k_bsgs_mac3(u64* __restrict__ res, InPtrs in, long long bstride, int nb, int inputs, int G,
                 const u64* __restrict__ pts, long long pstride, int limbs, ModSrc ms, int log_n) {
-  using Geo = M3Geom<IW, GPT>;
-  constexpr int WPI = kMacGG / GPT;  // warps per input
+  using Geo = M3Geom<IW, GPT, GG>;
+  constexpr int WPI = GG / GPT;  // warps per input
   extern __shared__ __align__(16) u64 mac_smem[];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int itiles = (inputs + IW - 1) / IW;
   const int j0 = (blockIdx.x / itiles) * 32;
   const int i0 = (blockIdx.x % itiles) * IW;
   const int iw = w / WPI, gq = w % WPI;
-  const int limb = blockIdx.y, g0 = blockIdx.z * kMacGG;
+  const int limb = blockIdx.y, g0 = blockIdx.z * GG;
   const Mod m = ms.get(limb);
   const size_t lpos = ((size_t)limb << log_n) + j0;
   const bool active = i0 + iw < inputs;
@@ -668,16 +668,19 @@ __global__ void __launch_bounds__(M3Geom<IW, GPT>::THREADS, M3Geom<IW, GPT>::MIN
   }
 }
 
-template <int IW, int GPT>
+constexpr int kMacTile1 = 12;   // default tiles (IW x GPT) for one and two inputs
+constexpr int kMacTile2 = 24;
+
+template <int IW, int GPT, int GG = kMacGG>
 static int launch_mac3(u64* res, const InPtrs& in, long long bstride, int nb, int inputs, int groups, const u64* pts,
                        long long pstride, int limbs, const ModSrc& ms, int log_n, int n, cudaStream_t st) {
-  using Geo = M3Geom<IW, GPT>;
-  cudaError_t e = set_smem_once((const void*)k_bsgs_mac3<IW, GPT>, Geo::SMEM);
+  using Geo = M3Geom<IW, GPT, GG>;
+  cudaError_t e = set_smem_once((const void*)k_bsgs_mac3<IW, GPT, GG>, Geo::SMEM);
   if (e != cudaSuccess) return (int)e;
-  dim3 grid((unsigned)((n / 32) * ((inputs + IW - 1) / IW)), (unsigned)limbs, (unsigned)((groups + kMacGG - 1) / kMacGG));
+  dim3 grid((unsigned)((n / 32) * ((inputs + IW - 1) / IW)), (unsigned)limbs, (unsigned)((groups + GG - 1) / GG));
   count_launch();
-  k_bsgs_mac3<IW, GPT><<<grid, Geo::THREADS, Geo::SMEM, st>>>(res, in, bstride, nb, inputs, groups, pts, pstride,
-                                                               limbs, ms, log_n);
+  k_bsgs_mac3<IW, GPT, GG><<<grid, Geo::THREADS, Geo::SMEM, st>>>(res, in, bstride, nb, inputs, groups, pts, pstride,
+                                                                   limbs, ms, log_n);
   return (int)cudaGetLastError();
 }
 
@@ -726,9 +729,19 @@ int bsgs_mac(ModSrc ms, u64* res, const u64* const* c0s, const u64* const* c1s,
     k_bsgs_mac2<<<grid, 256, smem, st>>>(res, in, bstride, nb, inputs, groups, pts, pstride, limbs, ms, log_n);
     return (int)cudaGetLastError();
   }
+  // the tile's inputs match the call's: a 4-input tile given one input leaves three quarters of its warps idle (the
+  // reference's operators MAC one ciphertext per call)
   const char* cfg = getenv("HOLMES_MAC_TILE");  // A/B timing of tile shapes: "IWxGPT"
-  const int c = cfg && cfg[0] && cfg[1] == 'x' ? atoi(cfg) * 10 + atoi(cfg + 2) : 44;
+  const int c = cfg && cfg[0] && cfg[1] == 'x' ? atoi(cfg) * 10 + atoi(cfg + 2)
+                                                : (inputs == 1 ? kMacTile1 : inputs == 2 ? kMacTile2 : 44);
+  // one giant (a bootstrap transform level: the diagonals of one level summed): a tile of one giant per block, not
+  // eight copies of it
+  if (!(cfg && cfg[0]) && groups == 1 && inputs == 1)
+    return launch_mac3<1, 1, 1>(res, in, bstride, nb, inputs, groups, pts, pstride, limbs, ms, log_n, n, st);
   switch (c) {
+    case 11: return launch_mac3<1, 1>(res, in, bstride, nb, inputs, groups, pts, pstride, limbs, ms, log_n, n, st);
+    case 12: return launch_mac3<1, 2>(res, in, bstride, nb, inputs, groups, pts, pstride, limbs, ms, log_n, n, st);
+    case 14: return launch_mac3<1, 4>(res, in, bstride, nb, inputs, groups, pts, pstride, limbs, ms, log_n, n, st);
     case 22: return launch_mac3<2, 2>(res, in, bstride, nb, inputs, groups, pts, pstride, limbs, ms, log_n, n, st);
     case 24: return launch_mac3<2, 4>(res, in, bstride, nb, inputs, groups, pts, pstride, limbs, ms, log_n, n, st);
     case 42: return launch_mac3<4, 2>(res, in, bstride, nb, inputs, groups, pts, pstride, limbs, ms, log_n, n, st);

@@ -258,10 +258,13 @@ def test_elementwise_rescale_mul_i_relin_bitexact(pair):
     assert np.abs(got - za * zb).max() < 1e-4
 
 
-def test_bsgs_mac_bitexact(pair):
+@pytest.mark.parametrize("inputs,G,nb", [(3, 3, 5), (1, 8, 19), (1, 1, 9), (2, 9, 8), (5, 2, 17)])
+def test_bsgs_mac_bitexact(pair, inputs, G, nb):
+    """Every tile the MAC dispatches by input count (one, two, four inputs per block), with giant counts below, at
+    and above the block's 8 and baby counts that leave a short last stage."""
     o, _, ctx = pair
-    rng = np.random.default_rng(12)
-    nb, G, inputs, cur = 5, 3, 3, 4
+    rng = np.random.default_rng(12 + inputs + G)
+    cur = 4
     pts = np.stack([residues(o.pr.q, cur, o.pr.n, rng) for _ in range(G * nb)])
     babies = [[(residues(o.pr.q, cur, o.pr.n, rng), residues(o.pr.q, cur, o.pr.n, rng)) for _ in range(nb)]
               for _ in range(inputs)]
