@@ -581,13 +581,81 @@ struct ModKsQ {
   __device__ int operator()(int p) const { return (p % (2 * cur)) % cur; }
 };
 
+// One ciphertext (the reference's rotations are per ciphertext): nothing is reused across items, so every load of
+// a word -- the beta digit words, both components' key words, the addends -- is issued before the first product
+// (three times beta independent loads in flight per thread), and the kernel is held to 64 registers for four CTAs per
+// SM; the multi-item kernel keeps the key words in registers across items instead (70 registers, three CTAs per SM,
+// gathered digit loads one item at a time).  Same sums, same residues.
+template <int MAXB>
+__global__ void __launch_bounds__(256, 4) k_ks_inner1(KsInnerArgs a, int log_n, const Mod* __restrict__ mods) {
+  const size_t dstep = (size_t)(a.cur + a.K) << log_n, kstep = (size_t)(a.cap + a.K) << log_n;
+  const size_t kcomp = (size_t)a.key_beta * kstep;
+  const int n = blockIdx.x * blockDim.x + threadIdx.x;
+  const int r = blockIdx.y;
+  const u32 src = a.galois > 1 ? automorph_src((u32)n, a.galois, log_n) : (u32)n;
+  const bool qlimb = r < a.cur;
+  const int kr = qlimb ? r : a.cap + (r - a.cur);
+  const Mod m = mods[qlimb ? r : a.L + (r - a.cur)];
+  const u64* kp = a.key + ((size_t)kr << log_n) + n;
+  const size_t roff = (size_t)r << log_n;
+  const u64* d = a.digits + roff + src;
+  u64 dv[MAXB], k0[MAXB], k1[MAXB];
+#pragma unroll
+  for (int j = 0; j < MAXB; ++j) {
+    if (j < a.beta) {
+      dv[j] = d[j * dstep];
+      k0[j] = kp[j * kstep];
+      k1[j] = kp[kcomp + j * kstep];
+    }
+  }
+  u64 ad0 = 0, ad1 = 0;
+  if (qlimb) {
+    if (a.add0) ad0 = a.add0[roff + src];
+    if (a.add1) ad1 = a.add1[roff + src];
+  }
+  Split4 s0{0, 0, 0, 0}, s1{0, 0, 0, 0};
+#pragma unroll
+  for (int j = 0; j < MAXB; ++j) {
+    if (j < a.beta) {
+      split_mac(s0, dv[j], k0[j]);
+      split_mac(s1, dv[j], k1[j]);
+    }
+  }
+  if (qlimb) {
+    u64 u0 = fold_split(s0, m), u1 = fold_split(s1, m);
+    if (a.add0) u0 = add_mod(u0, ad0, m.q);
+    if (a.add1) u1 = add_mod(u1, ad1, m.q);
+    if (a.post0) u0 = add_mod(u0, a.post0[roff + n], m.q);
+    if (a.post1) u1 = add_mod(u1, a.post1[roff + n], m.q);
+    if (a.qscale) {
+      u0 = shoup(u0, a.qscale[r], m.q);
+      u1 = shoup(u1, a.qscale[r], m.q);
+    }
+    a.out0[roff + n] = u0;
+    a.out1[roff + n] = u1;
+  } else {
+    const size_t po = ((size_t)(r - a.cur) << log_n) + n;
+    a.p0[po] = fold_split(s0, m);
+    a.p1[po] = fold_split(s1, m);
+  }
+}
+
 static int ks_inner_launch(const HolmesCtx& c, const KsInnerArgs& ia, cudaStream_t st) {
   if (c.n < 256) return -5;
   if (ia.beta > 16) return -3;   // the split sums hold 16 products
   count_launch();
   const dim3 grid((unsigned)(c.n / 256), (unsigned)(ia.cur + ia.K));
   // (the generic loop, k_ks_inner<0>, fits 5 CTAs per SM at 50 registers but measured 2% slower than these on the
-  // config-3 layer's single-ciphertext key switches)
+  // config-3 layer's single-ciphertext key switches: its loads wait one digit at a time)
+  static const bool single = [] {   // A/B timing: HOLMES_KS_INNER1=0 keeps single items on the multi-item kernel
+    const char* v = getenv("HOLMES_KS_INNER1");
+    return !(v && v[0] == '0');
+  }();
+  if (ia.items == 1 && ia.beta <= 5 && single) {
+    if (ia.beta <= 2) k_ks_inner1<2><<<grid, 256, 0, st>>>(ia, c.log_n, c.d_mod);
+    else k_ks_inner1<5><<<grid, 256, 0, st>>>(ia, c.log_n, c.d_mod);
+    return (int)cudaGetLastError();
+  }
   if (ia.beta <= 2) k_ks_inner<2><<<grid, 256, 0, st>>>(ia, c.log_n, c.d_mod);
   else if (ia.beta <= 5) k_ks_inner<5><<<grid, 256, 0, st>>>(ia, c.log_n, c.d_mod);
   else k_ks_inner<0><<<grid, 256, 0, st>>>(ia, c.log_n, c.d_mod);
