@@ -772,9 +772,10 @@ def _modup_forget(ctx: Context, *tensors) -> None:
 
 
 def _keyswitch(ctx: Context, digits: torch.Tensor, dig_item: int, cur: int, galois: int, key, add0, add1, add_item,
-               out0: torch.Tensor, out1: torch.Tensor, items: int, post0=None, post1=None, post_item: int = 0) -> None:
+               out0: torch.Tensor, out1: torch.Tensor, items: int, post0=None, post1=None, post_item: int = 0,
+               workspace: str = "ks") -> None:
     key_t, cap = key
-    scratch = ctx.workspace("ks", items * 2 * (ctx.K + cur) * ctx.N)
+    scratch = ctx.workspace(workspace, items * 2 * (ctx.K + cur) * ctx.N)
     beta = ctx.beta(cur)
     words = items * (beta * (cur + ctx.K) + 2 * cur) + 2 * beta * (cur + ctx.K)
     words += items * cur * ((add0 is not None) + (add1 is not None) + (post0 is not None) + (post1 is not None))
@@ -956,18 +957,53 @@ def prepare_hoisted_baby_rotations(a: Cipher, baby_offsets, ctx, strategy: str =
     offsets = [int(o) for o in baby_offsets]
     cur = int(a.state.cur_limbs)
     block = _new_cipher(ctx, len(offsets), cur, a.state, a.slots)
-    digits = dig_item = None
+    switches = []
     for b, off in enumerate(offsets):
         g = ctx.galois(off)
         if g == 1:
             block.cv[0][b].copy_(a.cv[0][0, :cur])
             block.cv[1][b].copy_(a.cv[1][0, :cur])
-            continue
-        if digits is None:
-            digits, dig_item = _modup(ctx, a.cv[1], cur, 1, True)
-        _keyswitch(ctx, digits, dig_item, cur, g, ctx.switch_key(g, cur), a.cv[0], None, 0, block.cv[0][b:b + 1],
-                   block.cv[1][b:b + 1], 1)
+        else:
+            switches.append((b, g, ctx.switch_key(g, cur)))   # keys fetched (or generated) on the caller's stream
+    if not switches:
+        return (block,)
+    digits, dig_item = _modup(ctx, a.cv[1], cur, 1, True)
+    # The offsets' key switches are independent (one ciphertext's key switch fills less than the GPU): they run on
+    # the caller's stream and KS_STREAMS - 1 side streams, each with its own scratch, after the ModUp; the caller's
+    # stream waits for all of them before returning, so every later use of the block is ordered after them.
+    lanes = _ks_lanes(ctx, len(switches))
+    for i, (b, g, key) in enumerate(switches):
+        k = i % len(lanes)
+        with torch.cuda.stream(lanes[k]):
+            _keyswitch(ctx, digits, dig_item, cur, g, key, a.cv[0], None, 0, block.cv[0][b:b + 1],
+                       block.cv[1][b:b + 1], 1, workspace=f"ks{k}")
+    _ks_join(lanes)
     return (block,)
+
+
+#: streams the independent key switches of one hoisted rotation set are spread over (the caller's and side streams)
+KS_STREAMS = 4
+
+
+def _ks_lanes(ctx: Context, jobs: int) -> list:
+    """The caller's stream, then side streams (created once per context) that first wait for everything the caller's
+    stream has queued."""
+    main = torch.cuda.current_stream(ctx.device)
+    n = max(1, min(int(KS_STREAMS), int(jobs)))
+    if n == 1:
+        return [main]
+    side = ctx.__dict__.get("_side_streams")
+    if side is None:
+        side = ctx._side_streams = [torch.cuda.Stream(device=ctx.device) for _ in range(int(KS_STREAMS) - 1)]
+    lanes = [main] + side[:n - 1]
+    for s in lanes[1:]:
+        s.wait_stream(main)
+    return lanes
+
+
+def _ks_join(lanes: list) -> None:
+    for s in lanes[1:]:
+        lanes[0].wait_stream(s)
 
 
 def bsgs_partial_sums(ctx: Context, baby_blocks, plaintexts: Plaintext, giants: int) -> torch.Tensor:
