@@ -992,7 +992,7 @@ def run_layer(args) -> None:
             "kernels": {k: {"launches": val["launches"], "ms_per_step": round(val["ms"], 2)} for k, val in ops.items()},
             "cpu_baseline": cpu, "gpu_launches": int(launches), "clocks": ck,
             "e2e": {"value": round(statistics.median(e2e_times), 4), "unit": "s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "steps": e2e_steps},
+                    "d2h_bytes_per_step": d2h, "steps": e2e_steps, "step_times_s": [round(t, 3) for t in e2e_times]},
             "setup_s": round(setup.setup_seconds, 1), "step_times_s": [round(t, 3) for t in times],
             "device_memory_per_step": memory}
     if check is not None:

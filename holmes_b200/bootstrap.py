@@ -432,17 +432,23 @@ def linear_level(ct: F.Cipher, offsets, pt: F.Plaintext) -> F.Cipher:
     items = ct.batch_size
     nb = len(offsets)
     store = torch.empty((2, nb, items, cur, ctx.N), dtype=torch.uint64, device=ctx.device)
-    digits = dig_item = None
+    switches = []
     for b, off in enumerate(offsets):
         g = ctx.galois(int(off))
         if g == 1:
             store[0, b].copy_(ct.cv[0][:, :cur])
             store[1, b].copy_(ct.cv[1][:, :cur])
-            continue
-        if digits is None:
-            digits, dig_item = F._modup(ctx, ct.cv[1], cur, items)
-        F._keyswitch(ctx, digits, dig_item, cur, g, ctx.switch_key(g, cur), ct.cv[0], None, F._item_stride(ct.cv[0]),
-                     store[0, b], store[1, b], items)
+        else:
+            switches.append((b, g, ctx.switch_key(g, cur)))
+    if switches:
+        digits, dig_item = F._modup(ctx, ct.cv[1], cur, items)
+        lanes = F._ks_lanes(ctx, len(switches))   # the level's key switches are independent: spread over streams
+        for i, (b, g, key) in enumerate(switches):
+            k = i % len(lanes)
+            with torch.cuda.stream(lanes[k]):
+                F._keyswitch(ctx, digits, dig_item, cur, g, key, ct.cv[0], None, F._item_stride(ct.cv[0]),
+                             store[0, b], store[1, b], items, workspace=f"ks{k}")
+        F._ks_join(lanes)
     blocks = [F.Cipher([store[0, :, i], store[1, :, i]], ct.state, ct.slots, False, nb, ctx) for i in range(items)]
     res = F.bsgs_partial_sums(ctx, blocks, pt, 1)          # [2][1][items][cur][N]
     out = F.Cipher([res[0, 0], res[1, 0]], F.CipherState(cur, 2, float(ct.state.scaling_factor) * float(ctx.q(cur - 1))),

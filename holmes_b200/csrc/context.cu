@@ -259,6 +259,23 @@ int build_context(HolmesCtx& c, int log_n, int limbs, int dnum, int dcrt_bits, i
 void free_context(HolmesCtx& c) {
   for (void* p : c.owned) cudaFree(p);
   c.owned.clear();
+  if (c.side_ready) {
+    for (cudaStream_t& s : c.side) cudaStreamDestroy(s);
+    for (cudaEvent_t& e : c.ev) cudaEventDestroy(e);
+    c.side_ready = false;
+  }
+}
+
+int ensure_side(const HolmesCtx& c) {
+  if (c.side_ready) return 0;
+  int dev = 0;
+  HOLMES_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev != c.device) HOLMES_CUDA_TRY(cudaSetDevice(c.device));
+  for (cudaStream_t& s : c.side) HOLMES_CUDA_TRY(cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking));
+  for (cudaEvent_t& e : c.ev) HOLMES_CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+  if (dev != c.device) HOLMES_CUDA_TRY(cudaSetDevice(dev));
+  c.side_ready = true;
+  return 0;
 }
 
 // ------------------------------------------------------------------ ChaCha20 block (RFC 8439), host copy

@@ -40,12 +40,21 @@ struct HolmesCtx {
   double* d_fft_tw = nullptr;    // [N/2 - 1][2] special-FFT roots by stage: stage len at len/2 - 1 + j
   u64* d_secret = nullptr;       // [T][N] secret key, NTT form (client side of the simulation context)
   std::vector<void*> owned;
+  // side streams and events for independent chains inside one call (ModUp's digits), created on first use;
+  // every call joins them back into its own stream before returning
+  static constexpr int kSide = 3, kEvents = 17;
+  mutable cudaStream_t side[kSide] = {};
+  mutable cudaEvent_t ev[kEvents] = {};
+  mutable bool side_ready = false;
 
   int beta(int cur) const { return (cur + alpha - 1) / alpha; }
   const Tw* mu_scale(int cur) const { return d_mu_scale + (size_t)cur * beta_max * alpha; }
   const u64* mu_hat(int cur) const { return d_mu_hat + (size_t)cur * beta_max * alpha * T; }
   const Tw* rs_qinv(int cur) const { return d_rs_qinv + (size_t)cur * L; }
 };
+
+// create the context's side streams and events (once; on the context's device)
+int ensure_side(const HolmesCtx& c);
 
 // host modular helpers shared by the C-ABI layer
 u64 host_mul_mod(u64 a, u64 b, u64 q);

@@ -354,11 +354,23 @@ int modup(const HolmesCtx& c, const u64* c1, long long c1_item, int cur, int ite
   }
   const int beta = c.beta(cur);
   const size_t dstride = (size_t)(cur + K) * N;
+  // The digits' chains (conversion, then NTT of its targets) are independent once the iNTT above is done: with few
+  // items one chain fills a fraction of the GPU, so digit j > 0 runs on side stream (j - 1) % 3 after an event on
+  // `st`, and `st` waits for every side chain before returning.
+  const bool fan = beta > 1 && items <= 2 && c.log_n == 16;
+  if (fan) {
+    const int e = ensure_side(c);
+    if (e) return e;
+    HOLMES_CUDA_TRY(cudaEventRecord(c.ev[0], st));
+    for (int k = 0; k < HolmesCtx::kSide && k + 1 < beta; ++k) HOLMES_CUDA_TRY(cudaStreamWaitEvent(c.side[k], c.ev[0], 0));
+  }
+  const cudaStream_t main_st = st;
   for (int j = 0; j < beta; ++j) {
     const int lo = j * A, w = std::min(A, cur - lo);
     u64* dj = digits + (size_t)j * dstride;
     NttTables T{c.d_tw, c.d_mod};
     const int ntgt = cur + K - w;
+    st = fan && j > 0 ? c.side[(j - 1) % HolmesCtx::kSide] : main_st;
     // the digit's own limbs are the input limbs times P^-1, written by the conversion kernel
     ConvArgs ca{scratch + (size_t)lo * N, y_item, dj, dig_item, c.mu_hat(cur) + (size_t)j * A * c.T, c.T,
                 w, ntgt, lo, cur, c.L, items, c1 + (size_t)lo * N, c1_item, c.d_md_pinv + lo};
@@ -382,6 +394,13 @@ int modup(const HolmesCtx& c, const u64* c1, long long c1_item, int cur, int ite
   }
     HOLMES_LOGN_SWITCH(c.log_n, L_)
 #undef L_
+  }
+  if (fan) {
+    const int used = std::min(HolmesCtx::kSide, beta - 1);
+    for (int k = 0; k < used; ++k) {
+      HOLMES_CUDA_TRY(cudaEventRecord(c.ev[1 + k], c.side[k]));
+      HOLMES_CUDA_TRY(cudaStreamWaitEvent(main_st, c.ev[1 + k], 0));
+    }
   }
   return 0;
 }

@@ -842,7 +842,7 @@ def fast_rotate(a: Cipher, rotations, ctx, output_ext: bool = False) -> Cipher:
     offsets = [int(r) for r in rotations]
     block = _new_cipher(ctx, len(offsets), cur + ctx.K, a.state, a.slots)
     block.is_ext = True
-    digits = dig_item = None
+    switches = []
     for b, off in enumerate(offsets):
         g = ctx.galois(off)
         if g == 1:   # (P c0, P c1): P is 0 modulo the special primes
@@ -852,13 +852,18 @@ def fast_rotate(a: Cipher, rotations, ctx, output_ext: bool = False) -> Cipher:
                 _lib.call("holmes_mul_const", ctx.handle, a.cv[c][:1, :cur].data_ptr(), pm.data_ptr(),
                           block.cv[c][b:b + 1].data_ptr(), 1, cur, _item_stride(a.cv[c]), _item_stride(block.cv[c]),
                           _stream())
-            continue
-        if digits is None:
-            digits, dig_item = _modup(ctx, a.cv[1], cur, 1, True)
-        key_t, cap = ctx.switch_key(g, cur)
-        _lib.call("holmes_keyswitch_ext", ctx.handle, digits.data_ptr(), dig_item, cur, key_t.data_ptr(), cap, int(g),
-                  a.cv[0].data_ptr(), _item_stride(a.cv[0]), block.cv[0][b:b + 1].data_ptr(),
-                  block.cv[1][b:b + 1].data_ptr(), _item_stride(block.cv[0]), 1, _stream())
+        else:
+            switches.append((b, g, ctx.switch_key(g, cur)))
+    if not switches:
+        return block
+    digits, dig_item = _modup(ctx, a.cv[1], cur, 1, True)
+    lanes = _ks_lanes(ctx, len(switches))        # independent key switches: the caller's and side streams
+    for i, (b, g, (key_t, cap)) in enumerate(switches):
+        with torch.cuda.stream(lanes[i % len(lanes)]):
+            _lib.call("holmes_keyswitch_ext", ctx.handle, digits.data_ptr(), dig_item, cur, key_t.data_ptr(), cap,
+                      int(g), a.cv[0].data_ptr(), _item_stride(a.cv[0]), block.cv[0][b:b + 1].data_ptr(),
+                      block.cv[1][b:b + 1].data_ptr(), _item_stride(block.cv[0]), 1, _stream())
+    _ks_join(lanes)
     return block
 
 
