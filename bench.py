@@ -728,16 +728,18 @@ class _LayerSetup:
         self.setup_seconds = time.perf_counter() - t0
 
     def release_transients(self) -> None:
-        """Dead temporaries back to the allocator between steps (the reference runner's
+        """Between steps: dead temporaries back to the allocator (the reference runner's
         ``_release_transient_device_memory``, ``llama3fhe/application/session.py``, without its ``empty_cache``:
         with expandable segments the pool does not fragment across steps, and handing the segments back to the driver
-        makes the next step map them again, 0.6 s per layer)."""
+        makes the next step map them again, 0.6 s per layer), and the engine's reusable ModUp digits dropped, so that
+        a step never reuses work of an earlier one (the same input ciphertexts are fed to every step)."""
         import gc
 
         import torch
 
         gc.collect()
         torch.cuda.synchronize()
+        self.context.context.forget_digits()
 
     def layers(self):
         return self._stream_cls(loader=None, synthetic_weights=self.weights, approx_config=self.approx,
