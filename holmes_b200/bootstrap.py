@@ -558,8 +558,12 @@ def bootstrap(ct: F.Cipher, ctx, program: BootstrapProgram) -> F.Cipher:
     conj = F.homo_rotate(y, ctx.M - 1, ctx)
     re = F.homo_add(y, conj, ctx)
     im = F.homo_mul_i(F.homo_sub(conj, y, ctx), ctx)
-    re = eval_mod(re, program)
-    im = eval_mod(im, program)
+    # the real and imaginary parts go through EvalMod as one batch (same level and scale; every op acts item by item,
+    # so each part's residues are those of its own evaluation), half the launches of two evaluations
+    items = re.batch_size
+    both = eval_mod(F.pack_cipher_batch([re, im]), program)
+    re = both.cipher_like([c[:items] for c in both.cv], batch_size=items)
+    im = both.cipher_like([c[items:] for c in both.cv], batch_size=items)
     z = F.homo_add(re, F.homo_mul_i(im, ctx), ctx)
     # S2C's constant assumes the message at the nominal scale: z carries the input's message at scale
     # S_z Delta / m_scale.  The first S2C level also multiplies by rho = Delta / that, so the output lands exactly on
