@@ -936,11 +936,23 @@ def run_layer(args) -> None:
         d2h = sum(int(t.numel()) * 8 for t in outs)
         e2e_times.append(slowest(a.elapsed_time(b) / 1e3))
     # kernel-family breakdown: one more (untimed) step with the per-family CUDA-event timers
+    # the same step also carries the reference's own stage timers, with their device synchronisations on
+    from llama3fhe.backend import set_stage_sync
+
     F.OPTIMER.reset()
     F.OPTIMER.enabled = True
-    setup.forward()
+    setup.release_transients()
+    set_stage_sync(True)
+    prof = setup.forward()
+    set_stage_sync(False)
     F.OPTIMER.enabled = False
     ops = F.OPTIMER.summary()
+    phases = None
+    try:
+        phases = {str(k): round(float(v), 3) for k, v in prof.per_layer[0]["stage_seconds"].items()}
+    except (AttributeError, IndexError, KeyError, TypeError, ValueError):
+        pass
+    del prof
     if args.kernel_list and rank == 0:
         write_kernel_list(setup, args.kernel_list)
     check = setup.check(result) if args.check and rank == 0 else None
@@ -996,7 +1008,8 @@ def run_layer(args) -> None:
             "e2e": {"value": round(statistics.median(e2e_times), 4), "unit": "s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "steps": e2e_steps, "step_times_s": [round(t, 3) for t in e2e_times]},
             "setup_s": round(setup.setup_seconds, 1), "step_times_s": [round(t, 3) for t in times],
-            "device_memory_per_step": memory}
+            "device_memory_per_step": memory,
+            "phases_s": phases}
     if check is not None:
         line["parity_vs_reference_poly_model"] = check
     if args.write_volume:
