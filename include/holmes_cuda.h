@@ -12,6 +12,9 @@
  *   - NTT-domain words use the reference's root order (bench/cmp/kernels/holmes_encode.cu:65-71).
  * No function allocates device memory except holmes_ctx_create (its tables) and
  * holmes_ctx_create's secret upload; scratch buffers are passed in.
+ * A context is used by one host thread at a time: some calls (holmes_modup with one or two items)
+ * run independent parts on side streams and events the context owns (created on first use), and
+ * join them into `stream` before returning, so their work is ordered on `stream` as a whole.
  */
 #ifndef HOLMES_CUDA_H
 #define HOLMES_CUDA_H
