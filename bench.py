@@ -741,10 +741,21 @@ class _LayerSetup:
         torch.cuda.synchronize()
         self.context.context.forget_digits()
 
+    num_layers = 1
+
+    def set_layers(self, n: int) -> None:
+        """A model of ``n`` decoder layers (the same synthetic layer weights in every layer, layers after the first
+        refreshing their input as the reference's model does)."""
+        from llama3fhe.model import Llama3Model
+
+        self.num_layers = int(n)
+        self.model = Llama3Model(config=self.config, num_layers=self.num_layers, feature_layout=self.feature,
+                                 attention_layout=self.attention)
+
     def layers(self):
         return self._stream_cls(loader=None, synthetic_weights=self.weights, approx_config=self.approx,
                                 config=self.config, feature_layout=self.feature, attention_layout=self.attention,
-                                num_layers=1, rope_theta=self.rope_theta)
+                                num_layers=self.num_layers, rope_theta=self.rope_theta)
 
     def forward(self, inputs=None):
         return self.model.forward(self.hidden, crypto_context=self.context,
@@ -846,6 +857,50 @@ def write_kernel_list(setup, path: str) -> None:
         lines.append(f"| `{short}` | {n} | {us / 1e3:.1f} | {us / total:.3f} |")
     with open(path, "w", encoding="utf-8") as f:
         f.write("\n".join(lines) + "\n")
+
+
+def run_prefill_model(args) -> None:
+    """BASELINE config 4 at world size 1, as a supplementary measurement: ``--layers`` decoder layers of the reference's
+    own model (``Llama3Model.forward``, the synthetic one-layer preset's weights in every layer) on one GPU, after
+    ``--warmup`` single-layer forwards (the keys of every layer are generated on first use there); ``--steps`` timed
+    forwards of the whole model, CUDA events on the launching stream.  The full model takes minutes per step, so this
+    is not the bench's default step."""
+    import torch
+
+    from holmes_b200 import _lib
+
+    setup = _LayerSetup(seed=int(args.seed))
+    for _ in range(max(1, args.warmup)):
+        setup.forward()
+    torch.cuda.synchronize()
+    setup.set_layers(int(args.layers))
+    clocks = ClockSampler(0)
+    clocks.start()
+    clocks.ready()
+    n0 = ctypes_launches(_lib)
+    times = []
+    for _ in range(max(1, args.steps)):
+        setup.release_transients()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        result = setup.forward()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b) / 1e3)
+        del result
+    launches = (ctypes_launches(_lib) - n0) // max(1, args.steps)
+    ck = clocks.stop()
+    v = statistics.median(times)
+    print(json.dumps({"metric": f"encrypted Llama-3-8B prefill-128 latency ({setup.num_layers} layers, 1 B200)",
+                      "value": round(v, 3), "unit": "s", "n_gpus": 1, "steps": len(times),
+                      "warmup": f"{max(1, args.warmup)} single-layer forward(s)", "higher_is_better": False,
+                      "per_layer_s": round(v / setup.num_layers, 3), "step_times_s": [round(t, 3) for t in times],
+                      "dtype": "u64 (RNS residues, 59/60-bit primes)",
+                      "data": "synthetic (the reference's seeded one-layer preset's weights in every layer)",
+                      "config": {"workload": f"BASELINE config 4 at world size 1: {setup.num_layers}-layer encrypted "
+                                             "prefill of 128 tokens through the reference's Llama3Model.forward",
+                                 "ckks": "N=2^16, 38 limbs, dnum 5, 59/60-bit"},
+                      "gpu_launches": int(launches), "clocks": ck}), flush=True)
 
 
 def run_layer(args) -> None:
@@ -1242,6 +1297,8 @@ def main() -> None:
                     help="layer workload: record the per-family volume of one layer in profiles/layer_op_volume.json")
     ap.add_argument("--vs-ref", action="store_true",
                     help="with --kernel mac|encode: time the reference's in-tree kernel beside the engine's")
+    ap.add_argument("--layers", type=int, default=1,
+                    help="layer workload: decoder layers per step (> 1: the supplementary config-4 run at world size 1)")
     ap.add_argument("--kernel-list", default=None,
                     help="layer workload: write the per-kernel device time of one more (untimed) layer to this file")
     ap.add_argument("--cpu-rates-json", action="store_true", help=argparse.SUPPRESS)
@@ -1258,6 +1315,8 @@ def main() -> None:
         run_vs_ref(args)
     elif args.kernel:
         run_kernel(args)
+    elif args.workload == "layer" and args.layers > 1 and args.impl != "reference":
+        run_prefill_model(args)
     elif args.workload == "layer":
         run_reference_layer(args) if args.impl == "reference" else run_layer(args)
     elif args.workload == "bootstrap":
