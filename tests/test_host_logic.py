@@ -35,3 +35,21 @@ def test_easyfhe_from_numpy_tensor():
     assert type(t.to("cpu")) is torch.Tensor                     # host targets and dtype casts: plain Tensor.to
     np.testing.assert_array_equal(t.to(torch.float32).numpy(), a.astype(np.float32))
     np.testing.assert_array_equal(t.to(dtype=torch.int64).numpy(), a.astype(np.int64))
+
+
+def test_bench_traffic_and_cpu_estimate():
+    """The roofline line's traffic is the ncu capture's DRAM bytes scaled by algorithmic bytes (the capture's own
+    launch gives back its measured bytes); the CPU estimate is the sum over families of bytes times seconds per byte,
+    families without a sampled rate taking the key switch's."""
+    import os
+
+    import bench
+
+    with open(os.path.join(bench.ROOT, "profiles", "traffic.txt"), encoding="utf-8") as f:
+        family, measured, algorithmic = next(ln.split()[:3] for ln in f if ln.strip() and not ln.startswith("#"))
+    assert bench.measured_traffic(family, int(algorithmic)) == int(measured)
+    assert bench.measured_traffic(family, 2 * int(algorithmic)) == 2 * int(measured)
+    assert bench.measured_traffic("no-such-family", 1) is None
+    rates = {"rates_s_per_byte": {"keyswitch": 2e-9, "modup": 1e-9}}
+    volume = {"keyswitch": {"bytes": 10}, "modup": {"bytes": 100}, "rescale": {"bytes": 5}}
+    assert abs(bench.layer_cpu_estimate(volume, rates) - (10 * 2e-9 + 100 * 1e-9 + 5 * 2e-9)) < 1e-18
